@@ -1,0 +1,375 @@
+#!/usr/bin/env python
+"""Benchmark: Qwen3-8B-shaped W8A8 pipeline decode on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl s8b|reference]
+    torchrun --nproc-per-node N ... bench.py --gpus N ...     (N > 1: one stage per rank)
+
+A step is one decode step of every sequence: ``micro_batch`` (64) rows per micro-batch,
+``N`` micro-batches in flight through ``N`` stages of 36/N layers (``i*L//S`` split), KV cache
+pre-filled synthetically to 2048 tokens, random int8 weights. Per-GPU work is fixed as N grows
+(weak scaling): global batch = 64*N. Inputs (7.6 GB of weights, 10 GB of KV) are far larger
+than L2, so no flush is needed between steps.
+
+Prints ONE JSON line (rank 0). `value` is whole-job tokens/s with inputs resident in HBM
+(CUDA-graph replay, device timed with CUDA events, max over ranks); `e2e` is the same step
+through the engine's host API (token ids H2D from pinned memory, next tokens D2H, each step).
+`roofline` is the dominant kernel timed live with CUDA events; `cpu_baseline` is the CPU
+oracle on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "decode tokens/s (whole box) at 1/2/4/8 pipeline stages; % HBM roofline per stage"
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.path = tempfile.mktemp(suffix=".csv")
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ----------------------------------------------------------------------- CPU baseline ----
+
+def cpu_sample_tokens_per_s(batch=64, ctx=2048, n_layers=1, head_frac=16, seed=0):
+    """CPU oracle on a bounded sample of the config-3 step: `n_layers` Qwen3-8B layers at
+    batch `batch`, context `ctx`, plus 1/`head_frac` of the LM head; extrapolated to the full
+    36-layer step. Returns (tokens/s, seconds spent, sample description)."""
+    from oracle.kernels import gemm_acc, rope_tables
+    from oracle.model import PagedPool, Shape, layer_decode
+    from superl8_serve_b200.config import qwen3_8b
+
+    cfg = qwen3_8b()
+    s = Shape(cfg.vocab_size, cfg.hidden_size, 1, cfg.num_attention_heads,
+              cfg.num_key_value_heads, 128, cfg.intermediate_size, 1e-6, 1e6, ctx + 8, False)
+    rng = np.random.default_rng(seed)
+    H, F, D, nh, nkv = s.hidden_size, s.intermediate_size, 128, s.num_attention_heads, s.num_key_value_heads
+
+    def w(n, k):
+        return (rng.integers(-127, 128, (n, k), dtype=np.int8),
+                np.full(n, 0.02 / 73.3, dtype=np.float32))
+
+    g = lambda n: (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)  # noqa: E731
+    L = {"qkv": w((nh + 2 * nkv) * D, H), "o": w(H, nh * D), "gu": w(2 * F, H), "down": w(H, F),
+         "in_norm": g(H), "post_norm": g(H), "q_norm": g(D), "k_norm": g(D)}
+    pool = PagedPool(1, batch, nkv, ctx + 8, D)
+    pool.kc[:] = rng.integers(-127, 128, pool.kc.shape, dtype=np.int8)
+    pool.vc[:] = rng.integers(-127, 128, pool.vc.shape, dtype=np.int8)
+    pool.ks[:] = rng.uniform(0.01, 0.05, pool.ks.shape)
+    pool.vs[:] = rng.uniform(0.01, 0.05, pool.vs.shape)
+    slots = [pool.alloc() for _ in range(batch)]
+    pool.ensure_capacity(slots, [ctx + 1] * batch)
+    sm = pool.slot_mapping(slots, [ctx] * batch)
+    bt = pool.block_table(slots)
+    cl = np.full(batch, ctx + 1, dtype=np.int32)
+    tabs = rope_tables(D, ctx + 8, 1e6)
+    h = (0.5 * rng.standard_normal((batch, H))).astype(np.float32)
+    res = (rng.standard_normal((batch, H))).astype(np.float32)
+    t0 = time.perf_counter()
+    for _ in range(n_layers):
+        layer_decode(L, 0, h, res, [ctx] * batch, sm, bt, cl, pool, s, tabs)
+    t_layer = (time.perf_counter() - t0) / n_layers
+    hw, _ = w(cfg.vocab_size // head_frac, H)
+    xq = rng.integers(-127, 128, (batch, H), dtype=np.int8)
+    t1 = time.perf_counter()
+    gemm_acc(xq, hw)
+    t_head = (time.perf_counter() - t1) * head_frac
+    step = t_layer * cfg.num_hidden_layers + t_head
+    spent = time.perf_counter() - t0
+    desc = (f"oracle (numpy, BLAS GEMMs on {os.cpu_count()} host threads, Python attention loop):"
+            f" {n_layers} of 36 Qwen3-8B layers + 1/{head_frac} of the LM head at batch {batch},"
+            f" ctx {ctx}, extrapolated to one 36-layer decode step")
+    return batch / step, spent, desc
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    for _ in range(args.warmup):
+        cpu_sample_tokens_per_s(batch=args.batch, ctx=args.ctx, n_layers=1)
+    vals, spent = [], 0.0
+    desc = ""
+    for _ in range(args.steps):
+        v, t, desc = cpu_sample_tokens_per_s(batch=args.batch, ctx=args.ctx, n_layers=1)
+        vals.append(v)
+        spent += t
+    v = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": args.batch / v * 1000.0, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "qwen3-8b-shaped W8A8 decode, config 3", "micro_batch": args.batch,
+                   "ctx": args.ctx, "stages": 1, "note": "superl8 kernels are not vendored; "
+                   "the reference arm is the CPU oracle restating them"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------ GPU (N=1) ----
+
+def time_kernel(fn, reps: int) -> float:
+    """Average ms of fn() (one launch per call) with CUDA events on the current stream."""
+    fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        fn()
+    b.record()
+    b.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def kernel_rooflines(pipe, hbm_peak):
+    """Live CUDA-event timing of the two HBM-heavy kernels on the bench's own buffers,
+    rotating through all layers so every launch streams its operands from HBM."""
+    from superl8_serve_b200._lib import call, ptr, stream
+
+    r = pipe.runners[0]
+    mb = pipe.mbs[0][0]
+    M = pipe.rows[0]
+    L = len(r.model.layers)
+    out = {}
+    # W8A8 gate_up GEMM (largest weight matrix: 2F x H int8)
+    it = iter(range(10 ** 9))
+
+    def gemm():
+        li = next(it) % L
+        lw = r.model.layers[li]
+        call("s8b_gemm_w8a8", ptr(r.xq), ptr(r.xs), ptr(lw.gu_w), ptr(lw.gu_s), ptr(r.gu), 0, M,
+             lw.gu_w.shape[0], lw.gu_w.shape[1], 0, stream())
+
+    ms = time_kernel(gemm, 4 * L)
+    lw = r.model.layers[0]
+    N, K = lw.gu_w.shape
+    byts = N * K + N * 4 + M * K + M * 4 + M * N * 2
+    out["gemm_w8a8_gate_up"] = {"ms": ms, "bytes": byts, "gbs": byts / ms / 1e6,
+                                "launches_per_step": 36}
+    # paged decode attention (partition + combine) for one layer
+    it2 = iter(range(10 ** 9))
+
+    def attn():
+        li = next(it2) % L
+        kc, ks, vc, vs = r.pool.layer(li)
+        call("s8b_paged_decode_q8", ptr(r.q_i8), ptr(r.q_s), ptr(kc), ptr(ks), ptr(vc), ptr(vs),
+             ptr(mb.block_table), ptr(mb.context_lens), ptr(r.attn), ptr(r.xq), ptr(r.xs), M,
+             r.Hq, r.Hkv, r.D, r.pool.block_size, mb.block_table.shape[1], r.max_ctx, r.scale,
+             ptr(r.ws), r.ws.numel(), 0, stream())
+
+    ms = time_kernel(attn, 4 * L)
+    ctx = int(mb.context_lens[0].item())
+    byts = M * ctx * r.Hkv * (2 * 128 + 2 * 4) + M * r.Hq * (128 + 4) + M * r.Hq * 128 * 3
+    out["paged_decode_attention"] = {"ms": ms, "bytes": byts, "gbs": byts / ms / 1e6,
+                                     "launches_per_step": 36}
+    for v in out.values():
+        v["frac"] = v["gbs"] / hbm_peak
+    return out
+
+
+def step_bytes(cfg, batch, ctx, layers, last):
+    """Algorithmic HBM bytes of one decode step of one stage (weights + scales + KV read +
+    KV write + LM head on the last stage)."""
+    H, F, D = cfg.hidden_size, cfg.intermediate_size, 128
+    nh, nkv = cfg.num_attention_heads, cfg.num_key_value_heads
+    rows = (nh + 2 * nkv) * D + H + 2 * F + H
+    w = layers * (((nh + 2 * nkv) * D + 2 * F) * H + H * nh * D + H * F + 4 * rows)
+    kv = layers * batch * (ctx * nkv * (2 * D + 8) + nkv * (2 * D + 8))
+    head = (cfg.vocab_size * H + 4 * cfg.vocab_size) if last else 0
+    return w + kv + head
+
+
+def run_single(args):
+    from superl8_serve_b200 import _lib
+    from superl8_serve_b200.config import qwen3_8b
+    from superl8_serve_b200.engine import DecodePipeline
+    from superl8_serve_b200.runtime import StageModel
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    cfg = qwen3_8b()
+    B, ctx = args.batch, args.ctx
+    max_len = ctx + args.warmup + args.steps + 16
+    model = StageModel.synthetic(cfg, 0, cfg.num_hidden_layers, dev, first=True, last=True, seed=1)
+    pipe = DecodePipeline([model], batch=B, n_micro=1, max_len=max_len, wire_scheme=args.scheme)
+    pipe.pools[0].fill_random(seed=2)
+    pipe.add_sequences()
+    ids0 = np.random.default_rng(3).integers(0, cfg.vocab_size, B).tolist()
+    pipe.set_state([ctx] * B, ids0, reserve=args.warmup + args.steps + 8)
+    pipe._enqueue()  # eager warm-up: kernel attributes, lazy init
+    torch.cuda.synchronize()
+    pipe.set_state([ctx] * B, ids0, reserve=args.warmup + args.steps + 8)
+    pipe.capture()
+    for _ in range(args.warmup):
+        pipe.step()
+    torch.cuda.synchronize()
+    n0 = _lib.load().s8b_launch_count()
+    pipe._enqueue()  # count launches of one step (eager), then restore state
+    per_step_launches = _lib.load().s8b_launch_count() - n0
+    torch.cuda.synchronize()
+    pipe.set_state([ctx] * B, ids0, reserve=args.warmup + args.steps + 8)
+    for _ in range(args.warmup):
+        pipe.step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        time.sleep(0.3)
+        a.record()
+        for _ in range(args.steps):
+            pipe.step()
+        b.record()
+        b.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    value = B / (ms / 1e3)
+    clocks = clk.summary()
+
+    # e2e through the engine's host API: ids H2D (pinned), step, next ids D2H, every step
+    pipe.set_state([ctx] * B, ids0, reserve=args.warmup + args.steps + 8)
+    ids_h = torch.tensor(ids0, dtype=torch.int32).pin_memory()
+    out_h = torch.empty(B, dtype=torch.int32).pin_memory()
+    mbids = pipe.mbs[0][0].ids
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ea.record()
+    for _ in range(args.steps):
+        mbids[:B].copy_(ids_h, non_blocking=True)
+        pipe.step()
+        out_h.copy_(pipe.mbs[-1][0].ids[:B], non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        ids_h.copy_(out_h)
+    eb.record()
+    eb.synchronize()
+    e2e_ms = ea.elapsed_time(eb) / args.steps
+    hbm, _, peak_kind = peaks()
+    kr = kernel_rooflines(pipe, hbm)
+    top_name, top = max(kr.items(), key=lambda kv: kv[1]["ms"] * kv[1]["launches_per_step"])
+    sb = step_bytes(cfg, B, ctx, cfg.num_hidden_layers, True)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8 x int8 -> int32 GEMM, bf16 activations",
+        "data": "synthetic (random int8 weights, KV pre-filled with random codes)",
+        "config": {"workload": "qwen3-8b-shaped W8A8 decode (BASELINE config 3)",
+                   "micro_batch": B, "n_micro": 1, "global_batch": B, "ctx": ctx, "layers": 36,
+                   "block_size": 16, "parallelism": "pp1", "wire_scheme": args.scheme,
+                   "cuda_graph": True, "l2": "inputs (17.5 GB) > L2, no flush"},
+        "gpu_launches": int(per_step_launches) * args.steps,
+        "clocks": clocks,
+        "e2e": {"value": B / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 4 * B,
+                "d2h_bytes_per_step": 4 * B},
+        "roofline": {"bound": "hbm", "kernel": top_name, "achieved": top["gbs"], "peak": hbm,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": top["frac"],
+                     "traffic": None, "bytes_per_launch": top["bytes"],
+                     "ms_per_launch": top["ms"]},
+        "kernels": kr,
+        "step_roofline": {"bytes": sb, "achieved_gbs": sb / ms / 1e6, "frac": sb / ms / 1e6 / hbm},
+    }
+    if not args.no_cpu_baseline:
+        v, spent, desc = cpu_sample_tokens_per_s(batch=B, ctx=ctx, n_layers=1)
+        line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": os.cpu_count(),
+                                "kind": "port", "sample": desc, "seconds": spent}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="s8b", choices=["s8b", "reference"])
+    ap.add_argument("--batch", type=int, default=64, help="rows per micro-batch")
+    ap.add_argument("--ctx", type=int, default=2048)
+    ap.add_argument("--scheme", default="int8-had")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1 or args.gpus > 1:
+        from superl8_serve_b200.multistage import run_bench_multi
+
+        return run_bench_multi(args, METRIC, step_bytes, peaks, ClockSampler,
+                               cpu_sample_tokens_per_s)
+    return run_single(args)
+
+
+if __name__ == "__main__":
+    main()

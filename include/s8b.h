@@ -1,0 +1,205 @@
+/*
+ * s8b — B200 (sm_100a) kernels for superl8-serve's pipeline-parallel W8A8 decode step.
+ *
+ * Plain C ABI: device pointers, sizes and a CUDA stream (passed as void*, a cudaStream_t).
+ * The caller owns every buffer; apart from the set-up-time s8b_ipc_alloc, no entry point
+ * allocates device memory. Entry points that
+ * need scratch take a caller-provided workspace and report its size through a *_workspace_size
+ * query. Every entry point is stream-ordered, performs no host synchronisation and returns
+ * 0 on success or a negative S8B_ERR_* code (s8b_strerror gives the text). A kernel launch
+ * failure returns S8B_ERR_CUDA and records the cudaError_t for s8b_last_cuda_error().
+ *
+ * Citations name the superl8-serve (reference) interface each entry point replaces; the
+ * reference binds its kernels through the `superl8` Python package at those call sites.
+ *
+ * Numerics: every entry point reproduces the CPU oracle (oracle/ in this repository) bit for
+ * bit: binary32 operations in a fixed order without FMA contraction, int32 accumulation for
+ * integer products, float64 accumulation for the RMSNorm sums of squares.
+ */
+#ifndef S8B_H_
+#define S8B_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------------------- */
+#define S8B_OK 0
+#define S8B_ERR_SHAPE (-1)     /* unsupported or inconsistent sizes                        */
+#define S8B_ERR_DTYPE (-2)     /* unsupported activation dtype or codec scheme             */
+#define S8B_ERR_ALIGN (-3)     /* pointer or leading dimension not aligned as required     */
+#define S8B_ERR_CUDA (-4)      /* a CUDA runtime call or kernel launch failed              */
+#define S8B_ERR_PEER (-5)      /* peer memory not registered / peer access unavailable     */
+#define S8B_ERR_TIMEOUT (-6)   /* a bounded device-side wait gave up (see s8b_flag_status) */
+#define S8B_ERR_WORKSPACE (-7) /* workspace missing or smaller than *_workspace_size       */
+#define S8B_ERR_ARG (-8)       /* null pointer or invalid argument                         */
+
+/* ---- activation dtypes -------------------------------------------------------------- */
+#define S8B_BF16 0
+#define S8B_FP16 1
+
+/* ---- wire codec schemes (reference names: "fp16", "int8", "int8-had", "int4", "int4-had")
+ * fp16     : the activation itself, bit-exact (2 bytes/element, no scales)
+ * int8     : int8 codes, one fp32 scale per row
+ * int8-had : block-128 Hadamard, then int8 with one fp32 scale per row
+ * int4     : two's-complement nibbles (low nibble = even element), fp32 scale per 128-group
+ * int4-had : block-128 Hadamard, then int4 as above                                       */
+#define S8B_CODEC_FP16 0
+#define S8B_CODEC_INT8 1
+#define S8B_CODEC_INT8_HAD 2
+#define S8B_CODEC_INT4 3
+#define S8B_CODEC_INT4_HAD 4
+
+const char *s8b_strerror(int code);
+int s8b_version(void);
+int s8b_last_cuda_error(void);
+/* Number of kernels this library has launched in this process (all devices). */
+unsigned long long s8b_launch_count(void);
+
+/* Per-token int8 quantization of activations x[M,K]: scale = absmax/127,
+ * code = rint(x * (127/absmax)) clamped to +-127; an all-zero row gets scale 1.
+ * Replaces the activation-quant half of superl8.linear
+ * (superl8serve/layers/linear.py:122).                                                    */
+int s8b_quant_rows(const void *x, int dtype, int8_t *q, float *s, int M, int K, void *stream);
+
+/* Fused residual add + RMSNorm + per-token int8 quantization.
+ *   x = (residual_in ? h + residual_in : h) rounded to dtype; residual_out = x (nullable);
+ *   y = RMSNorm(x) * w (binary32, eps); optional y_out; (q, s) = quant_rows(y).
+ * Replaces superl8.rmsnorm (superl8serve/layers/norm.py:51) fused with the activation quant
+ * of the following superl8.linear.                                                        */
+int s8b_rmsnorm_quant(const void *h, const void *residual_in, void *residual_out,
+                      const void *w, float eps, int8_t *q, float *s, void *y_out, int M, int H,
+                      int dtype, void *stream);
+
+/* W8A8 GEMM on CUDA cores (dp4a), for small token counts:
+ *   acc[m,n] = sum_k xq[m,k]*w[n,k] (int32);  y[m,n] = dtype((float(acc)*xs[m])*ws[n]).
+ * out_kind 0: y is dtype [M,N];  out_kind 1: y is int32 [M,N] raw accumulators.
+ * K % 16 == 0; xq, w 16-byte aligned. Replaces superl8.linear / gemm_w8a8
+ * (superl8serve/layers/linear.py:122; superl8serve/layers/linear.py:9).                  */
+int s8b_gemm_w8a8(const int8_t *xq, const float *xs, const int8_t *w, const float *ws, void *y,
+                  int out_kind, int M, int N, int K, int dtype, void *stream);
+
+/* SwiGLU on a merged [gate | up] row (gu is [M, 2F]) followed by per-token int8 quant:
+ *   a = dtype(g / (1 + exp(-g))), y = dtype(a * u), (q, s) = quant_rows(y); y_out nullable.
+ * Replaces superl8.act_and_mul(x, "silu") (superl8serve/layers/activation.py:24) fused with
+ * the activation quant of the down projection.                                            */
+int s8b_silu_mul_quant(const void *gu, int M, int F, void *y_out, int8_t *q, float *s,
+                       int dtype, void *stream);
+
+/* Decode-branch head processing for a merged qkv row [M, (Hq+2*Hkv)*D]:
+ * per-head RMSNorm of q and k (q_norm_w, k_norm_w [D]), RoPE at positions[m] with binary32
+ * tables cos/sin [max_pos, D]; K rotated by the orthonormal Hadamard-128, rounded to dtype
+ * and written with V as int8 + fp32 scale into the paged stores at
+ * slot = block_table[m][pos/bs]*bs + pos%bs (or slot_mapping[m] when non-null);
+ * q is rotated by the same Hadamard and quantized per (token, head) into q_i8 [M,Hq,D],
+ * q_s [M,Hq]. q_out (nullable) receives the post-RoPE q in dtype.
+ * Replaces GQAAttention.forward's q/k norm + superl8.rope + quantize_kv_write_paged
+ * (superl8serve/layers/gqa_attention.py:66-74; superl8serve/engine/kv_cache.py:1095-1116).
+ * D must be 128.                                                                          */
+int s8b_qkv_post(const void *qkv, const int32_t *positions, const float *cos_tab,
+                 const float *sin_tab, int max_pos, const void *q_norm_w, const void *k_norm_w,
+                 float eps, int M, int Hq, int Hkv, int D, int8_t *q_i8, float *q_s,
+                 void *q_out, int8_t *kc, float *ks, int8_t *vc, float *vs,
+                 const int32_t *slot_mapping, const int32_t *block_table, int max_blocks,
+                 int block_size, int dtype, void *stream);
+
+/* Quantize-on-write of new K/V rows k, v [T, Hkv, D] into one layer's paged stores
+ * kc/vc [num_blocks, Hkv, bs, D] int8, ks/vs [num_blocks, Hkv, bs] fp32 at
+ * row (slot/bs*Hkv + h)*bs + slot%bs. rotate_k != 0 applies the Hadamard-128 to K first.
+ * Replaces superl8.quantize_kv_write_paged (superl8serve/engine/kv_cache.py:1108-1116). */
+int s8b_kv_write_paged(const void *k, const void *v, int8_t *kc, float *ks, int8_t *vc,
+                       float *vs, const int32_t *slot_mapping, int T, int Hkv, int D,
+                       int block_size, int rotate_k, int dtype, void *stream);
+
+/* Paged int8 GQA decode attention over block tables, for pre-quantized queries
+ * (q_i8 [B,Hq,D], q_s [B,Hq] from s8b_qkv_post). out [B, Hq*D] in dtype; out_q/out_s
+ * (nullable, together) additionally receive the per-token int8 quantization of the output
+ * row (the o_proj input). context_lens[b] >= 1 tokens of row b are attended; max_ctx is an
+ * upper bound on every context_lens[b] (sizes the partition grid). Workspace: see
+ * s8b_paged_decode_workspace_size. D must be 128.
+ * Replaces superl8.attn_paged_decode_cached (superl8serve/engine/kv_cache.py:1190-1201). */
+size_t s8b_paged_decode_workspace_size(int B, int Hq, int D, int max_ctx);
+int s8b_paged_decode_q8(const int8_t *q_i8, const float *q_s, const int8_t *kc, const float *ks,
+                        const int8_t *vc, const float *vs, const int32_t *block_table,
+                        const int32_t *context_lens, void *out, int8_t *out_q, float *out_s,
+                        int B, int Hq, int Hkv, int D, int block_size, int max_blocks,
+                        int max_ctx, float scale, void *workspace, size_t workspace_bytes,
+                        int dtype, void *stream);
+
+/* Same attention with the reference's query layout: q [B, Hq, D] in dtype (rotated and
+ * quantized internally into the workspace). out [B, Hq, D] in dtype.                     */
+size_t s8b_paged_decode_ref_workspace_size(int B, int Hq, int D, int max_ctx);
+int s8b_paged_decode(const void *q, const int8_t *kc, const float *ks, const int8_t *vc,
+                     const float *vs, const int32_t *block_table, const int32_t *context_lens,
+                     void *out, int B, int Hq, int Hkv, int D, int block_size, int max_blocks,
+                     int max_ctx, float scale, void *workspace, size_t workspace_bytes,
+                     int dtype, void *stream);
+
+/* Token embedding gather: out[m] = table[ids[m]] ([V, H] in dtype).
+ * Replaces VocabEmbedding.forward (superl8serve/layers/embedding.py:60-69).               */
+int s8b_embed(const int32_t *ids, const void *table, int M, int H, void *out, int dtype,
+              void *stream);
+
+/* Greedy sampling: out[m] = argmax_v logits[m, v] (lowest index on ties).
+ * Replaces the all-greedy Sampler fast path (superl8serve/layers/sampler.py:51-63).       */
+int s8b_argmax(const void *logits, int M, int V, int32_t *out, int dtype, void *stream);
+
+/* Inter-stage codec. Rows are the concatenation [a | b] of a [T, Da] and b [T, Db]
+ * (b nullable, Db = 0), i.e. the pipeline's packed (hidden, residual) boundary
+ * (superl8serve/dist/pipeline.py:246-250). (Da+Db) % 128 == 0 for the int4 / -had schemes.
+ * payload: fp16 -> dtype [T, D]; int8* -> int8 [T, D]; int4* -> uint8 [T, D/2].
+ * scales : int8* -> fp32 [T]; int4* -> fp32 [T, D/128]; fp16 -> unused.
+ * payload / scales may be peer pointers (another GPU's memory, peer access enabled or IPC
+ * mapped): the encoder then stores straight across NVLink.
+ * Replace superl8.compress_activation / decompress_activation as bound in send / recv
+ * (superl8serve/dist/__init__.py:189,300).                                                */
+size_t s8b_codec_payload_bytes(int T, int D, int scheme, int dtype);
+size_t s8b_codec_scale_count(int T, int D, int scheme);
+int s8b_codec_encode(const void *a, const void *b, int T, int Da, int Db, int scheme,
+                     void *payload, float *scales, int dtype, void *stream);
+int s8b_codec_decode(const void *payload, const float *scales, int T, int Da, int Db,
+                     int scheme, void *out_a, void *out_b, int dtype, void *stream);
+
+/* ---- stage-to-stage signalling (no counterpart call in the reference, whose send()
+ * synchronises the host instead: superl8serve/dist/__init__.py:243-247) ---------------------
+ * A flag is a uint32 in device memory, usually the consumer's, written by the producer across
+ * NVLink. Values are epochs read from device memory (*value + add), so a captured CUDA graph
+ * replays with fresh values. s8b_flag_set stores the epoch with release semantics at system
+ * scope after all prior work on the stream. s8b_flag_wait spins, stream-ordered on the
+ * device, until (int32)(*flag - epoch) >= 0 or about timeout_ns nanoseconds pass; on timeout
+ * it writes S8B_ERR_TIMEOUT, the awaited and the last seen value into status[0..2] (device
+ * memory, nullable) and returns, so the stream never hangs. s8b_counter_add bumps an epoch
+ * counter on the stream. s8b_flag_status reads status[0] from a host copy.              */
+int s8b_flag_set(uint32_t *flag, const uint32_t *value, uint32_t add, void *stream);
+int s8b_flag_wait(const uint32_t *flag, const uint32_t *value, uint32_t add,
+                  uint64_t timeout_ns, int32_t *status, void *stream);
+int s8b_counter_add(uint32_t *ctr, uint32_t inc, void *stream);
+int s8b_flag_status(const int32_t *status_host_copy);
+
+/* Decode-step bookkeeping on the device: positions[i] += inc; context_lens[i] =
+ * positions[i] + 1 (context_lens nullable). Keeps the per-step position state in device
+ * memory so a captured step replays correctly (the reference rebuilds these tensors on the
+ * host every step: superl8serve/dist/pipeline.py:1008-1009).                             */
+int s8b_advance(int32_t *positions, int32_t *context_lens, int M, int inc, void *stream);
+
+/* ---- set-up-time peer plumbing (not on the hot path) --------------------------------------
+ * The reference moves boundary codes with tensor.to(dst) inside send()
+ * (superl8serve/dist/__init__.py:214-247), which enables peer access implicitly. Here the
+ * producer's encoder stores straight into the consumer's buffer, so peer access (one
+ * process, several GPUs) or a CUDA IPC mapping (one process per GPU) is set up explicitly.
+ * s8b_ipc_alloc is the only allocating entry point: it cudaMalloc's an exportable receive
+ * buffer (zero-filled) and writes its s8b_ipc_handle_size()-byte handle to handle_out.      */
+int s8b_enable_peer_access(int dev, int peer);
+int s8b_ipc_handle_size(void);
+int s8b_ipc_alloc(size_t bytes, void **ptr, void *handle_out);
+int s8b_ipc_free(void *ptr);
+int s8b_ipc_open(const void *handle, void **ptr);
+int s8b_ipc_close(void *ptr);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* S8B_H_ */

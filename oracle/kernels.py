@@ -24,12 +24,32 @@ ATTN_PART = 256  # tokens per attention partition (fixes the accumulation order)
 
 # ------------------------------------------------------------------------ W8A8 GEMM ----
 
+_F32_CACHE: dict[int, tuple[np.ndarray, np.ndarray]] = {}
+_KCHUNK = 1024  # 1024 * 127^2 < 2^24: every fp32 partial sum of a chunk is an exact integer
+
+
+def _f32_weight(wq: np.ndarray) -> np.ndarray:
+    hit = _F32_CACHE.get(id(wq))
+    if hit is not None and hit[0] is wq:
+        return hit[1]
+    wf = wq.astype(np.float32)
+    if wq.size >= (1 << 20):
+        _F32_CACHE[id(wq)] = (wq, wf)
+    return wf
+
+
 def gemm_acc(xq: np.ndarray, wq: np.ndarray) -> np.ndarray:
     """int32 accumulators acc[m, n] = sum_k xq[m, k] * wq[n, k] (exact: |acc| < 2^31).
 
-    Computed as a float64 GEMM on int8-valued operands, exact because K*127^2 < 2^53."""
-    acc = xq.astype(np.float64) @ wq.astype(np.float64).T
-    return acc.astype(np.int64).astype(np.int32)
+    Computed as float32 GEMMs over K-chunks of 1024 (each chunk's partial sums are integers
+    below 2^24, hence exact in any summation order) and summed in int64."""
+    wf = _f32_weight(wq)
+    xf = xq.astype(np.float32)
+    K = xq.shape[-1]
+    acc = np.zeros((xq.shape[0], wq.shape[0]), dtype=np.int64)
+    for k0 in range(0, K, _KCHUNK):
+        acc += (xf[:, k0:k0 + _KCHUNK] @ wf[:, k0:k0 + _KCHUNK].T).astype(np.int64)
+    return acc.astype(np.int32)
 
 
 def linear_w8a8(x: np.ndarray, wq: np.ndarray, ws: np.ndarray) -> np.ndarray:

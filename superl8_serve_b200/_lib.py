@@ -1,0 +1,122 @@
+"""ctypes binding of ``libs8b.so`` (the C ABI declared in ``include/s8b.h``).
+
+There is no fallback: if the library is missing, or a tensor handed to it is not on a CUDA
+device, the call raises. Status codes other than 0 become ``S8BError``.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "libs8b.so"
+
+S8B_BF16, S8B_FP16 = 0, 1
+CODEC = {"fp16": 0, "int8": 1, "int8-had": 2, "int4": 3, "int4-had": 4}
+ERR_TIMEOUT = -6
+
+_vp, _i, _f, _sz, _u32, _u64 = C.c_void_p, C.c_int, C.c_float, C.c_size_t, C.c_uint32, C.c_uint64
+
+# name -> (restype, argtypes)
+SIGNATURES: dict[str, tuple] = {
+    "s8b_strerror": (C.c_char_p, [_i]),
+    "s8b_version": (_i, []),
+    "s8b_last_cuda_error": (_i, []),
+    "s8b_launch_count": (C.c_ulonglong, []),
+    "s8b_quant_rows": (_i, [_vp, _i, _vp, _vp, _i, _i, _vp]),
+    "s8b_rmsnorm_quant": (_i, [_vp, _vp, _vp, _vp, _f, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "s8b_gemm_w8a8": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
+    "s8b_silu_mul_quant": (_i, [_vp, _i, _i, _vp, _vp, _vp, _i, _vp]),
+    "s8b_qkv_post": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp, _f, _i, _i, _i, _i, _vp, _vp, _vp,
+                          _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "s8b_kv_write_paged": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
+    "s8b_paged_decode_workspace_size": (_sz, [_i, _i, _i, _i]),
+    "s8b_paged_decode_q8": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i,
+                                 _i, _i, _i, _i, _i, _f, _vp, _sz, _i, _vp]),
+    "s8b_paged_decode_ref_workspace_size": (_sz, [_i, _i, _i, _i]),
+    "s8b_paged_decode": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i,
+                              _i, _f, _vp, _sz, _i, _vp]),
+    "s8b_embed": (_i, [_vp, _vp, _i, _i, _vp, _i, _vp]),
+    "s8b_argmax": (_i, [_vp, _i, _i, _vp, _i, _vp]),
+    "s8b_codec_payload_bytes": (_sz, [_i, _i, _i, _i]),
+    "s8b_codec_scale_count": (_sz, [_i, _i, _i]),
+    "s8b_codec_encode": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _i, _vp]),
+    "s8b_codec_decode": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _i, _vp]),
+    "s8b_flag_set": (_i, [_vp, _vp, _u32, _vp]),
+    "s8b_flag_wait": (_i, [_vp, _vp, _u32, _u64, _vp, _vp]),
+    "s8b_counter_add": (_i, [_vp, _u32, _vp]),
+    "s8b_flag_status": (_i, [_vp]),
+    "s8b_advance": (_i, [_vp, _vp, _i, _i, _vp]),
+    "s8b_enable_peer_access": (_i, [_i, _i]),
+    "s8b_ipc_handle_size": (_i, []),
+    "s8b_ipc_alloc": (_i, [_sz, _vp, _vp]),
+    "s8b_ipc_free": (_i, [_vp]),
+    "s8b_ipc_open": (_i, [_vp, _vp]),
+    "s8b_ipc_close": (_i, [_vp]),
+}
+
+
+class S8BError(RuntimeError):
+    def __init__(self, name: str, code: int, detail: str = ""):
+        self.code = code
+        super().__init__(f"{name} failed: {code} ({strerror(code)}){detail}")
+
+
+_LIB: C.CDLL | None = None
+
+
+def load() -> C.CDLL:
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not LIB_PATH.exists():
+        raise RuntimeError(
+            f"{LIB_PATH} is not built; run `python -m superl8_serve_b200.csrc.build` "
+            "(there is no CPU fallback for the s8b kernels)")
+    lib = C.CDLL(os.fspath(LIB_PATH))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _LIB = lib
+    return lib
+
+
+def strerror(code: int) -> str:
+    return load().s8b_strerror(code).decode()
+
+
+def call(name: str, *args) -> int:
+    fn = getattr(load(), name)
+    rc = fn(*args)
+    if rc != 0:
+        detail = ""
+        if rc == -4:
+            detail = f"; cudaError {load().s8b_last_cuda_error()}"
+        raise S8BError(name, rc, detail)
+    return rc
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise RuntimeError("s8b kernels take CUDA tensors only (no CPU fallback)")
+    if not t.is_contiguous():
+        raise RuntimeError("s8b kernels take contiguous tensors")
+    return t.data_ptr()
+
+
+def stream(device=None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.bfloat16:
+        return S8B_BF16
+    if dt == torch.float16:
+        return S8B_FP16
+    raise RuntimeError(f"s8b activation dtype must be bf16 or fp16, got {dt}")

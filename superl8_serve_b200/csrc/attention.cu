@@ -1,0 +1,495 @@
+// Attention side of the decode step on paged int8 KV.
+//
+// KV layout (one layer): codes [num_blocks, Hkv, bs, 128] int8, scales [num_blocks, Hkv, bs]
+// fp32; token (block, off) of kv head g lives at row (block*Hkv + g)*bs + off, so the bs
+// tokens of one (block, head) are 128*bs contiguous bytes. K is stored Hadamard-rotated; the
+// query is rotated by the same orthonormal matrix, so q.k is unchanged.
+//
+// Decode attention runs in two kernels:
+//  1. partitions: one CTA per (256-token partition, kv head, row). It stages the partition's
+//     K and V codes with cp.async (144-byte K row pitch keeps 16-byte shared loads
+//     conflict-free), forms exact int32 q.k dot products with dp4a, and accumulates
+//     softmax numerator / denominator per query head in token order.
+//  2. combine: one CTA per row merges the partitions in index order, writes the output in the
+//     activation dtype and, fused, its per-token int8 codes for the o_proj GEMM.
+// The fixed partition size and accumulation order make the result bit-identical to the CPU
+// oracle (oracle/kernels.py: paged_decode).
+#include "common.cuh"
+
+namespace s8b {
+namespace {
+
+constexpr int kPart = 256;     // tokens per partition
+constexpr int kKPitch = 144;   // shared-memory pitch of a K row (128 codes + 16 pad)
+constexpr int kHd = 128;       // head dim handled by these kernels
+
+__device__ __forceinline__ int slot_of(const int32_t *slot_mapping, const int32_t *block_table,
+                                       int max_blocks, int bs, int m, int pos) {
+  if (slot_mapping) return slot_mapping[m];
+  return block_table[static_cast<size_t>(m) * max_blocks + pos / bs] * bs + pos % bs;
+}
+
+template <typename T>
+__device__ __forceinline__ void load4(const T *p, float v[4]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = to_f32(p[i]);
+}
+
+// Per-head RMSNorm over 128 elements held 4 per lane.
+template <typename T>
+__device__ __forceinline__ void head_rmsnorm(float v[4], const T *w, float eps) {
+  double ss = 0.0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) ss += static_cast<double>(v[i]) * static_cast<double>(v[i]);
+  ss = warp_sum_d(ss);
+  const float r = rms_factor(ss, kHd, eps);
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    v[i] = round_to<T>(__fmul_rn(__fmul_rn(v[i], r), to_f32(w[4 * lane + i])));
+}
+
+// rotate-half RoPE: out[e] = x[e]*cos[e] + rot[e]*sin[e], rot = (-x[64:], x[:64]).
+template <typename T>
+__device__ __forceinline__ void head_rope(float v[4], const float *cs, const float *sn) {
+  const int lane = threadIdx.x & 31;
+  float o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o[i] = __shfl_xor_sync(0xffffffffu, v[i], 16);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int e = 4 * lane + i;
+    const float rot = lane < 16 ? -o[i] : o[i];
+    v[i] = round_to<T>(__fadd_rn(__fmul_rn(v[i], cs[e]), __fmul_rn(rot, sn[e])));
+  }
+}
+
+// Quantize 128 values (4 per lane) to int8 with one scale; writes 4 codes per lane.
+__device__ __forceinline__ float head_quant_store(const float v[4], int8_t *dst) {
+  float a = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+  a = warp_max(a);
+  const QParams p = qparams(a, 127.0f);
+  char4 c;
+  c.x = static_cast<signed char>(qcode(v[0], p.inv, 127));
+  c.y = static_cast<signed char>(qcode(v[1], p.inv, 127));
+  c.z = static_cast<signed char>(qcode(v[2], p.inv, 127));
+  c.w = static_cast<signed char>(qcode(v[3], p.inv, 127));
+  reinterpret_cast<char4 *>(dst)[threadIdx.x & 31] = c;
+  return p.scale;
+}
+
+// K path shared by qkv_post and kv_write: Hadamard, round to T, quantize, store.
+template <typename T>
+__device__ __forceinline__ void store_k_row(float v[4], bool rotate, int8_t *kc, float *ks,
+                                            size_t row) {
+  if (rotate) {
+    fwht128_warp(v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = round_to<T>(__fmul_rn(v[i], kHadScale));
+  }
+  const float sc = head_quant_store(v, kc + row * kHd);
+  if ((threadIdx.x & 31) == 0) ks[row] = sc;
+}
+
+__device__ __forceinline__ void store_v_row(const float v[4], int8_t *vc, float *vs, size_t row) {
+  const float sc = head_quant_store(v, vc + row * kHd);
+  if ((threadIdx.x & 31) == 0) vs[row] = sc;
+}
+
+// --------------------------------------------------------------------------- qkv_post ----
+template <typename T>
+__global__ void __launch_bounds__(512)
+    qkv_post_kernel(const T *__restrict__ qkv, const int32_t *__restrict__ positions,
+                    const float *__restrict__ cos_tab, const float *__restrict__ sin_tab,
+                    const T *__restrict__ qn, const T *__restrict__ kn, float eps, int Hq,
+                    int Hkv, int8_t *__restrict__ q_i8, float *__restrict__ q_s,
+                    T *__restrict__ q_out, int8_t *__restrict__ kc, float *__restrict__ ks,
+                    int8_t *__restrict__ vc, float *__restrict__ vs,
+                    const int32_t *__restrict__ slot_mapping,
+                    const int32_t *__restrict__ block_table, int max_blocks, int bs) {
+  const int m = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int HR = Hq + 2 * Hkv;
+  const int pos = positions[m];
+  const int slot = slot_of(slot_mapping, block_table, max_blocks, bs, m, pos);
+  const int blk = slot / bs, off = slot % bs;
+  const float *cs = cos_tab + static_cast<size_t>(pos) * kHd;
+  const float *sn = sin_tab + static_cast<size_t>(pos) * kHd;
+  for (int hr = warp; hr < HR; hr += nwarps) {
+    float v[4];
+    load4(qkv + (static_cast<size_t>(m) * HR + hr) * kHd + 4 * lane, v);
+    if (hr < Hq) {
+      head_rmsnorm<T>(v, qn, eps);
+      head_rope<T>(v, cs, sn);
+      if (q_out) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          q_out[(static_cast<size_t>(m) * Hq + hr) * kHd + 4 * lane + i] = from_f32<T>(v[i]);
+      }
+      fwht128_warp(v);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = __fmul_rn(v[i], kHadScale);
+      const float sc = head_quant_store(v, q_i8 + (static_cast<size_t>(m) * Hq + hr) * kHd);
+      if (lane == 0) q_s[static_cast<size_t>(m) * Hq + hr] = sc;
+    } else if (hr < Hq + Hkv) {
+      const int g = hr - Hq;
+      head_rmsnorm<T>(v, kn, eps);
+      head_rope<T>(v, cs, sn);
+      store_k_row<T>(v, true, kc, ks, (static_cast<size_t>(blk) * Hkv + g) * bs + off);
+    } else {
+      const int g = hr - Hq - Hkv;
+      store_v_row(v, vc, vs, (static_cast<size_t>(blk) * Hkv + g) * bs + off);
+    }
+  }
+}
+
+// ----------------------------------------------------------------------- kv_write_paged ----
+template <typename T>
+__global__ void __launch_bounds__(256)
+    kv_write_kernel(const T *__restrict__ k, const T *__restrict__ v, int8_t *__restrict__ kc,
+                    float *__restrict__ ks, int8_t *__restrict__ vc, float *__restrict__ vs,
+                    const int32_t *__restrict__ slot_mapping, int Hkv, int bs, int rotate_k) {
+  const int t = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int slot = slot_mapping[t];
+  const int blk = slot / bs, off = slot % bs;
+  for (int hr = warp; hr < 2 * Hkv; hr += nwarps) {
+    const int g = hr % Hkv;
+    float x[4];
+    const size_t row = (static_cast<size_t>(blk) * Hkv + g) * bs + off;
+    if (hr < Hkv) {
+      load4(k + (static_cast<size_t>(t) * Hkv + g) * kHd + 4 * lane, x);
+      store_k_row<T>(x, rotate_k != 0, kc, ks, row);
+    } else {
+      load4(v + (static_cast<size_t>(t) * Hkv + g) * kHd + 4 * lane, x);
+      store_v_row(x, vc, vs, row);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ q rotate + quantize ----
+template <typename T>
+__global__ void __launch_bounds__(256) q_rotate_quant_kernel(const T *__restrict__ q, int Hq,
+                                                             int8_t *__restrict__ q_i8,
+                                                             float *__restrict__ q_s) {
+  const int b = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  for (int h = warp; h < Hq; h += nwarps) {
+    float v[4];
+    const size_t base = (static_cast<size_t>(b) * Hq + h) * kHd;
+    load4(q + base + 4 * lane, v);
+    fwht128_warp(v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __fmul_rn(v[i], kHadScale);
+    const float sc = head_quant_store(v, q_i8 + base);
+    if (lane == 0) q_s[static_cast<size_t>(b) * Hq + h] = sc;
+  }
+}
+
+// ------------------------------------------------------------------- decode partitions ----
+struct PartSmem {
+  static size_t bytes(int G) {
+    return static_cast<size_t>(kPart) * kKPitch + static_cast<size_t>(kPart) * kHd +
+           2 * kPart * sizeof(float) + static_cast<size_t>(G) * kPart * sizeof(float) +
+           static_cast<size_t>(G) * kHd + 3 * 8 * sizeof(float);
+  }
+};
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
+}
+
+__global__ void __launch_bounds__(1024)
+    attn_partition_kernel(const int8_t *__restrict__ q_i8, const float *__restrict__ q_s,
+                          const int8_t *__restrict__ kc, const float *__restrict__ ks,
+                          const int8_t *__restrict__ vc, const float *__restrict__ vs,
+                          const int32_t *__restrict__ block_table,
+                          const int32_t *__restrict__ context_lens, int Hq, int Hkv, int bs,
+                          int max_blocks, int P, float scale, float *__restrict__ part_o,
+                          float *__restrict__ part_ml) {
+  const int p = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int n = context_lens[b];
+  const int lo = p * kPart;
+  if (lo >= n) return;
+  const int cnt = min(kPart, n - lo);
+  const int G = Hq / Hkv;
+  const int tid = threadIdx.x, nthreads = blockDim.x;
+
+  extern __shared__ __align__(16) uint8_t smem[];
+  int8_t *Ks = reinterpret_cast<int8_t *>(smem);
+  int8_t *Vs = Ks + kPart * kKPitch;
+  float *ksc = reinterpret_cast<float *>(Vs + kPart * kHd);
+  float *vsc = ksc + kPart;
+  float *S = vsc + kPart;                                  // [G][kPart]
+  int8_t *Qs = reinterpret_cast<int8_t *>(S + G * kPart);  // [G][128]
+  float *qsc = reinterpret_cast<float *>(Qs + G * kHd);    // [G]
+  float *mx = qsc + 8;                                     // [G]
+
+  // Stage K, V codes (cp.async) and their scales for the partition's tokens.
+  const int32_t *bt = block_table + static_cast<size_t>(b) * max_blocks;
+  const int blk0 = lo / bs;
+  for (int idx = tid; idx < cnt * 8; idx += nthreads) {
+    const int t = idx >> 3, c = idx & 7;
+    const int j = lo + t;
+    const size_t row = (static_cast<size_t>(bt[blk0 + t / bs]) * Hkv + g) * bs + (j % bs);
+    cp_async16(Ks + t * kKPitch + c * 16, kc + row * kHd + c * 16);
+    cp_async16(Vs + t * kHd + c * 16, vc + row * kHd + c * 16);
+  }
+  for (int t = tid; t < cnt; t += nthreads) {
+    const int j = lo + t;
+    const size_t row = (static_cast<size_t>(bt[blk0 + t / bs]) * Hkv + g) * bs + (j % bs);
+    ksc[t] = ks[row];
+    vsc[t] = vs[row];
+  }
+  for (int idx = tid; idx < G * (kHd / 16); idx += nthreads) {
+    const int h = idx / (kHd / 16), c = idx % (kHd / 16);
+    reinterpret_cast<int4 *>(Qs + h * kHd)[c] =
+        reinterpret_cast<const int4 *>(q_i8 + (static_cast<size_t>(b) * Hq + g * G + h) * kHd)[c];
+  }
+  if (tid < G) qsc[tid] = __fmul_rn(q_s[static_cast<size_t>(b) * Hq + g * G + tid], scale);
+  cp_async_wait_all();
+  __syncthreads();
+
+  // Scores s = (f32(q.k) * (q_s*scale)) * k_s, exact int32 dot products.
+  for (int pr = tid; pr < G * kPart; pr += nthreads) {
+    const int h = pr / kPart, t = pr % kPart;
+    if (t >= cnt) continue;
+    const int4 *kr = reinterpret_cast<const int4 *>(Ks + t * kKPitch);
+    const int4 *qr = reinterpret_cast<const int4 *>(Qs + h * kHd);
+    int acc = 0;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const int4 a = kr[c], q = qr[c];
+      acc = __dp4a(a.x, q.x, acc);
+      acc = __dp4a(a.y, q.y, acc);
+      acc = __dp4a(a.z, q.z, acc);
+      acc = __dp4a(a.w, q.w, acc);
+    }
+    S[h * kPart + t] = __fmul_rn(__fmul_rn(static_cast<float>(acc), qsc[h]), ksc[t]);
+  }
+  __syncthreads();
+  const int lane = tid & 31, warp = tid >> 5, nwarps = nthreads >> 5;
+  for (int h = warp; h < G; h += nwarps) {
+    float m = -__int_as_float(0x7f800000);
+    for (int t = lane; t < cnt; t += 32) m = fmaxf(m, S[h * kPart + t]);
+    m = warp_max(m);
+    if (lane == 0) mx[h] = m;
+  }
+  __syncthreads();
+  for (int pr = tid; pr < G * kPart; pr += nthreads) {
+    const int h = pr / kPart, t = pr % kPart;
+    if (t < cnt) S[pr] = exp_s8b(__fsub_rn(S[pr], mx[h]));
+  }
+  __syncthreads();
+
+  // Numerator and denominator, accumulated sequentially in token order.
+  for (int hd = tid; hd < G * kHd; hd += nthreads) {
+    const int h = hd / kHd, d = hd % kHd;
+    const float *e = S + h * kPart;
+    float o = 0.0f, l = 0.0f;
+    for (int t = 0; t < cnt; ++t) {
+      const float et = e[t];
+      const float v = __fmul_rn(static_cast<float>(Vs[t * kHd + d]), vsc[t]);
+      o = __fadd_rn(o, __fmul_rn(et, v));
+      l = __fadd_rn(l, et);
+    }
+    const size_t hq = static_cast<size_t>(b) * Hq + g * G + h;
+    part_o[(hq * P + p) * kHd + d] = o;
+    if (d == 0) {
+      part_ml[(hq * P + p) * 2 + 0] = mx[h];
+      part_ml[(hq * P + p) * 2 + 1] = l;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------ combine ----
+template <typename T>
+__global__ void __launch_bounds__(256)
+    attn_combine_kernel(const float *__restrict__ part_o, const float *__restrict__ part_ml,
+                        const int32_t *__restrict__ context_lens, int Hq, int P,
+                        T *__restrict__ out, int8_t *__restrict__ out_q,
+                        float *__restrict__ out_s) {
+  extern __shared__ float cs[];
+  float *W = cs;                  // [Hq][P]
+  float *L = W + Hq * P;          // [Hq]
+  float *row = L + Hq;            // [Hq*128]
+  __shared__ float red[32];
+  const int b = blockIdx.x;
+  const int n = context_lens[b];
+  const int np = (n + kPart - 1) / kPart;
+  for (int h = threadIdx.x; h < Hq; h += blockDim.x) {
+    const float *ml = part_ml + (static_cast<size_t>(b) * Hq + h) * P * 2;
+    float M = -__int_as_float(0x7f800000);
+    for (int p = 0; p < np; ++p) M = fmaxf(M, ml[2 * p]);
+    float Ls = 0.0f;
+    for (int p = 0; p < np; ++p) {
+      const float w = exp_s8b(__fsub_rn(ml[2 * p], M));
+      W[h * P + p] = w;
+      Ls = __fadd_rn(Ls, __fmul_rn(w, ml[2 * p + 1]));
+    }
+    L[h] = Ls;
+  }
+  __syncthreads();
+  float amax = 0.0f;
+  for (int i = threadIdx.x; i < Hq * kHd; i += blockDim.x) {
+    const int h = i / kHd, d = i % kHd;
+    const float *po = part_o + (static_cast<size_t>(b) * Hq + h) * P * kHd + d;
+    float O = 0.0f;
+    for (int p = 0; p < np; ++p) O = __fadd_rn(O, __fmul_rn(W[h * P + p], po[p * kHd]));
+    const float y = round_to<T>(__fdiv_rn(O, L[h]));
+    out[static_cast<size_t>(b) * Hq * kHd + i] = from_f32<T>(y);
+    row[i] = y;
+    amax = fmaxf(amax, fabsf(y));
+  }
+  if (!out_q) return;
+  amax = block_max(amax, red);
+  const QParams qp = qparams(amax, 127.0f);
+  for (int i = threadIdx.x; i < Hq * kHd; i += blockDim.x)
+    out_q[static_cast<size_t>(b) * Hq * kHd + i] = static_cast<int8_t>(qcode(row[i], qp.inv, 127));
+  if (threadIdx.x == 0) out_s[b] = qp.scale;
+}
+
+inline int num_parts(int max_ctx) { return (max_ctx + kPart - 1) / kPart; }
+
+size_t part_bytes(int B, int Hq, int max_ctx) {
+  const size_t P = num_parts(max_ctx);
+  return static_cast<size_t>(B) * Hq * P * (kHd + 2) * sizeof(float);
+}
+
+template <typename T>
+int launch_decode(const int8_t *q_i8, const float *q_s, const int8_t *kc, const float *ks,
+                  const int8_t *vc, const float *vs, const int32_t *block_table,
+                  const int32_t *context_lens, void *out, int8_t *out_q, float *out_s, int B,
+                  int Hq, int Hkv, int bs, int max_blocks, int max_ctx, float scale,
+                  float *part, cudaStream_t st) {
+  const int P = num_parts(max_ctx);
+  const int G = Hq / Hkv;
+  float *part_o = part;
+  float *part_ml = part + static_cast<size_t>(B) * Hq * P * kHd;
+  const size_t smem = PartSmem::bytes(G);
+  ensure_smem(reinterpret_cast<const void *>(attn_partition_kernel), smem);
+  attn_partition_kernel<<<dim3(P, Hkv, B), G * kHd, smem, st>>>(
+      q_i8, q_s, kc, ks, vc, vs, block_table, context_lens, Hq, Hkv, bs, max_blocks, P, scale,
+      part_o, part_ml);
+  const size_t csmem = (static_cast<size_t>(Hq) * P + Hq + static_cast<size_t>(Hq) * kHd) * sizeof(float);
+  auto comb = attn_combine_kernel<T>;
+  ensure_smem(reinterpret_cast<const void *>(comb), csmem);
+  comb<<<B, 256, csmem, st>>>(part_o, part_ml, context_lens, Hq, P, static_cast<T *>(out), out_q,
+                              out_s);
+  return check_launch(2);
+}
+
+int check_attn_shape(int B, int Hq, int Hkv, int D, int bs, int max_blocks, int max_ctx) {
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || Hq / Hkv > 8 || D != kHd)
+    return S8B_ERR_SHAPE;
+  if (bs <= 0 || kPart % bs != 0 || max_ctx <= 0 || max_blocks * bs < max_ctx)
+    return S8B_ERR_SHAPE;
+  if (num_parts(max_ctx) * Hq > 8192) return S8B_ERR_SHAPE;  // combine smem bound
+  return S8B_OK;
+}
+
+}  // namespace
+}  // namespace s8b
+
+using namespace s8b;
+
+extern "C" int s8b_qkv_post(const void *qkv, const int32_t *positions, const float *cos_tab,
+                            const float *sin_tab, int max_pos, const void *q_norm_w,
+                            const void *k_norm_w, float eps, int M, int Hq, int Hkv, int D,
+                            int8_t *q_i8, float *q_s, void *q_out, int8_t *kc, float *ks,
+                            int8_t *vc, float *vs, const int32_t *slot_mapping,
+                            const int32_t *block_table, int max_blocks, int block_size,
+                            int dtype, void *stream) {
+  if (!qkv || !positions || !cos_tab || !sin_tab || !q_norm_w || !k_norm_w || !q_i8 || !q_s ||
+      !kc || !ks || !vc || !vs || (!slot_mapping && !block_table))
+    return S8B_ERR_ARG;
+  if (M < 0 || D != kHd || Hq <= 0 || Hkv <= 0 || block_size <= 0 || max_pos <= 0)
+    return S8B_ERR_SHAPE;
+  if (!aligned(q_i8, 16) || !aligned(kc, 16) || !aligned(vc, 16)) return S8B_ERR_ALIGN;
+  if (M == 0) return S8B_OK;
+  S8B_DISPATCH_DTYPE(dtype, T,
+                     qkv_post_kernel<T><<<M, 512, 0, (cudaStream_t)stream>>>(
+                         static_cast<const T *>(qkv), positions, cos_tab, sin_tab,
+                         static_cast<const T *>(q_norm_w), static_cast<const T *>(k_norm_w), eps,
+                         Hq, Hkv, q_i8, q_s, static_cast<T *>(q_out), kc, ks, vc, vs,
+                         slot_mapping, block_table, max_blocks, block_size));
+  return check_launch();
+}
+
+extern "C" int s8b_kv_write_paged(const void *k, const void *v, int8_t *kc, float *ks, int8_t *vc,
+                                  float *vs, const int32_t *slot_mapping, int T_, int Hkv, int D,
+                                  int block_size, int rotate_k, int dtype, void *stream) {
+  if (!k || !v || !kc || !ks || !vc || !vs || !slot_mapping) return S8B_ERR_ARG;
+  if (T_ < 0 || Hkv <= 0 || D != kHd || block_size <= 0) return S8B_ERR_SHAPE;
+  if (!aligned(kc, 16) || !aligned(vc, 16)) return S8B_ERR_ALIGN;
+  if (T_ == 0) return S8B_OK;
+  S8B_DISPATCH_DTYPE(dtype, T,
+                     kv_write_kernel<T><<<T_, 256, 0, (cudaStream_t)stream>>>(
+                         static_cast<const T *>(k), static_cast<const T *>(v), kc, ks, vc, vs,
+                         slot_mapping, Hkv, block_size, rotate_k));
+  return check_launch();
+}
+
+extern "C" size_t s8b_paged_decode_workspace_size(int B, int Hq, int D, int max_ctx) {
+  (void)D;
+  return part_bytes(B, Hq, max_ctx);
+}
+
+extern "C" int s8b_paged_decode_q8(const int8_t *q_i8, const float *q_s, const int8_t *kc,
+                                   const float *ks, const int8_t *vc, const float *vs,
+                                   const int32_t *block_table, const int32_t *context_lens,
+                                   void *out, int8_t *out_q, float *out_s, int B, int Hq, int Hkv,
+                                   int D, int block_size, int max_blocks, int max_ctx,
+                                   float scale, void *workspace, size_t workspace_bytes,
+                                   int dtype, void *stream) {
+  if (!q_i8 || !q_s || !kc || !ks || !vc || !vs || !block_table || !context_lens || !out ||
+      ((out_q == nullptr) != (out_s == nullptr)))
+    return S8B_ERR_ARG;
+  const int e = check_attn_shape(B, Hq, Hkv, D, block_size, max_blocks, max_ctx);
+  if (e) return e;
+  if (!aligned(q_i8, 16) || !aligned(kc, 16) || !aligned(vc, 16)) return S8B_ERR_ALIGN;
+  if (!workspace || workspace_bytes < part_bytes(B, Hq, max_ctx)) return S8B_ERR_WORKSPACE;
+  if (B == 0) return S8B_OK;
+  S8B_DISPATCH_DTYPE(dtype, T,
+                     return launch_decode<T>(q_i8, q_s, kc, ks, vc, vs, block_table,
+                                             context_lens, out, out_q, out_s, B, Hq, Hkv,
+                                             block_size, max_blocks, max_ctx, scale,
+                                             static_cast<float *>(workspace),
+                                             (cudaStream_t)stream));
+}
+
+extern "C" size_t s8b_paged_decode_ref_workspace_size(int B, int Hq, int D, int max_ctx) {
+  const size_t part = (part_bytes(B, Hq, max_ctx) + 255) / 256 * 256;
+  const size_t q = (static_cast<size_t>(B) * Hq * D + 255) / 256 * 256;
+  const size_t qs = (static_cast<size_t>(B) * Hq * sizeof(float) + 255) / 256 * 256;
+  return part + q + qs;
+}
+
+extern "C" int s8b_paged_decode(const void *q, const int8_t *kc, const float *ks, const int8_t *vc,
+                                const float *vs, const int32_t *block_table,
+                                const int32_t *context_lens, void *out, int B, int Hq, int Hkv,
+                                int D, int block_size, int max_blocks, int max_ctx, float scale,
+                                void *workspace, size_t workspace_bytes, int dtype, void *stream) {
+  if (!q || !out) return S8B_ERR_ARG;
+  const int e = check_attn_shape(B, Hq, Hkv, D, block_size, max_blocks, max_ctx);
+  if (e) return e;
+  if (!workspace || workspace_bytes < s8b_paged_decode_ref_workspace_size(B, Hq, D, max_ctx))
+    return S8B_ERR_WORKSPACE;
+  if (!aligned(workspace, 256)) return S8B_ERR_ALIGN;
+  if (B == 0) return S8B_OK;
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  float *part = reinterpret_cast<float *>(ws);
+  int8_t *q8 = reinterpret_cast<int8_t *>(ws + (part_bytes(B, Hq, max_ctx) + 255) / 256 * 256);
+  float *qsc = reinterpret_cast<float *>(q8 + (static_cast<size_t>(B) * Hq * D + 255) / 256 * 256);
+  cudaStream_t st = (cudaStream_t)stream;
+  S8B_DISPATCH_DTYPE(dtype, T, {
+    q_rotate_quant_kernel<T><<<B, 256, 0, st>>>(static_cast<const T *>(q), Hq, q8, qsc);
+    check_launch(1);
+    return launch_decode<T>(q8, qsc, kc, ks, vc, vs, block_table, context_lens, out, nullptr,
+                            nullptr, B, Hq, Hkv, block_size, max_blocks, max_ctx, scale, part, st);
+  });
+}

@@ -1,0 +1,163 @@
+// Shared device helpers for the s8b kernels (sm_100a).
+//
+// Numerics contract: every floating-point step that feeds a stored value is a correctly
+// rounded binary32 operation written with __fmul_rn / __fadd_rn / __fsub_rn / __fdiv_rn /
+// __fsqrt_rn, so nvcc cannot contract it into an FMA. The CPU oracle performs the same
+// operations in the same order, which makes the two bit-identical.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/s8b.h"
+
+namespace s8b {
+
+// --------------------------------------------------------------------- error plumbing ----
+void record_cuda_error(cudaError_t e);
+int check_launch(int launches = 1);  // S8B_OK or S8B_ERR_CUDA; counts kernel launches
+// Raise a kernel's dynamic shared-memory limit to `bytes` on the current device, once per
+// (kernel, device): the attribute call happens on the first (eager) launch, never again
+// while a stream is being captured into a CUDA graph.
+void ensure_smem(const void *kernel, size_t bytes);
+
+inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// ----------------------------------------------------------------------------- dtypes ----
+__device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+// Round a binary32 value to the activation dtype and back (exact after the first rounding).
+template <typename T> __device__ __forceinline__ float round_to(float x) {
+  return to_f32(from_f32<T>(x));
+}
+
+// ---------------------------------------------------------------------------- exp -----
+// exp(x) by range reduction to 2^t = 2^k * 2^f (k = rint(t), |f| <= 1/2) and the degree-7
+// Taylor polynomial of 2^f = sum (f ln2)^i / i!. Coefficients are the binary32 roundings of
+// ln(2)^i / i!; Horner with separate multiply and add; 2^k built from its exponent bits.
+__device__ __forceinline__ float exp_s8b(float x) {
+  const float t = __fmul_rn(x, 0x1.715476p+0f);  // x * log2(e)
+  if (t < -125.0f) return 0.0f;
+  if (t > 127.0f) return __int_as_float(0x7f800000);
+  const float k = rintf(t);
+  const float f = __fsub_rn(t, k);
+  float p = 0x1.ffcbfcp-17f;
+  p = __fadd_rn(__fmul_rn(p, f), 0x1.430912p-13f);
+  p = __fadd_rn(__fmul_rn(p, f), 0x1.5d87fep-10f);
+  p = __fadd_rn(__fmul_rn(p, f), 0x1.3b2ab6p-7f);
+  p = __fadd_rn(__fmul_rn(p, f), 0x1.c6b08ep-5f);
+  p = __fadd_rn(__fmul_rn(p, f), 0x1.ebfbe0p-3f);
+  p = __fadd_rn(__fmul_rn(p, f), 0x1.62e430p-1f);
+  p = __fadd_rn(__fmul_rn(p, f), 1.0f);
+  return __fmul_rn(p, __int_as_float((static_cast<int>(k) + 127) << 23));
+}
+
+constexpr float kHadScale = 0x1.6a09e6p-4f;  // binary32 rounding of 128^-1/2
+
+// ------------------------------------------------------- Hadamard-128 in one warp -----
+// A warp holds one 128-vector, lane l owning elements 4l..4l+3 in v[0..3]. Stage h pairs
+// (j, j+h) with j's bit h clear and replaces them by (a+b, a-b). Stages 1 and 2 are inside a
+// lane; stages 4..64 pair lane l with lane l ^ (h/4).
+__device__ __forceinline__ void fwht128_warp(float v[4]) {
+  float a, b;
+  a = v[0]; b = v[1]; v[0] = __fadd_rn(a, b); v[1] = __fsub_rn(a, b);
+  a = v[2]; b = v[3]; v[2] = __fadd_rn(a, b); v[3] = __fsub_rn(a, b);
+  a = v[0]; b = v[2]; v[0] = __fadd_rn(a, b); v[2] = __fsub_rn(a, b);
+  a = v[1]; b = v[3]; v[1] = __fadd_rn(a, b); v[3] = __fsub_rn(a, b);
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int dl = 1; dl < 32; dl <<= 1) {
+    const bool lower = (lane & dl) == 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float o = __shfl_xor_sync(0xffffffffu, v[i], dl);
+      v[i] = lower ? __fadd_rn(v[i], o) : __fsub_rn(o, v[i]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------- reductions -----
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide reductions (all threads receive the result). `red` holds >= 32 elements.
+__device__ __forceinline__ float block_max(float v, float *red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  v = lane < nw ? red[lane] : 0.0f;
+  return warp_max(v);
+}
+__device__ __forceinline__ double block_sum_d(double v, double *red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  v = warp_sum_d(v);
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  v = lane < nw ? red[lane] : 0.0;
+  return warp_sum_d(v);
+}
+
+// ----------------------------------------------------------------------- quantizer -----
+// Symmetric round-to-nearest: inv = qmax/amax, code = clamp(rint(x*inv)), scale = amax/qmax.
+struct QParams {
+  float inv, scale;
+};
+__device__ __forceinline__ QParams qparams(float amax, float qmax) {
+  QParams p;
+  if (amax > 0.0f) {
+    p.inv = __fdiv_rn(qmax, amax);
+    p.scale = __fdiv_rn(amax, qmax);
+  } else {
+    p.inv = 0.0f;
+    p.scale = 1.0f;
+  }
+  return p;
+}
+__device__ __forceinline__ int qcode(float x, float inv, int qmax) {
+  int c = __float2int_rn(__fmul_rn(x, inv));
+  return c > qmax ? qmax : (c < -qmax ? -qmax : c);
+}
+
+// RMSNorm factor r = 1 / sqrt(f32(ss / n) + eps), ss accumulated in float64.
+__device__ __forceinline__ float rms_factor(double ss, int n, float eps) {
+  const float ms = static_cast<float>(ss / static_cast<double>(n));
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+}
+
+}  // namespace s8b
+
+#define S8B_DISPATCH_DTYPE(dtype, T, ...)                 \
+  do {                                                    \
+    if ((dtype) == S8B_BF16) {                            \
+      using T = __nv_bfloat16;                            \
+      __VA_ARGS__;                                        \
+    } else if ((dtype) == S8B_FP16) {                     \
+      using T = __half;                                   \
+      __VA_ARGS__;                                        \
+    } else {                                              \
+      return S8B_ERR_DTYPE;                               \
+    }                                                     \
+  } while (0)

@@ -1,0 +1,163 @@
+"""Pipeline-parallel decode with the reference's stage API
+(``superl8serve/dist/pipeline.py``: ``make_pipeline``, ``PipelineStage``, ``PipelineEngine``).
+
+``make_pipeline`` splits the layer stack at ``i*L//S`` (``:452``), places each slice's
+int8 weights on its GPU and gives each stage a paged KV pool sized to its own layers
+(``:486-494``). ``PipelineEngine.generate`` runs greedy decode through
+``engine.DecodePipeline``: micro-batches flow stage to stage with the codec fused at every
+boundary and no host synchronisation inside a step.
+
+Differences from the reference, all on purpose: prompts are consumed by decode steps (the
+varlen prefill path is a separate, later component), sampling is greedy-only (temperature /
+top-k / top-p are not on this path), and the boundary scheme is fixed per engine
+(``wire_scheme``, default "int8") instead of re-running the int4 gate every step, which
+would need a host read-back inside the step.
+"""
+
+from __future__ import annotations
+
+import itertools
+from dataclasses import dataclass, field
+
+import torch
+
+from ..engine import DecodePipeline
+from ..runtime import StageModel
+
+
+@dataclass
+class SamplingParams:
+    temperature: float = 0.0
+    max_tokens: int = 16
+    top_p: float = 1.0
+    top_k: int = 0
+    repetition_penalty: float = 1.0
+    logit_processors: list = field(default_factory=list)
+
+
+class PipelineStage:
+    """One contiguous slice of layers on one GPU (``superl8serve/dist/pipeline.py:361-427``)."""
+
+    def __init__(self, stage_id: int, *, model: StageModel, layer_offset: int, num_stages: int):
+        self.stage_id = stage_id
+        self.model = model
+        self.layer_offset = layer_offset
+        self.num_stages = num_stages
+        self.kv_cache = None  # set by the engine's DecodePipeline (its KVPool of this stage)
+
+    @property
+    def layers(self):
+        return self.model.layers
+
+    @property
+    def is_first(self) -> bool:
+        return self.stage_id == 0
+
+    @property
+    def is_last(self) -> bool:
+        return self.stage_id == self.num_stages - 1
+
+    @property
+    def _device(self):
+        return self.model.device
+
+
+def stage_bounds(n_layers: int, n_stages: int) -> list[int]:
+    return [i * n_layers // n_stages for i in range(n_stages + 1)]
+
+
+def make_pipeline(cfg, weights, *, devices: tuple[int, ...] = (0, 1), max_num_seqs: int = 16,
+                  max_len: int = 2048, block_size: int = 16, seed: int = 0,
+                  allow_single_stage: bool = False) -> tuple[PipelineStage, ...]:
+    """weights: an HF-style state dict (numpy or torch, bf16-valued floats; quantized per row
+    here) or the string "synthetic" (random int8 weights generated on each GPU)."""
+    n_layers = cfg.num_hidden_layers
+    n_stages = len(devices)
+    if n_stages < 2 and not allow_single_stage:
+        raise ValueError("pipeline parallelism needs at least two devices")
+    if n_stages > n_layers:
+        raise ValueError("pipeline stage count cannot exceed the model layer count")
+    bounds = stage_bounds(n_layers, n_stages)
+    stages = []
+    for sid, dev in enumerate(devices):
+        start, end = bounds[sid], bounds[sid + 1]
+        first, last = sid == 0, sid == n_stages - 1
+        device = torch.device("cuda", dev) if isinstance(dev, int) else torch.device(dev)
+        if isinstance(weights, str) and weights == "synthetic":
+            model = StageModel.synthetic(cfg, start, end, device, first=first, last=last, seed=seed)
+        else:
+            model = StageModel.from_state_dict(cfg, weights, start, end, device, first=first,
+                                               last=last)
+        stages.append(PipelineStage(sid, model=model, layer_offset=start, num_stages=n_stages))
+    return tuple(stages)
+
+
+class PipelineEngine:
+    """Greedy pipeline-parallel generation over stages from ``make_pipeline``."""
+
+    def __init__(self, stage0: PipelineStage, stage1: PipelineStage, cfg, *, max_num_seqs: int = 16,
+                 max_len: int = 2048, max_batch_tokens: int = 8192, eos_id: int | None = None,
+                 wire_scheme: str | None = None, n_micro: int | None = None):
+        self.stages = (stage0, stage1)
+        self.cfg = cfg
+        self.max_num_seqs, self.max_len = max_num_seqs, max_len
+        self.eos_id = eos_id
+        self.wire_scheme = wire_scheme or "int8"
+        self.n_micro = n_micro
+        self._ids = itertools.count()
+        self._pending: dict[int, tuple[list[int], SamplingParams]] = {}
+        self._out: dict[int, list[int]] = {}
+        self._pipe: DecodePipeline | None = None
+
+    @classmethod
+    def from_stages(cls, stages, cfg, **kwargs):
+        if len(stages) < 1:
+            raise ValueError("PipelineEngine needs at least one stage")
+        eng = cls(stages[0], stages[-1], cfg, **kwargs)
+        eng.stages = tuple(stages)
+        return eng
+
+    @property
+    def devices(self):
+        return tuple(s._device.index or 0 for s in self.stages)
+
+    def add_request(self, prompt_ids: list[int], params: SamplingParams | None = None) -> int:
+        sid = next(self._ids)
+        self._pending[sid] = (list(prompt_ids), params or SamplingParams())
+        return sid
+
+    def _pipeline(self, batch: int) -> DecodePipeline:
+        n_micro = self.n_micro or min(len(self.stages), batch)
+        if self._pipe is None or self._pipe.batch != batch or self._pipe.n_micro != n_micro:
+            self._pipe = DecodePipeline([s.model for s in self.stages], batch=batch,
+                                        n_micro=n_micro, max_len=self.max_len,
+                                        wire_scheme=self.wire_scheme)
+            for s, pool in zip(self.stages, self._pipe.pools):
+                s.kv_cache = pool
+        else:
+            self._pipe.alloc = type(self._pipe.alloc)(self._pipe.alloc.num_blocks, batch,
+                                                      self._pipe.block_size, self._pipe.max_blocks)
+            self._pipe.slots = []
+        return self._pipe
+
+    def run_pending(self):
+        if not self._pending:
+            return
+        ids = list(self._pending)
+        prompts = [self._pending[i][0] for i in ids]
+        params = [self._pending[i][1] for i in ids]
+        if any(p.temperature != 0.0 for p in params):
+            raise NotImplementedError("only greedy sampling is on the s8b decode path")
+        max_new = max(p.max_tokens for p in params)
+        outs = self._pipeline(len(prompts)).generate(prompts, max_new)
+        for sid, out, p in zip(ids, outs, params):
+            out = out[: p.max_tokens]
+            if self.eos_id is not None and self.eos_id in out:
+                out = out[: out.index(self.eos_id) + 1]
+            self._out[sid] = out
+        self._pending.clear()
+
+    def generate(self, prompts: list[list[int]], params: SamplingParams | None = None):
+        sids = [self.add_request(p, params) for p in prompts]
+        self.run_pending()
+        return [self._out[s] for s in sids]

@@ -1,0 +1,249 @@
+"""In-process pipeline decode: S stages (one device each, or several on one device), a batch
+split into micro-batches, the codec at every stage boundary.
+
+Scheduling. Stage s of micro-batch k waits only for stage s-1 of micro-batch k (a CUDA event,
+no host synchronisation), so while stage s works on micro-batch k, stage s-1 already runs
+k+1: the 1F pipeline the reference's docstring describes
+(``superl8serve/dist/pipeline.py:11-13``) but its loop serialises
+(``_decode_microbatched``, ``:986-1040``). The codec encoder of stage s writes straight into
+stage s+1's receive buffer for that micro-batch; the argmax of the last stage writes the next
+token ids that stage 0 reads on the following step.
+
+Sequence state (positions, context lengths, block tables) lives on the device and is advanced
+by a kernel, so one step needs no host round trip and, on a single device, the whole step is
+captured into one CUDA graph.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from ._lib import call, ptr, stream
+from .runtime import KVPool, MicroBatch, StageModel, StageRunner
+
+
+class BlockAllocator:
+    """Host-side block bookkeeping (``PagedKVCache.alloc/ensure_capacity/free``,
+    ``superl8serve/engine/kv_cache.py:703-749``): free-list of physical blocks, one block
+    list per slot."""
+
+    def __init__(self, num_blocks: int, num_slots: int, block_size: int, max_blocks_per_seq: int):
+        self.block_size = block_size
+        self.max_blocks_per_seq = max_blocks_per_seq
+        self.num_blocks = num_blocks
+        self._free_blocks = list(range(num_blocks))
+        self._free_slots = list(range(num_slots))
+        self._slot_blocks: list[list[int]] = [[] for _ in range(num_slots)]
+
+    def alloc(self) -> int:
+        if not self._free_slots:
+            raise RuntimeError("PagedKVCache: no free slots")
+        return self._free_slots.pop()
+
+    def free(self, slot: int):
+        self._free_blocks.extend(self._slot_blocks[slot])
+        self._slot_blocks[slot] = []
+        self._free_slots.append(slot)
+
+    def ensure_capacity(self, slots, lengths):
+        for slot, n in zip(slots, lengths):
+            blocks = self._slot_blocks[slot]
+            need = (n + self.block_size - 1) // self.block_size
+            if need > self.max_blocks_per_seq:
+                raise RuntimeError("sequence longer than max_len")
+            while len(blocks) < need:
+                if not self._free_blocks:
+                    raise RuntimeError("PagedKVCache: no free blocks")
+                blocks.append(self._free_blocks.pop())
+
+    def block_table(self, slots) -> torch.Tensor:
+        bt = torch.zeros(len(slots), self.max_blocks_per_seq, dtype=torch.int32)
+        for i, s in enumerate(slots):
+            b = self._slot_blocks[s]
+            if b:
+                bt[i, : len(b)] = torch.tensor(b, dtype=torch.int32)
+        return bt
+
+
+class DecodePipeline:
+    """Greedy W8A8 decode through ``len(models)`` stages.
+
+    models[s] holds stage s's layers on its device. ``batch`` rows are split into
+    ``n_micro`` micro-batches of ``m = ceil(batch / n_micro)`` rows.
+    """
+
+    def __init__(self, models: list[StageModel], *, batch: int, n_micro: int = 1,
+                 max_len: int = 2048, block_size: int = 16, wire_scheme: str = "int8-had",
+                 num_blocks: int | None = None, dtype=torch.bfloat16):
+        self.models = models
+        self.cfg = models[0].cfg
+        self.S = len(models)
+        self.batch, self.n_micro = batch, n_micro
+        self.m = math.ceil(batch / n_micro)
+        self.max_len = max_len
+        self.block_size = block_size
+        self.wire_scheme = wire_scheme
+        self.max_blocks = (max_len + block_size - 1) // block_size
+        nb = num_blocks or batch * self.max_blocks
+        cfg = self.cfg
+        self.alloc = BlockAllocator(nb, batch, block_size, self.max_blocks)
+        self.pools = [KVPool(len(mdl.layers), nb, cfg.num_key_value_heads, cfg.resolved_head_dim(),
+                             block_size, mdl.device) for mdl in models]
+        self.runners = [StageRunner(mdl, pool, self.m, max_len, dtype)
+                        for mdl, pool in zip(models, self.pools)]
+        self.mbs: list[list[MicroBatch]] = []
+        for mdl in models:
+            dev = mdl.device
+            row = []
+            for k in range(n_micro):
+                row.append(MicroBatch(
+                    ids=torch.zeros(self.m, dtype=torch.int32, device=dev),
+                    positions=torch.zeros(self.m, dtype=torch.int32, device=dev),
+                    context_lens=torch.ones(self.m, dtype=torch.int32, device=dev),
+                    block_table=torch.zeros(self.m, self.max_blocks, dtype=torch.int32, device=dev)))
+            self.mbs.append(row)
+        from .ops import codec_sizes
+
+        H = cfg.hidden_size
+        nbytes, nsc = codec_sizes(self.m, 2 * H, wire_scheme)
+        # boundary s -> s+1 buffers live on stage s+1's device, one per micro-batch
+        self.bufs = [[(torch.empty(nbytes, dtype=torch.uint8, device=models[s + 1].device),
+                       torch.empty(max(nsc, 1), dtype=torch.float32, device=models[s + 1].device),
+                       wire_scheme) for _ in range(n_micro)] for s in range(self.S - 1)]
+        self.single_device = len({str(mdl.device) for mdl in models}) == 1
+        if not self.single_device:
+            for a, b in zip(models[:-1], models[1:]):
+                call("s8b_enable_peer_access", a.device.index, b.device.index)
+        self.streams = [torch.cuda.Stream(device=mdl.device) for mdl in models]
+        self.events = [[torch.cuda.Event() for _ in range(n_micro)] for _ in models]
+        self.slots: list[int] = []
+        self.graph = None
+        self.rows = [min(self.m, batch - k * self.m) for k in range(n_micro)]
+
+    # ----------------------------------------------------------------- sequence state ----
+    def add_sequences(self, n: int | None = None):
+        n = self.batch if n is None else n
+        self.slots = [self.alloc.alloc() for _ in range(n)]
+        return self.slots
+
+    def set_state(self, positions: list[int], ids: list[int] | None = None, reserve: int = 1):
+        """Host -> device: block tables covering positions + reserve tokens, positions,
+        context lengths and (optionally) the input ids of every row."""
+        lengths = [p + reserve for p in positions]
+        self.alloc.ensure_capacity(self.slots, lengths)
+        bt = self.alloc.block_table(self.slots)
+        pos = torch.tensor(positions, dtype=torch.int32)
+        ids_t = None if ids is None else torch.tensor(ids, dtype=torch.int32)
+        for s in range(self.S):
+            for k in range(self.n_micro):
+                lo, r = k * self.m, self.rows[k]
+                mb = self.mbs[s][k]
+                mb.block_table[:r].copy_(bt[lo:lo + r])
+                mb.positions[:r].copy_(pos[lo:lo + r])
+                mb.context_lens[:r].copy_(pos[lo:lo + r] + 1)
+                if ids_t is not None and s == 0:
+                    mb.ids[:r].copy_(ids_t[lo:lo + r])
+
+    def set_ids(self, ids: list[int]):
+        ids_t = torch.tensor(ids, dtype=torch.int32)
+        for k in range(self.n_micro):
+            lo, r = k * self.m, self.rows[k]
+            self.mbs[0][k].ids[:r].copy_(ids_t[lo:lo + r])
+
+    def tokens(self) -> torch.Tensor:
+        """Next-token ids of the last step, all rows (on the last stage's device)."""
+        return torch.cat([self.mbs[-1][k].ids[: self.rows[k]] for k in range(self.n_micro)])
+
+    def logits(self, k: int = 0) -> torch.Tensor:
+        return self.runners[-1].logits[: self.rows[k]]
+
+    # ----------------------------------------------------------------------- stepping ----
+    def _enqueue(self):
+        """Enqueue one decode step (all micro-batches, all stages) and advance positions."""
+        for k in range(self.n_micro):
+            r = self.rows[k]
+            for s in range(self.S):
+                dev = self.models[s].device
+                st = torch.cuda.current_stream(dev) if self.single_device else self.streams[s]
+                with torch.cuda.device(dev), torch.cuda.stream(st):
+                    if s > 0 and not self.single_device:
+                        st.wait_event(self.events[s - 1][k])
+                    if s < self.S - 1 and not self.single_device:
+                        # do not overwrite stage s+1's receive buffer before it was decoded
+                        st.wait_event(self.events[s + 1][k])
+                    self.runners[s].run(self.mbs[s][k], r,
+                                        boundary_in=self.bufs[s - 1][k] if s > 0 else None,
+                                        boundary_out=self.bufs[s][k] if s < self.S - 1 else None)
+                    call("s8b_advance", ptr(self.mbs[s][k].positions),
+                         ptr(self.mbs[s][k].context_lens), r, 1, stream())
+                    if not self.single_device:
+                        self.events[s][k].record(st)
+            if self.S > 1:
+                # next step's input ids of micro-batch k: last stage -> stage 0
+                last, first = self.mbs[-1][k], self.mbs[0][k]
+                if self.single_device:
+                    first.ids.copy_(last.ids)
+                else:
+                    with torch.cuda.device(self.models[0].device), torch.cuda.stream(self.streams[0]):
+                        self.streams[0].wait_event(self.events[-1][k])
+                        first.ids.copy_(last.ids, non_blocking=True)
+
+    def step(self):
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._enqueue()
+
+    def capture(self):
+        """Capture one whole step into a CUDA graph (single-device pipelines)."""
+        if not self.single_device:
+            raise RuntimeError("graph capture of a multi-device in-process pipeline is not used")
+        dev = self.models[0].device
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.device(dev), torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                self._enqueue()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        self.graph = g
+        return g
+
+    def synchronize(self):
+        for mdl in self.models:
+            torch.cuda.synchronize(mdl.device)
+
+    # ------------------------------------------------------------------- generation ----
+    def generate(self, prompts: list[list[int]], max_new_tokens: int, *, keep_logits=False):
+        """Greedy generation; every row advances one token per step (prompt tokens are fed
+        teacher-forced, exactly as ``oracle.model.OraclePipeline.generate``)."""
+        n = len(prompts)
+        if n != self.batch:
+            raise ValueError("generate() expects exactly `batch` prompts")
+        if not self.slots:
+            self.add_sequences(n)
+        seqs = [list(p) for p in prompts]
+        outs = [[] for _ in prompts]
+        logit_log = [[] for _ in prompts]
+        step = 0
+        total = max(len(p) for p in prompts) + max_new_tokens
+        self.set_state([0] * n, [sq[0] for sq in seqs], reserve=total)
+        while any(len(o) < max_new_tokens for o in outs):
+            self.set_ids([sq[step] for sq in seqs])
+            self._enqueue()
+            self.synchronize()
+            toks = self.tokens().cpu().tolist()
+            if keep_logits:
+                lg = torch.cat([self.runners[-1].logits[: self.rows[k]].float().cpu()
+                                for k in range(self.n_micro)]) if self.n_micro == 1 else None
+            for i, sq in enumerate(seqs):
+                if step >= len(prompts[i]) - 1 and len(outs[i]) < max_new_tokens:
+                    outs[i].append(int(toks[i]))
+                    if keep_logits and lg is not None:
+                        logit_log[i].append(lg[i])
+                if step + 1 >= len(sq):
+                    sq.append(int(toks[i]))
+            step += 1
+        return (outs, logit_log) if keep_logits else outs

@@ -1,0 +1,180 @@
+"""Tensor-level wrappers over the s8b C ABI (CUDA tensors only; outputs allocated here when
+not passed in). The stage runner passes preallocated buffers; tests and the reference-shaped
+layer API use the allocating forms."""
+
+from __future__ import annotations
+
+import torch
+
+from ._lib import CODEC, call, dtype_code, ptr, stream
+
+__all__ = [
+    "quant_rows", "rmsnorm_quant", "gemm_w8a8", "silu_mul_quant", "qkv_post", "kv_write_paged",
+    "paged_decode_q8", "paged_decode", "embed", "argmax", "codec_encode", "codec_decode",
+    "codec_sizes", "decode_workspace_bytes",
+]
+
+
+def quant_rows(x: torch.Tensor):
+    x = x.contiguous()
+    K = x.shape[-1]
+    M = x.numel() // K
+    q = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+    s = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device)
+    call("s8b_quant_rows", ptr(x), dtype_code(x.dtype), ptr(q), ptr(s), M, K, stream(x.device))
+    return q, s
+
+
+def rmsnorm_quant(h, residual, w, eps, *, residual_out=None, y_out=False, q=None, s=None):
+    """Returns (new residual, q, s, y or None). residual None = first layer (no add)."""
+    h = h.contiguous()
+    H = h.shape[-1]
+    M = h.numel() // H
+    if residual_out is None:
+        residual_out = torch.empty_like(h)
+    q = torch.empty(h.shape, dtype=torch.int8, device=h.device) if q is None else q
+    s = torch.empty(h.shape[:-1], dtype=torch.float32, device=h.device) if s is None else s
+    y = torch.empty_like(h) if y_out else None
+    call("s8b_rmsnorm_quant", ptr(h), ptr(residual), ptr(residual_out), ptr(w), float(eps),
+         ptr(q), ptr(s), ptr(y), M, H, dtype_code(h.dtype), stream(h.device))
+    return residual_out, q, s, y
+
+
+def gemm_w8a8(xq, xs, w, ws, *, out=None, out_dtype=torch.bfloat16, raw=False):
+    """y = dequant(xq @ w^T). raw=True returns the int32 accumulators."""
+    K = xq.shape[-1]
+    M = xq.numel() // K
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((*xq.shape[:-1], N), dtype=torch.int32 if raw else out_dtype,
+                          device=xq.device)
+    dt = dtype_code(out_dtype if raw else out.dtype)
+    call("s8b_gemm_w8a8", ptr(xq), ptr(xs), ptr(w), ptr(ws), ptr(out), 1 if raw else 0, M, N, K,
+         dt, stream(xq.device))
+    return out
+
+
+def silu_mul_quant(gu, *, y_out=False, q=None, s=None):
+    F = gu.shape[-1] // 2
+    M = gu.numel() // (2 * F)
+    shp = (*gu.shape[:-1], F)
+    q = torch.empty(shp, dtype=torch.int8, device=gu.device) if q is None else q
+    s = torch.empty(shp[:-1], dtype=torch.float32, device=gu.device) if s is None else s
+    y = torch.empty(shp, dtype=gu.dtype, device=gu.device) if y_out else None
+    call("s8b_silu_mul_quant", ptr(gu), M, F, ptr(y), ptr(q), ptr(s), dtype_code(gu.dtype),
+         stream(gu.device))
+    return q, s, y
+
+
+def qkv_post(qkv, positions, cos, sin, q_norm_w, k_norm_w, eps, Hq, Hkv, kc, ks, vc, vs, *,
+             slot_mapping=None, block_table=None, q_out=False, q_i8=None, q_s=None):
+    """Returns (q_i8 [M,Hq,D], q_s [M,Hq], q_out or None); writes K/V into the paged stores."""
+    M = qkv.shape[0]
+    D = cos.shape[-1]
+    dev = qkv.device
+    q_i8 = torch.empty((M, Hq, D), dtype=torch.int8, device=dev) if q_i8 is None else q_i8
+    q_s = torch.empty((M, Hq), dtype=torch.float32, device=dev) if q_s is None else q_s
+    qo = torch.empty((M, Hq, D), dtype=qkv.dtype, device=dev) if q_out else None
+    bs = kc.shape[-2]
+    maxb = block_table.shape[-1] if block_table is not None else 0
+    call("s8b_qkv_post", ptr(qkv), ptr(positions), ptr(cos), ptr(sin), cos.shape[0], ptr(q_norm_w),
+         ptr(k_norm_w), float(eps), M, Hq, Hkv, D, ptr(q_i8), ptr(q_s), ptr(qo), ptr(kc), ptr(ks),
+         ptr(vc), ptr(vs), ptr(slot_mapping), ptr(block_table), maxb, bs, dtype_code(qkv.dtype),
+         stream(dev))
+    return q_i8, q_s, qo
+
+
+def kv_write_paged(k, v, kc, ks, vc, vs, slot_mapping, *, rotate_k=True):
+    T, Hkv, D = k.shape
+    call("s8b_kv_write_paged", ptr(k.contiguous()), ptr(v.contiguous()), ptr(kc), ptr(ks), ptr(vc),
+         ptr(vs), ptr(slot_mapping), T, Hkv, D, kc.shape[-2], 1 if rotate_k else 0,
+         dtype_code(k.dtype), stream(k.device))
+
+
+def decode_workspace_bytes(B, Hq, D, max_ctx, *, ref=False) -> int:
+    from ._lib import load
+
+    fn = load().s8b_paged_decode_ref_workspace_size if ref else load().s8b_paged_decode_workspace_size
+    return int(fn(B, Hq, D, max_ctx))
+
+
+def paged_decode_q8(q_i8, q_s, kc, ks, vc, vs, block_table, context_lens, max_ctx, scale, *,
+                    out=None, out_q=None, out_s=None, workspace=None, dtype=torch.bfloat16):
+    B, Hq, D = q_i8.shape
+    Hkv, bs = kc.shape[-3], kc.shape[-2]
+    dev = q_i8.device
+    out = torch.empty((B, Hq * D), dtype=dtype, device=dev) if out is None else out
+    need = decode_workspace_bytes(B, Hq, D, max_ctx)
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+    call("s8b_paged_decode_q8", ptr(q_i8), ptr(q_s), ptr(kc), ptr(ks), ptr(vc), ptr(vs),
+         ptr(block_table), ptr(context_lens), ptr(out), ptr(out_q), ptr(out_s), B, Hq, Hkv, D, bs,
+         block_table.shape[-1], int(max_ctx), float(scale), ptr(workspace), workspace.numel(),
+         dtype_code(out.dtype), stream(dev))
+    return out
+
+
+def paged_decode(q, kc, ks, vc, vs, block_table, context_lens, max_ctx, scale, *, out=None,
+                 workspace=None):
+    """Reference layout: q [B, Hq, D] (or [B, Hq, 1, D]) -> [B, Hq, D]."""
+    qq = q.reshape(q.shape[0], q.shape[1], q.shape[-1]).contiguous()
+    B, Hq, D = qq.shape
+    Hkv, bs = kc.shape[-3], kc.shape[-2]
+    out = torch.empty_like(qq) if out is None else out
+    need = decode_workspace_bytes(B, Hq, D, max_ctx, ref=True)
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    call("s8b_paged_decode", ptr(qq), ptr(kc), ptr(ks), ptr(vc), ptr(vs), ptr(block_table),
+         ptr(context_lens), ptr(out), B, Hq, Hkv, D, bs, block_table.shape[-1], int(max_ctx),
+         float(scale), ptr(workspace), workspace.numel(), dtype_code(qq.dtype), stream(q.device))
+    return out
+
+
+def embed(ids, table, *, out=None):
+    M = ids.numel()
+    H = table.shape[-1]
+    out = torch.empty((M, H), dtype=table.dtype, device=table.device) if out is None else out
+    call("s8b_embed", ptr(ids), ptr(table), M, H, ptr(out), dtype_code(table.dtype),
+         stream(table.device))
+    return out
+
+
+def argmax(logits, *, out=None):
+    V = logits.shape[-1]
+    M = logits.numel() // V
+    out = torch.empty(M, dtype=torch.int32, device=logits.device) if out is None else out
+    call("s8b_argmax", ptr(logits), M, V, ptr(out), dtype_code(logits.dtype), stream(logits.device))
+    return out
+
+
+def codec_sizes(T: int, D: int, scheme: str) -> tuple[int, int]:
+    """(payload bytes, fp32 scale count) of one encoded [T, D] block."""
+    from ._lib import load
+
+    sc = CODEC[scheme]
+    return int(load().s8b_codec_payload_bytes(T, D, sc, 0)), int(load().s8b_codec_scale_count(T, D, sc))
+
+
+def codec_encode(a, b, scheme, *, payload=None, scales=None, dtype=None):
+    """Encode rows [a | b] (b may be None). payload/scales may live on another GPU."""
+    T, Da = a.shape[0], a.shape[-1]
+    Db = 0 if b is None else b.shape[-1]
+    nbytes, nsc = codec_sizes(T, Da + Db, scheme)
+    if payload is None:
+        payload = torch.empty(nbytes, dtype=torch.uint8, device=a.device)
+    if scales is None:
+        scales = torch.empty(max(nsc, 1), dtype=torch.float32, device=a.device)
+    call("s8b_codec_encode", ptr(a.contiguous()), ptr(None if b is None else b.contiguous()), T, Da,
+         Db, CODEC[scheme], payload.data_ptr(), scales.data_ptr(), dtype_code(a.dtype),
+         stream(a.device))
+    return payload, scales
+
+
+def codec_decode(payload, scales, T, Da, Db, scheme, dtype, *, out_a=None, out_b=None):
+    dev = payload.device
+    out_a = torch.empty((T, Da), dtype=dtype, device=dev) if out_a is None else out_a
+    if Db:
+        out_b = torch.empty((T, Db), dtype=dtype, device=dev) if out_b is None else out_b
+    call("s8b_codec_decode", ptr(payload), ptr(scales), T, Da, Db, CODEC[scheme], ptr(out_a),
+         ptr(out_b) if Db else None, dtype_code(dtype), stream(dev))
+    return out_a, out_b

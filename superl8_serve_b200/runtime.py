@@ -1,0 +1,289 @@
+"""Stage runtime: device-resident weights, paged KV pools and the per-micro-batch kernel
+sequence of one pipeline stage.
+
+One decode step of a stage, for one micro-batch of m rows (the reference's per-stage loop
+in ``PipelineEngine._decode_microbatched``, ``superl8serve/dist/pipeline.py:997-1040``, over
+``Qwen3DecoderLayer.forward``, ``superl8serve/models/qwen3.py:70-80``):
+
+    [stage 0] embed(ids)                       or  [stage > 0] decode boundary -> (h, res)
+    per layer:  rmsnorm_quant -> W8A8 qkv -> qkv_post (norms, RoPE, paged KV write, q quant)
+                -> paged decode attention (+ fused o_proj input quant) -> W8A8 o
+                -> rmsnorm_quant -> W8A8 gate_up -> SwiGLU + quant -> W8A8 down
+    [last]      rmsnorm_quant(final norm) -> W8A8 lm_head -> argmax
+    [not last]  encode (h, res) straight into the next stage's receive buffer
+
+Every buffer is allocated once here; ``StageRunner.run`` only launches kernels, so a whole
+step can be captured into one CUDA graph per stage.
+
+HBM layout (per stage, all device-resident): int8 weights row-major [out, in] with an fp32
+scale per row (qkv and gate_up merged on the out axis), bf16 norm gains, bf16 embedding
+table (stage 0), int8 LM head (last stage); KV pools [layers, blocks, Hkv, 16, 128] int8 with
+[layers, blocks, Hkv, 16] fp32 scales; per-micro-batch activations of a few MB.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import ops
+from ._lib import CODEC, call, ptr, stream
+from .weights import quantize_rowwise_np
+
+
+@dataclass
+class LayerWeights:
+    qkv_w: torch.Tensor
+    qkv_s: torch.Tensor
+    o_w: torch.Tensor
+    o_s: torch.Tensor
+    gu_w: torch.Tensor
+    gu_s: torch.Tensor
+    d_w: torch.Tensor
+    d_s: torch.Tensor
+    in_norm: torch.Tensor
+    post_norm: torch.Tensor
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in vars(self).values())
+
+
+@dataclass
+class StageModel:
+    """Weights of layers [start, end) of a Qwen3 model on one device."""
+
+    cfg: object
+    start: int
+    end: int
+    device: torch.device
+    layers: list[LayerWeights]
+    embed: torch.Tensor | None = None
+    norm: torch.Tensor | None = None
+    head_w: torch.Tensor | None = None
+    head_s: torch.Tensor | None = None
+
+    @property
+    def is_first(self) -> bool:
+        return self.embed is not None
+
+    @property
+    def is_last(self) -> bool:
+        return self.head_w is not None
+
+    def weight_bytes(self) -> int:
+        n = sum(L.nbytes() for L in self.layers)
+        for t in (self.head_w, self.head_s, self.norm):
+            if t is not None:
+                n += t.numel() * t.element_size()
+        return n
+
+    @classmethod
+    def from_state_dict(cls, cfg, sd: dict, start: int, end: int, device, *, first: bool,
+                        last: bool, dtype=torch.bfloat16) -> "StageModel":
+        """Quantize an HF-style float state dict (numpy or torch, bf16-valued) on the host with
+        the per-row recipe and upload layers [start, end)."""
+        dev = torch.device(device)
+
+        def f(name):
+            v = sd[name]
+            return v.float().cpu().numpy() if isinstance(v, torch.Tensor) else np.asarray(v, np.float32)
+
+        def q(w):
+            qq, ss = quantize_rowwise_np(w)
+            return torch.from_numpy(qq).to(dev), torch.from_numpy(ss).to(dev)
+
+        def g(name):
+            return torch.from_numpy(f(name)).to(dtype).to(dev)
+
+        layers = []
+        for i in range(start, end):
+            p = f"model.layers.{i}"
+            qkv = np.concatenate([f(f"{p}.self_attn.{n}_proj.weight") for n in "qkv"], 0)
+            gu = np.concatenate([f(f"{p}.mlp.gate_proj.weight"), f(f"{p}.mlp.up_proj.weight")], 0)
+            layers.append(LayerWeights(*q(qkv), *q(f(f"{p}.self_attn.o_proj.weight")), *q(gu),
+                                       *q(f(f"{p}.mlp.down_proj.weight")),
+                                       g(f"{p}.input_layernorm.weight"),
+                                       g(f"{p}.post_attention_layernorm.weight"),
+                                       g(f"{p}.self_attn.q_norm.weight"),
+                                       g(f"{p}.self_attn.k_norm.weight")))
+        m = cls(cfg, start, end, dev, layers)
+        if first:
+            m.embed = g("model.embed_tokens.weight")
+        if last:
+            m.norm = g("model.norm.weight")
+            head = "model.embed_tokens.weight" if cfg.tie_word_embeddings else "lm_head.weight"
+            m.head_w, m.head_s = q(f(head))
+        return m
+
+    @classmethod
+    def synthetic(cls, cfg, start: int, end: int, device, *, first: bool, last: bool,
+                  seed: int = 0, dtype=torch.bfloat16) -> "StageModel":
+        """Random int8 weights generated on the device (benchmarks of large shapes): uniform
+        codes in [-127, 127] with row scales giving an effective N(0, 0.02)-sized weight."""
+        dev = torch.device(device)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed * 1000 + start)
+        H, D = cfg.hidden_size, cfg.resolved_head_dim()
+        nh, nkv, F = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.intermediate_size
+        sw = 0.02 / 73.3
+
+        def w(n, k):
+            codes = torch.randint(-127, 128, (n, k), generator=gen, device=dev, dtype=torch.int8)
+            return codes, torch.full((n,), sw, dtype=torch.float32, device=dev)
+
+        def gain(n):
+            return (1.0 + 0.1 * torch.randn(n, generator=gen, device=dev)).to(dtype)
+
+        layers = [LayerWeights(*w((nh + 2 * nkv) * D, H), *w(H, nh * D), *w(2 * F, H),
+                               *w(H, F), gain(H), gain(H), gain(D), gain(D))
+                  for _ in range(start, end)]
+        m = cls(cfg, start, end, dev, layers)
+        if first:
+            m.embed = (0.02 * torch.randn(cfg.vocab_size, H, generator=gen, device=dev)).to(dtype)
+        if last:
+            m.norm = gain(H)
+            m.head_w, m.head_s = w(cfg.vocab_size, H)
+        return m
+
+
+class KVPool:
+    """Paged int8 KV storage of one stage (``PagedKVCache`` layout,
+    ``superl8serve/engine/kv_cache.py:484-512``)."""
+
+    def __init__(self, n_layers, num_blocks, nkv, head_dim, block_size, device):
+        shp = (n_layers, num_blocks, nkv, block_size, head_dim)
+        self.kc = torch.zeros(shp, dtype=torch.int8, device=device)
+        self.vc = torch.zeros(shp, dtype=torch.int8, device=device)
+        self.ks = torch.ones(shp[:-1], dtype=torch.float32, device=device)
+        self.vs = torch.ones(shp[:-1], dtype=torch.float32, device=device)
+        self.block_size = block_size
+        self.num_blocks = num_blocks
+
+    def layer(self, i):
+        return self.kc[i], self.ks[i], self.vc[i], self.vs[i]
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.kc, self.vc, self.ks, self.vs))
+
+    def fill_random(self, seed: int = 0):
+        """Synthetic pre-filled context (benchmarks): random codes and scales."""
+        g = torch.Generator(device=self.kc.device)
+        g.manual_seed(seed)
+        for t in (self.kc, self.vc):
+            t.view(torch.uint8).random_(0, 255, generator=g)
+            t.clamp_(-127, 127)
+        for t in (self.ks, self.vs):
+            t.uniform_(0.01, 0.05, generator=g)
+
+
+@dataclass
+class MicroBatch:
+    """Device-side per-micro-batch decode state (stable addresses: graph-capturable)."""
+
+    ids: torch.Tensor            # [m] int32 (stage 0 input; last stage writes next tokens)
+    positions: torch.Tensor      # [m] int32, write position of the token being decoded
+    context_lens: torch.Tensor   # [m] int32, positions + 1
+    block_table: torch.Tensor    # [m, max_blocks] int32
+    extra: dict = field(default_factory=dict)
+
+
+class StageRunner:
+    """Launches one stage's decode kernels for a micro-batch of up to ``m`` rows."""
+
+    def __init__(self, model: StageModel, pool: KVPool, m: int, max_ctx: int,
+                 dtype=torch.bfloat16):
+        cfg = model.cfg
+        self.model, self.pool, self.m, self.max_ctx, self.dtype = model, pool, m, max_ctx, dtype
+        self.H = cfg.hidden_size
+        self.D = cfg.resolved_head_dim()
+        self.Hq, self.Hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        self.F = cfg.intermediate_size
+        self.V = cfg.vocab_size
+        self.eps = cfg.rms_norm_eps
+        self.scale = self.D ** -0.5
+        dev = model.device
+        from .layers import rope_tables
+
+        cos, sin = rope_tables(self.D, cfg.max_position_embeddings, cfg.rope_theta)
+        self.cos, self.sin = cos.to(dev), sin.to(dev)
+        e = lambda *s, dt=dtype: torch.empty(s, dtype=dt, device=dev)  # noqa: E731
+        kmax = max(self.H, self.Hq * self.D, self.F)
+        self.h = e(m, self.H)
+        self.res = e(m, self.H)
+        self.xq = e(m, kmax, dt=torch.int8)
+        self.xs = e(m, dt=torch.float32)
+        self.qkv = e(m, (self.Hq + 2 * self.Hkv) * self.D)
+        self.q_i8 = e(m, self.Hq, self.D, dt=torch.int8)
+        self.q_s = e(m, self.Hq, dt=torch.float32)
+        self.attn = e(m, self.Hq * self.D)
+        self.gu = e(m, 2 * self.F)
+        self.ws = torch.empty(ops.decode_workspace_bytes(m, self.Hq, self.D, max_ctx),
+                              dtype=torch.uint8, device=dev)
+        if model.is_last:
+            self.logits = e(m, self.V)
+        self.dev = dev
+
+    # ---------------------------------------------------------------------- pieces ----
+    def _gemm(self, xq, xs, w, s, out, M):
+        call("s8b_gemm_w8a8", ptr(xq), ptr(xs), ptr(w), ptr(s), ptr(out), 0, M, w.shape[0],
+             w.shape[1], 0, stream())
+
+    def _rms_quant(self, h, res_in, res_out, w, M, K):
+        call("s8b_rmsnorm_quant", ptr(h), ptr(res_in), ptr(res_out), ptr(w), self.eps, ptr(self.xq),
+             ptr(self.xs), None, M, K, 0, stream())
+
+    def layer(self, li: int, mb: MicroBatch, M: int, first_layer_of_model: bool):
+        L = self.model.layers[li]
+        kc, ks, vc, vs = self.pool.layer(li)
+        H, st = self.H, stream()
+        # input_layernorm (fused residual add, except on the model's first layer)
+        self._rms_quant(self.h, None if first_layer_of_model else self.res, self.res, L.in_norm, M, H)
+        self._gemm(self.xq, self.xs, L.qkv_w, L.qkv_s, self.qkv, M)
+        call("s8b_qkv_post", ptr(self.qkv), ptr(mb.positions), ptr(self.cos), ptr(self.sin),
+             self.cos.shape[0], ptr(L.q_norm), ptr(L.k_norm), self.eps, M, self.Hq, self.Hkv,
+             self.D, ptr(self.q_i8), ptr(self.q_s), None, ptr(kc), ptr(ks), ptr(vc), ptr(vs),
+             None, ptr(mb.block_table), mb.block_table.shape[1], self.pool.block_size, 0, st)
+        call("s8b_paged_decode_q8", ptr(self.q_i8), ptr(self.q_s), ptr(kc), ptr(ks), ptr(vc),
+             ptr(vs), ptr(mb.block_table), ptr(mb.context_lens), ptr(self.attn), ptr(self.xq),
+             ptr(self.xs), M, self.Hq, self.Hkv, self.D, self.pool.block_size,
+             mb.block_table.shape[1], self.max_ctx, self.scale, ptr(self.ws), self.ws.numel(), 0,
+             st)
+        self._gemm(self.xq, self.xs, L.o_w, L.o_s, self.h, M)
+        self._rms_quant(self.h, self.res, self.res, L.post_norm, M, H)
+        self._gemm(self.xq, self.xs, L.gu_w, L.gu_s, self.gu, M)
+        call("s8b_silu_mul_quant", ptr(self.gu), M, self.F, None, ptr(self.xq), ptr(self.xs), 0, st)
+        self._gemm(self.xq, self.xs, L.d_w, L.d_s, self.h, M)
+
+    def run(self, mb: MicroBatch, M: int | None = None, *, boundary_in=None, boundary_out=None):
+        """Enqueue the stage's work for one micro-batch on the current stream.
+
+        boundary_in: (payload, scales, scheme) received from the previous stage.
+        boundary_out: (payload, scales, scheme) in the next stage's memory (may be a peer's).
+        """
+        M = self.m if M is None else M
+        st = stream()
+        first_model_layer = self.model.start == 0
+        if self.model.is_first:
+            call("s8b_embed", ptr(mb.ids), ptr(self.model.embed), M, self.H, ptr(self.h), 0, st)
+        else:
+            pay, sc, scheme = boundary_in
+            call("s8b_codec_decode", pay.data_ptr(), sc.data_ptr(), M, self.H, self.H,
+                 CODEC[scheme], ptr(self.h), ptr(self.res), 0, st)
+        for li in range(len(self.model.layers)):
+            self.layer(li, mb, M, first_model_layer and li == 0)
+        if self.model.is_last:
+            self._rms_quant(self.h, self.res, self.res, self.model.norm, M, self.H)
+            self._gemm(self.xq, self.xs, self.model.head_w, self.model.head_s, self.logits, M)
+            call("s8b_argmax", ptr(self.logits), M, self.V, ptr(mb.ids), 0, st)
+        else:
+            pay, sc, scheme = boundary_out
+            call("s8b_codec_encode", ptr(self.h), ptr(self.res), M, self.H, self.H, CODEC[scheme],
+                 pay.data_ptr(), sc.data_ptr(), 0, st)
+
+    def kernels_per_run(self) -> int:
+        n = 1 + 9 * len(self.model.layers)
+        return n + (3 if self.model.is_last else 1)

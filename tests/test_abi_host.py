@@ -1,0 +1,162 @@
+"""CPU: the C-ABI library loads and exports every entry point include/s8b.h declares; the
+host-side logic (block allocator, stage split, peer-route policy, wire accounting) matches the
+reference's own behaviour recorded in tests/golden/host_logic.json."""
+
+import json
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from superl8_serve_b200 import _lib
+from superl8_serve_b200.dist import peer_routes as pr
+from superl8_serve_b200.dist.pipeline import stage_bounds
+from superl8_serve_b200.engine import BlockAllocator
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+def declared_symbols() -> list[str]:
+    names = []
+    for h in (REPO / "include").glob("*.h"):
+        txt = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names += re.findall(r"\b(s8b_[a-z0-9_]+)\s*\(", txt)
+    return sorted(set(names))
+
+
+def test_library_exports_every_declared_symbol(lib):
+    names = declared_symbols()
+    assert len(names) >= 25
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(names) <= set(_lib.SIGNATURES), set(names) - set(_lib.SIGNATURES)
+
+
+def test_strerror_and_version(lib):
+    assert _lib.strerror(0) == "ok"
+    assert "timed out" in _lib.strerror(-6)
+    assert lib.s8b_version() >= 1
+    assert lib.s8b_ipc_handle_size() == 64
+
+
+@pytest.mark.parametrize("call", [
+    lambda L: L.s8b_quant_rows(None, 0, None, None, 4, 16, None),
+    lambda L: L.s8b_gemm_w8a8(None, None, None, None, None, 0, 1, 1, 16, 0, None),
+    lambda L: L.s8b_paged_decode_q8(*([None] * 11), 1, 4, 2, 128, 16, 4, 64, 0.1, None, 0, 0, None),
+    lambda L: L.s8b_codec_encode(None, None, 1, 128, 0, 1, None, None, 0, None),
+    lambda L: L.s8b_flag_wait(None, None, 0, 1000, None, None),
+])
+def test_null_arguments_are_rejected_without_touching_the_gpu(lib, call):
+    assert call(lib) == -8
+
+
+def test_shape_and_scheme_validation(lib):
+    buf = 1  # any non-null pointer: validation happens before dereference
+    assert lib.s8b_gemm_w8a8(buf, buf, buf, buf, buf, 0, 1, 1, 17, 0, None) == -1  # K % 16
+    assert lib.s8b_codec_encode(buf, None, 1, 100, 0, 2, buf, buf, 0, None) == -1  # -had needs 128
+    assert lib.s8b_codec_encode(buf, None, 1, 128, 0, 9, buf, buf, 0, None) == -2  # scheme
+    assert lib.s8b_quant_rows(buf, 7, buf, buf, 1, 16, None) == -2  # dtype
+    # workspace too small
+    assert lib.s8b_paged_decode_q8(*([16] * 11), 1, 4, 2, 128, 16, 4, 64, 0.1, 16, 1, 0, None) == -7
+
+
+def test_workspace_and_codec_sizes(lib):
+    P = (2049 + 255) // 256
+    assert lib.s8b_paged_decode_workspace_size(64, 32, 128, 2049) == 64 * 32 * P * 130 * 4
+    assert lib.s8b_codec_payload_bytes(4, 8192, 2, 0) == 4 * 8192
+    assert lib.s8b_codec_scale_count(4, 8192, 2) == 4
+    assert lib.s8b_codec_payload_bytes(4, 8192, 4, 0) == 4 * 4096
+    assert lib.s8b_codec_scale_count(4, 8192, 4) == 4 * 64
+    assert lib.s8b_codec_payload_bytes(4, 8192, 0, 0) == 4 * 8192 * 2
+
+
+def test_product_fails_loudly_on_cpu_tensors():
+    from superl8_serve_b200 import ops
+
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.quant_rows(torch.zeros(2, 16, dtype=torch.bfloat16))
+
+
+@pytest.fixture(scope="module")
+def host_golden(golden_dir):
+    return json.loads((golden_dir / "host_logic.json").read_text())
+
+
+def test_stage_bounds_match_reference(host_golden):
+    for key, bounds in host_golden["stage_bounds"].items():
+        L, S = map(int, key.split("_"))
+        assert stage_bounds(L, S) == bounds
+
+
+def test_block_allocator_matches_reference_paged_cache(host_golden):
+    g = host_golden["kv_alloc"]
+    a = BlockAllocator(num_blocks=4 * 4, num_slots=4, block_size=16, max_blocks_per_seq=4)
+    s0, s1 = a.alloc(), a.alloc()
+    a.ensure_capacity([s0, s1], [20, 33])
+    s2 = a.alloc()
+    a.free(s0)
+    a.ensure_capacity([s2, s1], [5, 50])
+    assert [s0, s1, s2] == g["slots"]
+    assert a._slot_blocks == g["slot_blocks"]
+    assert a.block_table([s1, s2]).tolist() == g["block_table_bc"]
+    bs = 16
+    sm = [a._slot_blocks[s][p // bs] * bs + p % bs for s, p in zip([s1, s2, s1], [0, 3, 49])]
+    assert sm == g["slot_mapping"]
+    from oracle.kernels import flat_rows
+
+    assert flat_rows(np.array([0, 17, 49]), 2, 16).reshape(-1).tolist() == g["flat_rows"]
+    assert a.num_blocks - len(a._free_blocks) == g["used_blocks"]
+
+
+def test_parse_validated_pairs_matches_reference(host_golden):
+    for spec, want in host_golden["parse_validated_pairs"].items():
+        if isinstance(want, str):
+            with pytest.raises(ValueError):
+                pr.parse_validated_pairs(spec)
+        else:
+            assert sorted(map(list, pr.parse_validated_pairs(spec))) == want
+
+
+def test_select_route_matches_reference(host_golden):
+    for spec, src, dst, cap, want in host_golden["select_route"]:
+        val = pr.parse_validated_pairs(spec)
+        assert list(pr.select_route(src, dst, validated=val, capability=cap)) == want
+
+
+def test_validated_pairs_env_names(monkeypatch):
+    monkeypatch.delenv(pr.VALIDATED_PAIRS_ENV, raising=False)
+    monkeypatch.setenv(pr.LEGACY_VALIDATED_PAIRS_ENV, "0,1")
+    assert pr.validated_pairs() == frozenset({(0, 1)})
+    monkeypatch.setenv(pr.VALIDATED_PAIRS_ENV, "2,3")
+    assert pr.validated_pairs() == frozenset({(2, 3)})
+    assert pr.peer_route_allowed(2, 3, capability=True) == (True, "validated-p2p")
+    assert pr.peer_route_allowed(0, 1, capability=True) == (False, "not-validated")
+    assert pr.all_pairs_spec([0, 1, 2]) == "0,1;0,2;1,2"
+
+
+def test_accuracy_report_matches_reference(golden_dir, host_golden):
+    from superl8_serve_b200.dist import accuracy_report
+
+    d = np.load(golden_dir / "acc_inputs.npz")
+    rep = accuracy_report(torch.from_numpy(d["x"]), torch.from_numpy(d["xr"]), "int8")
+    want = host_golden["accuracy_report"]
+    assert rep["sqnr_db"] == pytest.approx(want["sqnr_db"], rel=1e-6)
+    assert rep["cos"] == pytest.approx(want["cos"], rel=1e-6)
+    assert rep["sqnr_pass"] == want["sqnr_pass"] and rep["cos_pass"] == want["cos_pass"]
+    x = torch.from_numpy(d["x"])
+    assert accuracy_report(x, x.clone(), "fp16")["sqnr_db"] == float("inf")
+
+
+def test_transfer_handle_wire_bytes_match_reference(host_golden):
+    from superl8_serve_b200.dist import TransferHandle
+
+    pays = {"int8": ((4, 8192), torch.int8, (4,)), "int4": ((4, 4096), torch.int8, (4, 64)),
+            "fp16": ((4, 8192), torch.bfloat16, (0,))}
+    for scheme, want, want_ms in host_golden["on_wire_bytes"]:
+        shp, dt, sc = pays[scheme]
+        h = TransferHandle(0, 1, scheme, torch.Size((4, 1, 8192)), torch.bfloat16, None,
+                           torch.empty(shp, dtype=dt), torch.empty(sc), 0.0, 0.0)
+        assert h.on_wire_bytes == want
+        assert h.theoretical_wire_ms == pytest.approx(want_ms)

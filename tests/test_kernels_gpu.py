@@ -1,0 +1,284 @@
+"""GPU: every s8b kernel against the CPU oracle on the same seeded inputs, through the C ABI.
+
+Integer results (int32 accumulators, int8 codes, packed nibbles, argmax) must be identical;
+floating results (scales, bf16 outputs) must be identical too, because the oracle states the
+exact binary32 operation sequence the kernels perform."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import codec as oc
+from oracle import kernels as ok
+from oracle import numerics as on
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def bf16(x: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(torch.bfloat16).to(DEV)
+
+
+def f32(t: torch.Tensor) -> np.ndarray:
+    return t.float().cpu().numpy()
+
+
+def rand_act(rng, shape, scale=1.0, outliers=0):
+    x = rng.standard_normal(shape).astype(np.float32) * scale
+    if outliers:
+        cols = rng.choice(shape[-1], outliers, replace=False)
+        x[..., cols] *= 20
+    return on.round_bf16(x)
+
+
+@pytest.fixture
+def rng():
+    return np.random.default_rng(1234)
+
+
+@pytest.mark.parametrize("M,K", [(1, 4096), (5, 1024), (64, 12288), (3, 160)])
+def test_quant_rows(rng, M, K):
+    from superl8_serve_b200 import ops
+
+    x = rand_act(rng, (M, K), 3.0)
+    x[0] = 0.0  # all-zero row -> scale 1, zero codes
+    q, s = ops.quant_rows(bf16(x))
+    qo, so = on.quant_rows_i8(x)
+    assert np.array_equal(q.cpu().numpy(), qo)
+    assert np.array_equal(s.cpu().numpy(), so)
+
+
+@pytest.mark.parametrize("M,H,first", [(4, 1024, True), (7, 4096, False), (64, 4096, False),
+                                       (2, 5120, False)])
+def test_rmsnorm_quant(rng, M, H, first):
+    from superl8_serve_b200 import ops
+
+    h = rand_act(rng, (M, H), 2.0)
+    r = None if first else rand_act(rng, (M, H), 4.0)
+    w = on.round_bf16(1 + 0.1 * rng.standard_normal(H).astype(np.float32))
+    res, q, s, y = ops.rmsnorm_quant(bf16(h), None if first else bf16(r), bf16(w), 1e-6, y_out=True)
+    xo, qo, so, yo = ok.rmsnorm_quant(h, r, w, 1e-6)
+    assert np.array_equal(f32(res), xo)
+    assert np.array_equal(f32(y), yo)
+    assert np.array_equal(q.cpu().numpy(), qo)
+    assert np.array_equal(s.cpu().numpy(), so)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 6144, 4096), (4, 4096, 4096), (8, 24576, 4096),
+                                   (13, 4096, 12288), (64, 1024, 3072), (3, 100, 48)])
+def test_gemm_w8a8_int32_accumulators_bit_exact(rng, M, N, K):
+    from superl8_serve_b200 import ops
+
+    xq = rng.integers(-127, 128, (M, K), dtype=np.int8)
+    w = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    w[0] = 127  # extreme row: |acc| up to K*127^2
+    xq[0] = 127
+    xs = rng.uniform(0.001, 0.05, M).astype(np.float32)
+    ws = rng.uniform(0.0001, 0.001, N).astype(np.float32)
+    t = lambda a: torch.from_numpy(a).to(DEV)  # noqa: E731
+    acc = ops.gemm_w8a8(t(xq), t(xs), t(w), t(ws), raw=True)
+    acc_o = ok.gemm_acc(xq, w)
+    assert np.array_equal(acc.cpu().numpy(), acc_o)
+    y = ops.gemm_w8a8(t(xq), t(xs), t(w), t(ws))
+    assert np.array_equal(f32(y), ok.gemm_w8a8(xq, xs, w, ws))
+
+
+@pytest.mark.parametrize("M,F", [(1, 3072), (6, 12288), (64, 12288)])
+def test_silu_mul_quant(rng, M, F):
+    from superl8_serve_b200 import ops
+
+    gu = rand_act(rng, (M, 2 * F), 3.0)
+    gu[0, :8] = [-100, -30, -0.0, 0.0, 30, 100, -88, 88]
+    q, s, y = ops.silu_mul_quant(bf16(gu), y_out=True)
+    yo = ok.silu_mul(gu)
+    qo, so = on.quant_rows_i8(yo)
+    assert np.array_equal(f32(y), yo)
+    assert np.array_equal(q.cpu().numpy(), qo)
+    assert np.array_equal(s.cpu().numpy(), so)
+
+
+def make_pool(rng, nb, hkv, bs=16):
+    kc = rng.integers(-127, 128, (nb, hkv, bs, 128), dtype=np.int8)
+    vc = rng.integers(-127, 128, (nb, hkv, bs, 128), dtype=np.int8)
+    ks = rng.uniform(0.01, 0.05, (nb, hkv, bs)).astype(np.float32)
+    vs = rng.uniform(0.01, 0.05, (nb, hkv, bs)).astype(np.float32)
+    return kc, ks, vc, vs
+
+
+def to_dev(*arrs):
+    return [torch.from_numpy(np.ascontiguousarray(a)).to(DEV) for a in arrs]
+
+
+@pytest.mark.parametrize("M,Hq,Hkv", [(4, 32, 8), (3, 16, 8), (2, 40, 8)])
+def test_qkv_post_and_paged_kv_write(rng, M, Hq, Hkv):
+    from superl8_serve_b200 import ops
+
+    D, bs, nb = 128, 16, 32
+    qkv = rand_act(rng, (M, (Hq + 2 * Hkv) * D), 2.0)
+    qn = on.round_bf16(1 + 0.1 * rng.standard_normal(D).astype(np.float32))
+    kn = on.round_bf16(1 + 0.1 * rng.standard_normal(D).astype(np.float32))
+    cos, sin = ok.rope_tables(D, 40960, 1e6)
+    pos = np.array([0, 17, 2048, 40959, 5][:M], dtype=np.int32)
+    bt = np.stack([rng.permutation(nb) for _ in range(M)]).astype(np.int32)[:, :]
+    bt_big = np.zeros((M, 2560), dtype=np.int32)
+    bt_big[:, :nb] = bt
+    # positions beyond nb*bs map through the table modulo the pool for this unit test
+    slots = np.array([bt_big[i, (p // bs) % nb] * bs + p % bs for i, p in enumerate(pos)], np.int32)
+    kc, ks, vc, vs = make_pool(rng, nb, Hkv)
+    kcd, ksd, vcd, vsd, sm = to_dev(kc, ks, vc, vs, slots)
+    q_i8, q_s, q_out = ops.qkv_post(bf16(qkv), to_dev(pos)[0], torch.from_numpy(cos).to(DEV),
+                                    torch.from_numpy(sin).to(DEV), bf16(qn), bf16(kn), 1e-6, Hq, Hkv,
+                                    kcd, ksd, vcd, vsd, slot_mapping=sm, q_out=True)
+    q, k, v = ok.qkv_post(qkv, pos, Hq, Hkv, D, qn, kn, 1e-6, cos, sin)
+    assert np.array_equal(f32(q_out), q)
+    qq, qs = ok.quant_q_for_attn(q)
+    assert np.array_equal(q_i8.cpu().numpy(), qq)
+    assert np.array_equal(q_s.cpu().numpy(), qs)
+    ok.kv_write_paged(k, v, kc, ks, vc, vs, slots, bs)
+    assert np.array_equal(kcd.cpu().numpy(), kc) and np.array_equal(ksd.cpu().numpy(), ks)
+    assert np.array_equal(vcd.cpu().numpy(), vc) and np.array_equal(vsd.cpu().numpy(), vs)
+
+
+@pytest.mark.parametrize("rotate", [True, False])
+def test_kv_write_paged_standalone(rng, rotate):
+    from superl8_serve_b200 import ops
+
+    T, Hkv, nb = 9, 8, 16
+    k = rand_act(rng, (T, Hkv, 128), 1.5)
+    v = rand_act(rng, (T, Hkv, 128), 1.5)
+    slots = rng.choice(nb * 16, T, replace=False).astype(np.int32)
+    kc, ks, vc, vs = make_pool(rng, nb, Hkv)
+    kcd, ksd, vcd, vsd, sm = to_dev(kc, ks, vc, vs, slots)
+    ops.kv_write_paged(bf16(k), bf16(v), kcd, ksd, vcd, vsd, sm, rotate_k=rotate)
+    ok.kv_write_paged(k, v, kc, ks, vc, vs, slots, 16, rotate_k=rotate)
+    assert np.array_equal(kcd.cpu().numpy(), kc) and np.array_equal(ksd.cpu().numpy(), ks)
+    assert np.array_equal(vcd.cpu().numpy(), vc) and np.array_equal(vsd.cpu().numpy(), vs)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,lens", [
+    (4, 32, 8, [1, 17, 256, 257]),       # partition edges, single token
+    (3, 16, 8, [600, 33, 1000]),         # ragged, several partitions
+    (2, 40, 8, [2049, 129]),             # 5:1 GQA (27B shape)
+    (1, 32, 4, [4096]),                  # 8:1 GQA (30B-A3B shape), 16 partitions
+])
+def test_paged_decode_bit_exact(rng, B, Hq, Hkv, lens):
+    from superl8_serve_b200 import ops
+
+    bs = 16
+    maxb = (max(lens) + bs - 1) // bs
+    nb = B * maxb + 3
+    kc, ks, vc, vs = make_pool(rng, nb, Hkv)
+    perm = rng.permutation(nb)
+    bt = np.zeros((B, maxb + 2), dtype=np.int32)
+    for b in range(B):
+        bt[b, :maxb] = perm[b * maxb:(b + 1) * maxb]
+    qq = rng.integers(-127, 128, (B, Hq, 128), dtype=np.int8)
+    qs = rng.uniform(0.002, 0.02, (B, Hq)).astype(np.float32)
+    cl = np.array(lens, dtype=np.int32)
+    scale = 128 ** -0.5
+    qqd, qsd, kcd, ksd, vcd, vsd, btd, cld = to_dev(qq, qs, kc, ks, vc, vs, bt, cl)
+    oq = torch.empty((B, Hq * 128), dtype=torch.int8, device=DEV)
+    osc = torch.empty(B, dtype=torch.float32, device=DEV)
+    out = ops.paged_decode_q8(qqd, qsd, kcd, ksd, vcd, vsd, btd, cld, max(lens) + 5, scale,
+                              out_q=oq, out_s=osc)
+    ref = ok.paged_decode(qq, qs, kc, ks, vc, vs, bt, cl, bs, scale).reshape(B, -1)
+    assert np.array_equal(f32(out), ref)
+    rq, rs = on.quant_rows_i8(ref)
+    assert np.array_equal(oq.cpu().numpy(), rq) and np.array_equal(osc.cpu().numpy(), rs)
+
+
+def test_paged_decode_reference_layout(rng):
+    """s8b_paged_decode takes the reference's [B, H, 1, D] bf16 query."""
+    from superl8_serve_b200 import ops
+
+    B, Hq, Hkv, bs, n = 2, 32, 8, 16, 300
+    maxb = (n + bs - 1) // bs
+    kc, ks, vc, vs = make_pool(rng, B * maxb, Hkv)
+    bt = rng.permutation(B * maxb).reshape(B, maxb).astype(np.int32)
+    q = rand_act(rng, (B, Hq, 128), 1.0)
+    cl = np.array([n, 77], dtype=np.int32)
+    kcd, ksd, vcd, vsd, btd, cld = to_dev(kc, ks, vc, vs, bt, cl)
+    out = ops.paged_decode(bf16(q).reshape(B, Hq, 1, 128), kcd, ksd, vcd, vsd, btd, cld, n, 0.088)
+    qq, qs = ok.quant_q_for_attn(q)
+    ref = ok.paged_decode(qq, qs, kc, ks, vc, vs, bt, cl, bs, 0.088)
+    assert np.array_equal(f32(out).reshape(B, Hq, 128), ref)
+
+
+def test_embed_and_argmax(rng):
+    from superl8_serve_b200 import ops
+
+    V, H = 1000, 1024
+    table = rand_act(rng, (V, H), 0.02)
+    ids = np.array([0, 999, 5, 5], dtype=np.int32)
+    out = ops.embed(to_dev(ids)[0], bf16(table))
+    assert np.array_equal(f32(out), table[ids])
+    logits = rand_act(rng, (5, 151936), 1.0)
+    logits[1, 10] = logits[1, 20] = 50.0   # tie -> lowest index
+    logits[2, 151935] = 60.0               # last column
+    logits[3] = -3.0                       # all equal -> 0
+    tok = ops.argmax(bf16(logits))
+    assert np.array_equal(tok.cpu().numpy(), ok.argmax_rows(logits))
+
+
+@pytest.mark.parametrize("scheme", ["fp16", "int8", "int8-had", "int4", "int4-had"])
+@pytest.mark.parametrize("T", [1, 16, 64, 256, 1024])
+def test_codec_bit_exact_config2(rng, scheme, T):
+    """BASELINE config 2 inputs: [T, 4096] N(0,1) with 0.1% channels x20 (bf16)."""
+    from superl8_serve_b200 import ops
+
+    x = rand_act(rng, (T, 4096), 1.0, outliers=4)
+    pay, sc = ops.codec_encode(bf16(x), None, scheme)
+    po, so = oc.encode(x, scheme)
+    nb = po.size * po.itemsize
+    got = pay.cpu().numpy()[:nb].view(po.dtype).reshape(po.shape)
+    assert np.array_equal(got, po)
+    if so.size:
+        assert np.array_equal(sc.cpu().numpy()[: so.size].reshape(so.shape), so)
+    rec, _ = ops.codec_decode(pay, sc, T, 4096, 0, scheme, torch.bfloat16)
+    assert np.array_equal(f32(rec), oc.decode(po, so, scheme, 4096))
+
+
+@pytest.mark.parametrize("scheme", ["int8", "int8-had", "int4-had"])
+def test_codec_two_sources_pipeline_boundary(rng, scheme):
+    """(hidden, residual) packed as one [T, 2H] row without materialising the concat."""
+    from superl8_serve_b200 import ops
+
+    T, H = 5, 4096
+    h = rand_act(rng, (T, H), 1.0)
+    r = rand_act(rng, (T, H), 8.0)
+    pay, sc = ops.codec_encode(bf16(h), bf16(r), scheme)
+    po, so = oc.encode(np.concatenate([h, r], -1), scheme)
+    assert np.array_equal(pay.cpu().numpy()[: po.nbytes].view(po.dtype).reshape(po.shape), po)
+    oa, ob = ops.codec_decode(pay, sc, T, H, H, scheme, torch.bfloat16)
+    ref = oc.decode(po, so, scheme, 2 * H)
+    assert np.array_equal(f32(oa), ref[:, :H]) and np.array_equal(f32(ob), ref[:, H:])
+
+
+def test_fp16_activation_dtype(rng):
+    """fp16 activations: same recipes, fp16 rounding."""
+    from superl8_serve_b200 import ops
+
+    x = rng.standard_normal((3, 512)).astype(np.float32).astype(np.float16).astype(np.float32)
+    q, s = ops.quant_rows(torch.from_numpy(x).half().to(DEV))
+    qo, so = on.quant_rows_i8(x)
+    assert np.array_equal(q.cpu().numpy(), qo) and np.array_equal(s.cpu().numpy(), so)
+
+
+def test_flag_wait_times_out_and_reports(rng):
+    """A flag nobody sets: the bounded wait returns, the stream stays usable, status says why."""
+    from superl8_serve_b200._lib import call, ptr, stream
+
+    flag = torch.zeros(1, dtype=torch.int32, device=DEV)
+    epoch = torch.tensor([5], dtype=torch.int32, device=DEV)
+    status = torch.zeros(3, dtype=torch.int32, device=DEV)
+    call("s8b_flag_wait", ptr(flag), ptr(epoch), 1, 20_000_000, ptr(status), stream())
+    torch.cuda.synchronize()
+    st = status.cpu().tolist()
+    assert st[0] == -6 and st[1] == 6 and st[2] == 0
+    # set then wait: completes immediately
+    status.zero_()
+    call("s8b_flag_set", ptr(flag), ptr(epoch), 1, stream())
+    call("s8b_flag_wait", ptr(flag), ptr(epoch), 1, 1_000_000_000, ptr(status), stream())
+    torch.cuda.synchronize()
+    assert status.cpu().tolist()[0] == 0 and flag.item() == 6
