@@ -27,7 +27,9 @@ static std::mutex g_smem_mu;
 static std::map<std::pair<const void *, int>, size_t> g_smem_set;
 
 void ensure_smem(const void *kernel, size_t bytes) {
-  if (bytes <= 48 * 1024) return;
+  // Static shared memory counts against the same limit, so raise it for any dynamic size
+  // beyond a few KB rather than only above 48 KB.
+  if (bytes <= 8 * 1024) return;
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lk(g_smem_mu);
