@@ -36,6 +36,7 @@ extern "C" {
 #define S8B_ERR_TIMEOUT (-6)   /* a bounded device-side wait gave up (see s8b_flag_status) */
 #define S8B_ERR_WORKSPACE (-7) /* workspace missing or smaller than *_workspace_size       */
 #define S8B_ERR_ARG (-8)       /* null pointer or invalid argument                         */
+#define S8B_ERR_SCRATCH_LIMIT (-9) /* problem needs more than the no-allocation scratch limit */
 
 /* ---- activation dtypes -------------------------------------------------------------- */
 #define S8B_BF16 0
@@ -128,6 +129,27 @@ int s8b_paged_decode_q8(const int8_t *q_i8, const float *q_s, const int8_t *kc, 
                         int B, int Hq, int Hkv, int D, int block_size, int max_blocks,
                         int max_ctx, float scale, void *workspace, size_t workspace_bytes,
                         int dtype, void *stream);
+
+/* No-allocation form of s8b_paged_decode_q8, for callers that cannot allocate device
+ * memory: a host-language binding (cgo, JNI, ctypes) that is handed device buffers but owns no
+ * allocator, or a serving runtime that reserved all of HBM up front (KV pool sized to fill
+ * the GPU) and must not call cudaMalloc on the decode path, where it could fail or stall the
+ * device. It takes no workspace: the partition partials live in a fixed 16 MiB array in the
+ * library's device memory (held on every GPU that loads the library, until exit). Requests
+ * needing more than that, i.e. B*Hq*ceil(max_ctx/256)*(D+2)*4 bytes > 16 MiB, return
+ * S8B_ERR_SCRATCH_LIMIT without launching. The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress, with that device current); make that first call
+ * before any stream capture. All calls share the one array, so calls that overlap on the GPU
+ * (different streams, or different host threads on the same device) race; serialize them.
+ * The array keeps the last call's contents; nothing in it needs to start at zero.
+ * It calls no cudaMalloc / cudaFree or other allocating routine.
+ * This entry point has no counterpart in the reference.                                   */
+int s8b_paged_decode_q8_noalloc(const int8_t *q_i8, const float *q_s, const int8_t *kc,
+                                const float *ks, const int8_t *vc, const float *vs,
+                                const int32_t *block_table, const int32_t *context_lens,
+                                void *out, int8_t *out_q, float *out_s, int B, int Hq, int Hkv,
+                                int D, int block_size, int max_blocks, int max_ctx, float scale,
+                                int dtype, void *stream);
 
 /* Same attention with the reference's query layout: q [B, Hq, D] in dtype (rotated and
  * quantized internally into the workspace). out [B, Hq, D] in dtype.                     */

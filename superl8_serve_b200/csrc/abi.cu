@@ -53,6 +53,8 @@ extern "C" const char *s8b_strerror(int code) {
     case S8B_ERR_TIMEOUT: return "bounded device-side wait timed out";
     case S8B_ERR_WORKSPACE: return "workspace missing or too small";
     case S8B_ERR_ARG: return "null pointer or invalid argument";
+    case S8B_ERR_SCRATCH_LIMIT:
+      return "problem needs more scratch than the 16 MiB static limit of the no-allocation entry point";
     default: return "unknown s8b status";
   }
 }

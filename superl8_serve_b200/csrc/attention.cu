@@ -14,6 +14,9 @@
 //     activation dtype and, fused, its per-token int8 codes for the o_proj GEMM.
 // The fixed partition size and accumulation order make the result bit-identical to the CPU
 // oracle (oracle/kernels.py: paged_decode).
+#include <map>
+#include <mutex>
+
 #include "common.cuh"
 
 namespace s8b {
@@ -459,6 +462,71 @@ extern "C" int s8b_paged_decode_q8(const int8_t *q_i8, const float *q_s, const i
                                              context_lens, out, out_q, out_s, B, Hq, Hkv,
                                              block_size, max_blocks, max_ctx, scale,
                                              static_cast<float *>(workspace),
+                                             (cudaStream_t)stream));
+}
+
+// ---------------------------------------------------------- no-allocation variant ----
+// Scratch for s8b_paged_decode_q8_noalloc: the per-partition partial sums live in this
+// fixed device array instead of a caller workspace. Every GPU that loads the library holds
+// it until the process exits. Host code must not pass `g_decode_static_scratch` itself to a
+// kernel: on the host that name is only a stand-in for the device symbol, so its device
+// address is looked up once per device with cudaGetSymbolAddress.
+constexpr size_t kStaticScratchBytes = size_t(16) << 20;  // 16 MiB
+static __device__ __align__(256) float g_decode_static_scratch[kStaticScratchBytes / sizeof(float)];
+
+namespace {
+std::mutex g_static_scratch_mu;
+std::map<int, float *> g_static_scratch_addr;  // device ordinal -> device address
+
+// Runs on the calling thread's current device; the first call per device does the lookup.
+int static_scratch_address(float **out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    record_cuda_error(e);
+    return S8B_ERR_CUDA;
+  }
+  std::lock_guard<std::mutex> lk(g_static_scratch_mu);
+  auto it = g_static_scratch_addr.find(dev);
+  if (it == g_static_scratch_addr.end()) {
+    float *p = nullptr;
+    e = cudaGetSymbolAddress(reinterpret_cast<void **>(&p), g_decode_static_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      record_cuda_error(e);
+      return S8B_ERR_CUDA;
+    }
+    it = g_static_scratch_addr.emplace(dev, p).first;
+  }
+  *out = it->second;
+  return S8B_OK;
+}
+}  // namespace
+
+extern "C" int s8b_paged_decode_q8_noalloc(const int8_t *q_i8, const float *q_s, const int8_t *kc,
+                                           const float *ks, const int8_t *vc, const float *vs,
+                                           const int32_t *block_table,
+                                           const int32_t *context_lens, void *out, int8_t *out_q,
+                                           float *out_s, int B, int Hq, int Hkv, int D,
+                                           int block_size, int max_blocks, int max_ctx,
+                                           float scale, int dtype, void *stream) {
+  if (!q_i8 || !q_s || !kc || !ks || !vc || !vs || !block_table || !context_lens || !out ||
+      ((out_q == nullptr) != (out_s == nullptr)))
+    return S8B_ERR_ARG;
+  const int e = check_attn_shape(B, Hq, Hkv, D, block_size, max_blocks, max_ctx);
+  if (e) return e;
+  if (!aligned(q_i8, 16) || !aligned(kc, 16) || !aligned(vc, 16)) return S8B_ERR_ALIGN;
+  if (part_bytes(B, Hq, max_ctx) > kStaticScratchBytes) return S8B_ERR_SCRATCH_LIMIT;
+  if (dtype != S8B_BF16 && dtype != S8B_FP16) return S8B_ERR_DTYPE;
+  if (B == 0) return S8B_OK;
+  float *part = nullptr;
+  const int rc = static_scratch_address(&part);
+  if (rc) return rc;
+  // Partition partials are fully written before the combine reads them, so nothing in the
+  // shared array has to start at zero.
+  S8B_DISPATCH_DTYPE(dtype, T,
+                     return launch_decode<T>(q_i8, q_s, kc, ks, vc, vs, block_table,
+                                             context_lens, out, out_q, out_s, B, Hq, Hkv,
+                                             block_size, max_blocks, max_ctx, scale, part,
                                              (cudaStream_t)stream));
 }
 
