@@ -83,6 +83,19 @@ int s8b_rmsnorm_quant(const void *h, const void *residual_in, void *residual_out
 int s8b_gemm_w8a8(const int8_t *xq, const float *xs, const int8_t *w, const float *ws, void *y,
                   int out_kind, int M, int N, int K, int dtype, void *stream);
 
+/* W8A8 GEMM on the tensor cores (tcgen05.mma kind::i8, TMA-fed, TMEM accumulators), same
+ * arithmetic and outputs as s8b_gemm_w8a8, for token counts where the contraction is dense
+ * (M >= 16; M > 256 runs in 256-token passes). K % 128 == 0. The workspace
+ * (s8b_gemm_tc_workspace_size bytes, 256-byte aligned) must be zero-filled once by the
+ * caller; every completed launch leaves it zero again. workspace[0] (int32) receives
+ * S8B_ERR_TIMEOUT if a bounded wait inside the kernel gave up, after which the caller must
+ * re-zero the workspace. Launches sharing one workspace must be stream-ordered.
+ * Replaces superl8.linear / gemm_w8a8 (superl8serve/layers/linear.py:122).               */
+size_t s8b_gemm_tc_workspace_size(int M, int N);
+int s8b_gemm_w8a8_tc(const int8_t *xq, const float *xs, const int8_t *w, const float *ws,
+                     void *y, int out_kind, int M, int N, int K, int dtype, void *workspace,
+                     size_t workspace_bytes, void *stream);
+
 /* SwiGLU on a merged [gate | up] row (gu is [M, 2F]) followed by per-token int8 quant:
  *   a = dtype(g / (1 + exp(-g))), y = dtype(a * u), (q, s) = quant_rows(y); y_out nullable.
  * Replaces superl8.act_and_mul(x, "silu") (superl8serve/layers/activation.py:24) fused with

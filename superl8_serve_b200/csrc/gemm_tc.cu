@@ -1,0 +1,496 @@
+// W8A8 GEMM on the 5th-generation tensor cores (tcgen05.mma kind::i8) for decode token counts
+// that make the contraction dense enough (16..256 tokens per launch).
+//
+// Shape: y[m, n] = dequant( sum_k xq[m, k] * w[n, k] ). The MMA is issued "swap-AB":
+// A = 128 weight rows x 32 K-bytes, B = NT tokens x 32 K-bytes, D = 128 x NT int32 in TMEM,
+// so the weight matrix (the HBM stream) fills the 128-row MMA dimension and the small token
+// count is the N dimension.
+//
+// Work split. A unit is one 128-row x 128-byte weight chunk (16 KB). The units of all row
+// tiles are laid out tile-major and cut into one contiguous range per persistent CTA (one CTA
+// per SM), so every SM streams the same number of weight bytes whatever N and K are. A range
+// that covers a whole row tile stores the result directly; ranges that cover part of a tile
+// add their int32 partial sums into a workspace with red.global.add (exact: integer addition
+// is associative), and the CTA that completes a tile's K range (per-tile counter) dequantizes,
+// stores, and clears the workspace tile and counter for the next launch.
+//
+// Roles (192 threads): warp 0 issues TMA loads (128B swizzle, no multicast), warp 1 issues the
+// MMAs (one thread) and owns the TMEM allocation, warps 2-5 drain TMEM (32 lanes each). The
+// accumulator is double-buffered in TMEM so a tile's epilogue overlaps the next tile's MMAs.
+// Every mbarrier wait is bounded: on timeout the kernel records S8B_ERR_TIMEOUT in the
+// workspace status word, lets in-flight copies land, frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <map>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace s8b {
+namespace {
+
+constexpr int kBM = 128;          // weight rows per tile (MMA M)
+constexpr int kBK = 128;          // K bytes per stage (one 128B swizzle atom row)
+constexpr int kABytes = kBM * kBK;
+constexpr int kThreads = 192;
+constexpr int kMaxStages = 8;
+constexpr int kSmemBudget = 220 * 1024;
+constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s per wait before giving up
+
+struct TcSmemHeader {
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint32_t tmem_base;
+  int abort;
+  int is_last;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait. Returns false (and raises the CTA abort flag and the global status) on timeout
+// or when another role of the CTA already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
+                                          int32_t *status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = now_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if (now_ns() - t0 > kWaitNs) {
+      *abort = 1;
+      atomicExch(status, S8B_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor, K-major operand in 128B-swizzled 8-row x 128-byte atoms:
+// start >> 4 in [0,14), SBO = 1024 B (stride between 8-row groups) in [32,46), descriptor
+// version 1 in [46,48), layout SWIZZLE_128B (2) in [61,64). LBO is unused for this layout.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFF);
+  d |= static_cast<uint64_t>(1) << 16;
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+// Instruction descriptor kind::i8: D s32 [4,6)=2, A s8 [7,10)=1, B s8 [10,13)=1, both K-major,
+// N>>3 in [17,23), M>>4 in [24,29).
+template <int NT>
+__device__ __forceinline__ constexpr uint32_t i8_idesc() {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(NT >> 3) << 17) |
+         (static_cast<uint32_t>(kBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(
+          tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z));
+}
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15])
+      : "r"(addr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void epi_bar_sync() {
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+template <int NT>
+struct TcLayout {
+  static constexpr int kBBytes = NT * kBK;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages =
+      (kSmemBudget - 2048) / kStageBytes < kMaxStages ? (kSmemBudget - 2048) / kStageBytes
+                                                      : kMaxStages;
+  static constexpr int kTmemCols = 2 * NT < 32 ? 32 : 2 * NT;
+  static constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * kStageBytes + 1024;
+};
+
+struct TcArgs {
+  const float *xs;
+  const float *ws;
+  void *y;
+  int32_t *acc;       // workspace [NT][N] int32 (zero between launches)
+  int32_t *counters;  // workspace [n_tiles]
+  int32_t *status;    // workspace status word
+  int out_kind, M, N, K, m0, n_tiles, kc;
+};
+
+template <typename T, int NT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_w,
+                   const __grid_constant__ CUtensorMap tmap_x, TcArgs a) {
+  using Lay = TcLayout<NT>;
+  constexpr int S = Lay::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  TcSmemHeader *hdr = reinterpret_cast<TcSmemHeader *>(smem + static_cast<size_t>(S) * Lay::kStageBytes);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const long long U = static_cast<long long>(a.n_tiles) * a.kc;
+  const long long u0 = U * blockIdx.x / gridDim.x;
+  const long long u1 = U * (blockIdx.x + 1) / gridDim.x;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&hdr->full[s], 1);
+      mbar_init(&hdr->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&hdr->tmem_full[b], 1);
+      mbar_init(&hdr->tmem_empty[b], 128);
+    }
+    hdr->abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&hdr->tmem_base)),
+                 "r"(Lay::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = hdr->tmem_base;
+  volatile int *abort = &hdr->abort;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------- TMA producer ----
+    if (lane == 0) {
+      long long issued = 0;
+      for (long long u = u0; u < u1; ++u, ++issued) {
+        const int s = static_cast<int>(issued % S);
+        const uint32_t ph = static_cast<uint32_t>((issued / S) & 1);
+        if (!mbar_wait(&hdr->empty[s], ph ^ 1, abort, a.status)) break;
+        uint8_t *sa = smem + static_cast<size_t>(s) * Lay::kStageBytes;
+        const int tile = static_cast<int>(u / a.kc), kk = static_cast<int>(u % a.kc);
+        mbar_expect_tx(&hdr->full[s], Lay::kStageBytes);
+        tma_load_2d(sa, &tmap_w, kk * kBK, tile * kBM, &hdr->full[s]);
+        tma_load_2d(sa + kABytes, &tmap_x, kk * kBK, a.m0, &hdr->full[s]);
+      }
+      if (*abort) {
+        // let the copies already issued land before the CTA's shared memory goes away
+        const long long first = issued > S ? issued - S : 0;
+        for (long long i = first; i < issued; ++i) {
+          const uint64_t t0 = now_ns();
+          while (!mbar_try_wait(&hdr->full[i % S], static_cast<uint32_t>((i / S) & 1)) &&
+                 now_ns() - t0 < 100000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // -------------------------------------------------------------- MMA issuer ----
+    if (lane == 0) {
+      constexpr uint32_t idesc = i8_idesc<NT>();
+      long long it = 0;
+      int seg = 0;
+      for (long long u = u0; u < u1 && !*abort; ++u, ++it) {
+        const int kk = static_cast<int>(u % a.kc);
+        const bool first = (u == u0) || kk == 0;
+        const bool last = (u == u1 - 1) || kk == a.kc - 1;
+        const int buf = seg & 1;
+        if (first) {
+          if (!mbar_wait(&hdr->tmem_empty[buf], ((seg >> 1) & 1) ^ 1, abort, a.status)) break;
+          tc_fence_after();
+        }
+        const int s = static_cast<int>(it % S);
+        if (!mbar_wait(&hdr->full[s], static_cast<uint32_t>((it / S) & 1), abort, a.status)) break;
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + static_cast<size_t>(s) * Lay::kStageBytes);
+        const uint64_t ad = sw128_desc(sa), bd = sw128_desc(sa + kABytes);
+#pragma unroll
+        for (int k = 0; k < kBK / 32; ++k)
+          mma_i8(tmem + buf * NT, ad + 2 * k, bd + 2 * k, idesc, (first && k == 0) ? 0u : 1u);
+        mma_commit(&hdr->empty[s]);
+        if (last) {
+          mma_commit(&hdr->tmem_full[buf]);
+          ++seg;
+        }
+      }
+    }
+  } else {
+    // --------------------------------------------------------------- epilogue ----
+    const int quad = warp & 3;              // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;       // weight row within the tile
+    const int et = threadIdx.x - 64;        // 0..127
+    int seg = 0;
+    long long u = u0;
+    while (u < u1) {
+      const int tile = static_cast<int>(u / a.kc);
+      const int kk0 = static_cast<int>(u % a.kc);
+      const long long tile_end = static_cast<long long>(tile + 1) * a.kc;
+      const long long ue = u1 < tile_end ? u1 : tile_end;
+      const int nk = static_cast<int>(ue - u);
+      const bool whole = kk0 == 0 && nk == a.kc;
+      const int buf = seg & 1;
+      // One thread waits (bounded); the named barrier then releases the other 127 together,
+      // so on a timeout all epilogue threads leave the loop at the same point.
+      if (et == 0) mbar_wait(&hdr->tmem_full[buf], (seg >> 1) & 1, abort, a.status);
+      epi_bar_sync();
+      if (*abort) break;
+      tc_fence_after();
+      const int n = tile * kBM + row;
+      const float wsn = (n < a.N && a.out_kind == 0) ? a.ws[n] : 0.0f;
+#pragma unroll 1
+      for (int c0 = 0; c0 < NT; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * NT + c0, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int t = c0 + j, m = a.m0 + t;
+          if (m >= a.M || n >= a.N) continue;
+          const int32_t accv = static_cast<int32_t>(v[j]);
+          if (whole) {
+            const size_t o = static_cast<size_t>(m) * a.N + n;
+            if (a.out_kind == 1)
+              static_cast<int32_t *>(a.y)[o] = accv;
+            else
+              static_cast<T *>(a.y)[o] =
+                  from_f32<T>(__fmul_rn(__fmul_rn(static_cast<float>(accv), a.xs[m]), wsn));
+          } else {
+            atomicAdd(a.acc + static_cast<size_t>(t) * a.N + n, accv);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&hdr->tmem_empty[buf]);
+      if (!whole) {
+        __threadfence();
+        epi_bar_sync();
+        if (et == 0) {
+          const int old = atomicAdd(a.counters + tile, nk);
+          hdr->is_last = (old + nk == a.kc);
+        }
+        epi_bar_sync();
+        if (hdr->is_last) {
+          __threadfence();
+          for (int t = 0; t < NT; ++t) {
+            const int m = a.m0 + t;
+            if (m >= a.M || n >= a.N) continue;
+            int32_t *p = a.acc + static_cast<size_t>(t) * a.N + n;
+            const int32_t accv = __ldcg(p);
+            *p = 0;
+            const size_t o = static_cast<size_t>(m) * a.N + n;
+            if (a.out_kind == 1)
+              static_cast<int32_t *>(a.y)[o] = accv;
+            else
+              static_cast<T *>(a.y)[o] =
+                  from_f32<T>(__fmul_rn(__fmul_rn(static_cast<float>(accv), a.xs[m]), wsn));
+          }
+          if (et == 0) a.counters[tile] = 0;
+        }
+        epi_bar_sync();
+      }
+      ++seg;
+      u = ue;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(Lay::kTmemCols)
+                 : "memory");
+}
+
+// ----------------------------------------------------------------------- host side ----
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void *p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int make_map(CUtensorMap *map, const void *base, int inner, int outer, int box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return S8B_ERR_CUDA;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(inner)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_outer)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? S8B_OK : S8B_ERR_ALIGN;
+}
+
+int sm_count() {
+  static std::mutex mu;
+  static std::map<int, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  cache[dev] = n > 0 ? n : 148;
+  return cache[dev];
+}
+
+inline int pick_nt(int m) {
+  return m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : 256;
+}
+
+size_t ws_layout(int M, int N, size_t *counters_off, size_t *acc_off) {
+  const int nt = pick_nt(M < 256 ? M : 256);
+  const size_t n_tiles = (static_cast<size_t>(N) + kBM - 1) / kBM;
+  *counters_off = 256;
+  *acc_off = (256 + n_tiles * 4 + 255) / 256 * 256;
+  return *acc_off + static_cast<size_t>(nt) * N * 4;
+}
+
+template <typename T, int NT>
+int launch_tc_nt(const CUtensorMap &mw, const CUtensorMap &mx, const TcArgs &args, cudaStream_t st) {
+  using Lay = TcLayout<NT>;
+  auto kern = gemm_tc_kernel<T, NT>;
+  ensure_smem(reinterpret_cast<const void *>(kern), Lay::kSmem);
+  const long long U = static_cast<long long>(args.n_tiles) * args.kc;
+  const int grid = static_cast<int>(U < sm_count() ? U : sm_count());
+  kern<<<grid, kThreads, Lay::kSmem, st>>>(mw, mx, args);
+  return check_launch();
+}
+
+template <typename T>
+int launch_tc(const int8_t *xq, const float *xs, const int8_t *w, const float *ws, void *y,
+              int out_kind, int M, int N, int K, void *workspace, cudaStream_t st) {
+  size_t coff, aoff;
+  ws_layout(M, N, &coff, &aoff);
+  uint8_t *wsb = static_cast<uint8_t *>(workspace);
+  TcArgs args;
+  args.xs = xs;
+  args.ws = ws;
+  args.y = y;
+  args.status = reinterpret_cast<int32_t *>(wsb);
+  args.counters = reinterpret_cast<int32_t *>(wsb + coff);
+  args.acc = reinterpret_cast<int32_t *>(wsb + aoff);
+  args.out_kind = out_kind;
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.n_tiles = (N + kBM - 1) / kBM;
+  args.kc = K / kBK;
+  CUtensorMap mw;
+  int rc = make_map(&mw, w, K, N, kBM);
+  if (rc) return rc;
+  for (int m0 = 0; m0 < M; m0 += 256) {
+    const int mt = M - m0 < 256 ? M - m0 : 256;
+    const int nt = pick_nt(mt);
+    CUtensorMap mx;
+    rc = make_map(&mx, xq, K, M, nt);
+    if (rc) return rc;
+    args.m0 = m0;
+    switch (nt) {
+      case 16: rc = launch_tc_nt<T, 16>(mw, mx, args, st); break;
+      case 32: rc = launch_tc_nt<T, 32>(mw, mx, args, st); break;
+      case 64: rc = launch_tc_nt<T, 64>(mw, mx, args, st); break;
+      case 128: rc = launch_tc_nt<T, 128>(mw, mx, args, st); break;
+      default: rc = launch_tc_nt<T, 256>(mw, mx, args, st); break;
+    }
+    if (rc) return rc;
+  }
+  return S8B_OK;
+}
+
+}  // namespace
+}  // namespace s8b
+
+using namespace s8b;
+
+extern "C" size_t s8b_gemm_tc_workspace_size(int M, int N) {
+  size_t c, a;
+  return ws_layout(M, N, &c, &a);
+}
+
+extern "C" int s8b_gemm_w8a8_tc(const int8_t *xq, const float *xs, const int8_t *w,
+                                const float *ws, void *y, int out_kind, int M, int N, int K,
+                                int dtype, void *workspace, size_t workspace_bytes, void *stream) {
+  if (!xq || !w || !y || (out_kind == 0 && (!xs || !ws))) return S8B_ERR_ARG;
+  if (out_kind != 0 && out_kind != 1) return S8B_ERR_ARG;
+  if (M < 0 || N <= 0 || K <= 0 || K % kBK != 0) return S8B_ERR_SHAPE;
+  if (!aligned(xq, 16) || !aligned(w, 16)) return S8B_ERR_ALIGN;
+  if (!workspace || workspace_bytes < s8b_gemm_tc_workspace_size(M, N)) return S8B_ERR_WORKSPACE;
+  if (!aligned(workspace, 256)) return S8B_ERR_ALIGN;
+  if (M == 0) return S8B_OK;
+  S8B_DISPATCH_DTYPE(dtype, T,
+                     return launch_tc<T>(xq, xs, w, ws, y, out_kind, M, N, K, workspace,
+                                         (cudaStream_t)stream));
+}

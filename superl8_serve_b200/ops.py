@@ -9,7 +9,8 @@ import torch
 from ._lib import CODEC, call, dtype_code, ptr, stream
 
 __all__ = [
-    "quant_rows", "rmsnorm_quant", "gemm_w8a8", "silu_mul_quant", "qkv_post", "kv_write_paged",
+    "quant_rows", "rmsnorm_quant", "gemm_w8a8", "gemm_w8a8_tc", "gemm_tc_workspace",
+    "silu_mul_quant", "qkv_post", "kv_write_paged",
     "paged_decode_q8", "paged_decode", "embed", "argmax", "codec_encode", "codec_decode",
     "codec_sizes", "decode_workspace_bytes",
 ]
@@ -51,6 +52,30 @@ def gemm_w8a8(xq, xs, w, ws, *, out=None, out_dtype=torch.bfloat16, raw=False):
     dt = dtype_code(out_dtype if raw else out.dtype)
     call("s8b_gemm_w8a8", ptr(xq), ptr(xs), ptr(w), ptr(ws), ptr(out), 1 if raw else 0, M, N, K,
          dt, stream(xq.device))
+    return out
+
+
+def gemm_tc_workspace(M: int, N: int, device) -> torch.Tensor:
+    """Zero-filled workspace for s8b_gemm_w8a8_tc (kept zero by every completed launch)."""
+    from ._lib import load
+
+    n = int(load().s8b_gemm_tc_workspace_size(M, N))
+    return torch.zeros(n, dtype=torch.uint8, device=device)
+
+
+def gemm_w8a8_tc(xq, xs, w, ws, *, out=None, out_dtype=torch.bfloat16, raw=False, workspace=None):
+    """Tensor-core (tcgen05 kind::i8) form of gemm_w8a8; identical results."""
+    K = xq.shape[-1]
+    M = xq.numel() // K
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((*xq.shape[:-1], N), dtype=torch.int32 if raw else out_dtype,
+                          device=xq.device)
+    if workspace is None:
+        workspace = gemm_tc_workspace(M, N, xq.device)
+    dt = dtype_code(out_dtype if raw else out.dtype)
+    call("s8b_gemm_w8a8_tc", ptr(xq), ptr(xs), ptr(w), ptr(ws), ptr(out), 1 if raw else 0, M, N, K,
+         dt, ptr(workspace), workspace.numel(), stream(xq.device))
     return out
 
 

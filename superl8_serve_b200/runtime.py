@@ -194,8 +194,11 @@ class MicroBatch:
 class StageRunner:
     """Launches one stage's decode kernels for a micro-batch of up to ``m`` rows."""
 
+    # token count from which the W8A8 GEMMs run on the tensor cores (tcgen05) instead of dp4a
+    TC_MIN_TOKENS = 16
+
     def __init__(self, model: StageModel, pool: KVPool, m: int, max_ctx: int,
-                 dtype=torch.bfloat16):
+                 dtype=torch.bfloat16, tc_min_tokens: int | None = None):
         cfg = model.cfg
         self.model, self.pool, self.m, self.max_ctx, self.dtype = model, pool, m, max_ctx, dtype
         self.H = cfg.hidden_size
@@ -226,11 +229,19 @@ class StageRunner:
         if model.is_last:
             self.logits = e(m, self.V)
         self.dev = dev
+        self.tc_min = self.TC_MIN_TOKENS if tc_min_tokens is None else tc_min_tokens
+        n_max = max([L.gu_w.shape[0] for L in model.layers] + [L.qkv_w.shape[0] for L in model.layers]
+                    + ([model.head_w.shape[0]] if model.is_last else []) + [self.H])
+        self.tc_ws = ops.gemm_tc_workspace(m, n_max, dev) if m >= self.tc_min else None
 
     # ---------------------------------------------------------------------- pieces ----
     def _gemm(self, xq, xs, w, s, out, M):
-        call("s8b_gemm_w8a8", ptr(xq), ptr(xs), ptr(w), ptr(s), ptr(out), 0, M, w.shape[0],
-             w.shape[1], 0, stream())
+        if self.tc_ws is not None and M >= self.tc_min:
+            call("s8b_gemm_w8a8_tc", ptr(xq), ptr(xs), ptr(w), ptr(s), ptr(out), 0, M, w.shape[0],
+                 w.shape[1], 0, ptr(self.tc_ws), self.tc_ws.numel(), stream())
+        else:
+            call("s8b_gemm_w8a8", ptr(xq), ptr(xs), ptr(w), ptr(s), ptr(out), 0, M, w.shape[0],
+                 w.shape[1], 0, stream())
 
     def _rms_quant(self, h, res_in, res_out, w, M, K):
         call("s8b_rmsnorm_quant", ptr(h), ptr(res_in), ptr(res_out), ptr(w), self.eps, ptr(self.xq),
