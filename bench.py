@@ -212,15 +212,14 @@ def kernel_rooflines(pipe, hbm_peak):
     def gemm():
         li = next(it) % L
         lw = r.model.layers[li]
-        call("s8b_gemm_w8a8", ptr(r.xq), ptr(r.xs), ptr(lw.gu_w), ptr(lw.gu_s), ptr(r.gu), 0, M,
-             lw.gu_w.shape[0], lw.gu_w.shape[1], 0, stream())
+        r._gemm(r.xq, r.xs, lw.gu_w, lw.gu_s, r.gu, M)
 
     ms = time_kernel(gemm, 4 * L)
     lw = r.model.layers[0]
     N, K = lw.gu_w.shape
     byts = N * K + N * 4 + M * K + M * 4 + M * N * 2
-    out["gemm_w8a8_gate_up"] = {"ms": ms, "bytes": byts, "gbs": byts / ms / 1e6,
-                                "launches_per_step": 36}
+    name = "gemm_w8a8_tc_gate_up" if r.tc_ws is not None and M >= r.tc_min else "gemm_w8a8_gate_up"
+    out[name] = {"ms": ms, "bytes": byts, "gbs": byts / ms / 1e6, "launches_per_step": L}
     # paged decode attention (partition + combine) for one layer
     it2 = iter(range(10 ** 9))
 
@@ -236,7 +235,7 @@ def kernel_rooflines(pipe, hbm_peak):
     ctx = int(mb.context_lens[0].item())
     byts = M * ctx * r.Hkv * (2 * 128 + 2 * 4) + M * r.Hq * (128 + 4) + M * r.Hq * 128 * 3
     out["paged_decode_attention"] = {"ms": ms, "bytes": byts, "gbs": byts / ms / 1e6,
-                                     "launches_per_step": 36}
+                                     "launches_per_step": L}
     for v in out.values():
         v["frac"] = v["gbs"] / hbm_peak
     return out
@@ -263,6 +262,8 @@ def run_single(args):
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
     cfg = qwen3_8b()
+    if args.layers:
+        cfg = cfg.with_(num_hidden_layers=args.layers)
     B, ctx = args.batch, args.ctx
     max_len = ctx + args.warmup + args.steps + 16
     model = StageModel.synthetic(cfg, 0, cfg.num_hidden_layers, dev, first=True, last=True, seed=1)
@@ -326,7 +327,8 @@ def run_single(args):
         "vs_baseline": None, "dtype": "int8 x int8 -> int32 GEMM, bf16 activations",
         "data": "synthetic (random int8 weights, KV pre-filled with random codes)",
         "config": {"workload": "qwen3-8b-shaped W8A8 decode (BASELINE config 3)",
-                   "micro_batch": B, "n_micro": 1, "global_batch": B, "ctx": ctx, "layers": 36,
+                   "micro_batch": B, "n_micro": 1, "global_batch": B, "ctx": ctx,
+                   "layers": cfg.num_hidden_layers,
                    "block_size": 16, "parallelism": "pp1", "wire_scheme": args.scheme,
                    "cuda_graph": True, "l2": "inputs (17.5 GB) > L2, no flush"},
         "gpu_launches": int(per_step_launches) * args.steps,
@@ -357,6 +359,8 @@ def main():
     ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--scheme", default="int8-had")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="profiling only: fewer layers than the model's 36 (small ncu case)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
