@@ -96,6 +96,16 @@ int s8b_gemm_w8a8_tc(const int8_t *xq, const float *xs, const int8_t *w, const f
                      void *y, int out_kind, int M, int N, int K, int dtype, void *workspace,
                      size_t workspace_bytes, void *stream);
 
+/* Weight pre-packing for the tensor-core GEMM: W [N, K] row-major int8 -> units of 128 rows x
+ * 128 bytes, tile-major, each unit stored as the 128B-swizzled shared-memory image the MMA
+ * reads (rows beyond N zero). s8b_gemm_w8a8_tc_packed then streams every CTA's share of the
+ * matrix as one contiguous HBM range with plain bulk copies. Packing runs once at load.     */
+size_t s8b_tc_packed_bytes(int N, int K);
+int s8b_pack_weights_tc(const int8_t *w, int N, int K, int8_t *packed, void *stream);
+int s8b_gemm_w8a8_tc_packed(const int8_t *xq, const float *xs, const int8_t *wpacked,
+                            const float *ws, void *y, int out_kind, int M, int N, int K,
+                            int dtype, void *workspace, size_t workspace_bytes, void *stream);
+
 /* SwiGLU on a merged [gate | up] row (gu is [M, 2F]) followed by per-token int8 quant:
  *   a = dtype(g / (1 + exp(-g))), y = dtype(a * u), (q, s) = quant_rows(y); y_out nullable.
  * Replaces superl8.act_and_mul(x, "silu") (superl8serve/layers/activation.py:24) fused with

@@ -32,6 +32,10 @@ SIGNATURES: dict[str, tuple] = {
     "s8b_silu_mul_quant": (_i, [_vp, _i, _i, _vp, _vp, _vp, _i, _vp]),
     "s8b_gemm_tc_workspace_size": (_sz, [_i, _i]),
     "s8b_gemm_w8a8_tc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
+    "s8b_tc_packed_bytes": (_sz, [_i, _i]),
+    "s8b_pack_weights_tc": (_i, [_vp, _i, _i, _vp, _vp]),
+    "s8b_gemm_w8a8_tc_packed": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz,
+                                     _vp]),
     "s8b_qkv_post": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp, _f, _i, _i, _i, _i, _vp, _vp, _vp,
                           _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "s8b_kv_write_paged": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),

@@ -22,6 +22,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <map>
 #include <mutex>
 
@@ -103,6 +104,37 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
       : "memory");
 }
 
+// Plain bulk copy global -> shared of `bytes` contiguous bytes (16-byte aligned, multiple of
+// 16), completing on the stage's mbarrier like a TMA tile load.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
+                                          uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Pack W [N, K] (row-major int8) into unit images: unit (tile, kc) holds rows
+// tile*128..+127, bytes kc*128..+127 as the 128B-swizzled K-major shared-memory image
+// (16-byte chunk c of row r stored at chunk c ^ (r % 8)); rows beyond N are zero.
+__global__ void pack_tc_kernel(const int8_t *__restrict__ w, int N, int K,
+                               int8_t *__restrict__ packed) {
+  const int kc = K / kBK;
+  const size_t chunks = static_cast<size_t>((N + kBM - 1) / kBM) * kc * kBM * 8;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < chunks;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i & 7);
+    const int r = static_cast<int>((i >> 3) % kBM);
+    const size_t unit = (i >> 3) / kBM;
+    const int tile = static_cast<int>(unit / kc), kk = static_cast<int>(unit % kc);
+    const int n = tile * kBM + r;
+    int4 v = make_int4(0, 0, 0, 0);
+    if (n < N) v = *reinterpret_cast<const int4 *>(w + static_cast<size_t>(n) * K + kk * kBK + c * 16);
+    *reinterpret_cast<int4 *>(packed + unit * kABytes + r * kBK + ((c ^ (r & 7)) * 16)) = v;
+  }
+}
+
 // Shared-memory matrix descriptor, K-major operand in 128B-swizzled 8-row x 128-byte atoms:
 // start >> 4 in [0,14), SBO = 1024 B (stride between 8-row groups) in [32,46), descriptor
 // version 1 in [46,48), layout SWIZZLE_128B (2) in [61,64). LBO is unused for this layout.
@@ -172,6 +204,7 @@ struct TcLayout {
 };
 
 struct TcArgs {
+  const int8_t *wpacked;  // weights pre-packed into shared-memory images (null: TMA 2D path)
   const float *xs;
   const float *ws;
   void *y;
@@ -232,7 +265,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t *sa = smem + static_cast<size_t>(s) * Lay::kStageBytes;
         const int tile = static_cast<int>(u / a.kc), kk = static_cast<int>(u % a.kc);
         mbar_expect_tx(&hdr->full[s], Lay::kStageBytes);
-        tma_load_2d(sa, &tmap_w, kk * kBK, tile * kBM, &hdr->full[s]);
+        if (a.wpacked)
+          bulk_load(sa, a.wpacked + static_cast<size_t>(u) * kABytes, kABytes, &hdr->full[s]);
+        else
+          tma_load_2d(sa, &tmap_w, kk * kBK, tile * kBM, &hdr->full[s]);
         tma_load_2d(sa + kABytes, &tmap_x, kk * kBK, a.m0, &hdr->full[s]);
       }
       if (*abort) {
@@ -431,7 +467,8 @@ int launch_tc_nt(const CUtensorMap &mw, const CUtensorMap &mx, const TcArgs &arg
 
 template <typename T>
 int launch_tc(const int8_t *xq, const float *xs, const int8_t *w, const float *ws, void *y,
-              int out_kind, int M, int N, int K, void *workspace, cudaStream_t st) {
+              int out_kind, int M, int N, int K, void *workspace, cudaStream_t st,
+              bool packed = false) {
   size_t coff, aoff;
   ws_layout(M, N, &coff, &aoff);
   uint8_t *wsb = static_cast<uint8_t *>(workspace);
@@ -448,8 +485,13 @@ int launch_tc(const int8_t *xq, const float *xs, const int8_t *w, const float *w
   args.K = K;
   args.n_tiles = (N + kBM - 1) / kBM;
   args.kc = K / kBK;
+  args.wpacked = packed ? w : nullptr;
   CUtensorMap mw;
-  int rc = make_map(&mw, w, K, N, kBM);
+  int rc = S8B_OK;
+  if (packed)
+    memset(&mw, 0, sizeof(mw));
+  else
+    rc = make_map(&mw, w, K, N, kBM);
   if (rc) return rc;
   for (int m0 = 0; m0 < M; m0 += 256) {
     const int mt = M - m0 < 256 ? M - m0 : 256;
@@ -493,4 +535,33 @@ extern "C" int s8b_gemm_w8a8_tc(const int8_t *xq, const float *xs, const int8_t 
   S8B_DISPATCH_DTYPE(dtype, T,
                      return launch_tc<T>(xq, xs, w, ws, y, out_kind, M, N, K, workspace,
                                          (cudaStream_t)stream));
+}
+
+extern "C" size_t s8b_tc_packed_bytes(int N, int K) {
+  if (N <= 0 || K <= 0 || K % kBK != 0) return 0;
+  return static_cast<size_t>((N + kBM - 1) / kBM) * (K / kBK) * kABytes;
+}
+
+extern "C" int s8b_pack_weights_tc(const int8_t *w, int N, int K, int8_t *packed, void *stream) {
+  if (!w || !packed) return S8B_ERR_ARG;
+  if (N <= 0 || K <= 0 || K % kBK != 0) return S8B_ERR_SHAPE;
+  if (!aligned(w, 16) || !aligned(packed, 16)) return S8B_ERR_ALIGN;
+  pack_tc_kernel<<<4 * sm_count(), 256, 0, (cudaStream_t)stream>>>(w, N, K, packed);
+  return check_launch();
+}
+
+extern "C" int s8b_gemm_w8a8_tc_packed(const int8_t *xq, const float *xs, const int8_t *wpacked,
+                                       const float *ws, void *y, int out_kind, int M, int N,
+                                       int K, int dtype, void *workspace,
+                                       size_t workspace_bytes, void *stream) {
+  if (!xq || !wpacked || !y || (out_kind == 0 && (!xs || !ws))) return S8B_ERR_ARG;
+  if (out_kind != 0 && out_kind != 1) return S8B_ERR_ARG;
+  if (M < 0 || N <= 0 || K <= 0 || K % kBK != 0) return S8B_ERR_SHAPE;
+  if (!aligned(xq, 16) || !aligned(wpacked, 16)) return S8B_ERR_ALIGN;
+  if (!workspace || workspace_bytes < s8b_gemm_tc_workspace_size(M, N)) return S8B_ERR_WORKSPACE;
+  if (!aligned(workspace, 256)) return S8B_ERR_ALIGN;
+  if (M == 0) return S8B_OK;
+  S8B_DISPATCH_DTYPE(dtype, T,
+                     return launch_tc<T>(xq, xs, wpacked, ws, y, out_kind, M, N, K, workspace,
+                                         (cudaStream_t)stream, true));
 }

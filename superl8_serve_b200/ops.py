@@ -63,8 +63,20 @@ def gemm_tc_workspace(M: int, N: int, device) -> torch.Tensor:
     return torch.zeros(n, dtype=torch.uint8, device=device)
 
 
-def gemm_w8a8_tc(xq, xs, w, ws, *, out=None, out_dtype=torch.bfloat16, raw=False, workspace=None):
-    """Tensor-core (tcgen05 kind::i8) form of gemm_w8a8; identical results."""
+def pack_weights_tc(w: torch.Tensor) -> torch.Tensor:
+    """Pre-pack an int8 [N, K] weight into the tensor-core GEMM's unit images."""
+    from ._lib import load
+
+    N, K = w.shape
+    packed = torch.empty(int(load().s8b_tc_packed_bytes(N, K)), dtype=torch.int8, device=w.device)
+    call("s8b_pack_weights_tc", ptr(w.contiguous()), N, K, ptr(packed), stream(w.device))
+    return packed
+
+
+def gemm_w8a8_tc(xq, xs, w, ws, *, out=None, out_dtype=torch.bfloat16, raw=False, workspace=None,
+                 packed: torch.Tensor | None = None):
+    """Tensor-core (tcgen05 kind::i8) form of gemm_w8a8; identical results. With `packed`
+    (from pack_weights_tc(w)) the weight stream is read as contiguous unit images."""
     K = xq.shape[-1]
     M = xq.numel() // K
     N = w.shape[0]
@@ -74,8 +86,12 @@ def gemm_w8a8_tc(xq, xs, w, ws, *, out=None, out_dtype=torch.bfloat16, raw=False
     if workspace is None:
         workspace = gemm_tc_workspace(M, N, xq.device)
     dt = dtype_code(out_dtype if raw else out.dtype)
-    call("s8b_gemm_w8a8_tc", ptr(xq), ptr(xs), ptr(w), ptr(ws), ptr(out), 1 if raw else 0, M, N, K,
-         dt, ptr(workspace), workspace.numel(), stream(xq.device))
+    if packed is not None:
+        call("s8b_gemm_w8a8_tc_packed", ptr(xq), ptr(xs), ptr(packed), ptr(ws), ptr(out),
+             1 if raw else 0, M, N, K, dt, ptr(workspace), workspace.numel(), stream(xq.device))
+    else:
+        call("s8b_gemm_w8a8_tc", ptr(xq), ptr(xs), ptr(w), ptr(ws), ptr(out), 1 if raw else 0, M,
+             N, K, dt, ptr(workspace), workspace.numel(), stream(xq.device))
     return out
 
 

@@ -233,10 +233,24 @@ class StageRunner:
         n_max = max([L.gu_w.shape[0] for L in model.layers] + [L.qkv_w.shape[0] for L in model.layers]
                     + ([model.head_w.shape[0]] if model.is_last else []) + [self.H])
         self.tc_ws = ops.gemm_tc_workspace(m, n_max, dev) if m >= self.tc_min else None
+        # tensor-core path: every weight also kept as contiguous unit images (packed once)
+        self.packed: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
+        if self.tc_ws is not None:
+            mats = [w for L in model.layers for w in (L.qkv_w, L.o_w, L.gu_w, L.d_w)]
+            if model.is_last:
+                mats.append(model.head_w)
+            with torch.cuda.device(dev):
+                for w in mats:
+                    self.packed[id(w)] = (w, ops.pack_weights_tc(w))
 
     # ---------------------------------------------------------------------- pieces ----
     def _gemm(self, xq, xs, w, s, out, M):
         if self.tc_ws is not None and M >= self.tc_min:
+            pk = self.packed.get(id(w))
+            if pk is not None and pk[0] is w:
+                call("s8b_gemm_w8a8_tc_packed", ptr(xq), ptr(xs), ptr(pk[1]), ptr(s), ptr(out), 0,
+                     M, w.shape[0], w.shape[1], 0, ptr(self.tc_ws), self.tc_ws.numel(), stream())
+                return
             call("s8b_gemm_w8a8_tc", ptr(xq), ptr(xs), ptr(w), ptr(s), ptr(out), 0, M, w.shape[0],
                  w.shape[1], 0, ptr(self.tc_ws), self.tc_ws.numel(), stream())
         else:

@@ -86,3 +86,25 @@ def test_tiny_model_on_tensor_core_path_matches_oracle():
     assert outs == ref
     got = np.stack([np.stack([t.numpy() for t in row]) for row in logits])
     assert np.array_equal(got, np.array(ref_logits, dtype=np.float32))
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 24576, 4096), (64, 4096, 12288), (16, 1000, 256),
+                                   (200, 640, 384)])
+def test_tc_gemm_packed_weights_bit_exact(M, N, K):
+    """Pre-packed unit images (contiguous bulk loads) give the same int32 sums and outputs."""
+    from superl8_serve_b200 import ops
+
+    rng = np.random.default_rng(N + K)
+    xq = rng.integers(-127, 128, (M, K), dtype=np.int8)
+    w = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    xs = rng.uniform(0.001, 0.05, M).astype(np.float32)
+    ws = rng.uniform(0.0001, 0.001, N).astype(np.float32)
+    wd = _t(w)
+    packed = ops.pack_weights_tc(wd)
+    wsp = ops.gemm_tc_workspace(M, N, DEV)
+    acc = ops.gemm_w8a8_tc(_t(xq), _t(xs), wd, _t(ws), raw=True, workspace=wsp, packed=packed)
+    y = ops.gemm_w8a8_tc(_t(xq), _t(xs), wd, _t(ws), workspace=wsp, packed=packed)
+    torch.cuda.synchronize()
+    assert np.array_equal(acc.cpu().numpy(), ok.gemm_acc(xq, w))
+    assert np.array_equal(y.float().cpu().numpy(), ok.gemm_w8a8(xq, xs, w, ws))
+    assert int(wsp.count_nonzero()) == 0
