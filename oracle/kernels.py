@@ -184,11 +184,15 @@ def paged_decode(qq, qs, kc, ks, vc, vs, block_table, context_lens, block_size, 
     ``superl8serve/engine/kv_cache.py:1190-1201``). Accumulation order is fixed:
 
     * score s_j = (f32(qq . kq_j) * (qs * scale)) * ks_j, the dot an exact int32;
-    * the context is cut into partitions of ATTN_PART tokens; in partition p:
-      m_p = max s_j, e_j = exp(s_j - m_p), l_p = sum e_j and o_p = sum e_j * (f32(vq_j) * vs_j)
-      accumulated sequentially in token order (binary32 multiply, then add);
+    * the context is cut into partitions of ATTN_PART tokens; in partition p, per query head:
+      m_p = max s_j, e_j = exp(s_j - m_p), l_p = sum e_j accumulated sequentially in token
+      order (binary32); the value weights w_j = e_j * vs_j are quantized relative to their
+      maximum, W_j = clamp(rint(w_j * (32767 / wmax)), 0, 32767), the numerator is the exact
+      integer o_int = sum_j W_j * vq_j and o_p = f32(o_int) * (wmax / 32767);
     * combine: M = max m_p, w_p = exp(m_p - M), L = sum w_p*l_p, O = sum w_p*o_p over p in
       order; out = bf16(O / L).
+    The 15-bit weights keep every product exact (|o_int| < 2^31) so the numerator may be summed
+    in any order; the weight rounding is at most 1.5e-5 of the partition's largest weight.
 
     qq [B, Hq, D] int8, qs [B, Hq]; caches as in ``kv_write_paged``; block_table
     [B, max_blocks] int32; context_lens [B] int32 (>= 1). Returns [B, Hq, D] bf16-valued.
@@ -218,19 +222,23 @@ def paged_decode(qq, qs, kc, ks, vc, vs, block_table, context_lens, block_size, 
         dots = np.einsum("hd,nhd->nh", qq[b].astype(np.int64), kq[:, g_of_h, :])  # [n, Hq]
         s = (dots.astype(np.float32) * qsc[b][None, :]).astype(np.float32)
         s = (s * ksj[:, g_of_h]).astype(np.float32)
-        v = (vq[:, g_of_h, :] * vsj[:, g_of_h][:, :, None]).astype(np.float32)  # [n, Hq, D]
+        vcodes = vq[:, g_of_h, :].astype(np.int64)  # [n, Hq, D]
+        vsh = vsj[:, g_of_h]  # [n, Hq]
         nparts = (n + ATTN_PART - 1) // ATTN_PART
         ms, ls, os_ = [], [], []
         for p in range(nparts):
             lo, hi = p * ATTN_PART, min(n, (p + 1) * ATTN_PART)
             sp = s[lo:hi]
             m = sp.max(axis=0)
-            e = exp_s8b((sp - m[None, :]).astype(np.float32))
-            l = np.zeros(Hq, dtype=np.float32)
-            o = np.zeros((Hq, D), dtype=np.float32)
-            for t in range(hi - lo):
-                l = (l + e[t]).astype(np.float32)
-                o = (o + (e[t][:, None] * v[lo + t]).astype(np.float32)).astype(np.float32)
+            e = exp_s8b((sp - m[None, :]).astype(np.float32))  # [np, Hq]
+            l = np.add.accumulate(e, axis=0, dtype=np.float32)[-1]  # sequential binary32 sum
+            w = (e * vsh[lo:hi]).astype(np.float32)
+            wmax = w.max(axis=0)
+            winv = (F32(32767.0) / wmax).astype(np.float32)
+            qsc_p = (wmax / F32(32767.0)).astype(np.float32)
+            W = np.clip(np.rint((w * winv[None, :]).astype(np.float32)), 0, 32767).astype(np.int64)
+            o_int = np.einsum("nh,nhd->hd", W, vcodes[lo:hi])
+            o = (o_int.astype(np.float32) * qsc_p[:, None]).astype(np.float32)
             ms.append(m)
             ls.append(l)
             os_.append(o)

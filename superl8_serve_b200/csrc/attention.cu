@@ -190,23 +190,46 @@ __global__ void __launch_bounds__(256) q_rotate_quant_kernel(const T *__restrict
 }
 
 // ------------------------------------------------------------------- decode partitions ----
+constexpr int kPartThreads = 512;
+constexpr int kSlices = kPartThreads / 32;  // token slices of the P.V phase (one per warp)
+
+template <int G>
 struct PartSmem {
-  static size_t bytes(int G) {
-    return static_cast<size_t>(kPart) * kKPitch + static_cast<size_t>(kPart) * kHd +
-           2 * kPart * sizeof(float) + static_cast<size_t>(G) * kPart * sizeof(float) +
-           static_cast<size_t>(G) * kHd + 3 * 8 * sizeof(float);
-  }
+  // K and V codes [256 tokens][128], K with its 16-byte chunks XOR-swizzled by token % 8 so
+  // that 8 lanes reading 8 consecutive tokens hit 8 different bank groups. After the scores and
+  // the P.V loop, the same 64 KB hold the per-warp int32 partial sums [kSlices][G][128].
+  static constexpr size_t kKV = 2 * kPart * kHd;
+  static constexpr size_t kRed = static_cast<size_t>(kSlices) * G * kHd * 4;
+  static constexpr size_t kRegion = kKV > kRed ? kKV : kRed;
+  static constexpr size_t bytes = kRegion + 2 * kPart * 4 /*k,v scales*/ +
+                                  static_cast<size_t>(G) * kPart * 4 /*e*/ +
+                                  static_cast<size_t>(G) * kPart * 2 /*W*/ +
+                                  static_cast<size_t>(G) * kHd /*q*/ + 4 * 8 * 4;
 };
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
   const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
 }
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
+__device__ __forceinline__ int dp2a_lo(int a, int b, int c) { return __dp2a_lo(a, b, c); }
+__device__ __forceinline__ int dp2a_hi(int a, int b, int c) { return __dp2a_hi(a, b, c); }
 
-__global__ void __launch_bounds__(1024)
+// One CTA = one (256-token partition, kv head, row). Phases:
+//  1. cp.async K (group 0) and V (group 1) of the partition's tokens; scales and q directly.
+//  2. once K has landed: exact int32 q.k (dp4a), s = (f32(dot) * q_s*scale) * k_s; the V copy
+//     is still in flight meanwhile.
+//  3. per head: m = max s, e = exp(s - m), l = sequential sum of e, w = e * v_s, 15-bit
+//     weights W = rint(w * 32767/wmax).
+//  4. once V has landed: o_int = sum W * v over this warp's 16 tokens for 4 channels x G heads
+//     (dp2a: 2 tokens per instruction), partial sums reduced across the 16 warps in shared
+//     memory (integer, exact), o = f32(o_int) * wmax/32767.
+template <int G>
+__global__ void __launch_bounds__(kPartThreads)
     attn_partition_kernel(const int8_t *__restrict__ q_i8, const float *__restrict__ q_s,
                           const int8_t *__restrict__ kc, const float *__restrict__ ks,
                           const int8_t *__restrict__ vc, const float *__restrict__ vs,
@@ -214,97 +237,154 @@ __global__ void __launch_bounds__(1024)
                           const int32_t *__restrict__ context_lens, int Hq, int Hkv, int bs,
                           int max_blocks, int P, float scale, float *__restrict__ part_o,
                           float *__restrict__ part_ml) {
+  using Sm = PartSmem<G>;
   const int p = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int n = context_lens[b];
   const int lo = p * kPart;
   if (lo >= n) return;
   const int cnt = min(kPart, n - lo);
-  const int G = Hq / Hkv;
-  const int tid = threadIdx.x, nthreads = blockDim.x;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
 
   extern __shared__ __align__(16) uint8_t smem[];
   int8_t *Ks = reinterpret_cast<int8_t *>(smem);
-  int8_t *Vs = Ks + kPart * kKPitch;
-  float *ksc = reinterpret_cast<float *>(Vs + kPart * kHd);
+  int8_t *Vs = Ks + kPart * kHd;
+  int32_t *Red = reinterpret_cast<int32_t *>(smem);  // reuses K/V after phase 4
+  float *ksc = reinterpret_cast<float *>(smem + Sm::kRegion);
   float *vsc = ksc + kPart;
-  float *S = vsc + kPart;                                  // [G][kPart]
-  int8_t *Qs = reinterpret_cast<int8_t *>(S + G * kPart);  // [G][128]
-  float *qsc = reinterpret_cast<float *>(Qs + G * kHd);    // [G]
-  float *mx = qsc + 8;                                     // [G]
+  float *E = vsc + kPart;                                 // [G][kPart]
+  int16_t *W = reinterpret_cast<int16_t *>(E + G * kPart);  // [G][kPart]
+  int8_t *Qs = reinterpret_cast<int8_t *>(W + G * kPart);   // [G][128]
+  float *qsc = reinterpret_cast<float *>(Qs + G * kHd);     // [8]
+  float *mx = qsc + 8;
+  float *wsc = mx + 8;  // wmax / 32767
+  float *lsum = wsc + 8;
 
-  // Stage K, V codes (cp.async) and their scales for the partition's tokens.
   const int32_t *bt = block_table + static_cast<size_t>(b) * max_blocks;
   const int blk0 = lo / bs;
-  for (int idx = tid; idx < cnt * 8; idx += nthreads) {
+  // ---- phase 1: stage K then V (two cp.async groups) ----
+  for (int idx = tid; idx < cnt * 8; idx += kPartThreads) {
     const int t = idx >> 3, c = idx & 7;
-    const int j = lo + t;
-    const size_t row = (static_cast<size_t>(bt[blk0 + t / bs]) * Hkv + g) * bs + (j % bs);
-    cp_async16(Ks + t * kKPitch + c * 16, kc + row * kHd + c * 16);
+    const size_t row = (static_cast<size_t>(bt[blk0 + t / bs]) * Hkv + g) * bs + ((lo + t) % bs);
+    cp_async16(Ks + t * kHd + ((c ^ (t & 7)) * 16), kc + row * kHd + c * 16);
+  }
+  cp_async_commit();
+  for (int idx = tid; idx < cnt * 8; idx += kPartThreads) {
+    const int t = idx >> 3, c = idx & 7;
+    const size_t row = (static_cast<size_t>(bt[blk0 + t / bs]) * Hkv + g) * bs + ((lo + t) % bs);
     cp_async16(Vs + t * kHd + c * 16, vc + row * kHd + c * 16);
   }
-  for (int t = tid; t < cnt; t += nthreads) {
-    const int j = lo + t;
-    const size_t row = (static_cast<size_t>(bt[blk0 + t / bs]) * Hkv + g) * bs + (j % bs);
-    ksc[t] = ks[row];
-    vsc[t] = vs[row];
+  cp_async_commit();
+  for (int t = tid; t < kPart; t += kPartThreads) {
+    if (t < cnt) {
+      const size_t row = (static_cast<size_t>(bt[blk0 + t / bs]) * Hkv + g) * bs + ((lo + t) % bs);
+      ksc[t] = ks[row];
+      vsc[t] = vs[row];
+    }
   }
-  for (int idx = tid; idx < G * (kHd / 16); idx += nthreads) {
+  for (int idx = tid; idx < G * (kHd / 16); idx += kPartThreads) {
     const int h = idx / (kHd / 16), c = idx % (kHd / 16);
     reinterpret_cast<int4 *>(Qs + h * kHd)[c] =
         reinterpret_cast<const int4 *>(q_i8 + (static_cast<size_t>(b) * Hq + g * G + h) * kHd)[c];
   }
   if (tid < G) qsc[tid] = __fmul_rn(q_s[static_cast<size_t>(b) * Hq + g * G + tid], scale);
-  cp_async_wait_all();
+  cp_async_wait<1>();
   __syncthreads();
 
-  // Scores s = (f32(q.k) * (q_s*scale)) * k_s, exact int32 dot products.
-  for (int pr = tid; pr < G * kPart; pr += nthreads) {
+  // ---- phase 2: scores ----
+  for (int pr = tid; pr < G * kPart; pr += kPartThreads) {
     const int h = pr / kPart, t = pr % kPart;
     if (t >= cnt) continue;
-    const int4 *kr = reinterpret_cast<const int4 *>(Ks + t * kKPitch);
+    const int8_t *kr = Ks + t * kHd;
     const int4 *qr = reinterpret_cast<const int4 *>(Qs + h * kHd);
     int acc = 0;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-      const int4 a = kr[c], q = qr[c];
+      const int4 a = *reinterpret_cast<const int4 *>(kr + ((c ^ (t & 7)) * 16));
+      const int4 q = qr[c];
       acc = __dp4a(a.x, q.x, acc);
       acc = __dp4a(a.y, q.y, acc);
       acc = __dp4a(a.z, q.z, acc);
       acc = __dp4a(a.w, q.w, acc);
     }
-    S[h * kPart + t] = __fmul_rn(__fmul_rn(static_cast<float>(acc), qsc[h]), ksc[t]);
+    E[h * kPart + t] = __fmul_rn(__fmul_rn(static_cast<float>(acc), qsc[h]), ksc[t]);
   }
   __syncthreads();
-  const int lane = tid & 31, warp = tid >> 5, nwarps = nthreads >> 5;
-  for (int h = warp; h < G; h += nwarps) {
+  // ---- phase 3: softmax numerators and 15-bit value weights ----
+  for (int h = warp; h < G; h += kSlices) {
     float m = -__int_as_float(0x7f800000);
-    for (int t = lane; t < cnt; t += 32) m = fmaxf(m, S[h * kPart + t]);
+    for (int t = lane; t < cnt; t += 32) m = fmaxf(m, E[h * kPart + t]);
     m = warp_max(m);
-    if (lane == 0) mx[h] = m;
+    float wm = 0.0f;
+    for (int t = lane; t < cnt; t += 32) {
+      const float e = exp_s8b(__fsub_rn(E[h * kPart + t], m));
+      E[h * kPart + t] = e;
+      wm = fmaxf(wm, __fmul_rn(e, vsc[t]));
+    }
+    wm = warp_max(wm);
+    if (lane == 0) {
+      mx[h] = m;
+      wsc[h] = __fdiv_rn(wm, 32767.0f);
+    }
+    __syncwarp();
+    const float winv = __fdiv_rn(32767.0f, wm);
+    for (int t = lane; t < kPart; t += 32) {
+      int wq = 0;
+      if (t < cnt) {
+        wq = __float2int_rn(__fmul_rn(__fmul_rn(E[h * kPart + t], vsc[t]), winv));
+        wq = wq < 0 ? 0 : (wq > 32767 ? 32767 : wq);
+      }
+      W[h * kPart + t] = static_cast<int16_t>(wq);
+    }
+    if (lane == 0) {  // denominator: sequential binary32 sum in token order
+      float l = 0.0f;
+      for (int t = 0; t < cnt; ++t) l = __fadd_rn(l, E[h * kPart + t]);
+      lsum[h] = l;
+    }
   }
-  __syncthreads();
-  for (int pr = tid; pr < G * kPart; pr += nthreads) {
-    const int h = pr / kPart, t = pr % kPart;
-    if (t < cnt) S[pr] = exp_s8b(__fsub_rn(S[pr], mx[h]));
-  }
+  cp_async_wait<0>();
   __syncthreads();
 
-  // Numerator and denominator, accumulated sequentially in token order.
-  for (int hd = tid; hd < G * kHd; hd += nthreads) {
-    const int h = hd / kHd, d = hd % kHd;
-    const float *e = S + h * kPart;
-    float o = 0.0f, l = 0.0f;
-    for (int t = 0; t < cnt; ++t) {
-      const float et = e[t];
-      const float v = __fmul_rn(static_cast<float>(Vs[t * kHd + d]), vsc[t]);
-      o = __fadd_rn(o, __fmul_rn(et, v));
-      l = __fadd_rn(l, et);
+  // ---- phase 4: o_int = sum_t W[h][t] * V[t][d], warp = 16-token slice, lane = 4 channels ----
+  int acc[G][4];
+#pragma unroll
+  for (int h = 0; h < G; ++h)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[h][i] = 0;
+  const int t_begin = warp * (kPart / kSlices);
+  if (t_begin < cnt) {
+#pragma unroll 2
+    for (int t = t_begin; t < t_begin + kPart / kSlices; t += 2) {
+      const int v0 = *reinterpret_cast<const int *>(Vs + t * kHd + 4 * lane);
+      const int v1 = *reinterpret_cast<const int *>(Vs + (t + 1) * kHd + 4 * lane);
+      const int lo01 = __byte_perm(v0, v1, 0x5140);  // (t,d) (t+1,d) (t,d+1) (t+1,d+1)
+      const int hi23 = __byte_perm(v0, v1, 0x7362);  // same for d+2, d+3
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const int wpair = *reinterpret_cast<const int *>(W + h * kPart + t);
+        acc[h][0] = dp2a_lo(wpair, lo01, acc[h][0]);
+        acc[h][1] = dp2a_hi(wpair, lo01, acc[h][1]);
+        acc[h][2] = dp2a_lo(wpair, hi23, acc[h][2]);
+        acc[h][3] = dp2a_hi(wpair, hi23, acc[h][3]);
+      }
     }
+  }
+  __syncthreads();  // all warps done with K/V: the region now holds the partial sums
+#pragma unroll
+  for (int h = 0; h < G; ++h)
+    reinterpret_cast<int4 *>(Red + (static_cast<size_t>(warp) * G + h) * kHd)[lane] =
+        make_int4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+  __syncthreads();
+  for (int hd = tid; hd < G * kHd; hd += kPartThreads) {
+    const int h = hd / kHd, d = hd % kHd;
+    int o = 0;
+#pragma unroll
+    for (int sl = 0; sl < kSlices; ++sl) o += Red[(static_cast<size_t>(sl) * G + h) * kHd + d];
     const size_t hq = static_cast<size_t>(b) * Hq + g * G + h;
-    part_o[(hq * P + p) * kHd + d] = o;
+    part_o[(hq * P + p) * kHd + d] = __fmul_rn(static_cast<float>(o), wsc[h]);
     if (d == 0) {
       part_ml[(hq * P + p) * 2 + 0] = mx[h];
-      part_ml[(hq * P + p) * 2 + 1] = l;
+      part_ml[(hq * P + p) * 2 + 1] = lsum[h];
     }
   }
 }
@@ -373,11 +453,29 @@ int launch_decode(const int8_t *q_i8, const float *q_s, const int8_t *kc, const 
   const int G = Hq / Hkv;
   float *part_o = part;
   float *part_ml = part + static_cast<size_t>(B) * Hq * P * kHd;
-  const size_t smem = PartSmem::bytes(G);
-  ensure_smem(reinterpret_cast<const void *>(attn_partition_kernel), smem);
-  attn_partition_kernel<<<dim3(P, Hkv, B), G * kHd, smem, st>>>(
-      q_i8, q_s, kc, ks, vc, vs, block_table, context_lens, Hq, Hkv, bs, max_blocks, P, scale,
-      part_o, part_ml);
+  int rc_part = S8B_OK;
+  switch (G) {
+#define S8B_PART_CASE(GG)                                                                     \
+  case GG: {                                                                                  \
+    ensure_smem(reinterpret_cast<const void *>(attn_partition_kernel<GG>), PartSmem<GG>::bytes); \
+    attn_partition_kernel<GG><<<dim3(P, Hkv, B), kPartThreads, PartSmem<GG>::bytes, st>>>(      \
+        q_i8, q_s, kc, ks, vc, vs, block_table, context_lens, Hq, Hkv, bs, max_blocks, P,      \
+        scale, part_o, part_ml);                                                              \
+    break;                                                                                    \
+  }
+    S8B_PART_CASE(1)
+    S8B_PART_CASE(2)
+    S8B_PART_CASE(3)
+    S8B_PART_CASE(4)
+    S8B_PART_CASE(5)
+    S8B_PART_CASE(6)
+    S8B_PART_CASE(7)
+    S8B_PART_CASE(8)
+#undef S8B_PART_CASE
+    default:
+      rc_part = S8B_ERR_SHAPE;
+  }
+  if (rc_part) return rc_part;
   const size_t csmem = (static_cast<size_t>(Hq) * P + Hq + static_cast<size_t>(Hq) * kHd) * sizeof(float);
   auto comb = attn_combine_kernel<T>;
   ensure_smem(reinterpret_cast<const void *>(comb), csmem);

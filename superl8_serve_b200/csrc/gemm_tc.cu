@@ -47,6 +47,7 @@ struct TcSmemHeader {
   uint32_t tmem_base;
   int abort;
   int is_last;
+  float xs[256];  // per-token activation scales of this launch's token tile
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -197,10 +198,10 @@ struct TcLayout {
   static constexpr int kBBytes = NT * kBK;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages =
-      (kSmemBudget - 2048) / kStageBytes < kMaxStages ? (kSmemBudget - 2048) / kStageBytes
+      (kSmemBudget - 3072) / kStageBytes < kMaxStages ? (kSmemBudget - 3072) / kStageBytes
                                                       : kMaxStages;
   static constexpr int kTmemCols = 2 * NT < 32 ? 32 : 2 * NT;
-  static constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * kStageBytes + 1024;
+  static constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * kStageBytes + 2048;
 };
 
 struct TcArgs {
@@ -314,9 +315,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // --------------------------------------------------------------- epilogue ----
+    float *xs_s = hdr->xs;
     const int quad = warp & 3;              // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;       // weight row within the tile
     const int et = threadIdx.x - 64;        // 0..127
+    for (int t = et; t < NT; t += 128) {
+      const int m = a.m0 + t;
+      xs_s[t] = (a.out_kind == 0 && m < a.M) ? a.xs[m] : 0.0f;
+    }
+    epi_bar_sync();
     int seg = 0;
     long long u = u0;
     while (u < u1) {
@@ -351,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               static_cast<int32_t *>(a.y)[o] = accv;
             else
               static_cast<T *>(a.y)[o] =
-                  from_f32<T>(__fmul_rn(__fmul_rn(static_cast<float>(accv), a.xs[m]), wsn));
+                  from_f32<T>(__fmul_rn(__fmul_rn(static_cast<float>(accv), xs_s[t]), wsn));
           } else {
             atomicAdd(a.acc + static_cast<size_t>(t) * a.N + n, accv);
           }
@@ -369,18 +376,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         epi_bar_sync();
         if (hdr->is_last) {
           __threadfence();
-          for (int t = 0; t < NT; ++t) {
-            const int m = a.m0 + t;
-            if (m >= a.M || n >= a.N) continue;
-            int32_t *p = a.acc + static_cast<size_t>(t) * a.N + n;
-            const int32_t accv = __ldcg(p);
-            *p = 0;
-            const size_t o = static_cast<size_t>(m) * a.N + n;
-            if (a.out_kind == 1)
-              static_cast<int32_t *>(a.y)[o] = accv;
-            else
-              static_cast<T *>(a.y)[o] =
-                  from_f32<T>(__fmul_rn(__fmul_rn(static_cast<float>(accv), a.xs[m]), wsn));
+          // 16 independent L2 loads in flight per thread, then the stores (a load/store loop
+          // would serialise one L2 round trip per token on possible aliasing).
+#pragma unroll 1
+          for (int t0 = 0; t0 < NT; t0 += 16) {
+            int32_t vals[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int m = a.m0 + t0 + j;
+              vals[j] = (m < a.M && n < a.N)
+                            ? __ldcg(a.acc + static_cast<size_t>(t0 + j) * a.N + n) : 0;
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int m = a.m0 + t0 + j;
+              if (m >= a.M || n >= a.N) continue;
+              a.acc[static_cast<size_t>(t0 + j) * a.N + n] = 0;
+              const size_t o = static_cast<size_t>(m) * a.N + n;
+              if (a.out_kind == 1)
+                static_cast<int32_t *>(a.y)[o] = vals[j];
+              else
+                static_cast<T *>(a.y)[o] = from_f32<T>(
+                    __fmul_rn(__fmul_rn(static_cast<float>(vals[j]), xs_s[t0 + j]), wsn));
+            }
           }
           if (et == 0) a.counters[tile] = 0;
         }
