@@ -178,6 +178,24 @@ def quant_q_for_attn(q: np.ndarray):
     return qq.astype(np.int8), qs
 
 
+def lane_sum(e: np.ndarray) -> np.ndarray:
+    """Denominator order of one partition: pad the (<= 256) values of each head to 256, lane
+    l (0..31) sums e[l], e[32+l], ..., e[224+l] in that order, then the 32 lane sums are
+    combined by the xor butterfly (offsets 16, 8, 4, 2, 1), all in binary32. e: [n, H] ->
+    [H]."""
+    n, H = e.shape
+    pad = np.zeros((ATTN_PART, H), dtype=np.float32)
+    pad[:n] = e
+    lanes = pad.reshape(ATTN_PART // 32, 32, H)
+    acc = lanes[0].copy()
+    for i in range(1, ATTN_PART // 32):
+        acc = (acc + lanes[i]).astype(np.float32)
+    idx = np.arange(32)
+    for off in (16, 8, 4, 2, 1):
+        acc = (acc + acc[idx ^ off]).astype(np.float32)
+    return acc[0]
+
+
 def paged_decode(qq, qs, kc, ks, vc, vs, block_table, context_lens, block_size, scale,
                  return_parts=False):
     """Paged int8 GQA decode attention (``attn_paged_decode_cached`` call site,
@@ -185,8 +203,8 @@ def paged_decode(qq, qs, kc, ks, vc, vs, block_table, context_lens, block_size, 
 
     * score s_j = (f32(qq . kq_j) * (qs * scale)) * ks_j, the dot an exact int32;
     * the context is cut into partitions of ATTN_PART tokens; in partition p, per query head:
-      m_p = max s_j, e_j = exp(s_j - m_p), l_p = sum e_j accumulated sequentially in token
-      order (binary32); the value weights w_j = e_j * vs_j are quantized relative to their
+      m_p = max s_j, e_j = exp(s_j - m_p), l_p = sum e_j in the order of ``lane_sum``
+      (binary32); the value weights w_j = e_j * vs_j are quantized relative to their
       maximum, W_j = clamp(rint(w_j * (32767 / wmax)), 0, 32767), the numerator is the exact
       integer o_int = sum_j W_j * vq_j and o_p = f32(o_int) * (wmax / 32767);
     * combine: M = max m_p, w_p = exp(m_p - M), L = sum w_p*l_p, O = sum w_p*o_p over p in
@@ -231,7 +249,7 @@ def paged_decode(qq, qs, kc, ks, vc, vs, block_table, context_lens, block_size, 
             sp = s[lo:hi]
             m = sp.max(axis=0)
             e = exp_s8b((sp - m[None, :]).astype(np.float32))  # [np, Hq]
-            l = np.add.accumulate(e, axis=0, dtype=np.float32)[-1]  # sequential binary32 sum
+            l = lane_sum(e)
             w = (e * vsh[lo:hi]).astype(np.float32)
             wmax = w.max(axis=0)
             winv = (F32(32767.0) / wmax).astype(np.float32)

@@ -204,7 +204,7 @@ struct PartSmem {
   static constexpr size_t bytes = kRegion + 2 * kPart * 4 /*k,v scales*/ +
                                   static_cast<size_t>(G) * kPart * 4 /*e*/ +
                                   static_cast<size_t>(G) * kPart * 2 /*W*/ +
-                                  static_cast<size_t>(G) * kHd /*q*/ + 4 * 8 * 4;
+                                  static_cast<size_t>(G) * kHd /*q*/ + 4 * 8 * 4 + 2 * 64 * 4;
 };
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
@@ -259,6 +259,8 @@ __global__ void __launch_bounds__(kPartThreads)
   float *mx = qsc + 8;
   float *wsc = mx + 8;  // wmax / 32767
   float *lsum = wsc + 8;
+  float *pmax = lsum + 8;        // [G][8] per-warp maxima of s
+  float *pwmax = pmax + 64;      // [G][8] per-warp maxima of w
 
   const int32_t *bt = block_table + static_cast<size_t>(b) * max_blocks;
   const int blk0 = lo / bs;
@@ -291,56 +293,71 @@ __global__ void __launch_bounds__(kPartThreads)
   cp_async_wait<1>();
   __syncthreads();
 
-  // ---- phase 2: scores ----
+  // ---- phase 2: scores; each warp handles 32 consecutive tokens of one head ----
   for (int pr = tid; pr < G * kPart; pr += kPartThreads) {
-    const int h = pr / kPart, t = pr % kPart;
-    if (t >= cnt) continue;
-    const int8_t *kr = Ks + t * kHd;
-    const int4 *qr = reinterpret_cast<const int4 *>(Qs + h * kHd);
-    int acc = 0;
+    const int h = pr / kPart, t = pr % kPart;  // h is uniform within a warp
+    float sv = -__int_as_float(0x7f800000);
+    if (t < cnt) {
+      const int8_t *kr = Ks + t * kHd;
+      const int4 *qr = reinterpret_cast<const int4 *>(Qs + h * kHd);
+      int acc = 0;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const int4 a = *reinterpret_cast<const int4 *>(kr + ((c ^ (t & 7)) * 16));
-      const int4 q = qr[c];
-      acc = __dp4a(a.x, q.x, acc);
-      acc = __dp4a(a.y, q.y, acc);
-      acc = __dp4a(a.z, q.z, acc);
-      acc = __dp4a(a.w, q.w, acc);
+      for (int c = 0; c < 8; ++c) {
+        const int4 a = *reinterpret_cast<const int4 *>(kr + ((c ^ (t & 7)) * 16));
+        const int4 q = qr[c];
+        acc = __dp4a(a.x, q.x, acc);
+        acc = __dp4a(a.y, q.y, acc);
+        acc = __dp4a(a.z, q.z, acc);
+        acc = __dp4a(a.w, q.w, acc);
+      }
+      sv = __fmul_rn(__fmul_rn(static_cast<float>(acc), qsc[h]), ksc[t]);
+      E[pr] = sv;
     }
-    E[h * kPart + t] = __fmul_rn(__fmul_rn(static_cast<float>(acc), qsc[h]), ksc[t]);
+    const float wmx = warp_max(sv);
+    if (lane == 0) pmax[h * 8 + (t >> 5)] = wmx;
   }
   __syncthreads();
-  // ---- phase 3: softmax numerators and 15-bit value weights ----
-  for (int h = warp; h < G; h += kSlices) {
-    float m = -__int_as_float(0x7f800000);
-    for (int t = lane; t < cnt; t += 32) m = fmaxf(m, E[h * kPart + t]);
-    m = warp_max(m);
-    float wm = 0.0f;
-    for (int t = lane; t < cnt; t += 32) {
-      const float e = exp_s8b(__fsub_rn(E[h * kPart + t], m));
-      E[h * kPart + t] = e;
-      wm = fmaxf(wm, __fmul_rn(e, vsc[t]));
+  // ---- phase 3: e = exp(s - m), value weights w = e * v_s, partial maxima of w ----
+  for (int pr = tid; pr < G * kPart; pr += kPartThreads) {
+    const int h = pr / kPart, t = pr % kPart;
+    float m = pmax[h * 8];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) m = fmaxf(m, pmax[h * 8 + i]);
+    float w = 0.0f;
+    if (t < cnt) {
+      const float e = exp_s8b(__fsub_rn(E[pr], m));
+      E[pr] = e;
+      w = __fmul_rn(e, vsc[t]);
+    } else {
+      E[pr] = 0.0f;
     }
-    wm = warp_max(wm);
-    if (lane == 0) {
-      mx[h] = m;
-      wsc[h] = __fdiv_rn(wm, 32767.0f);
+    const float wmx = warp_max(w);
+    if (lane == 0) pwmax[h * 8 + (t >> 5)] = wmx;
+    if (t == 0) mx[h] = m;
+  }
+  __syncthreads();
+  // ---- 15-bit weights (all threads); denominators (warp h, fixed lane/butterfly order) ----
+  for (int pr = tid; pr < G * kPart; pr += kPartThreads) {
+    const int h = pr / kPart, t = pr % kPart;
+    float wm = pwmax[h * 8];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) wm = fmaxf(wm, pwmax[h * 8 + i]);
+    int wq = 0;
+    if (t < cnt) {
+      wq = __float2int_rn(__fmul_rn(__fmul_rn(E[pr], vsc[t]), __fdiv_rn(32767.0f, wm)));
+      wq = wq < 0 ? 0 : (wq > 32767 ? 32767 : wq);
     }
-    __syncwarp();
-    const float winv = __fdiv_rn(32767.0f, wm);
-    for (int t = lane; t < kPart; t += 32) {
-      int wq = 0;
-      if (t < cnt) {
-        wq = __float2int_rn(__fmul_rn(__fmul_rn(E[h * kPart + t], vsc[t]), winv));
-        wq = wq < 0 ? 0 : (wq > 32767 ? 32767 : wq);
-      }
-      W[h * kPart + t] = static_cast<int16_t>(wq);
-    }
-    if (lane == 0) {  // denominator: sequential binary32 sum in token order
-      float l = 0.0f;
-      for (int t = 0; t < cnt; ++t) l = __fadd_rn(l, E[h * kPart + t]);
-      lsum[h] = l;
-    }
+    W[pr] = static_cast<int16_t>(wq);
+    if (t == 0) wsc[h] = __fdiv_rn(wm, 32767.0f);
+  }
+  if (warp < G) {
+    const float *e = E + warp * kPart;
+    float l = e[lane];
+#pragma unroll
+    for (int i = 1; i < kPart / 32; ++i) l = __fadd_rn(l, e[i * 32 + lane]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, o));
+    if (lane == 0) lsum[warp] = l;
   }
   cp_async_wait<0>();
   __syncthreads();
