@@ -143,7 +143,9 @@ int s8b_kv_write_paged(const void *k, const void *v, int8_t *kc, float *ks, int8
  * (nullable, together) additionally receive the per-token int8 quantization of the output
  * row (the o_proj input). context_lens[b] >= 1 tokens of row b are attended; max_ctx is an
  * upper bound on every context_lens[b] (sizes the partition grid). Workspace: see
- * s8b_paged_decode_workspace_size. D must be 128.
+ * s8b_paged_decode_workspace_size; zero-fill it once before first use (it holds completion
+ * counters that every launch leaves at zero); launches sharing a workspace must be
+ * stream-ordered. D must be 128; block_size a power of two dividing 256.
  * Replaces superl8.attn_paged_decode_cached (superl8serve/engine/kv_cache.py:1190-1201). */
 size_t s8b_paged_decode_workspace_size(int B, int Hq, int D, int max_ctx);
 int s8b_paged_decode_q8(const int8_t *q_i8, const float *q_s, const int8_t *kc, const float *ks,
@@ -175,7 +177,8 @@ int s8b_paged_decode_q8_noalloc(const int8_t *q_i8, const float *q_s, const int8
                                 int dtype, void *stream);
 
 /* Same attention with the reference's query layout: q [B, Hq, D] in dtype (rotated and
- * quantized internally into the workspace). out [B, Hq, D] in dtype.                     */
+ * quantized internally into the workspace, which must be zero-filled once likewise).
+ * out [B, Hq, D] in dtype.                                                                */
 size_t s8b_paged_decode_ref_workspace_size(int B, int Hq, int D, int max_ctx);
 int s8b_paged_decode(const void *q, const int8_t *kc, const float *ks, const int8_t *vc,
                      const float *vs, const int32_t *block_table, const int32_t *context_lens,

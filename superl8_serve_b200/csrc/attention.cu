@@ -204,7 +204,9 @@ struct PartSmem {
   static constexpr size_t bytes = kRegion + 2 * kPart * 4 /*k,v scales*/ +
                                   static_cast<size_t>(G) * kPart * 4 /*e*/ +
                                   static_cast<size_t>(G) * kPart * 2 /*W*/ +
-                                  static_cast<size_t>(G) * kHd /*q*/ + 4 * 8 * 4 + 2 * 64 * 4;
+                                  static_cast<size_t>(G) * kHd /*q*/ +
+                                  (4 * 8 + 64 + 8) * 4 /*per-head scalars, partial maxima*/ +
+                                  kPart * 4 + 16 /*block row bases, flag*/;
 };
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
@@ -216,6 +218,13 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
+template <typename T>
+__device__ __forceinline__ float ldcg_act(const T *p) {
+  const unsigned short bits = __ldcg(reinterpret_cast<const unsigned short *>(p));
+  T v;
+  memcpy(&v, &bits, sizeof(v));
+  return to_f32(v);
+}
 __device__ __forceinline__ int dp2a_lo(int a, int b, int c) { return __dp2a_lo(a, b, c); }
 __device__ __forceinline__ int dp2a_hi(int a, int b, int c) { return __dp2a_hi(a, b, c); }
 
@@ -223,26 +232,38 @@ __device__ __forceinline__ int dp2a_hi(int a, int b, int c) { return __dp2a_hi(a
 //  1. cp.async K (group 0) and V (group 1) of the partition's tokens; scales and q directly.
 //  2. once K has landed: exact int32 q.k (dp4a), s = (f32(dot) * q_s*scale) * k_s; the V copy
 //     is still in flight meanwhile.
-//  3. per head: m = max s, e = exp(s - m), l = sequential sum of e, w = e * v_s, 15-bit
-//     weights W = rint(w * 32767/wmax).
+//  3. per head: m = max s, e = exp(s - m), l = denominator in the fixed lane/butterfly order,
+//     w = e * v_s, 15-bit weights W = rint(w * 32767/wmax).
 //  4. once V has landed: o_int = sum W * v over this warp's 16 tokens for 4 channels x G heads
 //     (dp2a: 2 tokens per instruction), partial sums reduced across the 16 warps in shared
-//     memory (integer, exact), o = f32(o_int) * wmax/32767.
-template <int G>
+//     memory (integer, exact), o = f32(o_int) * wmax/32767 -> workspace.
+//  5. the CTA that finishes a (row, kv head) last (counter) merges its partitions in index
+//     order into the output; the CTA that finishes a row last quantizes the row (o_proj input).
+//     Both counters return to zero, so the workspace needs zero-filling only once.
+struct DecodeWs {
+  int32_t *cnt_group;  // [B*Hq] (row, kv head) completion counters (B*Hkv used)
+  int32_t *cnt_row;    // [B]
+  float *part_o;       // [B, Hq, P, 128]
+  float *part_ml;      // [B, Hq, P, 2]
+};
+
+template <typename T, int G>
 __global__ void __launch_bounds__(kPartThreads)
     attn_partition_kernel(const int8_t *__restrict__ q_i8, const float *__restrict__ q_s,
                           const int8_t *__restrict__ kc, const float *__restrict__ ks,
                           const int8_t *__restrict__ vc, const float *__restrict__ vs,
                           const int32_t *__restrict__ block_table,
-                          const int32_t *__restrict__ context_lens, int Hq, int Hkv, int bs,
-                          int max_blocks, int P, float scale, float *__restrict__ part_o,
-                          float *__restrict__ part_ml) {
+                          const int32_t *__restrict__ context_lens, int Hq, int Hkv, int bs_log2,
+                          int max_blocks, int P, float scale, DecodeWs ws, T *__restrict__ out,
+                          int8_t *__restrict__ out_q, float *__restrict__ out_s) {
   using Sm = PartSmem<G>;
   const int p = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int n = context_lens[b];
   const int lo = p * kPart;
   if (lo >= n) return;
   const int cnt = min(kPart, n - lo);
+  const int np = (n + kPart - 1) / kPart;
+  const int bs = 1 << bs_log2;
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
 
@@ -252,44 +273,46 @@ __global__ void __launch_bounds__(kPartThreads)
   int32_t *Red = reinterpret_cast<int32_t *>(smem);  // reuses K/V after phase 4
   float *ksc = reinterpret_cast<float *>(smem + Sm::kRegion);
   float *vsc = ksc + kPart;
-  float *E = vsc + kPart;                                 // [G][kPart]
+  float *E = vsc + kPart;                                   // [G][kPart]
   int16_t *W = reinterpret_cast<int16_t *>(E + G * kPart);  // [G][kPart]
   int8_t *Qs = reinterpret_cast<int8_t *>(W + G * kPart);   // [G][128]
   float *qsc = reinterpret_cast<float *>(Qs + G * kHd);     // [8]
   float *mx = qsc + 8;
-  float *wsc = mx + 8;  // wmax / 32767
+  float *wsc = mx + 8;    // wmax / 32767
   float *lsum = wsc + 8;
-  float *pmax = lsum + 8;        // [G][8] per-warp maxima of s
-  float *pwmax = pmax + 64;      // [G][8] per-warp maxima of w
+  float *pmax = lsum + 8;   // [G][8] per-warp maxima of s, then of w
+  float *winv = pmax + 64;  // [8] 32767 / wmax
+  int *rowbase = reinterpret_cast<int *>(winv + 8);  // [kPart / bs] first row of each block
+  int *flag = rowbase + kPart;
 
-  const int32_t *bt = block_table + static_cast<size_t>(b) * max_blocks;
-  const int blk0 = lo / bs;
   // ---- phase 1: stage K then V (two cp.async groups) ----
+  const int32_t *bt = block_table + static_cast<size_t>(b) * max_blocks + (lo >> bs_log2);
+  const int nblk = (cnt + bs - 1) >> bs_log2;
+  if (tid < nblk) rowbase[tid] = (bt[tid] * Hkv + g) << bs_log2;
+  if (tid < G) qsc[tid] = __fmul_rn(q_s[static_cast<size_t>(b) * Hq + g * G + tid], scale);
+  __syncthreads();
   for (int idx = tid; idx < cnt * 8; idx += kPartThreads) {
     const int t = idx >> 3, c = idx & 7;
-    const size_t row = (static_cast<size_t>(bt[blk0 + t / bs]) * Hkv + g) * bs + ((lo + t) % bs);
+    const size_t row = static_cast<size_t>(rowbase[t >> bs_log2] + (t & (bs - 1)));
     cp_async16(Ks + t * kHd + ((c ^ (t & 7)) * 16), kc + row * kHd + c * 16);
   }
   cp_async_commit();
   for (int idx = tid; idx < cnt * 8; idx += kPartThreads) {
     const int t = idx >> 3, c = idx & 7;
-    const size_t row = (static_cast<size_t>(bt[blk0 + t / bs]) * Hkv + g) * bs + ((lo + t) % bs);
+    const size_t row = static_cast<size_t>(rowbase[t >> bs_log2] + (t & (bs - 1)));
     cp_async16(Vs + t * kHd + c * 16, vc + row * kHd + c * 16);
   }
   cp_async_commit();
-  for (int t = tid; t < kPart; t += kPartThreads) {
-    if (t < cnt) {
-      const size_t row = (static_cast<size_t>(bt[blk0 + t / bs]) * Hkv + g) * bs + ((lo + t) % bs);
-      ksc[t] = ks[row];
-      vsc[t] = vs[row];
-    }
+  if (tid < cnt) {
+    const size_t row = static_cast<size_t>(rowbase[tid >> bs_log2] + (tid & (bs - 1)));
+    ksc[tid] = ks[row];
+    vsc[tid] = vs[row];
   }
   for (int idx = tid; idx < G * (kHd / 16); idx += kPartThreads) {
     const int h = idx / (kHd / 16), c = idx % (kHd / 16);
     reinterpret_cast<int4 *>(Qs + h * kHd)[c] =
         reinterpret_cast<const int4 *>(q_i8 + (static_cast<size_t>(b) * Hq + g * G + h) * kHd)[c];
   }
-  if (tid < G) qsc[tid] = __fmul_rn(q_s[static_cast<size_t>(b) * Hq + g * G + tid], scale);
   cp_async_wait<1>();
   __syncthreads();
 
@@ -317,38 +340,45 @@ __global__ void __launch_bounds__(kPartThreads)
     if (lane == 0) pmax[h * 8 + (t >> 5)] = wmx;
   }
   __syncthreads();
+  if (tid < G) {
+    float m = pmax[tid * 8];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) m = fmaxf(m, pmax[tid * 8 + i]);
+    mx[tid] = m;
+  }
+  __syncthreads();
   // ---- phase 3: e = exp(s - m), value weights w = e * v_s, partial maxima of w ----
   for (int pr = tid; pr < G * kPart; pr += kPartThreads) {
     const int h = pr / kPart, t = pr % kPart;
-    float m = pmax[h * 8];
-#pragma unroll
-    for (int i = 1; i < 8; ++i) m = fmaxf(m, pmax[h * 8 + i]);
     float w = 0.0f;
     if (t < cnt) {
-      const float e = exp_s8b(__fsub_rn(E[pr], m));
+      const float e = exp_s8b(__fsub_rn(E[pr], mx[h]));
       E[pr] = e;
       w = __fmul_rn(e, vsc[t]);
     } else {
       E[pr] = 0.0f;
     }
     const float wmx = warp_max(w);
-    if (lane == 0) pwmax[h * 8 + (t >> 5)] = wmx;
-    if (t == 0) mx[h] = m;
+    if (lane == 0) pmax[h * 8 + (t >> 5)] = wmx;
+  }
+  __syncthreads();
+  if (tid < G) {
+    float wm = pmax[tid * 8];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) wm = fmaxf(wm, pmax[tid * 8 + i]);
+    wsc[tid] = __fdiv_rn(wm, 32767.0f);
+    winv[tid] = __fdiv_rn(32767.0f, wm);
   }
   __syncthreads();
   // ---- 15-bit weights (all threads); denominators (warp h, fixed lane/butterfly order) ----
   for (int pr = tid; pr < G * kPart; pr += kPartThreads) {
     const int h = pr / kPart, t = pr % kPart;
-    float wm = pwmax[h * 8];
-#pragma unroll
-    for (int i = 1; i < 8; ++i) wm = fmaxf(wm, pwmax[h * 8 + i]);
     int wq = 0;
     if (t < cnt) {
-      wq = __float2int_rn(__fmul_rn(__fmul_rn(E[pr], vsc[t]), __fdiv_rn(32767.0f, wm)));
+      wq = __float2int_rn(__fmul_rn(__fmul_rn(E[pr], vsc[t]), winv[h]));
       wq = wq < 0 ? 0 : (wq > 32767 ? 32767 : wq);
     }
     W[pr] = static_cast<int16_t>(wq);
-    if (t == 0) wsc[h] = __fdiv_rn(wm, 32767.0f);
   }
   if (warp < G) {
     const float *e = E + warp * kPart;
@@ -398,66 +428,93 @@ __global__ void __launch_bounds__(kPartThreads)
 #pragma unroll
     for (int sl = 0; sl < kSlices; ++sl) o += Red[(static_cast<size_t>(sl) * G + h) * kHd + d];
     const size_t hq = static_cast<size_t>(b) * Hq + g * G + h;
-    part_o[(hq * P + p) * kHd + d] = __fmul_rn(static_cast<float>(o), wsc[h]);
+    ws.part_o[(hq * P + p) * kHd + d] = __fmul_rn(static_cast<float>(o), wsc[h]);
     if (d == 0) {
-      part_ml[(hq * P + p) * 2 + 0] = mx[h];
-      part_ml[(hq * P + p) * 2 + 1] = lsum[h];
+      ws.part_ml[(hq * P + p) * 2 + 0] = mx[h];
+      ws.part_ml[(hq * P + p) * 2 + 1] = lsum[h];
     }
   }
-}
 
-// ------------------------------------------------------------------------------ combine ----
-template <typename T>
-__global__ void __launch_bounds__(256)
-    attn_combine_kernel(const float *__restrict__ part_o, const float *__restrict__ part_ml,
-                        const int32_t *__restrict__ context_lens, int Hq, int P,
-                        T *__restrict__ out, int8_t *__restrict__ out_q,
-                        float *__restrict__ out_s) {
-  extern __shared__ float cs[];
-  float *W = cs;                  // [Hq][P]
-  float *L = W + Hq * P;          // [Hq]
-  float *row = L + Hq;            // [Hq*128]
-  __shared__ float red[32];
-  const int b = blockIdx.x;
-  const int n = context_lens[b];
-  const int np = (n + kPart - 1) / kPart;
-  for (int h = threadIdx.x; h < Hq; h += blockDim.x) {
-    const float *ml = part_ml + (static_cast<size_t>(b) * Hq + h) * P * 2;
-    float M = -__int_as_float(0x7f800000);
-    for (int p = 0; p < np; ++p) M = fmaxf(M, ml[2 * p]);
-    float Ls = 0.0f;
-    for (int p = 0; p < np; ++p) {
-      const float w = exp_s8b(__fsub_rn(ml[2 * p], M));
-      W[h * P + p] = w;
-      Ls = __fadd_rn(Ls, __fmul_rn(w, ml[2 * p + 1]));
-    }
-    L[h] = Ls;
+  // ---- phase 5: the last partition of this (row, kv head) merges; the last group quantizes ----
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    int32_t *c = ws.cnt_group + static_cast<size_t>(b) * Hkv + g;
+    const int done = atomicAdd(c, 1) + 1;
+    flag[0] = done == np;
+    if (done == np) *c = 0;
   }
   __syncthreads();
-  float amax = 0.0f;
-  for (int i = threadIdx.x; i < Hq * kHd; i += blockDim.x) {
-    const int h = i / kHd, d = i % kHd;
-    const float *po = part_o + (static_cast<size_t>(b) * Hq + h) * P * kHd + d;
+  if (!flag[0]) return;
+  __threadfence();
+  // merge: per head h: M = max m_p, w_p = exp(m_p - M), L = sum w_p l_p, O = sum w_p o_p
+  float *Wp = reinterpret_cast<float *>(smem);  // [G][P] merge weights (K/V region is free)
+  float *Lh = Wp + G * P;
+  if (tid < G) {
+    const float *ml = ws.part_ml + (static_cast<size_t>(b) * Hq + g * G + tid) * P * 2;
+    float M = -__int_as_float(0x7f800000);
+    for (int q = 0; q < np; ++q) M = fmaxf(M, __ldcg(ml + 2 * q));
+    float Ls = 0.0f;
+    for (int q = 0; q < np; ++q) {
+      const float w = exp_s8b(__fsub_rn(__ldcg(ml + 2 * q), M));
+      Wp[tid * P + q] = w;
+      Ls = __fadd_rn(Ls, __fmul_rn(w, __ldcg(ml + 2 * q + 1)));
+    }
+    Lh[tid] = Ls;
+  }
+  __syncthreads();
+  for (int hd = tid; hd < G * kHd; hd += kPartThreads) {
+    const int h = hd / kHd, d = hd % kHd;
+    const float *po = ws.part_o + (static_cast<size_t>(b) * Hq + g * G + h) * P * kHd + d;
     float O = 0.0f;
-    for (int p = 0; p < np; ++p) O = __fadd_rn(O, __fmul_rn(W[h * P + p], po[p * kHd]));
-    const float y = round_to<T>(__fdiv_rn(O, L[h]));
-    out[static_cast<size_t>(b) * Hq * kHd + i] = from_f32<T>(y);
-    row[i] = y;
-    amax = fmaxf(amax, fabsf(y));
+    for (int q = 0; q < np; ++q) O = __fadd_rn(O, __fmul_rn(Wp[h * P + q], __ldcg(po + q * kHd)));
+    out[static_cast<size_t>(b) * Hq * kHd + (g * G + h) * kHd + d] = from_f32<T>(__fdiv_rn(O, Lh[h]));
   }
   if (!out_q) return;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const int done = atomicAdd(ws.cnt_row + b, 1) + 1;
+    flag[0] = done == Hkv;
+    if (done == Hkv) ws.cnt_row[b] = 0;
+  }
+  __syncthreads();
+  if (!flag[0]) return;
+  __threadfence();
+  // quantize the whole output row (all heads) for the o_proj GEMM
+  const T *row = out + static_cast<size_t>(b) * Hq * kHd;
+  float amax = 0.0f;
+  for (int i = tid; i < Hq * kHd; i += kPartThreads)  // written by other CTAs: read via L2
+    amax = fmaxf(amax, fabsf(ldcg_act(row + i)));
+  float *red = Wp;
   amax = block_max(amax, red);
   const QParams qp = qparams(amax, 127.0f);
-  for (int i = threadIdx.x; i < Hq * kHd; i += blockDim.x)
-    out_q[static_cast<size_t>(b) * Hq * kHd + i] = static_cast<int8_t>(qcode(row[i], qp.inv, 127));
-  if (threadIdx.x == 0) out_s[b] = qp.scale;
+  for (int i = tid; i < Hq * kHd; i += kPartThreads)
+    out_q[static_cast<size_t>(b) * Hq * kHd + i] =
+        static_cast<int8_t>(qcode(ldcg_act(row + i), qp.inv, 127));
+  if (tid == 0) out_s[b] = qp.scale;
 }
 
 inline int num_parts(int max_ctx) { return (max_ctx + kPart - 1) / kPart; }
 
+size_t counters_bytes(int B, int Hq) {
+  return (static_cast<size_t>(B) * Hq * 4 + static_cast<size_t>(B) * 4 + 255) / 256 * 256;
+}
+
 size_t part_bytes(int B, int Hq, int max_ctx) {
   const size_t P = num_parts(max_ctx);
-  return static_cast<size_t>(B) * Hq * P * (kHd + 2) * sizeof(float);
+  return counters_bytes(B, Hq) + static_cast<size_t>(B) * Hq * P * (kHd + 2) * sizeof(float);
+}
+
+DecodeWs carve_ws(void *base, int B, int Hq, int max_ctx) {
+  uint8_t *p = static_cast<uint8_t *>(base);
+  const size_t P = num_parts(max_ctx);
+  DecodeWs w;
+  w.cnt_group = reinterpret_cast<int32_t *>(p);
+  w.cnt_row = w.cnt_group + static_cast<size_t>(B) * Hq;
+  w.part_o = reinterpret_cast<float *>(p + counters_bytes(B, Hq));
+  w.part_ml = w.part_o + static_cast<size_t>(B) * Hq * P * kHd;
+  return w;
 }
 
 template <typename T>
@@ -465,20 +522,21 @@ int launch_decode(const int8_t *q_i8, const float *q_s, const int8_t *kc, const 
                   const int8_t *vc, const float *vs, const int32_t *block_table,
                   const int32_t *context_lens, void *out, int8_t *out_q, float *out_s, int B,
                   int Hq, int Hkv, int bs, int max_blocks, int max_ctx, float scale,
-                  float *part, cudaStream_t st) {
+                  void *workspace, cudaStream_t st) {
   const int P = num_parts(max_ctx);
   const int G = Hq / Hkv;
-  float *part_o = part;
-  float *part_ml = part + static_cast<size_t>(B) * Hq * P * kHd;
-  int rc_part = S8B_OK;
+  int bs_log2 = 0;
+  while ((1 << bs_log2) < bs) ++bs_log2;
+  const DecodeWs w = carve_ws(workspace, B, Hq, max_ctx);
   switch (G) {
-#define S8B_PART_CASE(GG)                                                                     \
-  case GG: {                                                                                  \
-    ensure_smem(reinterpret_cast<const void *>(attn_partition_kernel<GG>), PartSmem<GG>::bytes); \
-    attn_partition_kernel<GG><<<dim3(P, Hkv, B), kPartThreads, PartSmem<GG>::bytes, st>>>(      \
-        q_i8, q_s, kc, ks, vc, vs, block_table, context_lens, Hq, Hkv, bs, max_blocks, P,      \
-        scale, part_o, part_ml);                                                              \
-    break;                                                                                    \
+#define S8B_PART_CASE(GG)                                                                      \
+  case GG: {                                                                                   \
+    auto kern = attn_partition_kernel<T, GG>;                                                   \
+    ensure_smem(reinterpret_cast<const void *>(kern), PartSmem<GG>::bytes);                     \
+    kern<<<dim3(P, Hkv, B), kPartThreads, PartSmem<GG>::bytes, st>>>(                           \
+        q_i8, q_s, kc, ks, vc, vs, block_table, context_lens, Hq, Hkv, bs_log2, max_blocks, P,  \
+        scale, w, static_cast<T *>(out), out_q, out_s);                                         \
+    break;                                                                                     \
   }
     S8B_PART_CASE(1)
     S8B_PART_CASE(2)
@@ -490,21 +548,16 @@ int launch_decode(const int8_t *q_i8, const float *q_s, const int8_t *kc, const 
     S8B_PART_CASE(8)
 #undef S8B_PART_CASE
     default:
-      rc_part = S8B_ERR_SHAPE;
+      return S8B_ERR_SHAPE;
   }
-  if (rc_part) return rc_part;
-  const size_t csmem = (static_cast<size_t>(Hq) * P + Hq + static_cast<size_t>(Hq) * kHd) * sizeof(float);
-  auto comb = attn_combine_kernel<T>;
-  ensure_smem(reinterpret_cast<const void *>(comb), csmem);
-  comb<<<B, 256, csmem, st>>>(part_o, part_ml, context_lens, Hq, P, static_cast<T *>(out), out_q,
-                              out_s);
-  return check_launch(2);
+  return check_launch(1);
 }
 
 int check_attn_shape(int B, int Hq, int Hkv, int D, int bs, int max_blocks, int max_ctx) {
   if (B < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || Hq / Hkv > 8 || D != kHd)
     return S8B_ERR_SHAPE;
-  if (bs <= 0 || kPart % bs != 0 || max_ctx <= 0 || max_blocks * bs < max_ctx)
+  if (bs <= 0 || (bs & (bs - 1)) != 0 || kPart % bs != 0 || max_ctx <= 0 ||
+      max_blocks * bs < max_ctx)
     return S8B_ERR_SHAPE;
   if (num_parts(max_ctx) * Hq > 8192) return S8B_ERR_SHAPE;  // combine smem bound
   return S8B_OK;

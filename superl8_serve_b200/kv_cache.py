@@ -104,7 +104,7 @@ class PagedKVCache:
         B, Hq = q.shape[0], q.shape[1]
         need = ops.decode_workspace_bytes(B, Hq, self.head_dim, int(max_context_len), ref=True)
         if self._ws is None or self._ws.numel() < need:
-            self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+            self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
         out = ops.paged_decode(q, self.k_cache[layer], self.k_scale[layer], self.v_cache[layer],
                                self.v_scale[layer], block_table.to(torch.int32).contiguous(),
                                context_lens.to(torch.int32).contiguous(), int(max_context_len),

@@ -146,8 +146,8 @@ def paged_decode_q8(q_i8, q_s, kc, ks, vc, vs, block_table, context_lens, max_ct
     dev = q_i8.device
     out = torch.empty((B, Hq * D), dtype=dtype, device=dev) if out is None else out
     need = decode_workspace_bytes(B, Hq, D, max_ctx)
-    if workspace is None:
-        workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+    if workspace is None:  # zero-filled once; the kernel leaves its counters at zero
+        workspace = torch.zeros(need, dtype=torch.uint8, device=dev)
     call("s8b_paged_decode_q8", ptr(q_i8), ptr(q_s), ptr(kc), ptr(ks), ptr(vc), ptr(vs),
          ptr(block_table), ptr(context_lens), ptr(out), ptr(out_q), ptr(out_s), B, Hq, Hkv, D, bs,
          block_table.shape[-1], int(max_ctx), float(scale), ptr(workspace), workspace.numel(),
@@ -163,8 +163,8 @@ def paged_decode(q, kc, ks, vc, vs, block_table, context_lens, max_ctx, scale, *
     Hkv, bs = kc.shape[-3], kc.shape[-2]
     out = torch.empty_like(qq) if out is None else out
     need = decode_workspace_bytes(B, Hq, D, max_ctx, ref=True)
-    if workspace is None:
-        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    if workspace is None:  # zero-filled once; the kernel leaves its counters at zero
+        workspace = torch.zeros(need, dtype=torch.uint8, device=q.device)
     call("s8b_paged_decode", ptr(qq), ptr(kc), ptr(ks), ptr(vc), ptr(vs), ptr(block_table),
          ptr(context_lens), ptr(out), B, Hq, Hkv, D, bs, block_table.shape[-1], int(max_ctx),
          float(scale), ptr(workspace), workspace.numel(), dtype_code(qq.dtype), stream(q.device))

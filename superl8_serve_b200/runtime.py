@@ -224,7 +224,7 @@ class StageRunner:
         self.q_s = e(m, self.Hq, dt=torch.float32)
         self.attn = e(m, self.Hq * self.D)
         self.gu = e(m, 2 * self.F)
-        self.ws = torch.empty(ops.decode_workspace_bytes(m, self.Hq, self.D, max_ctx),
+        self.ws = torch.zeros(ops.decode_workspace_bytes(m, self.Hq, self.D, max_ctx),
                               dtype=torch.uint8, device=dev)
         if model.is_last:
             self.logits = e(m, self.V)

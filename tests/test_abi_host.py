@@ -64,7 +64,8 @@ def test_shape_and_scheme_validation(lib):
 
 def test_workspace_and_codec_sizes(lib):
     P = (2049 + 255) // 256
-    assert lib.s8b_paged_decode_workspace_size(64, 32, 128, 2049) == 64 * 32 * P * 130 * 4
+    counters = (64 * 32 * 4 + 64 * 4 + 255) // 256 * 256
+    assert lib.s8b_paged_decode_workspace_size(64, 32, 128, 2049) == counters + 64 * 32 * P * 130 * 4
     assert lib.s8b_codec_payload_bytes(4, 8192, 2, 0) == 4 * 8192
     assert lib.s8b_codec_scale_count(4, 8192, 2) == 4
     assert lib.s8b_codec_payload_bytes(4, 8192, 4, 0) == 4 * 4096
