@@ -1,0 +1,265 @@
+// Per-token row kernels with the whole row in registers: fused residual + RMSNorm + int8
+// quantization, SwiGLU + int8 quantization, and plain int8 quantization.
+//
+// One CTA per token row with up to 1024 threads; each thread owns VPT vectors of 4 elements
+// (8-byte loads), so a 4096-wide row is one load per thread and the row never round-trips
+// through shared memory. The arithmetic per element is exactly that of the oracle
+// (binary32, no contraction); only the reductions are block-wide (max is exact, the sum of
+// squares accumulates in float64).
+#include "common.cuh"
+
+namespace s8b {
+namespace {
+
+template <typename T>
+struct Vec4 {
+  uint2 raw;
+  __device__ __forceinline__ void load(const T *p) { raw = *reinterpret_cast<const uint2 *>(p); }
+  __device__ __forceinline__ void store(T *p) const { *reinterpret_cast<uint2 *>(p) = raw; }
+  __device__ __forceinline__ float get(int i) const {
+    const unsigned short b = static_cast<unsigned short>(
+        i < 2 ? (raw.x >> (16 * i)) & 0xffff : (raw.y >> (16 * (i - 2))) & 0xffff);
+    T v;
+    memcpy(&v, &b, 2);
+    return to_f32(v);
+  }
+  __device__ __forceinline__ void set(int i, float f) {
+    const T v = from_f32<T>(f);
+    unsigned short b;
+    memcpy(&b, &v, 2);
+    if (i < 2)
+      raw.x = (raw.x & ~(0xffffu << (16 * i))) | (static_cast<unsigned>(b) << (16 * i));
+    else
+      raw.y = (raw.y & ~(0xffffu << (16 * (i - 2)))) | (static_cast<unsigned>(b) << (16 * (i - 2)));
+  }
+};
+
+__device__ __forceinline__ void store_codes(int8_t *dst, const float v[4], float inv) {
+  char4 c;
+  c.x = static_cast<signed char>(qcode(v[0], inv, 127));
+  c.y = static_cast<signed char>(qcode(v[1], inv, 127));
+  c.z = static_cast<signed char>(qcode(v[2], inv, 127));
+  c.w = static_cast<signed char>(qcode(v[3], inv, 127));
+  *reinterpret_cast<char4 *>(dst) = c;
+}
+
+template <typename T, int VPT>
+__global__ void __launch_bounds__(1024)
+    rmsnorm_quant_v(const T *__restrict__ h, const T *__restrict__ res_in, T *__restrict__ res_out,
+                    const T *__restrict__ w, float eps, int8_t *__restrict__ q,
+                    float *__restrict__ s, T *__restrict__ y_out, int H) {
+  __shared__ double redd[32];
+  __shared__ float red[32];
+  const int m = blockIdx.x, nvec = H >> 2;
+  const size_t off = static_cast<size_t>(m) * H;
+  float x[VPT][4];
+  double ss = 0.0;
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int i = threadIdx.x + v * blockDim.x;
+    if (i < nvec) {
+      Vec4<T> a;
+      a.load(h + off + 4 * i);
+      if (res_in) {
+        Vec4<T> r;
+        r.load(res_in + off + 4 * i);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          x[v][j] = round_to<T>(__fadd_rn(a.get(j), r.get(j)));
+          a.set(j, x[v][j]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x[v][j] = a.get(j);
+      }
+      if (res_out) a.store(res_out + off + 4 * i);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ss += static_cast<double>(x[v][j]) * static_cast<double>(x[v][j]);
+    }
+  }
+  ss = block_sum_d(ss, redd);
+  const float rf = rms_factor(ss, H, eps);
+  float amax = 0.0f;
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int i = threadIdx.x + v * blockDim.x;
+    if (i < nvec) {
+      Vec4<T> wv;
+      wv.load(w + 4 * i);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        x[v][j] = round_to<T>(__fmul_rn(__fmul_rn(x[v][j], rf), wv.get(j)));
+        amax = fmaxf(amax, fabsf(x[v][j]));
+      }
+    }
+  }
+  amax = block_max(amax, red);
+  const QParams p = qparams(amax, 127.0f);
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int i = threadIdx.x + v * blockDim.x;
+    if (i < nvec) {
+      store_codes(q + off + 4 * i, x[v], p.inv);
+      if (y_out) {
+        Vec4<T> yv;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) yv.set(j, x[v][j]);
+        yv.store(y_out + off + 4 * i);
+      }
+    }
+  }
+  if (threadIdx.x == 0) s[m] = p.scale;
+}
+
+template <typename T, int VPT>
+__global__ void __launch_bounds__(1024)
+    silu_mul_quant_v(const T *__restrict__ gu, int F, T *__restrict__ y_out,
+                     int8_t *__restrict__ q, float *__restrict__ s) {
+  __shared__ float red[32];
+  const int m = blockIdx.x, nvec = F >> 2;
+  const T *row = gu + static_cast<size_t>(m) * 2 * F;
+  float y[VPT][4];
+  float amax = 0.0f;
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int i = threadIdx.x + v * blockDim.x;
+    if (i < nvec) {
+      Vec4<T> g, u;
+      g.load(row + 4 * i);
+      u.load(row + F + 4 * i);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float gf = g.get(j);
+        const float a = round_to<T>(__fdiv_rn(gf, __fadd_rn(1.0f, exp_s8b(-gf))));
+        y[v][j] = round_to<T>(__fmul_rn(a, u.get(j)));
+        amax = fmaxf(amax, fabsf(y[v][j]));
+      }
+    }
+  }
+  amax = block_max(amax, red);
+  const QParams p = qparams(amax, 127.0f);
+  const size_t off = static_cast<size_t>(m) * F;
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int i = threadIdx.x + v * blockDim.x;
+    if (i < nvec) {
+      store_codes(q + off + 4 * i, y[v], p.inv);
+      if (y_out) {
+        Vec4<T> yv;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) yv.set(j, y[v][j]);
+        yv.store(y_out + off + 4 * i);
+      }
+    }
+  }
+  if (threadIdx.x == 0) s[m] = p.scale;
+}
+
+template <typename T, int VPT>
+__global__ void __launch_bounds__(1024)
+    quant_rows_v(const T *__restrict__ x, int8_t *__restrict__ q, float *__restrict__ s, int K) {
+  __shared__ float red[32];
+  const int m = blockIdx.x, nvec = K >> 2;
+  const size_t off = static_cast<size_t>(m) * K;
+  float v4[VPT][4];
+  float amax = 0.0f;
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int i = threadIdx.x + v * blockDim.x;
+    if (i < nvec) {
+      Vec4<T> a;
+      a.load(x + off + 4 * i);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v4[v][j] = a.get(j);
+        amax = fmaxf(amax, fabsf(v4[v][j]));
+      }
+    }
+  }
+  amax = block_max(amax, red);
+  const QParams p = qparams(amax, 127.0f);
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int i = threadIdx.x + v * blockDim.x;
+    if (i < nvec) store_codes(q + off + 4 * i, v4[v], p.inv);
+  }
+  if (threadIdx.x == 0) s[m] = p.scale;
+}
+
+// threads = min(1024, nvec rounded up to a warp), VPT = ceil(nvec / threads) <= 8
+inline void row_shape(int nvec, int *threads, int *vpt) {
+  int t = ((nvec + 31) / 32) * 32;
+  if (t > 1024) t = 1024;
+  *threads = t;
+  *vpt = (nvec + t - 1) / t;
+}
+
+#define S8B_VPT_SWITCH(vpt, V, ...) \
+  switch (vpt) {                    \
+    case 1: { constexpr int V = 1; __VA_ARGS__; break; } \
+    case 2: { constexpr int V = 2; __VA_ARGS__; break; } \
+    case 3: { constexpr int V = 3; __VA_ARGS__; break; } \
+    case 4: { constexpr int V = 4; __VA_ARGS__; break; } \
+    case 5: { constexpr int V = 5; __VA_ARGS__; break; } \
+    case 6: { constexpr int V = 6; __VA_ARGS__; break; } \
+    case 7: { constexpr int V = 7; __VA_ARGS__; break; } \
+    case 8: { constexpr int V = 8; __VA_ARGS__; break; } \
+    default: return S8B_ERR_SHAPE; \
+  }
+
+}  // namespace
+}  // namespace s8b
+
+using namespace s8b;
+
+extern "C" int s8b_quant_rows(const void *x, int dtype, int8_t *q, float *s, int M, int K,
+                              void *stream) {
+  if (!x || !q || !s) return S8B_ERR_ARG;
+  if (M < 0 || K <= 0 || K % 4 != 0 || K > 32768) return S8B_ERR_SHAPE;
+  if (!aligned(x, 8) || !aligned(q, 4)) return S8B_ERR_ALIGN;
+  if (M == 0) return S8B_OK;
+  int th, vpt;
+  row_shape(K / 4, &th, &vpt);
+  S8B_DISPATCH_DTYPE(dtype, T,
+                     S8B_VPT_SWITCH(vpt, V,
+                                    quant_rows_v<T, V><<<M, th, 0, (cudaStream_t)stream>>>(
+                                        static_cast<const T *>(x), q, s, K)));
+  return check_launch();
+}
+
+extern "C" int s8b_rmsnorm_quant(const void *h, const void *residual_in, void *residual_out,
+                                 const void *w, float eps, int8_t *q, float *s, void *y_out,
+                                 int M, int H, int dtype, void *stream) {
+  if (!h || !w || !q || !s) return S8B_ERR_ARG;
+  if (M < 0 || H <= 0 || H % 4 != 0 || H > 32768) return S8B_ERR_SHAPE;
+  if (!aligned(h, 8) || !aligned(w, 8) || !aligned(q, 4) || !aligned(residual_in, 8) ||
+      !aligned(residual_out, 8) || !aligned(y_out, 8))
+    return S8B_ERR_ALIGN;
+  if (M == 0) return S8B_OK;
+  int th, vpt;
+  row_shape(H / 4, &th, &vpt);
+  S8B_DISPATCH_DTYPE(dtype, T,
+                     S8B_VPT_SWITCH(vpt, V,
+                                    rmsnorm_quant_v<T, V><<<M, th, 0, (cudaStream_t)stream>>>(
+                                        static_cast<const T *>(h),
+                                        static_cast<const T *>(residual_in),
+                                        static_cast<T *>(residual_out), static_cast<const T *>(w),
+                                        eps, q, s, static_cast<T *>(y_out), H)));
+  return check_launch();
+}
+
+extern "C" int s8b_silu_mul_quant(const void *gu, int M, int F, void *y_out, int8_t *q, float *s,
+                                  int dtype, void *stream) {
+  if (!gu || !q || !s) return S8B_ERR_ARG;
+  if (M < 0 || F <= 0 || F % 4 != 0 || F > 32768) return S8B_ERR_SHAPE;
+  if (!aligned(gu, 8) || !aligned(q, 4) || !aligned(y_out, 8)) return S8B_ERR_ALIGN;
+  if (M == 0) return S8B_OK;
+  int th, vpt;
+  row_shape(F / 4, &th, &vpt);
+  S8B_DISPATCH_DTYPE(dtype, T,
+                     S8B_VPT_SWITCH(vpt, V,
+                                    silu_mul_quant_v<T, V><<<M, th, 0, (cudaStream_t)stream>>>(
+                                        static_cast<const T *>(gu), F, static_cast<T *>(y_out), q,
+                                        s)));
+  return check_launch();
+}

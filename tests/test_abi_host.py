@@ -57,7 +57,8 @@ def test_shape_and_scheme_validation(lib):
     assert lib.s8b_gemm_w8a8(buf, buf, buf, buf, buf, 0, 1, 1, 17, 0, None) == -1  # K % 16
     assert lib.s8b_codec_encode(buf, None, 1, 100, 0, 2, buf, buf, 0, None) == -1  # -had needs 128
     assert lib.s8b_codec_encode(buf, None, 1, 128, 0, 9, buf, buf, 0, None) == -2  # scheme
-    assert lib.s8b_quant_rows(buf, 7, buf, buf, 1, 16, None) == -2  # dtype
+    assert lib.s8b_quant_rows(256, 7, 256, 256, 1, 16, None) == -2  # dtype
+    assert lib.s8b_quant_rows(buf, 0, buf, buf, 1, 16, None) == -3  # misaligned row pointer
     # workspace too small
     assert lib.s8b_paged_decode_q8(*([16] * 11), 1, 4, 2, 128, 16, 4, 64, 0.1, 16, 1, 0, None) == -7
 
