@@ -246,6 +246,9 @@ int s8b_ipc_alloc(size_t bytes, void **ptr, void *handle_out);
 int s8b_ipc_free(void *ptr);
 int s8b_ipc_open(const void *handle, void **ptr);
 int s8b_ipc_close(void *ptr);
+/* One stream-ordered cudaMemcpyAsync (cudaMemcpyDefault) between device, peer, IPC-mapped or
+ * pinned host addresses: host I/O around the step and set-up copies into raw buffers.      */
+int s8b_memcpy_async(void *dst, const void *src, size_t bytes, void *stream);
 
 #ifdef __cplusplus
 }

@@ -64,6 +64,7 @@ SIGNATURES: dict[str, tuple] = {
     "s8b_ipc_free": (_i, [_vp]),
     "s8b_ipc_open": (_i, [_vp, _vp]),
     "s8b_ipc_close": (_i, [_vp]),
+    "s8b_memcpy_async": (_i, [_vp, _vp, _sz, _vp]),
 }
 
 

@@ -81,3 +81,17 @@ extern "C" int s8b_ipc_close(void *ptr) {
 }
 
 extern "C" int s8b_ipc_handle_size(void) { return static_cast<int>(sizeof(cudaIpcMemHandle_t)); }
+
+// One stream-ordered copy between any two addresses the device can reach (device, peer, IPC
+// mapped or pinned host), for set-up and host I/O around the decode step.
+extern "C" int s8b_memcpy_async(void *dst, const void *src, size_t bytes, void *stream) {
+  if (!dst || !src) return S8B_ERR_ARG;
+  if (bytes == 0) return S8B_OK;
+  const cudaError_t e =
+      cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, (cudaStream_t)stream);
+  if (e != cudaSuccess) {
+    record_cuda_error(e);
+    return S8B_ERR_CUDA;
+  }
+  return S8B_OK;
+}

@@ -1,5 +1,398 @@
-"""One-process-per-GPU pipeline (torchrun): placeholder until the IPC stage runner lands."""
+"""One-process-per-GPU pipeline decode (torchrun): rank r runs stage r of S = world size.
+
+Stage-to-stage data never touches the host:
+
+* rank r > 0 owns S receive slots (one per micro-batch: boundary codes + scales) and rank 0
+  owns S token slots (next input ids). They are allocated with ``s8b_ipc_alloc``; the handles
+  are exchanged once over the process group and mapped by the producer (``s8b_ipc_open``).
+* the producer's codec encoder (or, on the last stage, the greedy argmax) stores straight into
+  the consumer's slot over NVLink, then raises the slot's ready flag to the step's epoch with a
+  system-scope release store (``s8b_flag_set``);
+* the consumer's first kernel for that micro-batch is a bounded device-side wait on its own
+  flag (``s8b_flag_wait``); a missing producer ends in S8B_ERR_TIMEOUT in a status word, never
+  a hang.
+
+Epochs live in device memory and advance by one per step inside the captured graph, so each
+rank replays one CUDA graph per step. Slots need no "free" handshake: micro-batch k of step
+t+1 starts from the tokens that micro-batch k produced at the end of step t, so every stage has
+consumed its step-t slot before the slot is written again.
+
+Micro-batches: S of ``m`` rows each (global batch m*S): per-GPU work is fixed as S grows.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import json
+import math
+import os
+import time
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from ._lib import CODEC, call, load, ptr, stream
+from .dist.pipeline import stage_bounds
+from .ops import codec_sizes
+from .runtime import KVPool, MicroBatch, StageModel, StageRunner
+
+FLAG_TIMEOUT_NS = 20_000_000_000  # 20 s: generous for cold first steps, still bounded
 
 
-def run_bench_multi(*a, **k):
-    raise NotImplementedError("multi-GPU pipeline bench is not built yet")
+class DevPtr:
+    """A raw device pointer with the few tensor-like attributes the launch helpers use."""
+
+    def __init__(self, addr: int, numel: int = 0):
+        self.addr = int(addr)
+        self.numel_ = numel
+        self.is_cuda = True
+
+    def data_ptr(self) -> int:
+        return self.addr
+
+    def is_contiguous(self) -> bool:
+        return True
+
+    def numel(self) -> int:
+        return self.numel_
+
+    def offset(self, nbytes: int, numel: int = 0) -> "DevPtr":
+        return DevPtr(self.addr + nbytes, numel)
+
+
+@dataclass
+class RankPlan:
+    """Pure host-side layout of one rank (testable without a GPU)."""
+
+    rank: int
+    world: int
+    layers: tuple[int, int]
+    m: int
+    n_micro: int
+    slot_payload: int
+    slot_scales: int
+    slot_bytes: int
+    recv_bytes: int
+    tok_bytes: int
+    flag_bytes: int
+
+    @property
+    def first(self) -> bool:
+        return self.rank == 0
+
+    @property
+    def last(self) -> bool:
+        return self.rank == self.world - 1
+
+
+def plan_rank(n_layers: int, hidden: int, rank: int, world: int, m: int, scheme: str,
+              payload_bytes_fn=None) -> RankPlan:
+    if world > n_layers:
+        raise ValueError("pipeline stage count cannot exceed the model layer count")
+    b = stage_bounds(n_layers, world)
+    fn = payload_bytes_fn or (lambda T, D, s: codec_sizes(T, D, s))
+    pay, nsc = fn(m, 2 * hidden, scheme)
+    pay_al = (pay + 255) // 256 * 256
+    sc_al = (max(nsc, 1) * 4 + 255) // 256 * 256
+    slot = pay_al + sc_al
+    n_micro = world
+    return RankPlan(rank, world, (b[rank], b[rank + 1]), m, n_micro, pay, max(nsc, 1), slot,
+                    slot * n_micro if rank > 0 else 0,
+                    ((m * 4 + 255) // 256 * 256) * n_micro if rank == 0 else 0,
+                    ((2 * n_micro * 4 + 255) // 256) * 256)
+
+
+def exchange_infos(info: dict, world: int, pg=None) -> list[dict]:
+    """All-gather every rank's exported handles (bytes) over the process group."""
+    import torch.distributed as dist
+
+    infos = [None] * world
+    dist.all_gather_object(infos, info, group=pg)
+    return infos
+
+
+def peer_handles(plan: RankPlan, infos: list[dict]) -> dict[str, bytes]:
+    """Handles this rank maps: the next stage's receive slots and flags (all but the last
+    stage), stage 0's token slots and flags (the last stage of a multi-stage pipeline)."""
+    out: dict[str, bytes] = {}
+    if not plan.last:
+        out["next_recv"] = infos[plan.rank + 1]["recv"]
+        out["next_flag"] = infos[plan.rank + 1]["flag"]
+    if plan.last and plan.world > 1:
+        out["first_tok"] = infos[0]["tok"]
+        out["first_flag"] = infos[0]["flag"]
+    return out
+
+
+def _alloc_ipc(nbytes: int):
+    lib = load()
+    hsz = lib.s8b_ipc_handle_size()
+    handle = (C.c_uint8 * hsz)()
+    p = C.c_void_p()
+    call("s8b_ipc_alloc", max(nbytes, 256), C.byref(p), handle)
+    return p.value, bytes(handle)
+
+
+def _open_ipc(handle: bytes) -> int:
+    buf = (C.c_uint8 * len(handle)).from_buffer_copy(handle)
+    p = C.c_void_p()
+    call("s8b_ipc_open", buf, C.byref(p))
+    return p.value
+
+
+class RankPipeline:
+    """Stage ``rank`` of an S-stage pipeline on the current CUDA device."""
+
+    def __init__(self, cfg, rank: int, world: int, *, m: int, max_len: int, ctx: int,
+                 scheme: str = "int8-had", seed: int = 0, pg=None):
+        self.cfg, self.rank, self.world = cfg, rank, world
+        self.dev = torch.device("cuda", torch.cuda.current_device())
+        self.plan = plan_rank(cfg.num_hidden_layers, cfg.hidden_size, rank, world, m, scheme)
+        self.scheme = scheme
+        S, H = world, cfg.hidden_size
+        lo, hi = self.plan.layers
+        self.model = StageModel.synthetic(cfg, lo, hi, self.dev, first=self.plan.first,
+                                          last=self.plan.last, seed=seed)
+        self.m = m
+        self.max_blocks = (max_len + 15) // 16
+        nb = m * S * self.max_blocks
+        self.pool = KVPool(hi - lo, nb, cfg.num_key_value_heads, cfg.resolved_head_dim(), 16,
+                           self.dev)
+        self.pool.fill_random(seed=seed * 7 + rank)
+        self.runner = StageRunner(self.model, self.pool, m, max_len)
+        # device-side per micro-batch state: sequence j = k*m + i owns blocks
+        # [j*max_blocks, (j+1)*max_blocks) (identical layout on every stage)
+        self.mbs = []
+        for k in range(S):
+            base = torch.arange(m, dtype=torch.int32).unsqueeze(1) + k * m
+            bt = (base * self.max_blocks + torch.arange(self.max_blocks, dtype=torch.int32)).to(self.dev)
+            pos = torch.full((m,), ctx, dtype=torch.int32, device=self.dev)
+            self.mbs.append(MicroBatch(ids=torch.zeros(m, dtype=torch.int32, device=self.dev),
+                                       positions=pos, context_lens=pos + 1, block_table=bt))
+        # IPC buffers: receive slots (r > 0), token slots (r == 0), flags (everyone)
+        self.own = []
+        self.recv_ptr = self.tok_ptr = None
+        recv_h = tok_h = b""
+        if self.plan.recv_bytes:
+            self.recv_ptr, recv_h = _alloc_ipc(self.plan.recv_bytes)
+            self.own.append(self.recv_ptr)
+        if self.plan.tok_bytes:
+            self.tok_ptr, tok_h = _alloc_ipc(self.plan.tok_bytes)
+            self.own.append(self.tok_ptr)
+        self.flag_ptr, flag_h = _alloc_ipc(self.plan.flag_bytes)
+        self.own.append(self.flag_ptr)
+        infos = exchange_infos({"rank": rank, "recv": recv_h, "tok": tok_h, "flag": flag_h},
+                               world, pg)
+        mapped = {k: _open_ipc(h) for k, h in peer_handles(self.plan, infos).items()}
+        self.opened = list(mapped.values())
+        self.next_recv, self.next_flag = mapped.get("next_recv"), mapped.get("next_flag")
+        self.first_tok, self.first_flag = mapped.get("first_tok"), mapped.get("first_flag")
+        if self.plan.last and world == 1:
+            self.first_tok, self.first_flag = self.tok_ptr, self.flag_ptr
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=self.dev)
+        self.status = torch.zeros(4, dtype=torch.int32, device=self.dev)
+        # token slots: stage 0 reads its ids there; the last stage writes the next ids there
+        tok_stride = (m * 4 + 255) // 256 * 256
+        for k in range(S):
+            if self.plan.first:
+                self.mbs[k].ids = DevPtr(self.tok_ptr + k * tok_stride, m)
+            elif self.plan.last:
+                self.mbs[k].ids = DevPtr(self.first_tok + k * tok_stride, m)
+        self.graph = None
+
+    # flags: [ready[S] | tok_ready[S]] uint32 in each rank's flag block
+    def _ready_flag(self, base: int, k: int) -> DevPtr:
+        return DevPtr(base + 4 * k)
+
+    def _tok_flag(self, base: int, k: int) -> DevPtr:
+        return DevPtr(base + 4 * (self.world + k))
+
+    def _slot(self, base: int, k: int):
+        p = self.plan
+        s = base + k * p.slot_bytes
+        pay_al = (p.slot_payload + 255) // 256 * 256
+        return (DevPtr(s, p.slot_payload), DevPtr(s + pay_al, p.slot_scales), self.scheme)
+
+    @property
+    def tok_stride(self) -> int:
+        return (self.m * 4 + 255) // 256 * 256
+
+    def put_ids(self, ids_host: torch.Tensor):
+        """Stage 0: copy the step's input ids (pinned host, m*S int32) into the token slots."""
+        st = stream()
+        for k in range(self.world):
+            call("s8b_memcpy_async", self.tok_ptr + k * self.tok_stride,
+                 ids_host.data_ptr() + 4 * k * self.m, 4 * self.m, st)
+
+    def get_tokens(self, out_host: torch.Tensor, epoch_add: int = 0):
+        """Stage 0: wait (on the device, bounded) until the last stage delivered this step's
+        tokens, then copy them to pinned host memory."""
+        st = stream()
+        for k in range(self.world):
+            if self.world > 1:
+                call("s8b_flag_wait", self._tok_flag(self.flag_ptr, k).addr, ptr(self.epoch),
+                     epoch_add, FLAG_TIMEOUT_NS, ptr(self.status), st)
+            call("s8b_memcpy_async", out_host.data_ptr() + 4 * k * self.m,
+                 self.tok_ptr + k * self.tok_stride, 4 * self.m, st)
+
+    def enqueue_step(self, *, token_return: bool = True):
+        S, st = self.world, stream()
+        for k in range(S):
+            mb = self.mbs[k]
+            if self.plan.first and S > 1 and token_return:
+                call("s8b_flag_wait", self._tok_flag(self.flag_ptr, k).addr, ptr(self.epoch), 0,
+                     FLAG_TIMEOUT_NS, ptr(self.status), st)
+            bin_ = bout = None
+            if not self.plan.first:
+                call("s8b_flag_wait", self._ready_flag(self.flag_ptr, k).addr, ptr(self.epoch), 1,
+                     FLAG_TIMEOUT_NS, ptr(self.status), st)
+                bin_ = self._slot(self.recv_ptr, k)
+            if not self.plan.last:
+                bout = self._slot(self.next_recv, k)
+            self.runner.run(mb, self.m, boundary_in=bin_, boundary_out=bout)
+            if not self.plan.last:
+                call("s8b_flag_set", self._ready_flag(self.next_flag, k).addr, ptr(self.epoch), 1, st)
+            elif S > 1:
+                call("s8b_flag_set", self._tok_flag(self.first_flag, k).addr, ptr(self.epoch), 1, st)
+            call("s8b_advance", ptr(mb.positions), ptr(mb.context_lens), self.m, 1, st)
+        call("s8b_counter_add", ptr(self.epoch), 1, st)
+
+    def capture(self):
+        s = torch.cuda.Stream(device=self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                self.enqueue_step()
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        self.graph = g
+
+    def step(self):
+        self.graph.replay()
+
+    def check_status(self):
+        st = self.status.cpu().tolist()
+        if st[0] != 0:
+            raise RuntimeError(f"rank {self.rank}: device wait timed out (awaited epoch {st[1]}, "
+                               f"saw {st[2]})")
+
+    def close(self, pg=None):
+        import torch.distributed as dist
+
+        torch.cuda.synchronize(self.dev)
+        self.graph = None
+        for p in self.opened:
+            call("s8b_ipc_close", p)
+        dist.barrier(group=pg)
+        for p in self.own:
+            call("s8b_ipc_free", p)
+        self.own, self.opened = [], []
+
+
+def run_bench_multi(args, metric, step_bytes, peaks, ClockSampler, cpu_sample):
+    """bench.py at N > 1: each rank one stage; rank 0 prints the JSON line."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from .config import qwen3_8b
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch with torchrun")
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    cfg = qwen3_8b()
+    if args.layers:
+        cfg = cfg.with_(num_hidden_layers=args.layers)
+    m, ctx = args.batch, args.ctx
+    total_steps = 1 + args.warmup + args.steps + args.steps + 8
+    pipe = RankPipeline(cfg, rank, world, m=m, max_len=ctx + total_steps + 16, ctx=ctx,
+                        scheme=args.scheme, seed=1)
+    rng = np.random.default_rng(3)
+    ids_h = torch.from_numpy(rng.integers(0, cfg.vocab_size, m * world).astype(np.int32)).pin_memory()
+    out_h = torch.zeros(m * world, dtype=torch.int32).pin_memory()
+    if pipe.plan.first:
+        pipe.put_ids(ids_h)
+    lib = load()
+    dist.barrier()
+    pipe.enqueue_step()  # eager warm-up step (kernel attributes, lazy module loads)
+    torch.cuda.synchronize()
+    n0 = lib.s8b_launch_count()
+    pipe.capture()
+    launches_per_step = int(lib.s8b_launch_count() - n0)
+    for _ in range(args.warmup):
+        pipe.step()
+    torch.cuda.synchronize()
+    pipe.check_status()
+    dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        time.sleep(0.3)
+        a.record()
+        for _ in range(args.steps):
+            pipe.step()
+        b.record()
+        b.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    torch.cuda.synchronize()
+    pipe.check_status()
+    dist.barrier()
+    # e2e through the host API: every rank synchronises its stream after each step; stage 0
+    # copies the step's ids in from pinned host memory and, once the last stage's tokens have
+    # landed in its slots (device-side flag wait), copies them back out
+    torch.cuda.synchronize()
+    dist.barrier()
+    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ea.record()
+    for _ in range(args.steps):
+        if pipe.plan.first:
+            pipe.put_ids(ids_h)
+        pipe.step()
+        if pipe.plan.first:
+            pipe.get_tokens(out_h)
+        torch.cuda.current_stream().synchronize()
+        if pipe.plan.first:
+            ids_h.copy_(out_h)
+    eb.record()
+    eb.synchronize()
+    e2e_ms = ea.elapsed_time(eb) / args.steps
+    pipe.check_status()
+    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=pipe.dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = t.tolist()
+    clocks = clk.summary()
+    hbm, _, peak_kind = peaks()
+    lo, hi = pipe.plan.layers
+    sb = step_bytes(cfg, m * world, ctx, hi - lo, pipe.plan.last)
+    pipe.close()
+    B = m * world
+    if rank == 0:
+        line = {
+            "metric": metric, "value": B / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 x int8 -> int32 GEMM, bf16 activations",
+            "data": "synthetic (random int8 weights, KV pre-filled with random codes)",
+            "config": {"workload": "qwen3-8b-shaped W8A8 decode (BASELINE config 3)",
+                       "micro_batch": m, "n_micro": world, "global_batch": B, "ctx": ctx,
+                       "layers": cfg.num_hidden_layers, "block_size": 16,
+                       "parallelism": f"pp{world}", "wire_scheme": args.scheme,
+                       "cuda_graph": True, "transport": "NVLink P2P stores + device flags",
+                       "l2": "inputs > L2, no flush"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+            "e2e": {"value": B / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B},
+            "step_roofline": {"bytes_rank0": sb, "achieved_gbs_rank0": sb / ms / 1e6,
+                              "frac_rank0": sb / ms / 1e6 / hbm, "peak": hbm,
+                              "peak_kind": peak_kind},
+        }
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
