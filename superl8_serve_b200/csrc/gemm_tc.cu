@@ -14,7 +14,7 @@
 // is associative), and the CTA that completes a tile's K range (per-tile counter) dequantizes,
 // stores, and clears the workspace tile and counter for the next launch.
 //
-// Roles (192 threads): warp 0 issues TMA loads (128B swizzle, no multicast), warp 1 issues the
+// Roles (192 threads): warp 0 issues TMA loads (128B swizzle, CTA-local destination), warp 1 issues the
 // MMAs (one thread) and owns the TMEM allocation, warps 2-5 drain TMEM (32 lanes each). The
 // accumulator is double-buffered in TMEM so a tile's epilogue overlaps the next tile's MMAs.
 // Every mbarrier wait is bounded: on timeout the kernel records S8B_ERR_TIMEOUT in the
