@@ -148,6 +148,16 @@ int s8b_kv_write_paged(const void *k, const void *v, int8_t *kc, float *ks, int8
  * stream-ordered. D must be 128; block_size a power of two dividing 256.
  * Replaces superl8.attn_paged_decode_cached (superl8serve/engine/kv_cache.py:1190-1201). */
 size_t s8b_paged_decode_workspace_size(int B, int Hq, int D, int max_ctx);
+/* Byte offset, inside the decode workspace, of an int32 status word: 0, or S8B_ERR_TIMEOUT
+ * when a bounded wait on a tensor-core completion barrier gave up (that launch's output is
+ * then invalid). Zero-filled with the workspace; the caller clears it after reading an error.
+ * No counterpart in the reference (its kernels have no bounded waits). */
+size_t s8b_paged_decode_status_offset(int B, int Hq);
+/* Selects the partition kernel behind every paged-decode entry point: 0 = tensor-core
+ * (tcgen05 kind::i8 for q.k and p.v, the default), 1 = CUDA-core (dp2a). Both give
+ * bit-identical results. Returns S8B_ERR_ARG for other values. No counterpart in the
+ * reference. */
+int s8b_set_attention_impl(int impl);
 int s8b_paged_decode_q8(const int8_t *q_i8, const float *q_s, const int8_t *kc, const float *ks,
                         const int8_t *vc, const float *vs, const int32_t *block_table,
                         const int32_t *context_lens, void *out, int8_t *out_q, float *out_s,

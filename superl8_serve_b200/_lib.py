@@ -40,6 +40,8 @@ SIGNATURES: dict[str, tuple] = {
                           _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "s8b_kv_write_paged": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "s8b_paged_decode_workspace_size": (_sz, [_i, _i, _i, _i]),
+    "s8b_paged_decode_status_offset": (_sz, [_i, _i]),
+    "s8b_set_attention_impl": (_i, [_i]),
     "s8b_paged_decode_q8": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i,
                                  _i, _i, _i, _i, _i, _f, _vp, _sz, _i, _vp]),
     "s8b_paged_decode_q8_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,

@@ -18,6 +18,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace s8b {
 namespace {
@@ -243,9 +244,79 @@ __device__ __forceinline__ int dp2a_hi(int a, int b, int c) { return __dp2a_hi(a
 struct DecodeWs {
   int32_t *cnt_group;  // [B*Hq] (row, kv head) completion counters (B*Hkv used)
   int32_t *cnt_row;    // [B]
+  int32_t *status;     // [1] S8B_ERR_TIMEOUT if a bounded wait of the tensor-core kernel gave up
   float *part_o;       // [B, Hq, P, 128]
   float *part_ml;      // [B, Hq, P, 2]
 };
+
+// Phase 5 shared by both partition kernels. The CTA that completes the last partition of its
+// (row, kv head) merges the partitions in index order: M = max m_p, w_p = exp(m_p - M),
+// L = sum w_p l_p, O = sum w_p o_p, out = dtype(O / L). The CTA that completes a row's last
+// kv head quantizes the whole output row for the o_proj GEMM. Counters return to zero.
+// `scratch` needs (G * P + G) floats and 32 floats of reduction space; `flag` one int.
+template <typename T, int G, int NTHR>
+__device__ __forceinline__ void merge_epilogue(float *scratch, int *flag, const DecodeWs &ws, int b,
+                                               int g, int Hq, int Hkv, int P, int np, T *out,
+                                               int8_t *out_q, float *out_s) {
+  const int tid = threadIdx.x;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    int32_t *c = ws.cnt_group + static_cast<size_t>(b) * Hkv + g;
+    const int done = atomicAdd(c, 1) + 1;
+    flag[0] = done == np;
+    if (done == np) *c = 0;
+  }
+  __syncthreads();
+  if (!flag[0]) return;
+  __threadfence();
+  // merge: per head h: M = max m_p, w_p = exp(m_p - M), L = sum w_p l_p, O = sum w_p o_p
+  float *Wp = scratch;  // [G][P] merge weights
+  float *Lh = Wp + G * P;
+  if (tid < G) {
+    const float *ml = ws.part_ml + (static_cast<size_t>(b) * Hq + g * G + tid) * P * 2;
+    float M = -__int_as_float(0x7f800000);
+    for (int q = 0; q < np; ++q) M = fmaxf(M, __ldcg(ml + 2 * q));
+    float Ls = 0.0f;
+    for (int q = 0; q < np; ++q) {
+      const float w = exp_s8b(__fsub_rn(__ldcg(ml + 2 * q), M));
+      Wp[tid * P + q] = w;
+      Ls = __fadd_rn(Ls, __fmul_rn(w, __ldcg(ml + 2 * q + 1)));
+    }
+    Lh[tid] = Ls;
+  }
+  __syncthreads();
+  for (int hd = tid; hd < G * kHd; hd += NTHR) {
+    const int h = hd / kHd, d = hd % kHd;
+    const float *po = ws.part_o + (static_cast<size_t>(b) * Hq + g * G + h) * P * kHd + d;
+    float O = 0.0f;
+    for (int q = 0; q < np; ++q) O = __fadd_rn(O, __fmul_rn(Wp[h * P + q], __ldcg(po + q * kHd)));
+    out[static_cast<size_t>(b) * Hq * kHd + (g * G + h) * kHd + d] = from_f32<T>(__fdiv_rn(O, Lh[h]));
+  }
+  if (!out_q) return;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const int done = atomicAdd(ws.cnt_row + b, 1) + 1;
+    flag[0] = done == Hkv;
+    if (done == Hkv) ws.cnt_row[b] = 0;
+  }
+  __syncthreads();
+  if (!flag[0]) return;
+  __threadfence();
+  // quantize the whole output row (all heads) for the o_proj GEMM
+  const T *row = out + static_cast<size_t>(b) * Hq * kHd;
+  float amax = 0.0f;
+  for (int i = tid; i < Hq * kHd; i += NTHR)  // written by other CTAs: read via L2
+    amax = fmaxf(amax, fabsf(ldcg_act(row + i)));
+  float *red = Wp;
+  amax = block_max(amax, red);
+  const QParams qp = qparams(amax, 127.0f);
+  for (int i = tid; i < Hq * kHd; i += NTHR)
+    out_q[static_cast<size_t>(b) * Hq * kHd + i] =
+        static_cast<int8_t>(qcode(ldcg_act(row + i), qp.inv, 127));
+  if (tid == 0) out_s[b] = qp.scale;
+}
 
 template <typename T, int G>
 __global__ void __launch_bounds__(kPartThreads)
@@ -436,69 +507,277 @@ __global__ void __launch_bounds__(kPartThreads)
   }
 
   // ---- phase 5: the last partition of this (row, kv head) merges; the last group quantizes ----
-  __threadfence();
-  __syncthreads();
+  merge_epilogue<T, G, kPartThreads>(reinterpret_cast<float *>(smem), flag, ws, b, g, Hq, Hkv, P,
+                                     np, out, out_q, out_s);
+}
+
+// ------------------------------------------------ tensor-core decode partitions ----
+// Same partition arithmetic as attn_partition_kernel, with both contractions on tcgen05:
+//  * q.k: D[token][head] (TMEM, int32) = K tile (A: 128 tokens x 128 ch, K-major, the SW128
+//    image the cp.async staging writes) x Q (B: 16 rows = G heads + zero rows, K-major);
+//    two 128-token tiles, 4 MMAs of K = 32 each;
+//  * p.v: O^T[ch][head] = V^T (A: 128 channels x tokens, MN-major, the same swizzled rows) x
+//    W (B: 16 rows x 256 tokens). The 15-bit weights are split into three signed byte planes,
+//    W = 2^14*a + 2^7*b + c (a in {0,1}; b, c in 0..127), three MMA chains,
+//    o = 2^14*D_a + 2^7*D_b + D_c: exact int32, hence bit-identical to the CUDA-core kernel
+//    and the oracle.
+// The per-token softmax work runs on 256 threads (thread = token, TMEM lane = token).
+constexpr int kTcThreads = 256;
+constexpr int kTcCols = 128;  // TMEM columns: S tile 0 | S tile 1 | O_a | O_b | O_c (16 each)
+
+template <int G>
+struct TcPartSmem {
+  static constexpr int kK = 0;                     // K codes, later W planes (12 KB) + e
+  static constexpr int kW = 0;                     // plane i at kW + 4096 i
+  static constexpr int kE = 12288;                 // [G][256] floats (<= 8 KB)
+  static constexpr int kV = kPart * kHd;           // V codes [256][128] (32 KB)
+  static constexpr int kQ = kV + kPart * kHd;      // Q [16][128] (2 KB)
+  static constexpr int kKsc = kQ + 16 * kHd;       // [256] floats
+  static constexpr int kVsc = kKsc + kPart * 4;    // [256] floats
+  static constexpr int kMisc = kVsc + kPart * 4;
+  static constexpr int kMiscBytes = 1536;
+  static constexpr size_t bytes = 1024 + kMisc + kMiscBytes;
+};
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+template <typename T, int G>
+__global__ void __launch_bounds__(kTcThreads)
+    attn_partition_tc_kernel(const int8_t *__restrict__ q_i8, const float *__restrict__ q_s,
+                             const int8_t *__restrict__ kc, const float *__restrict__ ks,
+                             const int8_t *__restrict__ vc, const float *__restrict__ vs,
+                             const int32_t *__restrict__ block_table,
+                             const int32_t *__restrict__ context_lens, int Hq, int Hkv,
+                             int bs_log2, int max_blocks, int P, float scale, DecodeWs ws,
+                             T *__restrict__ out, int8_t *__restrict__ out_q,
+                             float *__restrict__ out_s) {
+  using L = TcPartSmem<G>;
+  using namespace tc;
+  const int p = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int n = context_lens[b];
+  const int lo = p * kPart;
+  if (lo >= n) return;
+  const int cnt = min(kPart, n - lo);
+  const int np = (n + kPart - 1) / kPart;
+  const int bs = 1 << bs_log2;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  int8_t *Ks = reinterpret_cast<int8_t *>(sm + L::kK);
+  int8_t *Vs = reinterpret_cast<int8_t *>(sm + L::kV);
+  int8_t *Qs = reinterpret_cast<int8_t *>(sm + L::kQ);
+  uint8_t *Wpl = sm + L::kW;
+  float *E = reinterpret_cast<float *>(sm + L::kE);
+  float *ksc = reinterpret_cast<float *>(sm + L::kKsc);
+  float *vsc = reinterpret_cast<float *>(sm + L::kVsc);
+  float *qsc = reinterpret_cast<float *>(sm + L::kMisc);  // [8]
+  float *mx = qsc + 8, *wsc = mx + 8, *lsum = wsc + 8, *winv = lsum + 8;
+  float *pmax = winv + 8;                                 // [G][8 warps]
+  int *rowbase = reinterpret_cast<int *>(pmax + 64);      // [<= 256]
+  int *flag = rowbase + 256;
+  int *abort_flag = flag + 1;
+  uint32_t *tmem_base = reinterpret_cast<uint32_t *>(flag + 2);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(flag + 4);  // [2], 8-byte aligned
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_base)), "r"(kTcCols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
   if (tid == 0) {
-    int32_t *c = ws.cnt_group + static_cast<size_t>(b) * Hkv + g;
-    const int done = atomicAdd(c, 1) + 1;
-    flag[0] = done == np;
-    if (done == np) *c = 0;
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // ---- phase 1: stage K, V (cp.async, swizzled), Q (swizzled, zero rows G..15), scales ----
+  const int32_t *bt = block_table + static_cast<size_t>(b) * max_blocks + (lo >> bs_log2);
+  const int nblk = (cnt + bs - 1) >> bs_log2;
+  if (tid < nblk) rowbase[tid] = (bt[tid] * Hkv + g) << bs_log2;
+  if (tid < G) qsc[tid] = __fmul_rn(q_s[static_cast<size_t>(b) * Hq + g * G + tid], scale);
+  if (tid < 16 * 8) {
+    const int h = tid >> 3, c = tid & 7;
+    int4 v = make_int4(0, 0, 0, 0);
+    if (h < G)
+      v = reinterpret_cast<const int4 *>(q_i8 + (static_cast<size_t>(b) * Hq + g * G + h) * kHd)[c];
+    *reinterpret_cast<int4 *>(Qs + h * kHd + ((c ^ (h & 7)) * 16)) = v;
   }
   __syncthreads();
-  if (!flag[0]) return;
-  __threadfence();
-  // merge: per head h: M = max m_p, w_p = exp(m_p - M), L = sum w_p l_p, O = sum w_p o_p
-  float *Wp = reinterpret_cast<float *>(smem);  // [G][P] merge weights (K/V region is free)
-  float *Lh = Wp + G * P;
-  if (tid < G) {
-    const float *ml = ws.part_ml + (static_cast<size_t>(b) * Hq + g * G + tid) * P * 2;
-    float M = -__int_as_float(0x7f800000);
-    for (int q = 0; q < np; ++q) M = fmaxf(M, __ldcg(ml + 2 * q));
-    float Ls = 0.0f;
-    for (int q = 0; q < np; ++q) {
-      const float w = exp_s8b(__fsub_rn(__ldcg(ml + 2 * q), M));
-      Wp[tid * P + q] = w;
-      Ls = __fadd_rn(Ls, __fmul_rn(w, __ldcg(ml + 2 * q + 1)));
+  for (int idx = tid; idx < cnt * 8; idx += kTcThreads) {
+    const int t = idx >> 3, c = idx & 7;
+    const size_t row = static_cast<size_t>(rowbase[t >> bs_log2] + (t & (bs - 1)));
+    cp_async16(Ks + t * kHd + ((c ^ (t & 7)) * 16), kc + row * kHd + c * 16);
+  }
+  cp_async_commit();
+  for (int idx = tid; idx < cnt * 8; idx += kTcThreads) {
+    const int t = idx >> 3, c = idx & 7;
+    const size_t row = static_cast<size_t>(rowbase[t >> bs_log2] + (t & (bs - 1)));
+    cp_async16(Vs + t * kHd + ((c ^ (t & 7)) * 16), vc + row * kHd + c * 16);
+  }
+  cp_async_commit();
+  if (tid < cnt) {
+    const size_t row = static_cast<size_t>(rowbase[tid >> bs_log2] + (tid & (bs - 1)));
+    ksc[tid] = ks[row];
+    vsc[tid] = vs[row];
+  }
+  cp_async_wait<1>();
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_base;
+
+  // ---- phase 2: S = K Q^T on the tensor cores ----
+  if (tid == 0) {
+    constexpr uint32_t id_s = i8_idesc(128, 16);
+    const uint64_t qd = sw128_desc(smem_u32(Qs));
+#pragma unroll
+    for (int tile = 0; tile < 2; ++tile) {
+      const uint64_t kd = sw128_desc(smem_u32(Ks + tile * 128 * kHd));
+#pragma unroll
+      for (int k = 0; k < 4; ++k) mma_i8(tmem + tile * 16, kd + 2 * k, qd + 2 * k, id_s, k > 0);
     }
-    Lh[tid] = Ls;
+    mma_commit(&bars[0]);
+    mbar_wait(&bars[0], 0, abort_flag, ws.status);
   }
   __syncthreads();
-  for (int hd = tid; hd < G * kHd; hd += kPartThreads) {
-    const int h = hd / kHd, d = hd % kHd;
-    const float *po = ws.part_o + (static_cast<size_t>(b) * Hq + g * G + h) * P * kHd + d;
-    float O = 0.0f;
-    for (int q = 0; q < np; ++q) O = __fadd_rn(O, __fmul_rn(Wp[h * P + q], __ldcg(po + q * kHd)));
-    out[static_cast<size_t>(b) * Hq * kHd + (g * G + h) * kHd + d] = from_f32<T>(__fdiv_rn(O, Lh[h]));
+  const bool ok1 = !*abort_flag;
+  tc_fence_after();
+  const int t = tid;  // token of this thread (= TMEM lane of its tile)
+  float sv[G];
+  if (ok1) {
+    uint32_t v[16];
+    tmem_ld16(tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + (warp >> 2) * 16, v);
+    tmem_wait_ld();
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+      sv[h] = t < cnt ? __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(v[h])), qsc[h]), ksc[t])
+                      : -__int_as_float(0x7f800000);
   }
-  if (!out_q) return;
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const int done = atomicAdd(ws.cnt_row + b, 1) + 1;
-    flag[0] = done == Hkv;
-    if (done == Hkv) ws.cnt_row[b] = 0;
+  // ---- phase 3: softmax numerators, denominators, 15-bit value weights ----
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    const float m = warp_max(ok1 ? sv[h] : 0.0f);
+    if (lane == 0) pmax[h * 8 + warp] = m;
   }
   __syncthreads();
-  if (!flag[0]) return;
-  __threadfence();
-  // quantize the whole output row (all heads) for the o_proj GEMM
-  const T *row = out + static_cast<size_t>(b) * Hq * kHd;
-  float amax = 0.0f;
-  for (int i = tid; i < Hq * kHd; i += kPartThreads)  // written by other CTAs: read via L2
-    amax = fmaxf(amax, fabsf(ldcg_act(row + i)));
-  float *red = Wp;
-  amax = block_max(amax, red);
-  const QParams qp = qparams(amax, 127.0f);
-  for (int i = tid; i < Hq * kHd; i += kPartThreads)
-    out_q[static_cast<size_t>(b) * Hq * kHd + i] =
-        static_cast<int8_t>(qcode(ldcg_act(row + i), qp.inv, 127));
-  if (tid == 0) out_s[b] = qp.scale;
+  if (tid < G) {
+    float m = pmax[tid * 8];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) m = fmaxf(m, pmax[tid * 8 + i]);
+    mx[tid] = m;
+  }
+  __syncthreads();
+  float wv[G];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    float e = 0.0f;
+    if (t < cnt) e = exp_s8b(__fsub_rn(sv[h], mx[h]));
+    E[h * kPart + t] = e;
+    wv[h] = t < cnt ? __fmul_rn(e, vsc[t]) : 0.0f;
+    const float wm = warp_max(wv[h]);
+    if (lane == 0) pmax[h * 8 + warp] = wm;
+  }
+  __syncthreads();
+  if (tid < G) {
+    float wm = pmax[tid * 8];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) wm = fmaxf(wm, pmax[tid * 8 + i]);
+    wsc[tid] = __fdiv_rn(wm, 32767.0f);
+    winv[tid] = __fdiv_rn(32767.0f, wm);
+  }
+  __syncthreads();
+  {  // W planes, K-major SW128 images of [16 rows][256 tokens] (two 128-token blocks each)
+    const int blk = t >> 7, tt = t & 127;
+#pragma unroll
+    for (int h = 0; h < 16; ++h) {
+      int wq = 0;
+      if (h < G && t < cnt) {
+        wq = __float2int_rn(__fmul_rn(wv[h < G ? h : 0], winv[h < G ? h : 0]));
+        wq = wq < 0 ? 0 : (wq > 32767 ? 32767 : wq);
+      }
+      const int off = blk * 2048 + h * 128 + ((((tt >> 4) ^ (h & 7))) << 4) + (tt & 15);
+      Wpl[off] = static_cast<uint8_t>(wq >> 14);
+      Wpl[4096 + off] = static_cast<uint8_t>((wq >> 7) & 127);
+      Wpl[8192 + off] = static_cast<uint8_t>(wq & 127);
+    }
+  }
+  __syncthreads();
+  if (warp < G) {
+    const float *e = E + warp * kPart;
+    float l = e[lane];
+#pragma unroll
+    for (int i = 1; i < kPart / 32; ++i) l = __fadd_rn(l, e[i * 32 + lane]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, o));
+    if (lane == 0) lsum[warp] = l;
+  }
+  cp_async_wait<0>();
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  // ---- phase 4: O^T = V^T W^T on the tensor cores (three byte planes of W) ----
+  if (tid == 0 && ok1) {
+    constexpr uint32_t id_pv = i8_idesc(128, 16, true, true, /*a_mn_major=*/true, false);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint64_t vd = sw128_desc(smem_u32(Vs + j * 32 * kHd));
+#pragma unroll
+      for (int pl = 0; pl < 3; ++pl) {
+        const uint64_t wd = sw128_desc(smem_u32(Wpl + pl * 4096 + (j >> 2) * 2048)) + 2 * (j & 3);
+        mma_i8(tmem + 32 + 16 * pl, vd, wd, id_pv, j > 0);
+      }
+    }
+    mma_commit(&bars[1]);
+    mbar_wait(&bars[1], 0, abort_flag, ws.status);
+  }
+  __syncthreads();
+  const bool ok2 = !*abort_flag;
+  tc_fence_after();
+  if (ok2 && warp < 4) {
+    uint32_t da[16], db[16], dc[16];
+    const uint32_t lanes = static_cast<uint32_t>(warp * 32) << 16;
+    tmem_ld16(tmem + lanes + 32, da);
+    tmem_ld16(tmem + lanes + 48, db);
+    tmem_ld16(tmem + lanes + 64, dc);
+    tmem_wait_ld();
+    const int d = warp * 32 + lane;
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      const int o = static_cast<int32_t>(da[h]) * 16384 + static_cast<int32_t>(db[h]) * 128 +
+                    static_cast<int32_t>(dc[h]);
+      const size_t hq = static_cast<size_t>(b) * Hq + g * G + h;
+      ws.part_o[(hq * P + p) * kHd + d] = __fmul_rn(static_cast<float>(o), wsc[h]);
+    }
+  }
+  if (ok2 && tid < G) {
+    const size_t hq = static_cast<size_t>(b) * Hq + g * G + tid;
+    ws.part_ml[(hq * P + p) * 2 + 0] = mx[tid];
+    ws.part_ml[(hq * P + p) * 2 + 1] = lsum[tid];
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTcCols) : "memory");
+  if (!ok2) return;
+  // ---- phase 5 ----
+  merge_epilogue<T, G, kTcThreads>(reinterpret_cast<float *>(sm + L::kK), flag, ws, b, g, Hq, Hkv,
+                                   P, np, out, out_q, out_s);
 }
 
 inline int num_parts(int max_ctx) { return (max_ctx + kPart - 1) / kPart; }
 
+// 0: tensor-core partition kernel (default), 1: CUDA-core partition kernel
+int g_attn_impl = 0;
+
 size_t counters_bytes(int B, int Hq) {
-  return (static_cast<size_t>(B) * Hq * 4 + static_cast<size_t>(B) * 4 + 255) / 256 * 256;
+  return (static_cast<size_t>(B) * Hq * 4 + static_cast<size_t>(B) * 4 + 16 + 255) / 256 * 256;
 }
 
 size_t part_bytes(int B, int Hq, int max_ctx) {
@@ -512,6 +791,7 @@ DecodeWs carve_ws(void *base, int B, int Hq, int max_ctx) {
   DecodeWs w;
   w.cnt_group = reinterpret_cast<int32_t *>(p);
   w.cnt_row = w.cnt_group + static_cast<size_t>(B) * Hq;
+  w.status = w.cnt_row + B;
   w.part_o = reinterpret_cast<float *>(p + counters_bytes(B, Hq));
   w.part_ml = w.part_o + static_cast<size_t>(B) * Hq * P * kHd;
   return w;
@@ -528,6 +808,30 @@ int launch_decode(const int8_t *q_i8, const float *q_s, const int8_t *kc, const 
   int bs_log2 = 0;
   while ((1 << bs_log2) < bs) ++bs_log2;
   const DecodeWs w = carve_ws(workspace, B, Hq, max_ctx);
+  if (g_attn_impl == 0) {
+    switch (G) {
+#define S8B_TC_CASE(GG)                                                                        \
+  case GG: {                                                                                   \
+    auto kern = attn_partition_tc_kernel<T, GG>;                                                \
+    ensure_smem(reinterpret_cast<const void *>(kern), TcPartSmem<GG>::bytes);                   \
+    kern<<<dim3(P, Hkv, B), kTcThreads, TcPartSmem<GG>::bytes, st>>>(                           \
+        q_i8, q_s, kc, ks, vc, vs, block_table, context_lens, Hq, Hkv, bs_log2, max_blocks, P,  \
+        scale, w, static_cast<T *>(out), out_q, out_s);                                         \
+    return check_launch(1);                                                                    \
+  }
+      S8B_TC_CASE(1)
+      S8B_TC_CASE(2)
+      S8B_TC_CASE(3)
+      S8B_TC_CASE(4)
+      S8B_TC_CASE(5)
+      S8B_TC_CASE(6)
+      S8B_TC_CASE(7)
+      S8B_TC_CASE(8)
+#undef S8B_TC_CASE
+      default:
+        return S8B_ERR_SHAPE;
+    }
+  }
   switch (G) {
 #define S8B_PART_CASE(GG)                                                                      \
   case GG: {                                                                                   \
@@ -728,4 +1032,14 @@ extern "C" int s8b_paged_decode(const void *q, const int8_t *kc, const float *ks
     return launch_decode<T>(q8, qsc, kc, ks, vc, vs, block_table, context_lens, out, nullptr,
                             nullptr, B, Hq, Hkv, block_size, max_blocks, max_ctx, scale, part, st);
   });
+}
+
+extern "C" size_t s8b_paged_decode_status_offset(int B, int Hq) {
+  return static_cast<size_t>(B) * Hq * 4 + static_cast<size_t>(B) * 4;
+}
+
+extern "C" int s8b_set_attention_impl(int impl) {
+  if (impl != 0 && impl != 1) return S8B_ERR_ARG;
+  s8b::g_attn_impl = impl;
+  return S8B_OK;
 }

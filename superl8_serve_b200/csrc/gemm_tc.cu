@@ -27,9 +27,12 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace s8b {
 namespace {
+
+using namespace tc;
 
 constexpr int kBM = 128;          // weight rows per tile (MMA M)
 constexpr int kBK = 128;          // K bytes per stage (one 128B swizzle atom row)
@@ -37,7 +40,6 @@ constexpr int kABytes = kBM * kBK;
 constexpr int kThreads = 192;
 constexpr int kMaxStages = 8;
 constexpr int kSmemBudget = 220 * 1024;
-constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s per wait before giving up
 
 struct TcSmemHeader {
   uint64_t full[kMaxStages];
@@ -49,72 +51,6 @@ struct TcSmemHeader {
   int is_last;
   float xs[256];  // per-token activation scales of this launch's token tile
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ uint64_t now_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-      "selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait. Returns false (and raises the CTA abort flag and the global status) on timeout
-// or when another role of the CTA already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
-                                          int32_t *status) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = now_ns();
-  while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (*abort) return false;
-    if (now_ns() - t0 > kWaitNs) {
-      *abort = 1;
-      atomicExch(status, S8B_ERR_TIMEOUT);
-      return false;
-    }
-  }
-}
-
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
-                                            uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// Plain bulk copy global -> shared of `bytes` contiguous bytes (16-byte aligned, multiple of
-// 16), completing on the stage's mbarrier like a TMA tile load.
-__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
-                                          uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
 
 // Pack W [N, K] (row-major int8) into unit images: unit (tile, kc) holds rows
 // tile*128..+127, bytes kc*128..+127 as the 128B-swizzled K-major shared-memory image
@@ -134,63 +70,6 @@ __global__ void pack_tc_kernel(const int8_t *__restrict__ w, int N, int K,
     if (n < N) v = *reinterpret_cast<const int4 *>(w + static_cast<size_t>(n) * K + kk * kBK + c * 16);
     *reinterpret_cast<int4 *>(packed + unit * kABytes + r * kBK + ((c ^ (r & 7)) * 16)) = v;
   }
-}
-
-// Shared-memory matrix descriptor, K-major operand in 128B-swizzled 8-row x 128-byte atoms:
-// start >> 4 in [0,14), SBO = 1024 B (stride between 8-row groups) in [32,46), descriptor
-// version 1 in [46,48), layout SWIZZLE_128B (2) in [61,64). LBO is unused for this layout.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFF);
-  d |= static_cast<uint64_t>(1) << 16;
-  d |= static_cast<uint64_t>(1024 >> 4) << 32;
-  d |= static_cast<uint64_t>(1) << 46;
-  d |= static_cast<uint64_t>(2) << 61;
-  return d;
-}
-
-// Instruction descriptor kind::i8: D s32 [4,6)=2, A s8 [7,10)=1, B s8 [10,13)=1, both K-major,
-// N>>3 in [17,23), M>>4 in [24,29).
-template <int NT>
-__device__ __forceinline__ constexpr uint32_t i8_idesc() {
-  return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(NT >> 3) << 17) |
-         (static_cast<uint32_t>(kBM >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                       uint32_t idesc, uint32_t accumulate) {
-  const uint32_t z = 0;
-  asm volatile(
-      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(
-          tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z));
-}
-__device__ __forceinline__ void mma_commit(uint64_t *bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&v)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-      "%14,%15}, [%16];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
-        "=r"(v[14]), "=r"(v[15])
-      : "r"(addr));
-}
-__device__ __forceinline__ void tmem_wait_ld() {
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void epi_bar_sync() {
-  asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
 template <int NT>
@@ -286,7 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // -------------------------------------------------------------- MMA issuer ----
     if (lane == 0) {
-      constexpr uint32_t idesc = i8_idesc<NT>();
+      constexpr uint32_t idesc = i8_idesc(kBM, NT);
       long long it = 0;
       int seg = 0;
       for (long long u = u0; u < u1 && !*abort; ++u, ++it) {

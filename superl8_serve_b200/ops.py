@@ -139,6 +139,19 @@ def decode_workspace_bytes(B, Hq, D, max_ctx, *, ref=False) -> int:
     return int(fn(B, Hq, D, max_ctx))
 
 
+def set_attention_impl(impl: str) -> None:
+    """"tc" (tcgen05 partition kernel, default) or "cuda_core"; results are bit-identical."""
+    call("s8b_set_attention_impl", {"tc": 0, "cuda_core": 1}[impl])
+
+
+def decode_status(workspace, B, Hq) -> int:
+    """The workspace's status word (0, or the timeout code of a bounded tensor-core wait)."""
+    from ._lib import load
+
+    off = int(load().s8b_paged_decode_status_offset(B, Hq))
+    return int(workspace[off:off + 4].view(torch.int32).item())
+
+
 def paged_decode_q8(q_i8, q_s, kc, ks, vc, vs, block_table, context_lens, max_ctx, scale, *,
                     out=None, out_q=None, out_s=None, workspace=None, dtype=torch.bfloat16):
     B, Hq, D = q_i8.shape

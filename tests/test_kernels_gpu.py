@@ -156,19 +156,31 @@ def test_kv_write_paged_standalone(rng, rotate):
     assert np.array_equal(vcd.cpu().numpy(), vc) and np.array_equal(vsd.cpu().numpy(), vs)
 
 
-@pytest.mark.parametrize("B,Hq,Hkv,lens", [
-    (4, 32, 8, [1, 17, 256, 257]),       # partition edges, single token
-    (3, 16, 8, [600, 33, 1000]),         # ragged, several partitions
-    (2, 40, 8, [2049, 129]),             # 5:1 GQA (27B shape)
-    (1, 32, 4, [4096]),                  # 8:1 GQA (30B-A3B shape), 16 partitions
-])
-def test_paged_decode_bit_exact(rng, B, Hq, Hkv, lens):
+@pytest.fixture(params=["tc", "cuda_core"])
+def attn_impl(request):
     from superl8_serve_b200 import ops
 
-    bs = 16
+    ops.set_attention_impl(request.param)
+    yield request.param
+    ops.set_attention_impl("tc")
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,lens,bs", [
+    (4, 32, 8, [1, 17, 256, 257], 16),       # partition edges, single token
+    (3, 16, 8, [600, 33, 1000], 16),         # ragged, several partitions
+    (2, 40, 8, [2049, 129], 16),             # 5:1 GQA (27B shape)
+    (1, 32, 4, [4096], 16),                  # 8:1 GQA (30B-A3B shape), 16 partitions
+    (3, 8, 8, [128, 129, 511], 32),          # MHA (G = 1)
+    (2, 21, 3, [300, 64], 64),               # G = 7, wide blocks
+    (2, 24, 8, [255, 700], 256),             # G = 3, one block per partition
+    (2, 12, 2, [5, 90], 1),                  # G = 6, one token per block
+])
+def test_paged_decode_bit_exact(rng, attn_impl, B, Hq, Hkv, lens, bs):
+    from superl8_serve_b200 import ops
+
     maxb = (max(lens) + bs - 1) // bs
     nb = B * maxb + 3
-    kc, ks, vc, vs = make_pool(rng, nb, Hkv)
+    kc, ks, vc, vs = make_pool(rng, nb, Hkv, bs)
     perm = rng.permutation(nb)
     bt = np.zeros((B, maxb + 2), dtype=np.int32)
     for b in range(B):
@@ -180,8 +192,13 @@ def test_paged_decode_bit_exact(rng, B, Hq, Hkv, lens):
     qqd, qsd, kcd, ksd, vcd, vsd, btd, cld = to_dev(qq, qs, kc, ks, vc, vs, bt, cl)
     oq = torch.empty((B, Hq * 128), dtype=torch.int8, device=DEV)
     osc = torch.empty(B, dtype=torch.float32, device=DEV)
-    out = ops.paged_decode_q8(qqd, qsd, kcd, ksd, vcd, vsd, btd, cld, max(lens) + 5, scale,
-                              out_q=oq, out_s=osc)
+    max_ctx = min(max(lens) + 5, bt.shape[1] * bs)  # an upper bound the block table covers
+    ws = torch.zeros(ops.decode_workspace_bytes(B, Hq, 128, max_ctx), dtype=torch.uint8,
+                     device=DEV)
+    for _ in range(2):  # the second launch reuses the self-resetting counters
+        out = ops.paged_decode_q8(qqd, qsd, kcd, ksd, vcd, vsd, btd, cld, max_ctx, scale,
+                                  out_q=oq, out_s=osc, workspace=ws)
+    assert ops.decode_status(ws, B, Hq) == 0
     ref = ok.paged_decode(qq, qs, kc, ks, vc, vs, bt, cl, bs, scale).reshape(B, -1)
     assert np.array_equal(f32(out), ref)
     rq, rs = on.quant_rows_i8(ref)
