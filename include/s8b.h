@@ -153,10 +153,12 @@ size_t s8b_paged_decode_workspace_size(int B, int Hq, int D, int max_ctx);
  * then invalid). Zero-filled with the workspace; the caller clears it after reading an error.
  * No counterpart in the reference (its kernels have no bounded waits). */
 size_t s8b_paged_decode_status_offset(int B, int Hq);
-/* Selects the partition kernel behind every paged-decode entry point: 0 = tensor-core
- * (tcgen05 kind::i8 for q.k and p.v, the default), 1 = CUDA-core (dp2a). Both give
- * bit-identical results. Returns S8B_ERR_ARG for other values. No counterpart in the
- * reference. */
+/* Selects the kernel behind every paged-decode entry point: 0 (default) = the persistent
+ * warp-specialized tensor-core kernel (TMA ring, tcgen05 kind::i8 for q.k and p.v) where the
+ * shape allows it (block_size >= 8, 16-byte aligned scale arrays), else the per-partition
+ * tensor-core kernel; 1 = CUDA-core (dp2a) partition kernel; 2 = per-partition tensor-core
+ * kernel. All give bit-identical results. Returns S8B_ERR_ARG for other values. No
+ * counterpart in the reference. */
 int s8b_set_attention_impl(int impl);
 int s8b_paged_decode_q8(const int8_t *q_i8, const float *q_s, const int8_t *kc, const float *ks,
                         const int8_t *vc, const float *vs, const int32_t *block_table,

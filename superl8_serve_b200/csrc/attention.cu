@@ -249,27 +249,52 @@ struct DecodeWs {
   float *part_ml;      // [B, Hq, P, 2]
 };
 
-// Phase 5 shared by both partition kernels. The CTA that completes the last partition of its
-// (row, kv head) merges the partitions in index order: M = max m_p, w_p = exp(m_p - M),
-// L = sum w_p l_p, O = sum w_p o_p, out = dtype(O / L). The CTA that completes a row's last
+// Phase 5 shared by the partition kernels. The thread group that completes the last partition
+// of its (row, kv head) merges the partitions in index order: M = max m_p, w_p = exp(m_p - M),
+// L = sum w_p l_p, O = sum w_p o_p, out = dtype(O / L). The group that completes a row's last
 // kv head quantizes the whole output row for the o_proj GEMM. Counters return to zero.
-// `scratch` needs (G * P + G) floats and 32 floats of reduction space; `flag` one int.
-template <typename T, int G, int NTHR>
-__device__ __forceinline__ void merge_epilogue(float *scratch, int *flag, const DecodeWs &ws, int b,
-                                               int g, int Hq, int Hkv, int P, int np, T *out,
-                                               int8_t *out_q, float *out_s) {
-  const int tid = threadIdx.x;
-  __threadfence();
-  __syncthreads();
+// Arrival follows the grid-barrier pattern: the group synchronises, then one thread fences
+// (making the group's partial stores visible device-wide) and increments the counter; the
+// last arriver fences again before the group reads the others' partials through L2.
+// `tid` is the thread's index in the group of NTHR threads and `sync` synchronises exactly
+// that group. `scratch` needs (G * P + G) floats, `red` 32 floats, `flag` one int.
+struct CtaSync {
+  __device__ __forceinline__ void operator()() const { __syncthreads(); }
+};
+template <int NTHR>
+struct GroupSync {
+  int id;
+  __device__ __forceinline__ void operator()() const { tc::group_sync(id, NTHR); }
+};
+
+template <int NTHR, typename Sync>
+__device__ __forceinline__ float group_max(float v, float *red, int tid, Sync sync) {
+  v = warp_max(v);
+  sync();
+  if ((tid & 31) == 0) red[tid >> 5] = v;
+  sync();
+  v = (tid & 31) < NTHR / 32 ? red[tid & 31] : 0.0f;
+  return warp_max(v);
+}
+
+template <typename T, int G, int NTHR, typename Sync>
+__device__ __forceinline__ void merge_epilogue(float *scratch, float *red, int *flag,
+                                               const DecodeWs &ws, int b, int g, int Hq, int Hkv,
+                                               int P, int np, T *out, int8_t *out_q,
+                                               float *out_s, int tid, Sync sync) {
+  sync();
   if (tid == 0) {
+    __threadfence();
     int32_t *c = ws.cnt_group + static_cast<size_t>(b) * Hkv + g;
     const int done = atomicAdd(c, 1) + 1;
     flag[0] = done == np;
-    if (done == np) *c = 0;
+    if (done == np) {
+      *c = 0;
+      __threadfence();
+    }
   }
-  __syncthreads();
+  sync();
   if (!flag[0]) return;
-  __threadfence();
   // merge: per head h: M = max m_p, w_p = exp(m_p - M), L = sum w_p l_p, O = sum w_p o_p
   float *Wp = scratch;  // [G][P] merge weights
   float *Lh = Wp + G * P;
@@ -285,7 +310,7 @@ __device__ __forceinline__ void merge_epilogue(float *scratch, int *flag, const 
     }
     Lh[tid] = Ls;
   }
-  __syncthreads();
+  sync();
   for (int hd = tid; hd < G * kHd; hd += NTHR) {
     const int h = hd / kHd, d = hd % kHd;
     const float *po = ws.part_o + (static_cast<size_t>(b) * Hq + g * G + h) * P * kHd + d;
@@ -294,23 +319,24 @@ __device__ __forceinline__ void merge_epilogue(float *scratch, int *flag, const 
     out[static_cast<size_t>(b) * Hq * kHd + (g * G + h) * kHd + d] = from_f32<T>(__fdiv_rn(O, Lh[h]));
   }
   if (!out_q) return;
-  __threadfence();
-  __syncthreads();
+  sync();
   if (tid == 0) {
+    __threadfence();
     const int done = atomicAdd(ws.cnt_row + b, 1) + 1;
     flag[0] = done == Hkv;
-    if (done == Hkv) ws.cnt_row[b] = 0;
+    if (done == Hkv) {
+      ws.cnt_row[b] = 0;
+      __threadfence();
+    }
   }
-  __syncthreads();
+  sync();
   if (!flag[0]) return;
-  __threadfence();
   // quantize the whole output row (all heads) for the o_proj GEMM
   const T *row = out + static_cast<size_t>(b) * Hq * kHd;
   float amax = 0.0f;
   for (int i = tid; i < Hq * kHd; i += NTHR)  // written by other CTAs: read via L2
     amax = fmaxf(amax, fabsf(ldcg_act(row + i)));
-  float *red = Wp;
-  amax = block_max(amax, red);
+  amax = group_max<NTHR>(amax, red, tid, sync);
   const QParams qp = qparams(amax, 127.0f);
   for (int i = tid; i < Hq * kHd; i += NTHR)
     out_q[static_cast<size_t>(b) * Hq * kHd + i] =
@@ -507,8 +533,8 @@ __global__ void __launch_bounds__(kPartThreads)
   }
 
   // ---- phase 5: the last partition of this (row, kv head) merges; the last group quantizes ----
-  merge_epilogue<T, G, kPartThreads>(reinterpret_cast<float *>(smem), flag, ws, b, g, Hq, Hkv, P,
-                                     np, out, out_q, out_s);
+  merge_epilogue<T, G, kPartThreads>(reinterpret_cast<float *>(smem), pmax, flag, ws, b, g, Hq,
+                                     Hkv, P, np, out, out_q, out_s, tid, CtaSync{});
 }
 
 // ------------------------------------------------ tensor-core decode partitions ----
@@ -767,13 +793,494 @@ __global__ void __launch_bounds__(kTcThreads)
                  "r"(kTcCols) : "memory");
   if (!ok2) return;
   // ---- phase 5 ----
-  merge_epilogue<T, G, kTcThreads>(reinterpret_cast<float *>(sm + L::kK), flag, ws, b, g, Hq, Hkv,
-                                   P, np, out, out_q, out_s);
+  merge_epilogue<T, G, kTcThreads>(reinterpret_cast<float *>(sm + L::kK), pmax, flag, ws, b, g,
+                                   Hq, Hkv, P, np, out, out_q, out_s, tid, CtaSync{});
+}
+
+// ------------------------------------------ persistent warp-specialized decode ----
+// One CTA per SM walks the work units (row b, kv head g, partition p) in a static round-robin.
+// Roles:
+//   warps 0, 14  producers (TMA issue from one warp tops out near 5.7 TB/s for 2 KB boxes):
+//                per unit, warp 0 issues one 2-D TMA tensor copy per KV block of K plus one
+//                for the G query rows, warp 14 one per KV block of V (the 128B swizzle lands
+//                each row in the SW128 image the MMAs read) plus the K/V and query scales as
+//                cp.async spread over its lanes, tracked by the same stage barrier; 3-stage
+//                ring of 69 KB stages. Block-table rows (one per lane) are loaded three units
+//                ahead.
+//   warp 1       MMA issuer (one thread): S = K Q^T for unit k+1 is issued before
+//                O^T = V^T W^T of unit k. S and O are double-buffered in TMEM
+//                (S: 2 x 32 columns, O: 2 x 48 columns).
+//   warps 2-9    two softmax groups of 4 warps; group j takes the units with k % 2 == j, so
+//                each group has two unit-times for its latency-bound chain (thread = TMEM
+//                lane = tokens t and t + 128): scores, partition maxima, exp, the 15-bit
+//                weights as three byte planes over the consumed K tile, the lane-order
+//                denominators.
+//   warps 10-13  epilogue: O planes -> per-partition partials in the workspace.
+// No CTA waits for another: the partitions are merged afterwards by attn_merge_rows_kernel
+// (a device-wide fence per unit here would stall the pipeline behind in-flight TMA traffic).
+// The arithmetic per unit is exactly that of attn_partition_kernel. Every mbarrier wait is
+// bounded; a timeout raises a CTA abort flag, which each role group turns into a uniform
+// exit (barrier-reduce), and the workspace status word.
+//
+// p.v as one MMA of N = 48 per 32-token step: B rows 16*plane + head hold the byte planes of
+// W = 2^14*a + 2^7*b + c, so D columns [0,16), [16,32), [32,48) are O_a, O_b, O_c.
+namespace pk {
+constexpr int kStages = 3;
+constexpr int kStage = 70656;  // K/W/E 32 KB | V 32 KB | Q 2 KB | K, V scales 1 KB each | q scales
+constexpr int kOffV = 32768, kOffQ = 65536, kOffKs = 67584, kOffVs = 68608, kOffQs = 69632;
+constexpr int kWBlock = 6144;  // one 128-token block of the 48-row weight operand
+constexpr int kOffE = 12288;   // e values [G][256] floats, after the two weight blocks
+constexpr int kThreads = 480;
+constexpr int kTmemCols = 256;
+constexpr int kColO = 64;      // O buffer t at kColO + 48 t; S buffer t at 32 t
+constexpr int kMisc = 2048;    // barriers, TMEM base, abort flag, stats, reductions
+constexpr int kMaxRows = 1024; // context lengths cached in shared memory
+constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * kStage + kMisc + 4 * kMaxRows;
+}  // namespace pk
+
+// Walks units u = start, start + step, ... as (p, g, b) digits of u in radix (P, Hkv), with
+// the step's digits computed once: advancing is adds and carries, no division (a per-unit
+// division chain costs a single-warp role about a microsecond).
+struct UnitIter {
+  int p, g, b, dp, dg, db, P, Hkv;
+  __device__ UnitIter(int start, int step, int P_, int Hkv_) : P(P_), Hkv(Hkv_) {
+    p = start % P;
+    g = (start / P) % Hkv;
+    b = start / (P * Hkv);
+    dp = step % P;
+    dg = (step / P) % Hkv;
+    db = step / (P * Hkv);
+  }
+  __device__ __forceinline__ void next() {
+    p += dp;
+    int c = p >= P;
+    p -= c ? P : 0;
+    g += dg + c;
+    c = g >= Hkv;
+    g -= c ? Hkv : 0;
+    b += db + c;
+  }
+};
+
+template <typename T, int G>
+__global__ void __launch_bounds__(pk::kThreads, 1)
+    attn_persistent_kernel(const __grid_constant__ CUtensorMap map_k,
+                           const __grid_constant__ CUtensorMap map_v,
+                           const __grid_constant__ CUtensorMap map_q,
+                           const float *__restrict__ q_s, const float *__restrict__ ks,
+                           const float *__restrict__ vs, const int32_t *__restrict__ block_table,
+                           const int32_t *__restrict__ context_lens, int B, int Hq, int Hkv,
+                           int bs_log2, int max_blocks, int P, float scale, DecodeWs ws) {
+  using namespace tc;
+  using namespace pk;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *misc = sm + kStages * kStage;
+  uint64_t *full = reinterpret_cast<uint64_t *>(misc);  // [3] stage loaded (tx bytes)
+  uint64_t *empty = full + 3;                           // [3] stage free (p.v done + softmax done)
+  uint64_t *wfull = full + 6;                           // [3] W planes of the stage written
+  uint64_t *sfull = full + 9;                           // [2] S buffer holds a unit's scores
+  uint64_t *sempty = full + 11;                         // [2] S buffer read (4 warp arrivals)
+  uint64_t *ofull = full + 13;                          // [2] O buffer + stats ready
+  uint64_t *oempty = full + 15;                         // [2] O buffer read (4 warp arrivals)
+  uint64_t *drain = full + 17;                          // [1] MMA drain on exit
+  uint32_t *tmem_base = reinterpret_cast<uint32_t *>(misc + 256);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(misc + 260);
+  float *stats = reinterpret_cast<float *>(misc + 512);  // [2][3][8]: m, l, wmax/32767
+  float *red = reinterpret_cast<float *>(misc + 768);    // [2 groups][2][4 warps][8 heads]
+  int *ctx = reinterpret_cast<int *>(misc + kMisc);      // [B] context lengths
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_base)), "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&full[i], 2 + 32);  // two expect_tx arrivals + one cp.async arrival per V lane
+      mbar_init(&empty[i], 2);
+      mbar_init(&wfull[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sfull[i], 1);
+      mbar_init(&sempty[i], 4);
+      mbar_init(&ofull[i], 2);
+      mbar_init(&oempty[i], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  for (int i = threadIdx.x; i < B; i += kThreads) ctx[i] = context_lens[i];
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_base;
+  const int bs = 1 << bs_log2;
+
+  if (warp == 0 || warp == 14) {
+    // ----------------------------------------------------------------- producers ----
+    const bool vwarp = warp == 14;
+    const CUtensorMap *map = vwarp ? &map_v : &map_k;
+    auto next_valid = [&](UnitIter &it) {
+      while (it.b < B && it.p * kPart >= ctx[it.b]) it.next();
+    };
+    auto block_row = [&](const UnitIter &it) {  // this lane's KV block row (0 past the end)
+      if (it.b >= B) return 0;
+      const int nblk = (min(kPart, ctx[it.b] - it.p * kPart) + bs - 1) >> bs_log2;
+      if (lane >= nblk) return 0;
+      return (block_table[static_cast<size_t>(it.b) * max_blocks + ((it.p * kPart) >> bs_log2) +
+                          lane] * Hkv + it.g) << bs_log2;
+    };
+    // block-table rows three units ahead: under full HBM load a table miss takes a few us
+    int k = 0;
+    UnitIter i0(blockIdx.x, gridDim.x, P, Hkv);
+    next_valid(i0);
+    UnitIter i1 = i0;
+    i1.next();
+    next_valid(i1);
+    UnitIter i2 = i1;
+    i2.next();
+    next_valid(i2);
+    int row0 = block_row(i0), row1 = block_row(i1), row2 = block_row(i2);
+    while (i0.b < B) {
+      const int row = row0;
+      UnitIter i3 = i2;
+      i3.next();
+      next_valid(i3);
+      row0 = row1;
+      row1 = row2;
+      row2 = block_row(i3);
+      const int p = i0.p, g = i0.g, b = i0.b;
+      const int cnt = min(kPart, ctx[b] - p * kPart);
+      const int nblk = (cnt + bs - 1) >> bs_log2;
+      const int s = k % kStages;
+      bool ok = true;
+      if (lane == 0 && k >= kStages)
+        ok = mbar_wait(&empty[s], ((k / kStages) - 1) & 1, abort_flag, ws.status);
+      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+      uint8_t *st = sm + s * kStage;
+      if (lane == 0)
+        mbar_expect_tx(&full[s], static_cast<uint32_t>(nblk * bs * kHd + (vwarp ? 0 : G * kHd)));
+      __syncwarp();
+      if (lane < nblk) tma_load_2d(st + (vwarp ? kOffV : 0) + lane * bs * kHd, map, 0, row, &full[s]);
+      if (!vwarp) {
+        if (lane == 0) tma_load_2d(st + kOffQ, &map_q, 0, b * Hq + g * G, &full[s]);
+        i0 = i1;
+        i1 = i2;
+        i2 = i3;
+        ++k;
+        continue;
+      }
+      // scales: 16-byte chunks c of 4 tokens; chunk c of array a goes to lane c % 32
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int c = lane + 32 * (i & 1);  // chunk within the array
+        const int j = (4 * c) >> bs_log2;   // block of that chunk
+        const int rj = __shfl_sync(0xffffffffu, row, j & 31);
+        if (4 * c < nblk * bs) {
+          const float *src = (i < 2 ? ks : vs) + rj + ((4 * c) & (bs - 1));
+          cp_async16(st + (i < 2 ? kOffKs : kOffVs) + 16 * c, src);
+        }
+      }
+      if (lane < G)  // the G query scales of this (row, kv head)
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(st + kOffQs + 4 * lane)),
+                     "l"(q_s + static_cast<size_t>(b) * Hq + g * G + lane)
+                     : "memory");
+      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&full[s]))
+                   : "memory");
+      i0 = i1;
+      i1 = i2;
+      i2 = i3;
+      ++k;
+    }
+    if (*abort_flag && lane == 0)  // let issued copies land before the CTA exits
+      for (int j = k > kStages ? k - kStages : 0; j < k; ++j)
+        mbar_drain(&full[j % kStages], (j / kStages) & 1);
+  } else if (warp == 1) {
+    // -------------------------------------------------------------------- MMA issuer ----
+    if (lane == 0) {
+      constexpr uint32_t id_s = i8_idesc(128, 16);
+      constexpr uint32_t id_pv = i8_idesc(128, 48, true, true, /*a_mn_major=*/true, false);
+      auto issue_pv = [&](int j) -> bool {
+        const int s = j % kStages, t = j & 1;
+        if (!mbar_wait(&wfull[s], (j / kStages) & 1, abort_flag, ws.status)) return false;
+        if (j >= 2 && !mbar_wait(&oempty[t], ((j >> 1) - 1) & 1, abort_flag, ws.status)) return false;
+        tc_fence_after();
+        uint8_t *st = sm + s * kStage;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint64_t vd = sw128_desc(smem_u32(st + kOffV + i * 32 * kHd));
+          const uint64_t wd = sw128_desc(smem_u32(st + (i >> 2) * kWBlock)) + 2 * (i & 3);
+          mma_i8(tmem + kColO + 48 * t, vd, wd, id_pv, i > 0);
+        }
+        mma_commit(&ofull[t]);
+        mma_commit(&empty[s]);
+        return true;
+      };
+      int k = 0;
+      bool ok = true;
+      for (UnitIter it(blockIdx.x, gridDim.x, P, Hkv); it.b < B && ok; it.next()) {
+        if (it.p * kPart >= ctx[it.b]) continue;
+        const int s = k % kStages, t = k & 1;
+        ok = mbar_wait(&full[s], (k / kStages) & 1, abort_flag, ws.status) &&
+             (k < 2 || mbar_wait(&sempty[t], ((k >> 1) - 1) & 1, abort_flag, ws.status));
+        if (!ok) break;
+        tc_fence_after();
+        uint8_t *st = sm + s * kStage;
+        const uint64_t qd = sw128_desc(smem_u32(st + kOffQ));
+#pragma unroll
+        for (int tile = 0; tile < 2; ++tile) {
+          const uint64_t kd = sw128_desc(smem_u32(st + tile * 128 * kHd));
+#pragma unroll
+          for (int i = 0; i < 4; ++i) mma_i8(tmem + 32 * t + 16 * tile, kd + 2 * i, qd + 2 * i, id_s, i > 0);
+        }
+        mma_commit(&sfull[t]);
+        if (k > 0) ok = issue_pv(k - 1);
+        ++k;
+      }
+      if (ok && k > 0) issue_pv(k - 1);
+      mma_commit(drain);  // all MMAs issued by this thread have completed once this arrives
+      mbar_drain(drain, 0);
+    }
+  } else if (warp < 10) {
+    // ------------------------------------------------------------------- softmax ----
+    const int grp = (warp - 2) >> 2, q4 = warp & 3, tid = (threadIdx.x - 64) & 127;
+    const int t0 = 32 * q4 + lane, t1 = t0 + 128;
+    float *red_s = red + grp * 64, *red_w = red_s + 32;
+    int k = 0;
+    for (UnitIter it(blockIdx.x, gridDim.x, P, Hkv); it.b < B; it.next()) {
+      const int p = it.p, g = it.g, b = it.b;
+      const int n = ctx[b], lo = p * kPart;
+      if (lo >= n) continue;
+      if ((k & 1) != grp) {
+        ++k;
+        continue;
+      }
+      const int s = k % kStages, t = k & 1;
+      bool ok = mbar_wait(&full[s], (k / kStages) & 1, abort_flag, ws.status) &&
+                mbar_wait(&sfull[t], (k >> 1) & 1, abort_flag, ws.status) &&
+                (k < 2 || mbar_wait(&oempty[t], ((k >> 1) - 1) & 1, abort_flag, ws.status));
+      if (group_any(1 + grp, 128, !ok || *abort_flag)) break;
+      const int cnt = min(kPart, n - lo);
+      tc_fence_after();
+      uint32_t a0[16], a1[16];
+      tmem_ld16(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + 32 * t, a0);
+      tmem_ld16(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + 32 * t + 16, a1);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sempty[t]);
+      uint8_t *st = sm + s * kStage;
+      const float *ksc = reinterpret_cast<const float *>(st + kOffKs);
+      const float *vsc = reinterpret_cast<const float *>(st + kOffVs);
+      const float *qsv = reinterpret_cast<const float *>(st + kOffQs);
+      const float ks0 = ksc[t0], ks1 = ksc[t1], vs0 = vsc[t0], vs1 = vsc[t1];
+      float s0[G], s1[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float qsc = __fmul_rn(qsv[h], scale);
+        s0[h] = t0 < cnt ? __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(a0[h])), qsc), ks0)
+                         : -__int_as_float(0x7f800000);
+        s1[h] = t1 < cnt ? __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(a1[h])), qsc), ks1)
+                         : -__int_as_float(0x7f800000);
+      }
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float m = warp_max(fmaxf(s0[h], s1[h]));
+        if (lane == 0) red_s[q4 * 8 + h] = m;
+      }
+      group_sync(1 + grp, 128);
+      float *E = reinterpret_cast<float *>(st + kOffE);
+      float w0[G], w1[G], mh[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        mh[h] = fmaxf(fmaxf(red_s[h], red_s[8 + h]), fmaxf(red_s[16 + h], red_s[24 + h]));
+        const float e0 = t0 < cnt ? exp_s8b(__fsub_rn(s0[h], mh[h])) : 0.0f;
+        const float e1 = t1 < cnt ? exp_s8b(__fsub_rn(s1[h], mh[h])) : 0.0f;
+        E[h * kPart + t0] = e0;
+        E[h * kPart + t1] = e1;
+        w0[h] = t0 < cnt ? __fmul_rn(e0, vs0) : 0.0f;
+        w1[h] = t1 < cnt ? __fmul_rn(e1, vs1) : 0.0f;
+      }
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float wm = warp_max(fmaxf(w0[h], w1[h]));
+        if (lane == 0) red_w[q4 * 8 + h] = wm;
+      }
+      group_sync(1 + grp, 128);
+      float wsc_h[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float wm = fmaxf(fmaxf(red_w[h], red_w[8 + h]), fmaxf(red_w[16 + h], red_w[24 + h]));
+        wsc_h[h] = __fdiv_rn(wm, 32767.0f);
+        const float winv = __fdiv_rn(32767.0f, wm);
+        int q0 = t0 < cnt ? __float2int_rn(__fmul_rn(w0[h], winv)) : 0;
+        int q1 = t1 < cnt ? __float2int_rn(__fmul_rn(w1[h], winv)) : 0;
+        q0 = q0 < 0 ? 0 : (q0 > 32767 ? 32767 : q0);
+        q1 = q1 < 0 ? 0 : (q1 > 32767 ? 32767 : q1);
+        // rows 16*plane + h of the K-major SW128 weight operand; t0 lies in token block 0 and
+        // t1 in block 1 at the same in-block position
+        const int off = h * 128 + ((((t0 >> 4) ^ (h & 7))) << 4) + (t0 & 15);
+        st[off] = static_cast<uint8_t>(q0 >> 14);
+        st[2048 + off] = static_cast<uint8_t>((q0 >> 7) & 127);
+        st[4096 + off] = static_cast<uint8_t>(q0 & 127);
+        st[kWBlock + off] = static_cast<uint8_t>(q1 >> 14);
+        st[kWBlock + 2048 + off] = static_cast<uint8_t>((q1 >> 7) & 127);
+        st[kWBlock + 4096 + off] = static_cast<uint8_t>(q1 & 127);
+      }
+      fence_proxy_async_smem();
+      group_sync(1 + grp, 128);
+      if (tid == 0) mbar_arrive(&wfull[s]);
+      float *st_t = stats + t * 24;
+#pragma unroll
+      for (int h = 0; h < G; ++h) {  // denominators, lane order of the CUDA-core kernel
+        if ((h & 3) != q4) continue;  // warp q4 takes heads q4, q4 + 4
+        const float *e = E + h * kPart;
+        float l = e[lane];
+#pragma unroll
+        for (int i = 1; i < kPart / 32; ++i) l = __fadd_rn(l, e[i * 32 + lane]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, o));
+        if (lane == 0) {
+          st_t[h] = mh[h];
+          st_t[8 + h] = l;
+          st_t[16 + h] = wsc_h[h];
+        }
+      }
+      group_sync(1 + grp, 128);
+      if (tid == 0) {
+        mbar_arrive(&empty[s]);
+        mbar_arrive(&ofull[t]);
+      }
+      ++k;
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue ----
+    const int q4 = warp & 3, tid = threadIdx.x - 320;
+    const int d = 32 * q4 + lane;
+    int k = 0;
+    for (UnitIter it(blockIdx.x, gridDim.x, P, Hkv); it.b < B; it.next()) {
+      const int p = it.p, g = it.g, b = it.b;
+      const int n = ctx[b], lo = p * kPart;
+      if (lo >= n) continue;
+      const int t = k & 1;
+      const bool ok = mbar_wait(&ofull[t], (k >> 1) & 1, abort_flag, ws.status);
+      if (group_any(3, 128, !ok || *abort_flag)) break;
+      tc_fence_after();
+      uint32_t da[16], db[16], dc[16];
+      const uint32_t lanes = static_cast<uint32_t>(q4 * 32) << 16;
+      tmem_ld16(tmem + lanes + kColO + 48 * t, da);
+      tmem_ld16(tmem + lanes + kColO + 48 * t + 16, db);
+      tmem_ld16(tmem + lanes + kColO + 48 * t + 32, dc);
+      tmem_wait_ld();
+      const float *st_t = stats + t * 24;
+      float wsc_h[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h) wsc_h[h] = st_t[16 + h];
+      float ml0 = 0.0f, ml1 = 0.0f;
+      if (tid < G) {
+        ml0 = st_t[tid];
+        ml1 = st_t[8 + tid];
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&oempty[t]);
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const int o = static_cast<int32_t>(da[h]) * 16384 + static_cast<int32_t>(db[h]) * 128 +
+                      static_cast<int32_t>(dc[h]);
+        const size_t hq = static_cast<size_t>(b) * Hq + g * G + h;
+        ws.part_o[(hq * P + p) * kHd + d] = __fmul_rn(static_cast<float>(o), wsc_h[h]);
+      }
+      if (tid < G) {
+        const size_t hq = static_cast<size_t>(b) * Hq + g * G + tid;
+        ws.part_ml[(hq * P + p) * 2 + 0] = ml0;
+        ws.part_ml[(hq * P + p) * 2 + 1] = ml1;
+      }
+      ++k;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols) : "memory");
+}
+
+// Merge of the persistent kernel's partials, one CTA per row: per head M = max m_p,
+// w_p = exp(m_p - M), L = sum w_p l_p, O = sum w_p o_p (partition order), out = dtype(O / L);
+// then the row's int8 quantization for o_proj. Same arithmetic as merge_epilogue.
+constexpr int kMergeThreads = 1024;
+constexpr int kMergeVpt = 8;  // Hq * 128 <= 8192 values per row held in registers
+template <typename T>
+__global__ void __launch_bounds__(kMergeThreads)
+    attn_merge_rows_kernel(DecodeWs ws, const int32_t *__restrict__ context_lens, int Hq, int P,
+                           T *__restrict__ out, int8_t *__restrict__ out_q,
+                           float *__restrict__ out_s) {
+  extern __shared__ float msm[];  // [Hq][P] (m, l) pairs, then weights; [Hq] denominators
+  __shared__ float red[32];
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const int np = (context_lens[b] + kPart - 1) / kPart;
+  float *Wp = msm, *Lh = msm + 2 * Hq * P;
+  const float *mlb = ws.part_ml + static_cast<size_t>(b) * Hq * P * 2;
+  for (int i = tid; i < Hq * P * 2; i += kMergeThreads) msm[i] = mlb[i];  // all loads in flight
+  __syncthreads();
+  for (int h = tid; h < Hq; h += kMergeThreads) {
+    const float *ml = msm + h * P * 2;
+    float M = -__int_as_float(0x7f800000);
+    for (int q = 0; q < np; ++q) M = fmaxf(M, ml[2 * q]);
+    float Ls = 0.0f;
+    for (int q = 0; q < np; ++q) {
+      const float w = exp_s8b(__fsub_rn(ml[2 * q], M));
+      Ls = __fadd_rn(Ls, __fmul_rn(w, ml[2 * q + 1]));
+      Wp[h * P * 2 + 2 * q] = w;  // overwrites m_q, already consumed
+    }
+    Lh[h] = Ls;
+  }
+  __syncthreads();
+  const int nv = Hq * kHd;
+  T *orow = out + static_cast<size_t>(b) * nv;
+  float v[kMergeVpt];
+  float amax = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kMergeVpt; ++j) {
+    const int i = tid + j * kMergeThreads;
+    v[j] = 0.0f;
+    if (i < nv) {
+      const int h = i / kHd, d = i % kHd;
+      const float *po = ws.part_o + (static_cast<size_t>(b) * Hq + h) * P * kHd + d;
+      float O = 0.0f;
+      for (int q0 = 0; q0 < np; q0 += 8) {  // 8 loads in flight, then the ordered sum
+        float x[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) x[q] = q0 + q < np ? po[(q0 + q) * kHd] : 0.0f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          if (q0 + q < np) O = __fadd_rn(O, __fmul_rn(Wp[h * P * 2 + 2 * (q0 + q)], x[q]));
+      }
+      v[j] = round_to<T>(__fdiv_rn(O, Lh[h]));
+      orow[i] = from_f32<T>(v[j]);
+      amax = fmaxf(amax, fabsf(v[j]));
+    }
+  }
+  if (!out_q) return;
+  amax = block_max(amax, red);
+  const QParams qp = qparams(amax, 127.0f);
+#pragma unroll
+  for (int j = 0; j < kMergeVpt; ++j) {
+    const int i = tid + j * kMergeThreads;
+    if (i < nv) out_q[static_cast<size_t>(b) * nv + i] = static_cast<int8_t>(qcode(v[j], qp.inv, 127));
+  }
+  if (tid == 0) out_s[b] = qp.scale;
 }
 
 inline int num_parts(int max_ctx) { return (max_ctx + kPart - 1) / kPart; }
 
-// 0: tensor-core partition kernel (default), 1: CUDA-core partition kernel
+// 0: persistent tensor-core kernel where the shape allows it, else the per-partition
+// tensor-core kernel (default); 1: CUDA-core partition kernel; 2: per-partition tensor-core
 int g_attn_impl = 0;
 
 size_t counters_bytes(int B, int Hq) {
@@ -797,6 +1304,63 @@ DecodeWs carve_ws(void *base, int B, int Hq, int max_ctx) {
   return w;
 }
 
+// The persistent kernel + row merge, when the shape allows it: blocks of >= 8 tokens (each
+// TMA box then starts on a 1024-byte swizzle atom), 16-byte aligned scale arrays (16-byte
+// cp.async), B <= 1024 rows, Hq * 128 <= 8192 and the merge weights within 96 KB of shared
+// memory, and K/V buffers whose allocation extent the driver reports (the tensor maps cover
+// exactly that). Returns 1 when not applicable.
+template <typename T>
+int launch_persistent(const int8_t *q_i8, const float *q_s, const int8_t *kc, const float *ks,
+                      const int8_t *vc, const float *vs, const int32_t *block_table,
+                      const int32_t *context_lens, void *out, int8_t *out_q, float *out_s, int B,
+                      int Hq, int Hkv, int bs, int bs_log2, int max_blocks, int P, float scale,
+                      const DecodeWs &w, cudaStream_t st) {
+  const int G = Hq / Hkv;
+  const size_t merge_smem = 4 * (2 * static_cast<size_t>(Hq) * P + Hq);
+  if (bs < 8 || B > pk::kMaxRows || Hq * kHd > kMergeThreads * kMergeVpt || merge_smem > 96 * 1024 ||
+      !aligned(ks, 16) || !aligned(vs, 16) || !aligned(q_i8, 16))
+    return 1;
+  const size_t kb = tc::bytes_to_alloc_end(kc), vb = tc::bytes_to_alloc_end(vc);
+  const uint64_t rows_k = kb / kHd, rows_v = vb / kHd;
+  if (rows_k < static_cast<uint64_t>(bs) || rows_v < static_cast<uint64_t>(bs) ||
+      rows_k > 0xffffffffull || rows_v > 0xffffffffull)
+    return 1;
+  CUtensorMap mk, mv, mq;
+  if (tc::make_map_2d(&mk, kc, kHd, rows_k, kHd, kHd, bs) ||
+      tc::make_map_2d(&mv, vc, kHd, rows_v, kHd, kHd, bs) ||
+      tc::make_map_2d(&mq, q_i8, kHd, static_cast<uint64_t>(B) * Hq, kHd, kHd, G))
+    return 1;
+  const long U = static_cast<long>(B) * Hkv * P;
+  const int grid = static_cast<int>(U < tc::sm_count() ? U : tc::sm_count());
+  switch (G) {
+#define S8B_PK_CASE(GG)                                                                        \
+  case GG: {                                                                                   \
+    auto kern = attn_persistent_kernel<T, GG>;                                                  \
+    ensure_smem(reinterpret_cast<const void *>(kern), pk::kSmem);                               \
+    kern<<<grid, pk::kThreads, pk::kSmem, st>>>(mk, mv, mq, q_s, ks, vs, block_table,           \
+                                                context_lens, B, Hq, Hkv, bs_log2, max_blocks,  \
+                                                P, scale, w);                                   \
+    break;                                                                                     \
+  }
+    S8B_PK_CASE(1)
+    S8B_PK_CASE(2)
+    S8B_PK_CASE(3)
+    S8B_PK_CASE(4)
+    S8B_PK_CASE(5)
+    S8B_PK_CASE(6)
+    S8B_PK_CASE(7)
+    S8B_PK_CASE(8)
+#undef S8B_PK_CASE
+    default:
+      return S8B_ERR_SHAPE;
+  }
+  auto merge = attn_merge_rows_kernel<T>;
+  ensure_smem(reinterpret_cast<const void *>(merge), 96 * 1024);
+  merge<<<B, kMergeThreads, merge_smem, st>>>(w, context_lens, Hq, P, static_cast<T *>(out), out_q,
+                                              out_s);
+  return check_launch(2);
+}
+
 template <typename T>
 int launch_decode(const int8_t *q_i8, const float *q_s, const int8_t *kc, const float *ks,
                   const int8_t *vc, const float *vs, const int32_t *block_table,
@@ -809,6 +1373,12 @@ int launch_decode(const int8_t *q_i8, const float *q_s, const int8_t *kc, const 
   while ((1 << bs_log2) < bs) ++bs_log2;
   const DecodeWs w = carve_ws(workspace, B, Hq, max_ctx);
   if (g_attn_impl == 0) {
+    const int rc = launch_persistent<T>(q_i8, q_s, kc, ks, vc, vs, block_table, context_lens, out,
+                                        out_q, out_s, B, Hq, Hkv, bs, bs_log2, max_blocks, P,
+                                        scale, w, st);
+    if (rc != 1) return rc;
+  }
+  if (g_attn_impl != 1) {
     switch (G) {
 #define S8B_TC_CASE(GG)                                                                        \
   case GG: {                                                                                   \
@@ -1039,7 +1609,7 @@ extern "C" size_t s8b_paged_decode_status_offset(int B, int Hq) {
 }
 
 extern "C" int s8b_set_attention_impl(int impl) {
-  if (impl != 0 && impl != 1) return S8B_ERR_ARG;
+  if (impl < 0 || impl > 2) return S8B_ERR_ARG;
   s8b::g_attn_impl = impl;
   return S8B_OK;
 }

@@ -297,46 +297,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ----------------------------------------------------------------------- host side ----
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaDriverEntryPointQueryResult q;
-    void *p = nullptr;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
 int make_map(CUtensorMap *map, const void *base, int inner, int outer, int box_outer) {
-  auto fn = encode_fn();
-  if (!fn) return S8B_ERR_CUDA;
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(inner)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_outer)};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims,
-                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? S8B_OK : S8B_ERR_ALIGN;
-}
-
-int sm_count() {
-  static std::mutex mu;
-  static std::map<int, int> cache;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  std::lock_guard<std::mutex> lk(mu);
-  auto it = cache.find(dev);
-  if (it != cache.end()) return it->second;
-  int n = 0;
-  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  cache[dev] = n > 0 ? n : 148;
-  return cache[dev];
+  return make_map_2d(map, base, static_cast<uint64_t>(inner), static_cast<uint64_t>(outer),
+                     static_cast<uint64_t>(inner), kBK, static_cast<uint32_t>(box_outer));
 }
 
 inline int pick_nt(int m) {

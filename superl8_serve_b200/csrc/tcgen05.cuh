@@ -4,6 +4,10 @@
 #pragma once
 
 #include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <map>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -66,6 +70,31 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
       : "memory");
 }
 
+// Bounded wait that ignores the abort flag: used on the way out of an aborted kernel, to let
+// copies already in flight land before the CTA's shared memory is released.
+__device__ __forceinline__ bool mbar_drain(uint64_t *bar, uint32_t parity,
+                                           unsigned long long limit_ns = 100000000ull) {
+  const uint64_t t0 = now_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (now_ns() - t0 > limit_ns) return false;
+  return true;
+}
+
+// Named barrier over `n` threads that also returns, to all of them, whether any passed `p`.
+__device__ __forceinline__ bool group_any(int id, int n, bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n.reg .pred a, b;\nsetp.ne.u32 a, %1, 0;\nbar.red.or.pred b, %2, %3, a;\n"
+      "selp.u32 %0, 1, 0, b;\n}\n"
+      : "=r"(r)
+      : "r"(p ? 1u : 0u), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void group_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
 // Plain bulk copy global -> shared of `bytes` contiguous bytes (16-byte aligned, multiple of
 // 16), completing on the stage's mbarrier like a TMA tile load.
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
@@ -89,8 +118,6 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor kind::i8: D s32 [4,6)=2, A s8 [7,10)=1, B s8 [10,13)=1, both K-major,
-// N>>3 in [17,23), M>>4 in [24,29).
 // Instruction descriptor kind::i8: D s32 [4,6)=2, A/B format (s8 = 1, u8 = 0) in [7,10) /
 // [10,13), A/B major (0 = K, 1 = MN) bits 15/16, N>>3 in [17,23), M>>4 in [24,29).
 __host__ __device__ constexpr uint32_t i8_idesc(int M, int N, bool a_signed = true,
@@ -138,6 +165,73 @@ __device__ __forceinline__ void epi_bar_sync() {
   asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
+
+// ------------------------------------------------------------------- host helpers ----
+inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void *p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D uint8 tensor map with 128B swizzle: `outer` rows of `inner` bytes, `pitch` bytes apart;
+// one copy moves a box of box_inner bytes x box_outer rows.
+inline int make_map_2d(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer,
+                       uint64_t pitch, uint32_t box_inner, uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return S8B_ERR_CUDA;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {pitch};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? S8B_OK : S8B_ERR_ALIGN;
+}
+
+// Bytes from `p` to the end of the device allocation that contains it (0 if unknown): the
+// extent a tensor map over a caller's buffer may cover.
+inline size_t bytes_to_alloc_end(const void *p) {
+  static PFN_cuMemGetAddressRange_v3020 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void *f = nullptr;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(f);
+  });
+  if (!fn) return 0;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (fn(&base, &size, reinterpret_cast<CUdeviceptr>(p)) != CUDA_SUCCESS) return 0;
+  const uint64_t a = reinterpret_cast<uint64_t>(p);
+  return a >= base && a < base + size ? static_cast<size_t>(base + size - a) : 0;
+}
+
+inline int sm_count() {
+  static std::mutex mu;
+  static std::map<int, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  cache[dev] = n > 0 ? n : 148;
+  return cache[dev];
+}
 
 }  // namespace tc
 }  // namespace s8b

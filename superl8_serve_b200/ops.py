@@ -139,9 +139,13 @@ def decode_workspace_bytes(B, Hq, D, max_ctx, *, ref=False) -> int:
     return int(fn(B, Hq, D, max_ctx))
 
 
+ATTENTION_IMPLS = {"auto": 0, "cuda_core": 1, "tc_partition": 2}
+
+
 def set_attention_impl(impl: str) -> None:
-    """"tc" (tcgen05 partition kernel, default) or "cuda_core"; results are bit-identical."""
-    call("s8b_set_attention_impl", {"tc": 0, "cuda_core": 1}[impl])
+    """"auto" (persistent tensor-core kernel where the shape allows, the default),
+    "cuda_core" or "tc_partition"; results are bit-identical."""
+    call("s8b_set_attention_impl", ATTENTION_IMPLS[impl])
 
 
 def decode_status(workspace, B, Hq) -> int:

@@ -156,13 +156,13 @@ def test_kv_write_paged_standalone(rng, rotate):
     assert np.array_equal(vcd.cpu().numpy(), vc) and np.array_equal(vsd.cpu().numpy(), vs)
 
 
-@pytest.fixture(params=["tc", "cuda_core"])
+@pytest.fixture(params=["auto", "tc_partition", "cuda_core"])
 def attn_impl(request):
     from superl8_serve_b200 import ops
 
     ops.set_attention_impl(request.param)
     yield request.param
-    ops.set_attention_impl("tc")
+    ops.set_attention_impl("auto")
 
 
 @pytest.mark.parametrize("B,Hq,Hkv,lens,bs", [
