@@ -85,11 +85,13 @@ int s8b_gemm_w8a8(const int8_t *xq, const float *xs, const int8_t *w, const floa
 
 /* W8A8 GEMM on the tensor cores (tcgen05.mma kind::i8, TMA-fed, TMEM accumulators), same
  * arithmetic and outputs as s8b_gemm_w8a8, for token counts where the contraction is dense
- * (M >= 16; M > 256 runs in 256-token passes). K % 128 == 0. The workspace
- * (s8b_gemm_tc_workspace_size bytes, 256-byte aligned) must be zero-filled once by the
- * caller; every completed launch leaves it zero again. workspace[0] (int32) receives
- * S8B_ERR_TIMEOUT if a bounded wait inside the kernel gave up, after which the caller must
- * re-zero the workspace. Launches sharing one workspace must be stream-ordered.
+ * (M >= 16; M > 256 runs in 256-token passes). K % 128 == 0. Split-K partial sums are
+ * reduced inside thread-block clusters (distributed shared memory), so the workspace
+ * (s8b_gemm_tc_workspace_size bytes, 256-byte aligned, zero-filled once by the caller) only
+ * holds a status word: workspace[0] (int32) receives S8B_ERR_TIMEOUT if a bounded wait
+ * inside the kernel gave up, after which the caller must re-zero it. The launch carries a
+ * programmatic dependency on the preceding kernel in the stream (weights prefetch early;
+ * activations, scales and outputs are touched only after that kernel has completed).
  * Replaces superl8.linear / gemm_w8a8 (superl8serve/layers/linear.py:122).               */
 size_t s8b_gemm_tc_workspace_size(int M, int N);
 int s8b_gemm_w8a8_tc(const int8_t *xq, const float *xs, const int8_t *w, const float *ws,

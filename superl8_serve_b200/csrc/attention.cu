@@ -111,6 +111,7 @@ __global__ void __launch_bounds__(512)
                     int8_t *__restrict__ vc, float *__restrict__ vs,
                     const int32_t *__restrict__ slot_mapping,
                     const int32_t *__restrict__ block_table, int max_blocks, int bs) {
+  griddep_launch();  // the next kernel may start its prologue
   const int m = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int HR = Hq + 2 * Hkv;
@@ -871,6 +872,7 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
                            const float *__restrict__ vs, const int32_t *__restrict__ block_table,
                            const int32_t *__restrict__ context_lens, int B, int Hq, int Hkv,
                            int bs_log2, int max_blocks, int P, float scale, DecodeWs ws) {
+  griddep_launch();  // the next kernel may start its prologue
   using namespace tc;
   using namespace pk;
   extern __shared__ uint8_t smem_raw[];
@@ -1220,6 +1222,7 @@ __global__ void __launch_bounds__(kMergeThreads)
     attn_merge_rows_kernel(DecodeWs ws, const int32_t *__restrict__ context_lens, int Hq, int P,
                            T *__restrict__ out, int8_t *__restrict__ out_q,
                            float *__restrict__ out_s) {
+  griddep_launch();  // the next kernel may start its prologue
   extern __shared__ float msm[];  // [Hq][P] (m, l) pairs, then weights; [Hq] denominators
   __shared__ float red[32];
   const int b = blockIdx.x, tid = threadIdx.x;

@@ -25,6 +25,16 @@ void ensure_smem(const void *kernel, size_t bytes);
 
 inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Programmatic dependent launch: wait for the preceding kernel's results (a no-op when the
+// launch carries no programmatic dependency) / let the next kernel in the stream start its
+// prologue early (its own wait still covers this kernel's completion).
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ----------------------------------------------------------------------------- dtypes ----
 __device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
 __device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }

@@ -6,19 +6,10 @@
 // so the weight matrix (the HBM stream) fills the 128-row MMA dimension and the small token
 // count is the N dimension.
 //
-// Work split. A unit is one 128-row x 128-byte weight chunk (16 KB). The units of all row
-// tiles are laid out tile-major and cut into one contiguous range per persistent CTA (one CTA
-// per SM), so every SM streams the same number of weight bytes whatever N and K are. A range
-// that covers a whole row tile stores the result directly; ranges that cover part of a tile
-// add their int32 partial sums into a workspace with red.global.add (exact: integer addition
-// is associative), and the CTA that completes a tile's K range (per-tile counter) dequantizes,
-// stores, and clears the workspace tile and counter for the next launch.
-//
-// Roles (192 threads): warp 0 issues TMA loads (128B swizzle, CTA-local destination), warp 1 issues the
-// MMAs (one thread) and owns the TMEM allocation, warps 2-5 drain TMEM (32 lanes each). The
-// accumulator is double-buffered in TMEM so a tile's epilogue overlaps the next tile's MMAs.
-// Every mbarrier wait is bounded: on timeout the kernel records S8B_ERR_TIMEOUT in the
-// workspace status word, lets in-flight copies land, frees TMEM and returns.
+// Work split: thread-block clusters of C CTAs walk the 128-row weight tiles; the C CTAs of a
+// cluster split each tile's K range and reduce their int32 partial tiles through distributed
+// shared memory (see gemm_tc_kernel). Launched with programmatic stream serialization: the
+// first weight tiles stream in while the preceding kernel finishes.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -37,7 +28,8 @@ using namespace tc;
 constexpr int kBM = 128;          // weight rows per tile (MMA M)
 constexpr int kBK = 128;          // K bytes per stage (one 128B swizzle atom row)
 constexpr int kABytes = kBM * kBK;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kEpi = 256;  // epilogue threads: two warps per TMEM lane quadrant
 constexpr int kMaxStages = 8;
 constexpr int kSmemBudget = 220 * 1024;
 
@@ -46,10 +38,12 @@ struct TcSmemHeader {
   uint64_t empty[kMaxStages];
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
+  uint64_t recv;     // split-K: receive buffer filled by every CTA of the cluster (tx bytes)
+  uint64_t done;     // split-K: every CTA of the cluster finished reducing its receive buffer
   uint32_t tmem_base;
   int abort;
-  int is_last;
-  float xs[256];  // per-token activation scales of this launch's token tile
+  float xs[256];     // per-token activation scales of this launch's token tile
+  float wsc[2][128];  // per-row weight scales of the tile in each TMEM buffer
 };
 
 // Pack W [N, K] (row-major int8) into unit images: unit (tile, kc) holds rows
@@ -76,11 +70,20 @@ template <int NT>
 struct TcLayout {
   static constexpr int kBBytes = NT * kBK;
   static constexpr int kStageBytes = kABytes + kBBytes;
+  // split-K buffers (token tiles up to 64 only), rows of NT int32 plus a 16-byte pad
+  // (conflict-free row-per-thread access): the staging tile [128 rows] this CTA sends from,
+  // and the receive buffer [C source slots][ceil(128/C) rows] (<= 136 rows for C <= 8)
+  static constexpr int kPartPitch = NT * 4 + 16;
+  static constexpr int kStageRows = NT <= 64 ? kBM : 0;
+  static constexpr int kRecvRows = NT <= 64 ? 136 : 0;
+  static constexpr int kPartBytes = (kStageRows + kRecvRows) * kPartPitch;
   static constexpr int kStages =
-      (kSmemBudget - 3072) / kStageBytes < kMaxStages ? (kSmemBudget - 3072) / kStageBytes
-                                                      : kMaxStages;
+      (kSmemBudget - 3072 - kPartBytes) / kStageBytes < kMaxStages
+          ? (kSmemBudget - 3072 - kPartBytes) / kStageBytes
+          : kMaxStages;
   static constexpr int kTmemCols = 2 * NT < 32 ? 32 : 2 * NT;
-  static constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * kStageBytes + 2048;
+  static constexpr size_t kSmem =
+      1024 + static_cast<size_t>(kStages) * kStageBytes + kPartBytes + 3072;
 };
 
 struct TcArgs {
@@ -88,12 +91,71 @@ struct TcArgs {
   const float *xs;
   const float *ws;
   void *y;
-  int32_t *acc;       // workspace [NT][N] int32 (zero between launches)
-  int32_t *counters;  // workspace [n_tiles]
-  int32_t *status;    // workspace status word
+  int32_t *status;  // workspace status word
   int out_kind, M, N, K, m0, n_tiles, kc;
+  int csplit;     // CTAs per cluster sharing each tile's K range (1: no split)
+  int nclusters;  // clusters in the grid
 };
 
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t mapa(uint32_t saddr, uint32_t cta) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(cta));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint64_t *bar, uint32_t cta) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                   mapa(smem_u32(bar), cta))
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\nmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait with cluster-scope acquire (peer CTAs arrive on this barrier).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity,
+                                                  volatile int *abort, int32_t *status) {
+  const uint64_t t0 = now_ns();
+  while (!mbar_try_wait_cluster(bar, parity)) {
+    if (*abort) return false;
+    if (now_ns() - t0 > 2000000000ull) {
+      *abort = 1;
+      atomicExch(status, S8B_ERR_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
+// W8A8 GEMM on the 5th-generation tensor cores (tcgen05.mma kind::i8), swap-AB: A = 128
+// weight rows x 32 K-bytes, B = NT tokens x 32 K-bytes, D = 128 x NT int32 in TMEM, so the
+// weight matrix (the HBM stream) fills the 128-row MMA dimension.
+//
+// Work split. Clusters of C CTAs walk the 128-row weight tiles round-robin; CTA r of a
+// cluster streams K chunks [r*kc/C, (r+1)*kc/C) of every tile of its cluster. With C > 1 the
+// epilogue stages its int32 partial tile in shared memory and one thread moves each CTA's
+// rows (rows [ceil(r*128/C), ceil((r+1)*128/C)) belong to CTA r) into that CTA's receive
+// buffer with one shared-to-shared bulk copy, completing on the owner's mbarrier as a byte
+// count; the owner then sums the C slots from its own shared memory (integer sums: exact in
+// any order), dequantizes and stores. No global workspace, atomics, device-wide fences or
+// remote loads. C is chosen per shape by the host to balance the tiles over the clusters.
+//
+// Roles (320 threads): warp 0 issues the loads (TMA or bulk copies of pre-packed weight
+// images; the weight copies of the first stages go out before griddepcontrol.wait, the
+// activations after it), warp 1 issues the MMAs (one thread) and owns the TMEM allocation,
+// warps 2-9 drain TMEM: warps w and w + 4 share lane quadrant w % 4 and take one half of the
+// token columns each. The accumulator is double-buffered in TMEM. Every mbarrier wait is
+// bounded: on timeout the kernel records S8B_ERR_TIMEOUT in the status word.
 template <typename T, int NT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_w,
@@ -102,13 +164,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int S = Lay::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  TcSmemHeader *hdr = reinterpret_cast<TcSmemHeader *>(smem + static_cast<size_t>(S) * Lay::kStageBytes);
+  uint8_t *part = smem + static_cast<size_t>(S) * Lay::kStageBytes;
+  TcSmemHeader *hdr = reinterpret_cast<TcSmemHeader *>(part + Lay::kPartBytes);
+  uint8_t *recvb = part + Lay::kStageRows * Lay::kPartPitch;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int C = a.csplit;
+  const uint32_t crank = C > 1 ? cluster_rank() : 0;
+  const int cid = blockIdx.x / C;
+  const int k_lo = static_cast<int>(crank) * a.kc / C, k_hi = (static_cast<int>(crank) + 1) * a.kc / C;
+  const int nk = k_hi - k_lo;
+  const int my_tiles = cid < a.n_tiles ? (a.n_tiles - 1 - cid) / a.nclusters + 1 : 0;
+  const long long n_units = static_cast<long long>(my_tiles) * nk;
+  // split-K row ownership: row r of a tile is reduced by CTA (r * C) / 128
+  const int r0 = (static_cast<int>(crank) * kBM + C - 1) / C;
+  const int r1 = ((static_cast<int>(crank) + 1) * kBM + C - 1) / C;
+  const int slot_rows = (kBM + C - 1) / C;
+  const uint32_t recv_bytes = static_cast<uint32_t>(C * (r1 - r0) * (NT * 4 + 16));
 
-  const long long U = static_cast<long long>(a.n_tiles) * a.kc;
-  const long long u0 = U * blockIdx.x / gridDim.x;
-  const long long u1 = U * (blockIdx.x + 1) / gridDim.x;
-
+  griddep_launch();
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&hdr->full[s], 1);
@@ -116,10 +189,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&hdr->tmem_full[b], 1);
-      mbar_init(&hdr->tmem_empty[b], 128);
+      mbar_init(&hdr->tmem_empty[b], kEpi);
     }
+    mbar_init(&hdr->recv, 1);
+    mbar_init(&hdr->done, C);
     hdr->abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    if (C > 1 && my_tiles > 0)  // the first tile's receive buffer: C slots of this CTA's rows
+      mbar_expect_tx(&hdr->recv, recv_bytes);
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -130,55 +207,79 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (C > 1) {  // peers arrive on this CTA's barriers: all must be initialised first
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+  }
   tc_fence_after();
   const uint32_t tmem = hdr->tmem_base;
   volatile int *abort = &hdr->abort;
 
   if (warp == 0) {
-    // ------------------------------------------------------------- TMA producer ----
+    // ------------------------------------------------------------------ producer ----
     if (lane == 0) {
-      long long issued = 0;
-      for (long long u = u0; u < u1; ++u, ++issued) {
-        const int s = static_cast<int>(issued % S);
-        const uint32_t ph = static_cast<uint32_t>((issued / S) & 1);
+      if (!a.wpacked)
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_w)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_x)) : "memory");
+      auto unit_of = [&](long long i, int *tile, int *kk) {
+        *tile = cid + static_cast<int>(i / nk) * a.nclusters;
+        *kk = k_lo + static_cast<int>(i % nk);
+      };
+      auto load_a = [&](long long i, uint8_t *sa, uint64_t *bar) {
+        int tile, kk;
+        unit_of(i, &tile, &kk);
+        if (a.wpacked)
+          bulk_load(sa, a.wpacked + (static_cast<size_t>(tile) * a.kc + kk) * kABytes, kABytes, bar);
+        else
+          tma_load_2d(sa, &tmap_w, kk * kBK, tile * kBM, bar);
+      };
+      auto load_b = [&](long long i, uint8_t *sa, uint64_t *bar) {
+        int tile, kk;
+        unit_of(i, &tile, &kk);
+        tma_load_2d(sa + kABytes, &tmap_x, kk * kBK, a.m0, bar);
+      };
+      // weights of the first stages before the previous kernel has finished
+      const long long pre = n_units < S ? n_units : S;
+      for (long long i = 0; i < pre; ++i) {
+        uint8_t *sa = smem + static_cast<size_t>(i) * Lay::kStageBytes;
+        mbar_expect_tx(&hdr->full[i], Lay::kStageBytes);
+        load_a(i, sa, &hdr->full[i]);
+      }
+      griddep_wait();
+      for (long long i = 0; i < pre; ++i)
+        load_b(i, smem + static_cast<size_t>(i) * Lay::kStageBytes, &hdr->full[i]);
+      long long issued = pre;
+      for (long long i = pre; i < n_units; ++i, ++issued) {
+        const int s = static_cast<int>(i % S);
+        const uint32_t ph = static_cast<uint32_t>((i / S) & 1);
         if (!mbar_wait(&hdr->empty[s], ph ^ 1, abort, a.status)) break;
         uint8_t *sa = smem + static_cast<size_t>(s) * Lay::kStageBytes;
-        const int tile = static_cast<int>(u / a.kc), kk = static_cast<int>(u % a.kc);
         mbar_expect_tx(&hdr->full[s], Lay::kStageBytes);
-        if (a.wpacked)
-          bulk_load(sa, a.wpacked + static_cast<size_t>(u) * kABytes, kABytes, &hdr->full[s]);
-        else
-          tma_load_2d(sa, &tmap_w, kk * kBK, tile * kBM, &hdr->full[s]);
-        tma_load_2d(sa + kABytes, &tmap_x, kk * kBK, a.m0, &hdr->full[s]);
+        load_a(i, sa, &hdr->full[s]);
+        load_b(i, sa, &hdr->full[s]);
       }
       if (*abort) {
         // let the copies already issued land before the CTA's shared memory goes away
         const long long first = issued > S ? issued - S : 0;
-        for (long long i = first; i < issued; ++i) {
-          const uint64_t t0 = now_ns();
-          while (!mbar_try_wait(&hdr->full[i % S], static_cast<uint32_t>((i / S) & 1)) &&
-                 now_ns() - t0 < 100000000ull) {
-          }
-        }
+        for (long long i = first; i < issued; ++i)
+          mbar_drain(&hdr->full[i % S], static_cast<uint32_t>((i / S) & 1));
       }
     }
   } else if (warp == 1) {
     // -------------------------------------------------------------- MMA issuer ----
     if (lane == 0) {
       constexpr uint32_t idesc = i8_idesc(kBM, NT);
-      long long it = 0;
       int seg = 0;
-      for (long long u = u0; u < u1 && !*abort; ++u, ++it) {
-        const int kk = static_cast<int>(u % a.kc);
-        const bool first = (u == u0) || kk == 0;
-        const bool last = (u == u1 - 1) || kk == a.kc - 1;
+      for (long long i = 0; i < n_units && !*abort; ++i) {
+        const int kk = static_cast<int>(i % nk);
+        const bool first = kk == 0, last = kk == nk - 1;
         const int buf = seg & 1;
         if (first) {
           if (!mbar_wait(&hdr->tmem_empty[buf], ((seg >> 1) & 1) ^ 1, abort, a.status)) break;
           tc_fence_after();
         }
-        const int s = static_cast<int>(it % S);
-        if (!mbar_wait(&hdr->full[s], static_cast<uint32_t>((it / S) & 1), abort, a.status)) break;
+        const int s = static_cast<int>(i % S);
+        if (!mbar_wait(&hdr->full[s], static_cast<uint32_t>((i / S) & 1), abort, a.status)) break;
         tc_fence_after();
         const uint32_t sa = smem_u32(smem + static_cast<size_t>(s) * Lay::kStageBytes);
         const uint64_t ad = sw128_desc(sa), bd = sw128_desc(sa + kABytes);
@@ -195,100 +296,144 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // --------------------------------------------------------------- epilogue ----
     float *xs_s = hdr->xs;
-    const int quad = warp & 3;              // TMEM lane quadrant this warp may access
-    const int row = quad * 32 + lane;       // weight row within the tile
-    const int et = threadIdx.x - 64;        // 0..127
-    for (int t = et; t < NT; t += 128) {
+    const int quad = warp & 3;               // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;        // weight row within the tile
+    const int et = threadIdx.x - 64;         // 0..255
+    constexpr int kHalf = NT >= 32 ? NT / 2 : NT;
+    const int cbeg = (et >> 7) * kHalf;      // this warp's token columns [cbeg, cbeg + kHalf)
+    const bool drains = cbeg < NT;
+    griddep_wait();  // activation scales, and the output buffer, belong to earlier kernels
+    for (int t = et; t < NT; t += kEpi) {
       const int m = a.m0 + t;
       xs_s[t] = (a.out_kind == 0 && m < a.M) ? a.xs[m] : 0.0f;
     }
-    epi_bar_sync();
-    int seg = 0;
-    long long u = u0;
-    while (u < u1) {
-      const int tile = static_cast<int>(u / a.kc);
-      const int kk0 = static_cast<int>(u % a.kc);
-      const long long tile_end = static_cast<long long>(tile + 1) * a.kc;
-      const long long ue = u1 < tile_end ? u1 : tile_end;
-      const int nk = static_cast<int>(ue - u);
-      const bool whole = kk0 == 0 && nk == a.kc;
+    epi_bar_sync(kEpi);
+    for (int seg = 0; seg < my_tiles; ++seg) {
+      const int tile = cid + seg * a.nclusters;
       const int buf = seg & 1;
-      // One thread waits (bounded); the named barrier then releases the other 127 together,
-      // so on a timeout all epilogue threads leave the loop at the same point.
-      if (et == 0) mbar_wait(&hdr->tmem_full[buf], (seg >> 1) & 1, abort, a.status);
-      epi_bar_sync();
+      if (et < kBM) {  // this tile's weight scales, loaded while its K range still streams
+        const int n = tile * kBM + et;
+        hdr->wsc[buf][et] = (n < a.N && a.out_kind == 0) ? a.ws[n] : 0.0f;
+      }
+      // One thread waits (bounded); the named barrier then releases the others together, so
+      // on a timeout all epilogue threads leave the loop at the same point.
+      if (et == 0) {
+        mbar_wait(&hdr->tmem_full[buf], (seg >> 1) & 1, abort, a.status);
+        if (C > 1 && seg >= 1) {
+          // the peers reduced the previous tile (receive buffers free) and this CTA's own
+          // copies out of the staging tile have been read
+          mbar_wait_cluster(&hdr->done, (seg - 1) & 1, abort, a.status);
+          asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        }
+      }
+      epi_bar_sync(kEpi);
       if (*abort) break;
       tc_fence_after();
-      const int n = tile * kBM + row;
-      const float wsn = (n < a.N && a.out_kind == 0) ? a.ws[n] : 0.0f;
+      if (C == 1) {
+        const int n = tile * kBM + row;
+        const float wsn = hdr->wsc[buf][row];
+        if (drains) {
 #pragma unroll 1
-      for (int c0 = 0; c0 < NT; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * NT + c0, v);
-        tmem_wait_ld();
+          for (int c0 = cbeg; c0 < cbeg + kHalf; c0 += 16) {
+            uint32_t v[16];
+            tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * NT + c0, v);
+            tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int t = c0 + j, m = a.m0 + t;
-          if (m >= a.M || n >= a.N) continue;
-          const int32_t accv = static_cast<int32_t>(v[j]);
-          if (whole) {
-            const size_t o = static_cast<size_t>(m) * a.N + n;
-            if (a.out_kind == 1)
-              static_cast<int32_t *>(a.y)[o] = accv;
-            else
-              static_cast<T *>(a.y)[o] =
-                  from_f32<T>(__fmul_rn(__fmul_rn(static_cast<float>(accv), xs_s[t]), wsn));
-          } else {
-            atomicAdd(a.acc + static_cast<size_t>(t) * a.N + n, accv);
+            for (int j = 0; j < 16; ++j) {
+              const int t = c0 + j, m = a.m0 + t;
+              if (m >= a.M || n >= a.N) continue;
+              const int32_t accv = static_cast<int32_t>(v[j]);
+              const size_t o = static_cast<size_t>(m) * a.N + n;
+              if (a.out_kind == 1)
+                static_cast<int32_t *>(a.y)[o] = accv;
+              else
+                static_cast<T *>(a.y)[o] =
+                    from_f32<T>(__fmul_rn(__fmul_rn(static_cast<float>(accv), xs_s[t]), wsn));
+            }
           }
+        }
+        tc_fence_before();
+        mbar_arrive(&hdr->tmem_empty[buf]);
+        continue;
+      }
+      // ---- split-K: TMEM rows -> staging tile; one bulk copy per peer moves the peer's rows
+      // into its receive buffer (completing on its barrier); then reduce the received rows ----
+      if (drains) {
+#pragma unroll 1
+        for (int c0 = cbeg; c0 < cbeg + kHalf; c0 += 16) {
+          uint32_t v[16];
+          tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * NT + c0, v);
+          tmem_wait_ld();
+          int4 *dst = reinterpret_cast<int4 *>(part + row * Lay::kPartPitch + c0 * 4);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            dst[j] = make_int4(static_cast<int>(v[4 * j]), static_cast<int>(v[4 * j + 1]),
+                               static_cast<int>(v[4 * j + 2]), static_cast<int>(v[4 * j + 3]));
         }
       }
       tc_fence_before();
       mbar_arrive(&hdr->tmem_empty[buf]);
-      if (!whole) {
-        __threadfence();
-        epi_bar_sync();
-        if (et == 0) {
-          const int old = atomicAdd(a.counters + tile, nk);
-          hdr->is_last = (old + nk == a.kc);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      epi_bar_sync(kEpi);
+      if (et == 0) {
+        for (int q = 0; q < C; ++q) {
+          const int q0 = (q * kBM + C - 1) / C, q1 = ((q + 1) * kBM + C - 1) / C;
+          const uint32_t dst =
+              mapa(smem_u32(recvb + static_cast<int>(crank) * slot_rows * Lay::kPartPitch), q);
+          asm volatile(
+              "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                  dst),
+              "r"(smem_u32(part + q0 * Lay::kPartPitch)), "r"((q1 - q0) * Lay::kPartPitch),
+              "r"(mapa(smem_u32(&hdr->recv), q))
+              : "memory");
         }
-        epi_bar_sync();
-        if (hdr->is_last) {
-          __threadfence();
-          // 16 independent L2 loads in flight per thread, then the stores (a load/store loop
-          // would serialise one L2 round trip per token on possible aliasing).
-#pragma unroll 1
-          for (int t0 = 0; t0 < NT; t0 += 16) {
-            int32_t vals[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int m = a.m0 + t0 + j;
-              vals[j] = (m < a.M && n < a.N)
-                            ? __ldcg(a.acc + static_cast<size_t>(t0 + j) * a.N + n) : 0;
-            }
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int m = a.m0 + t0 + j;
-              if (m >= a.M || n >= a.N) continue;
-              a.acc[static_cast<size_t>(t0 + j) * a.N + n] = 0;
-              const size_t o = static_cast<size_t>(m) * a.N + n;
-              if (a.out_kind == 1)
-                static_cast<int32_t *>(a.y)[o] = vals[j];
-              else
-                static_cast<T *>(a.y)[o] = from_f32<T>(
-                    __fmul_rn(__fmul_rn(static_cast<float>(vals[j]), xs_s[t0 + j]), wsn));
-            }
-          }
-          if (et == 0) a.counters[tile] = 0;
-        }
-        epi_bar_sync();
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        mbar_wait_cluster(&hdr->recv, seg & 1, abort, a.status);
       }
-      ++seg;
-      u = ue;
+      epi_bar_sync(kEpi);
+      if (*abort) break;
+      const int R = r1 - r0;
+      const uint8_t *pb = recvb;
+      const int items = R * (NT / 4);
+      for (int idx = et; idx < items; idx += kEpi) {
+        const int rl = idx % R, tq = idx / R;
+        int4 acc = *reinterpret_cast<const int4 *>(pb + rl * Lay::kPartPitch + tq * 16);
+        for (int q = 1; q < C; ++q) {
+          const int4 v = *reinterpret_cast<const int4 *>(pb + (q * slot_rows + rl) * Lay::kPartPitch + tq * 16);
+          acc.x += v.x;
+          acc.y += v.y;
+          acc.z += v.z;
+          acc.w += v.w;
+        }
+        const int rr = r0 + rl, n = tile * kBM + rr;
+        if (n >= a.N) continue;
+        const int accs[4] = {acc.x, acc.y, acc.z, acc.w};
+        const float wsn = hdr->wsc[buf][rr];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int t = 4 * tq + j, m = a.m0 + t;
+          if (m >= a.M) continue;
+          const size_t o = static_cast<size_t>(m) * a.N + n;
+          if (a.out_kind == 1)
+            static_cast<int32_t *>(a.y)[o] = accs[j];
+          else
+            static_cast<T *>(a.y)[o] =
+                from_f32<T>(__fmul_rn(__fmul_rn(static_cast<float>(accs[j]), xs_s[t]), wsn));
+        }
+      }
+      epi_bar_sync(kEpi);
+      if (et == 0) {  // re-arm the receive buffer for the next tile, then let the senders in
+        if (seg + 1 < my_tiles) mbar_expect_tx(&hdr->recv, recv_bytes);
+        for (int q = 0; q < C; ++q) mbar_arrive_remote(&hdr->done, q);
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
+  if (C > 1) {  // no CTA leaves while a peer may still read its buffers or arrive on them
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+  }
   tc_fence_after();
   if (warp == 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
@@ -306,22 +451,95 @@ inline int pick_nt(int m) {
   return m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : 256;
 }
 
-size_t ws_layout(int M, int N, size_t *counters_off, size_t *acc_off) {
-  const int nt = pick_nt(M < 256 ? M : 256);
-  const size_t n_tiles = (static_cast<size_t>(N) + kBM - 1) / kBM;
-  *counters_off = 256;
-  *acc_off = (256 + n_tiles * 4 + 255) / 256 * 256;
-  return *acc_off + static_cast<size_t>(nt) * N * 4;
-}
-
+// Clusters of C CTAs that can be resident at once for this kernel (cached per device).
 template <typename T, int NT>
-int launch_tc_nt(const CUtensorMap &mw, const CUtensorMap &mx, const TcArgs &args, cudaStream_t st) {
+int active_clusters(int C) {
+  static std::mutex mu;
+  static std::map<std::pair<int, int>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_pair(dev, C);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
   using Lay = TcLayout<NT>;
   auto kern = gemm_tc_kernel<T, NT>;
   ensure_smem(reinterpret_cast<const void *>(kern), Lay::kSmem);
-  const long long U = static_cast<long long>(args.n_tiles) * args.kc;
-  const int grid = static_cast<int>(U < sm_count() ? U : sm_count());
-  kern<<<grid, kThreads, Lay::kSmem, st>>>(mw, mx, args);
+  int n = 0;
+  if (C == 1) {
+    n = sm_count();
+  } else {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(C * (sm_count() / C), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Lay::kSmem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = C;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+  }
+  cache[key] = n;
+  return n;
+}
+
+// Cluster size for a GEMM of n_tiles 128-row tiles x kc K chunks: the fewest chunk-times per
+// CTA, counting each split tile's cluster reduction as about two chunks.
+template <typename T, int NT>
+int pick_split(int n_tiles, int kc, int *nclusters) {
+  int best_c = 1, best_ncl = active_clusters<T, NT>(1);
+  long best = static_cast<long>((n_tiles + best_ncl - 1) / best_ncl) * kc;
+  if (NT <= 64) {
+    for (int C = 2; C <= 8 && C <= kc; ++C) {
+      const int ncl = active_clusters<T, NT>(C);
+      if (ncl <= 0) continue;
+      const long rounds = (n_tiles + ncl - 1) / ncl;
+      const long cost = rounds * ((kc + C - 1) / C + 2);
+      if (cost < best) {
+        best = cost;
+        best_c = C;
+        best_ncl = ncl;
+      }
+    }
+  }
+  *nclusters = best_ncl < n_tiles ? best_ncl : n_tiles;
+  return best_c;
+}
+
+template <typename T, int NT>
+int launch_tc_nt(const CUtensorMap &mw, const CUtensorMap &mx, TcArgs args, cudaStream_t st) {
+  using Lay = TcLayout<NT>;
+  auto kern = gemm_tc_kernel<T, NT>;
+  ensure_smem(reinterpret_cast<const void *>(kern), Lay::kSmem);
+  int ncl = 0;
+  const int C = pick_split<T, NT>(args.n_tiles, args.kc, &ncl);
+  args.csplit = C;
+  args.nclusters = ncl;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(C * ncl, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Lay::kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = C;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mw, mx, args);
+  if (e != cudaSuccess) {
+    record_cuda_error(e);
+    return S8B_ERR_CUDA;
+  }
   return check_launch();
 }
 
@@ -329,16 +547,11 @@ template <typename T>
 int launch_tc(const int8_t *xq, const float *xs, const int8_t *w, const float *ws, void *y,
               int out_kind, int M, int N, int K, void *workspace, cudaStream_t st,
               bool packed = false) {
-  size_t coff, aoff;
-  ws_layout(M, N, &coff, &aoff);
-  uint8_t *wsb = static_cast<uint8_t *>(workspace);
   TcArgs args;
   args.xs = xs;
   args.ws = ws;
   args.y = y;
-  args.status = reinterpret_cast<int32_t *>(wsb);
-  args.counters = reinterpret_cast<int32_t *>(wsb + coff);
-  args.acc = reinterpret_cast<int32_t *>(wsb + aoff);
+  args.status = static_cast<int32_t *>(workspace);
   args.out_kind = out_kind;
   args.M = M;
   args.N = N;
@@ -378,8 +591,9 @@ int launch_tc(const int8_t *xq, const float *xs, const int8_t *w, const float *w
 using namespace s8b;
 
 extern "C" size_t s8b_gemm_tc_workspace_size(int M, int N) {
-  size_t c, a;
-  return ws_layout(M, N, &c, &a);
+  (void)M;
+  (void)N;
+  return 256;  // the status word (split-K partials are reduced on chip)
 }
 
 extern "C" int s8b_gemm_w8a8_tc(const int8_t *xq, const float *xs, const int8_t *w,

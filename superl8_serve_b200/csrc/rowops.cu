@@ -48,6 +48,7 @@ __global__ void __launch_bounds__(1024)
     rmsnorm_quant_v(const T *__restrict__ h, const T *__restrict__ res_in, T *__restrict__ res_out,
                     const T *__restrict__ w, float eps, int8_t *__restrict__ q,
                     float *__restrict__ s, T *__restrict__ y_out, int H) {
+  griddep_launch();  // the next kernel may start its prologue
   __shared__ double redd[32];
   __shared__ float red[32];
   const int m = blockIdx.x, nvec = H >> 2;
@@ -115,6 +116,7 @@ template <typename T, int VPT>
 __global__ void __launch_bounds__(1024)
     silu_mul_quant_v(const T *__restrict__ gu, int F, T *__restrict__ y_out,
                      int8_t *__restrict__ q, float *__restrict__ s) {
+  griddep_launch();  // the next kernel may start its prologue
   __shared__ float red[32];
   const int m = blockIdx.x, nvec = F >> 2;
   const T *row = gu + static_cast<size_t>(m) * 2 * F;
@@ -158,6 +160,7 @@ __global__ void __launch_bounds__(1024)
 template <typename T, int VPT>
 __global__ void __launch_bounds__(1024)
     quant_rows_v(const T *__restrict__ x, int8_t *__restrict__ q, float *__restrict__ s, int K) {
+  griddep_launch();  // the next kernel may start its prologue
   __shared__ float red[32];
   const int m = blockIdx.x, nvec = K >> 2;
   const size_t off = static_cast<size_t>(m) * K;
