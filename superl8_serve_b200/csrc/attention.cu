@@ -112,6 +112,7 @@ __global__ void __launch_bounds__(512)
                     const int32_t *__restrict__ slot_mapping,
                     const int32_t *__restrict__ block_table, int max_blocks, int bs) {
   griddep_launch();  // the next kernel may start its prologue
+  griddep_wait();    // launched with programmatic serialization
   const int m = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int HR = Hq + 2 * Hkv;
@@ -914,6 +915,7 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  griddep_wait();  // launched with programmatic serialization: the prologue above overlaps
   for (int i = threadIdx.x; i < B; i += kThreads) ctx[i] = context_lens[i];
   tc_fence_before();
   __syncthreads();
@@ -1223,6 +1225,7 @@ __global__ void __launch_bounds__(kMergeThreads)
                            T *__restrict__ out, int8_t *__restrict__ out_q,
                            float *__restrict__ out_s) {
   griddep_launch();  // the next kernel may start its prologue
+  griddep_wait();    // launched with programmatic serialization
   extern __shared__ float msm[];  // [Hq][P] (m, l) pairs, then weights; [Hq] denominators
   __shared__ float red[32];
   const int b = blockIdx.x, tid = threadIdx.x;
@@ -1340,7 +1343,7 @@ int launch_persistent(const int8_t *q_i8, const float *q_s, const int8_t *kc, co
   case GG: {                                                                                   \
     auto kern = attn_persistent_kernel<T, GG>;                                                  \
     ensure_smem(reinterpret_cast<const void *>(kern), pk::kSmem);                               \
-    kern<<<grid, pk::kThreads, pk::kSmem, st>>>(mk, mv, mq, q_s, ks, vs, block_table,           \
+    launch_pdl(kern, grid, pk::kThreads, pk::kSmem, st, mk, mv, mq, q_s, ks, vs, block_table,   \
                                                 context_lens, B, Hq, Hkv, bs_log2, max_blocks,  \
                                                 P, scale, w);                                   \
     break;                                                                                     \
@@ -1359,8 +1362,8 @@ int launch_persistent(const int8_t *q_i8, const float *q_s, const int8_t *kc, co
   }
   auto merge = attn_merge_rows_kernel<T>;
   ensure_smem(reinterpret_cast<const void *>(merge), 96 * 1024);
-  merge<<<B, kMergeThreads, merge_smem, st>>>(w, context_lens, Hq, P, static_cast<T *>(out), out_q,
-                                              out_s);
+  launch_pdl(merge, B, kMergeThreads, merge_smem, st, w, context_lens, Hq, P,
+             static_cast<T *>(out), out_q, out_s);
   return check_launch(2);
 }
 
@@ -1460,7 +1463,7 @@ extern "C" int s8b_qkv_post(const void *qkv, const int32_t *positions, const flo
   if (!aligned(q_i8, 16) || !aligned(kc, 16) || !aligned(vc, 16)) return S8B_ERR_ALIGN;
   if (M == 0) return S8B_OK;
   S8B_DISPATCH_DTYPE(dtype, T,
-                     qkv_post_kernel<T><<<M, 512, 0, (cudaStream_t)stream>>>(
+                     launch_pdl(qkv_post_kernel<T>, M, 512, 0, (cudaStream_t)stream,
                          static_cast<const T *>(qkv), positions, cos_tab, sin_tab,
                          static_cast<const T *>(q_norm_w), static_cast<const T *>(k_norm_w), eps,
                          Hq, Hkv, q_i8, q_s, static_cast<T *>(q_out), kc, ks, vc, vs,

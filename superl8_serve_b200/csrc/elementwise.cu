@@ -24,16 +24,12 @@ __device__ __forceinline__ void better(float &bv, int &bi, float v, int i) {
   }
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kRowThreads) argmax_kernel(const T *__restrict__ logits, int V,
-                                                             int32_t *__restrict__ out) {
-  __shared__ float sv[32];
-  __shared__ int si[32];
-  const int m = blockIdx.x;
-  const T *row = logits + static_cast<size_t>(m) * V;
-  float bv = -__int_as_float(0x7f800000);
-  int bi = 0x7fffffff;
-  for (int k = threadIdx.x; k < V; k += blockDim.x) better(bv, bi, to_f32(row[k]), k);
+// One CTA per row. (value, index) pairs are ordered by value, then lowest index, so the
+// result does not depend on the traversal order: each thread scans 8-value vectors (16-byte
+// loads, four in flight), then warp and CTA reductions merge the candidates.
+constexpr int kArgmaxThreads = 1024;
+
+__device__ __forceinline__ void reduce_best(float &bv, int &bi, float *sv, int *si) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -56,8 +52,41 @@ __global__ void __launch_bounds__(kRowThreads) argmax_kernel(const T *__restrict
       const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
       better(bv, bi, ov, oi);
     }
-    if (lane == 0) out[m] = bi;
   }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const T *__restrict__ logits, int V,
+                                                                int32_t *__restrict__ out) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  griddep_wait();  // launched with programmatic serialization
+  const int m = blockIdx.x;
+  const T *row = logits + static_cast<size_t>(m) * V;
+  float bv = -__int_as_float(0x7f800000);
+  int bi = 0x7fffffff;
+  const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
+  const int nvec = vec ? V / 8 : 0;
+  const uint4 *rv = reinterpret_cast<const uint4 *>(row);
+  for (int base = threadIdx.x; base < nvec; base += 4 * kArgmaxThreads) {
+    uint4 x[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = base + j * kArgmaxThreads;
+      if (i < nvec) x[j] = rv[i];
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = base + j * kArgmaxThreads;
+      if (i >= nvec) continue;
+      const T *e = reinterpret_cast<const T *>(&x[j]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) better(bv, bi, to_f32(e[k]), 8 * i + k);
+    }
+  }
+  for (int k = 8 * nvec + threadIdx.x; k < V; k += kArgmaxThreads) better(bv, bi, to_f32(row[k]), k);
+  reduce_best(bv, bi, sv, si);
+  if (threadIdx.x == 0) out[m] = bi;
 }
 
 }  // namespace
@@ -83,7 +112,7 @@ extern "C" int s8b_argmax(const void *logits, int M, int V, int32_t *out, int dt
   if (M < 0 || V <= 0) return S8B_ERR_SHAPE;
   if (M == 0) return S8B_OK;
   S8B_DISPATCH_DTYPE(dtype, T,
-                     argmax_kernel<T><<<M, kRowThreads, 0, (cudaStream_t)stream>>>(
+                     launch_pdl(argmax_kernel<T>, M, kArgmaxThreads, 0, (cudaStream_t)stream,
                          static_cast<const T *>(logits), V, out));
   return check_launch();
 }

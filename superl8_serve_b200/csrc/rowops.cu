@@ -49,6 +49,7 @@ __global__ void __launch_bounds__(1024)
                     const T *__restrict__ w, float eps, int8_t *__restrict__ q,
                     float *__restrict__ s, T *__restrict__ y_out, int H) {
   griddep_launch();  // the next kernel may start its prologue
+  griddep_wait();    // launched with programmatic serialization
   __shared__ double redd[32];
   __shared__ float red[32];
   const int m = blockIdx.x, nvec = H >> 2;
@@ -117,6 +118,7 @@ __global__ void __launch_bounds__(1024)
     silu_mul_quant_v(const T *__restrict__ gu, int F, T *__restrict__ y_out,
                      int8_t *__restrict__ q, float *__restrict__ s) {
   griddep_launch();  // the next kernel may start its prologue
+  griddep_wait();    // launched with programmatic serialization
   __shared__ float red[32];
   const int m = blockIdx.x, nvec = F >> 2;
   const T *row = gu + static_cast<size_t>(m) * 2 * F;
@@ -161,6 +163,7 @@ template <typename T, int VPT>
 __global__ void __launch_bounds__(1024)
     quant_rows_v(const T *__restrict__ x, int8_t *__restrict__ q, float *__restrict__ s, int K) {
   griddep_launch();  // the next kernel may start its prologue
+  griddep_wait();    // launched with programmatic serialization
   __shared__ float red[32];
   const int m = blockIdx.x, nvec = K >> 2;
   const size_t off = static_cast<size_t>(m) * K;
@@ -225,8 +228,8 @@ extern "C" int s8b_quant_rows(const void *x, int dtype, int8_t *q, float *s, int
   row_shape(K / 4, &th, &vpt);
   S8B_DISPATCH_DTYPE(dtype, T,
                      S8B_VPT_SWITCH(vpt, V,
-                                    quant_rows_v<T, V><<<M, th, 0, (cudaStream_t)stream>>>(
-                                        static_cast<const T *>(x), q, s, K)));
+                                    launch_pdl(quant_rows_v<T, V>, M, th, 0, (cudaStream_t)stream,
+                                               static_cast<const T *>(x), q, s, K)));
   return check_launch();
 }
 
@@ -243,11 +246,12 @@ extern "C" int s8b_rmsnorm_quant(const void *h, const void *residual_in, void *r
   row_shape(H / 4, &th, &vpt);
   S8B_DISPATCH_DTYPE(dtype, T,
                      S8B_VPT_SWITCH(vpt, V,
-                                    rmsnorm_quant_v<T, V><<<M, th, 0, (cudaStream_t)stream>>>(
-                                        static_cast<const T *>(h),
-                                        static_cast<const T *>(residual_in),
-                                        static_cast<T *>(residual_out), static_cast<const T *>(w),
-                                        eps, q, s, static_cast<T *>(y_out), H)));
+                                    launch_pdl(rmsnorm_quant_v<T, V>, M, th, 0, (cudaStream_t)stream,
+                                               static_cast<const T *>(h),
+                                               static_cast<const T *>(residual_in),
+                                               static_cast<T *>(residual_out),
+                                               static_cast<const T *>(w), eps, q, s,
+                                               static_cast<T *>(y_out), H)));
   return check_launch();
 }
 
@@ -261,8 +265,8 @@ extern "C" int s8b_silu_mul_quant(const void *gu, int M, int F, void *y_out, int
   row_shape(F / 4, &th, &vpt);
   S8B_DISPATCH_DTYPE(dtype, T,
                      S8B_VPT_SWITCH(vpt, V,
-                                    silu_mul_quant_v<T, V><<<M, th, 0, (cudaStream_t)stream>>>(
-                                        static_cast<const T *>(gu), F, static_cast<T *>(y_out), q,
-                                        s)));
+                                    launch_pdl(silu_mul_quant_v<T, V>, M, th, 0, (cudaStream_t)stream,
+                                               static_cast<const T *>(gu), F,
+                                               static_cast<T *>(y_out), q, s)));
   return check_launch();
 }
