@@ -1214,11 +1214,15 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
                  "r"(kTmemCols) : "memory");
 }
 
-// Merge of the persistent kernel's partials, one CTA per row: per head M = max m_p,
-// w_p = exp(m_p - M), L = sum w_p l_p, O = sum w_p o_p (partition order), out = dtype(O / L);
-// then the row's int8 quantization for o_proj. Same arithmetic as merge_epilogue.
-constexpr int kMergeThreads = 1024;
-constexpr int kMergeVpt = 8;  // Hq * 128 <= 8192 values per row held in registers
+// Merge of the persistent kernel's partials. A row is handled by a cluster of kMergeSplit CTAs,
+// CTA c taking heads [c*hpc, (c+1)*hpc): per head M = max m_p, w_p = exp(m_p - M),
+// L = sum w_p l_p, O = sum w_p o_p (partition order), out = dtype(O / L), one output value
+// per thread with all its partial loads in flight. The row's int8 quantization for o_proj
+// takes the row maximum over the cluster through distributed shared memory. Same
+// arithmetic as merge_epilogue.
+constexpr int kMergeThreads = 512;
+constexpr int kMergeSplit = 4;
+constexpr int kMergeVpt = 4;  // hpc * 128 <= 2048 values per CTA (Hq <= 64)
 template <typename T>
 __global__ void __launch_bounds__(kMergeThreads)
     attn_merge_rows_kernel(DecodeWs ws, const int32_t *__restrict__ context_lens, int Hq, int P,
@@ -1226,15 +1230,18 @@ __global__ void __launch_bounds__(kMergeThreads)
                            float *__restrict__ out_s) {
   griddep_launch();  // the next kernel may start its prologue
   griddep_wait();    // launched with programmatic serialization
-  extern __shared__ float msm[];  // [Hq][P] (m, l) pairs, then weights; [Hq] denominators
+  extern __shared__ float msm[];  // [hpc][P] (m, l) pairs, then weights; [hpc] denominators
   __shared__ float red[32];
-  const int b = blockIdx.x, tid = threadIdx.x;
+  __shared__ float cl_amax;
+  const int b = blockIdx.x / kMergeSplit, c = blockIdx.x % kMergeSplit, tid = threadIdx.x;
+  const int hpc = (Hq + kMergeSplit - 1) / kMergeSplit;
+  const int h0 = c * hpc, h1 = min(Hq, h0 + hpc), nh = max(0, h1 - h0);
   const int np = (context_lens[b] + kPart - 1) / kPart;
-  float *Wp = msm, *Lh = msm + 2 * Hq * P;
-  const float *mlb = ws.part_ml + static_cast<size_t>(b) * Hq * P * 2;
-  for (int i = tid; i < Hq * P * 2; i += kMergeThreads) msm[i] = mlb[i];  // all loads in flight
+  float *Wp = msm, *Lh = msm + 2 * hpc * P;
+  const float *mlb = ws.part_ml + (static_cast<size_t>(b) * Hq + h0) * P * 2;
+  for (int i = tid; i < nh * P * 2; i += kMergeThreads) msm[i] = mlb[i];  // all loads in flight
   __syncthreads();
-  for (int h = tid; h < Hq; h += kMergeThreads) {
+  for (int h = tid; h < nh; h += kMergeThreads) {
     const float *ml = msm + h * P * 2;
     float M = -__int_as_float(0x7f800000);
     for (int q = 0; q < np; ++q) M = fmaxf(M, ml[2 * q]);
@@ -1247,8 +1254,8 @@ __global__ void __launch_bounds__(kMergeThreads)
     Lh[h] = Ls;
   }
   __syncthreads();
-  const int nv = Hq * kHd;
-  T *orow = out + static_cast<size_t>(b) * nv;
+  const int nv = nh * kHd;
+  T *orow = out + static_cast<size_t>(b) * Hq * kHd + h0 * kHd;
   float v[kMergeVpt];
   float amax = 0.0f;
 #pragma unroll
@@ -1257,7 +1264,7 @@ __global__ void __launch_bounds__(kMergeThreads)
     v[j] = 0.0f;
     if (i < nv) {
       const int h = i / kHd, d = i % kHd;
-      const float *po = ws.part_o + (static_cast<size_t>(b) * Hq + h) * P * kHd + d;
+      const float *po = ws.part_o + ((static_cast<size_t>(b) * Hq + h0 + h) * P) * kHd + d;
       float O = 0.0f;
       for (int q0 = 0; q0 < np; q0 += 8) {  // 8 loads in flight, then the ordered sum
         float x[8];
@@ -1274,13 +1281,28 @@ __global__ void __launch_bounds__(kMergeThreads)
   }
   if (!out_q) return;
   amax = block_max(amax, red);
-  const QParams qp = qparams(amax, 127.0f);
+  if (tid == 0) cl_amax = amax;
+  // row maximum over the cluster (the barriers order the DSMEM reads against every CTA's
+  // write and against any CTA leaving)
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  float rmax = 0.0f;
+#pragma unroll
+  for (int q = 0; q < kMergeSplit; ++q) {
+    uint32_t ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(&cl_amax))), "r"(q));
+    float x;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(ra) : "memory");
+    rmax = fmaxf(rmax, x);
+  }
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  const QParams qp = qparams(rmax, 127.0f);
+  int8_t *qrow = out_q + static_cast<size_t>(b) * Hq * kHd + h0 * kHd;
 #pragma unroll
   for (int j = 0; j < kMergeVpt; ++j) {
     const int i = tid + j * kMergeThreads;
-    if (i < nv) out_q[static_cast<size_t>(b) * nv + i] = static_cast<int8_t>(qcode(v[j], qp.inv, 127));
+    if (i < nv) qrow[i] = static_cast<int8_t>(qcode(v[j], qp.inv, 127));
   }
-  if (tid == 0) out_s[b] = qp.scale;
+  if (c == 0 && tid == 0) out_s[b] = qp.scale;
 }
 
 inline int num_parts(int max_ctx) { return (max_ctx + kPart - 1) / kPart; }
@@ -1312,8 +1334,8 @@ DecodeWs carve_ws(void *base, int B, int Hq, int max_ctx) {
 
 // The persistent kernel + row merge, when the shape allows it: blocks of >= 8 tokens (each
 // TMA box then starts on a 1024-byte swizzle atom), 16-byte aligned scale arrays (16-byte
-// cp.async), B <= 1024 rows, Hq * 128 <= 8192 and the merge weights within 96 KB of shared
-// memory, and K/V buffers whose allocation extent the driver reports (the tensor maps cover
+// cp.async), B <= 1024 rows, Hq <= 64 and the merge weights within 96 KB of shared memory,
+// and K/V buffers whose allocation extent the driver reports (the tensor maps cover
 // exactly that). Returns 1 when not applicable.
 template <typename T>
 int launch_persistent(const int8_t *q_i8, const float *q_s, const int8_t *kc, const float *ks,
@@ -1322,8 +1344,9 @@ int launch_persistent(const int8_t *q_i8, const float *q_s, const int8_t *kc, co
                       int Hq, int Hkv, int bs, int bs_log2, int max_blocks, int P, float scale,
                       const DecodeWs &w, cudaStream_t st) {
   const int G = Hq / Hkv;
-  const size_t merge_smem = 4 * (2 * static_cast<size_t>(Hq) * P + Hq);
-  if (bs < 8 || B > pk::kMaxRows || Hq * kHd > kMergeThreads * kMergeVpt || merge_smem > 96 * 1024 ||
+  const int hpc = (Hq + kMergeSplit - 1) / kMergeSplit;
+  const size_t merge_smem = 4 * (2 * static_cast<size_t>(hpc) * P + hpc);
+  if (bs < 8 || B > pk::kMaxRows || hpc * kHd > kMergeThreads * kMergeVpt || merge_smem > 96 * 1024 ||
       !aligned(ks, 16) || !aligned(vs, 16) || !aligned(q_i8, 16))
     return 1;
   const size_t kb = tc::bytes_to_alloc_end(kc), vb = tc::bytes_to_alloc_end(vc);
@@ -1362,8 +1385,8 @@ int launch_persistent(const int8_t *q_i8, const float *q_s, const int8_t *kc, co
   }
   auto merge = attn_merge_rows_kernel<T>;
   ensure_smem(reinterpret_cast<const void *>(merge), 96 * 1024);
-  launch_pdl(merge, B, kMergeThreads, merge_smem, st, w, context_lens, Hq, P,
-             static_cast<T *>(out), out_q, out_s);
+  launch_pdl_cluster(merge, B * kMergeSplit, kMergeThreads, merge_smem, kMergeSplit, st, w,
+                     context_lens, Hq, P, static_cast<T *>(out), out_q, out_s);
   return check_launch(2);
 }
 
