@@ -196,6 +196,18 @@ def time_kernel(fn, reps: int) -> float:
     return a.elapsed_time(b) / reps
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum per launch from one ncu capture of the same
+# launch shape (profiles/attn_persistent_qwen3_8b_b64_ctx2048.md,
+# profiles/gemm_tc_gate_up_qwen3_8b_m64.md); re-captured whenever the kernel changes.
+NCU_TRAFFIC = {
+    "paged_decode_attention": {"bytes": 279352576 + 9795328,
+                               "source": "ncu dram bytes of attn_persistent_kernel (the row "
+                                         "merge reads its 8.4 MB of partials from L2)"},
+    "gemm_w8a8_tc_gate_up": {"bytes": 101067520 + 5717504,
+                             "source": "ncu dram bytes of gemm_tc_kernel (gate_up launch)"},
+}
+
+
 def kernel_rooflines(pipe, hbm_peak):
     """Live CUDA-event timing of the two HBM-heavy kernels on the bench's own buffers,
     rotating through all layers so every launch streams its operands from HBM."""
@@ -337,8 +349,9 @@ def run_single(args):
                 "d2h_bytes_per_step": 4 * B},
         "roofline": {"bound": "hbm", "kernel": top_name, "achieved": top["gbs"], "peak": hbm,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": top["frac"],
-                     "traffic": None, "bytes_per_launch": top["bytes"],
-                     "ms_per_launch": top["ms"]},
+                     "traffic": NCU_TRAFFIC.get(top_name, {}).get("bytes"),
+                     "traffic_source": NCU_TRAFFIC.get(top_name, {}).get("source"),
+                     "bytes_per_launch": top["bytes"], "ms_per_launch": top["ms"]},
         "kernels": kr,
         "step_roofline": {"bytes": sb, "achieved_gbs": sb / ms / 1e6, "frac": sb / ms / 1e6 / hbm},
     }
