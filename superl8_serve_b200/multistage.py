@@ -145,21 +145,31 @@ class RankPipeline:
     """Stage ``rank`` of an S-stage pipeline on the current CUDA device."""
 
     def __init__(self, cfg, rank: int, world: int, *, m: int, max_len: int, ctx: int,
-                 scheme: str = "int8-had", seed: int = 0, pg=None):
+                 scheme: str = "int8-had", seed: int = 0, pg=None, state_dict=None,
+                 fill_kv: bool = True):
+        """``state_dict`` (HF-style float weights) selects real weights for this rank's layer
+        range; without it the weights are synthetic (benchmarks). ``fill_kv`` pre-fills the
+        KV pool with random codes for a synthetic context of ``ctx`` tokens; with
+        ``fill_kv=False`` and ``ctx=0`` every sequence starts empty."""
         self.cfg, self.rank, self.world = cfg, rank, world
         self.dev = torch.device("cuda", torch.cuda.current_device())
         self.plan = plan_rank(cfg.num_hidden_layers, cfg.hidden_size, rank, world, m, scheme)
         self.scheme = scheme
         S, H = world, cfg.hidden_size
         lo, hi = self.plan.layers
-        self.model = StageModel.synthetic(cfg, lo, hi, self.dev, first=self.plan.first,
-                                          last=self.plan.last, seed=seed)
+        if state_dict is not None:
+            self.model = StageModel.from_state_dict(cfg, state_dict, lo, hi, self.dev,
+                                                    first=self.plan.first, last=self.plan.last)
+        else:
+            self.model = StageModel.synthetic(cfg, lo, hi, self.dev, first=self.plan.first,
+                                              last=self.plan.last, seed=seed)
         self.m = m
         self.max_blocks = (max_len + 15) // 16
         nb = m * S * self.max_blocks
         self.pool = KVPool(hi - lo, nb, cfg.num_key_value_heads, cfg.resolved_head_dim(), 16,
                            self.dev)
-        self.pool.fill_random(seed=seed * 7 + rank)
+        if fill_kv:
+            self.pool.fill_random(seed=seed * 7 + rank)
         self.runner = StageRunner(self.model, self.pool, m, max_len)
         # device-side per micro-batch state: sequence j = k*m + i owns blocks
         # [j*max_blocks, (j+1)*max_blocks) (identical layout on every stage)
