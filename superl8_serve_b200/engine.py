@@ -119,7 +119,7 @@ class DecodePipeline:
         self.streams = [torch.cuda.Stream(device=mdl.device) for mdl in models]
         self.events = [[torch.cuda.Event() for _ in range(n_micro)] for _ in models]
         self.slots: list[int] = []
-        self.graph = None
+        self.graph = self.graph_io = None
         self.rows = [min(self.m, batch - k * self.m) for k in range(n_micro)]
 
     # ----------------------------------------------------------------- sequence state ----
@@ -160,10 +160,24 @@ class DecodePipeline:
         return self.runners[-1].logits[: self.rows[k]]
 
     # ----------------------------------------------------------------------- stepping ----
-    def _enqueue(self):
-        """Enqueue one decode step (all micro-batches, all stages) and advance positions."""
+    def _enqueue(self, host_io: torch.Tensor | None = None):
+        """Enqueue one decode step (all micro-batches, all stages) and advance positions.
+
+        ``host_io`` (pinned int32, one slot per row) routes every micro-batch's input ids
+        through host memory on the way into stage 0: the ids left by the previous step are
+        copied device -> host into ``host_io`` and back host -> device, stream-ordered, so the
+        host holds each step's tokens without draining the pipeline."""
         for k in range(self.n_micro):
             r = self.rows[k]
+            if host_io is not None:
+                with torch.cuda.device(self.models[0].device):
+                    st0 = (torch.cuda.current_stream(self.models[0].device) if self.single_device
+                           else self.streams[0])
+                    with torch.cuda.stream(st0):
+                        dst = host_io.data_ptr() + 4 * k * self.m
+                        ids = self.mbs[0][k].ids
+                        call("s8b_memcpy_async", dst, ptr(ids), 4 * r, stream())
+                        call("s8b_memcpy_async", ptr(ids), dst, 4 * r, stream())
             for s in range(self.S):
                 dev = self.models[s].device
                 st = torch.cuda.current_stream(dev) if self.single_device else self.streams[s]
@@ -196,8 +210,14 @@ class DecodePipeline:
         else:
             self._enqueue()
 
-    def capture(self):
-        """Capture one whole step into a CUDA graph (single-device pipelines)."""
+    def step_host_io(self):
+        """One step of the host-I/O graph (see capture(host_io=...))."""
+        self.graph_io.replay()
+
+    def capture(self, host_io: torch.Tensor | None = None):
+        """Capture one whole step into a CUDA graph (single-device pipelines); with
+        ``host_io`` the graph carries the per-micro-batch host round trip of the input ids
+        and is replayed by step_host_io()."""
         if not self.single_device:
             raise RuntimeError("graph capture of a multi-device in-process pipeline is not used")
         dev = self.models[0].device
@@ -206,9 +226,12 @@ class DecodePipeline:
         g = torch.cuda.CUDAGraph()
         with torch.cuda.device(dev), torch.cuda.stream(s):
             with torch.cuda.graph(g, stream=s):
-                self._enqueue()
+                self._enqueue(host_io)
         torch.cuda.current_stream(dev).wait_stream(s)
-        self.graph = g
+        if host_io is None:
+            self.graph = g
+        else:
+            self.graph_io = g
         return g
 
     def synchronize(self):

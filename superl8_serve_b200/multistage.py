@@ -209,7 +209,7 @@ class RankPipeline:
                 self.mbs[k].ids = DevPtr(self.tok_ptr + k * tok_stride, m)
             elif self.plan.last:
                 self.mbs[k].ids = DevPtr(self.first_tok + k * tok_stride, m)
-        self.graph = None
+        self.graph = self.graph_io = None
 
     # flags: [ready[S] | tok_ready[S]] uint32 in each rank's flag block
     def _ready_flag(self, base: int, k: int) -> DevPtr:
@@ -246,13 +246,22 @@ class RankPipeline:
             call("s8b_memcpy_async", out_host.data_ptr() + 4 * k * self.m,
                  self.tok_ptr + k * self.tok_stride, 4 * self.m, st)
 
-    def enqueue_step(self, *, token_return: bool = True):
+    def enqueue_step(self, *, token_return: bool = True, host_io: torch.Tensor | None = None):
+        """Enqueue this rank's share of one step. On stage 0, ``host_io`` (pinned int32, m*S)
+        routes every micro-batch's input ids through host memory once they have arrived: the
+        token slot is copied device -> host into ``host_io`` and back, stream-ordered, so the
+        host holds each step's tokens without draining the pipeline."""
         S, st = self.world, stream()
         for k in range(S):
             mb = self.mbs[k]
             if self.plan.first and S > 1 and token_return:
                 call("s8b_flag_wait", self._tok_flag(self.flag_ptr, k).addr, ptr(self.epoch), 0,
                      FLAG_TIMEOUT_NS, ptr(self.status), st)
+            if self.plan.first and host_io is not None:
+                slot = self.tok_ptr + k * self.tok_stride
+                dst = host_io.data_ptr() + 4 * k * self.m
+                call("s8b_memcpy_async", dst, slot, 4 * self.m, st)
+                call("s8b_memcpy_async", slot, dst, 4 * self.m, st)
             bin_ = bout = None
             if not self.plan.first:
                 call("s8b_flag_wait", self._ready_flag(self.flag_ptr, k).addr, ptr(self.epoch), 1,
@@ -268,18 +277,34 @@ class RankPipeline:
             call("s8b_advance", ptr(mb.positions), ptr(mb.context_lens), self.m, 1, st)
         call("s8b_counter_add", ptr(self.epoch), 1, st)
 
-    def capture(self):
+    def capture(self, host_io: torch.Tensor | None = None):
+        """Capture one step into a CUDA graph; with ``host_io`` (stage 0's pinned token
+        buffer; other ranks pass None) the graph is replayed by step_host_io()."""
         s = torch.cuda.Stream(device=self.dev)
         s.wait_stream(torch.cuda.current_stream(self.dev))
         g = torch.cuda.CUDAGraph()
         with torch.cuda.stream(s):
             with torch.cuda.graph(g, stream=s):
-                self.enqueue_step()
+                self.enqueue_step(host_io=host_io)
         torch.cuda.current_stream(self.dev).wait_stream(s)
-        self.graph = g
+        if host_io is None and not getattr(self, "_capturing_io", False):
+            self.graph = g
+        else:
+            self.graph_io = g
+
+    def capture_host_io(self, host_io: torch.Tensor | None):
+        """The host-I/O variant of the step graph on every rank (stage 0 gets the copies)."""
+        self._capturing_io = True
+        try:
+            self.capture(host_io if self.plan.first else None)
+        finally:
+            self._capturing_io = False
 
     def step(self):
         self.graph.replay()
+
+    def step_host_io(self):
+        self.graph_io.replay()
 
     def check_status(self):
         st = self.status.cpu().tolist()
@@ -291,7 +316,7 @@ class RankPipeline:
         import torch.distributed as dist
 
         torch.cuda.synchronize(self.dev)
-        self.graph = None
+        self.graph = self.graph_io = None
         for p in self.opened:
             call("s8b_ipc_close", p)
         dist.barrier(group=pg)
@@ -320,7 +345,7 @@ def run_bench_multi(args, metric, step_bytes, peaks, ClockSampler, cpu_sample):
     if args.layers:
         cfg = cfg.with_(num_hidden_layers=args.layers)
     m, ctx = args.batch, args.ctx
-    total_steps = 1 + args.warmup + args.steps + args.steps + 8
+    total_steps = 1 + 2 * args.warmup + 3 * args.steps + 8  # graph, host-I/O and host-wait loops
     pipe = RankPipeline(cfg, rank, world, m=m, max_len=ctx + total_steps + 16, ctx=ctx,
                         scheme=args.scheme, seed=1)
     rng = np.random.default_rng(3)
@@ -353,12 +378,32 @@ def run_bench_multi(args, metric, step_bytes, peaks, ClockSampler, cpu_sample):
     torch.cuda.synchronize()
     pipe.check_status()
     dist.barrier()
-    # e2e through the host API: every rank synchronises its stream after each step; stage 0
-    # copies the step's ids in from pinned host memory and, once the last stage's tokens have
-    # landed in its slots (device-side flag wait), copies them back out
+    # e2e through the host API. Stage 0 routes every micro-batch's input ids through pinned
+    # host memory inside its step graph (stream-ordered D2H of the delivered tokens, H2D of
+    # the ids), so the host holds every step's tokens while the pipeline stays full.
+    if pipe.plan.first:
+        pipe.put_ids(ids_h)
     torch.cuda.synchronize()
     dist.barrier()
+    pipe.capture_host_io(ids_h)
+    for _ in range(args.warmup):
+        pipe.step_host_io()
+    torch.cuda.synchronize()
+    pipe.check_status()
+    dist.barrier()
     ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ea.record()
+    for _ in range(args.steps):
+        pipe.step_host_io()
+    eb.record()
+    eb.synchronize()
+    e2e_ms = ea.elapsed_time(eb) / args.steps
+    pipe.check_status()
+    dist.barrier()
+    # the same with every rank waiting on the host for each step: stage 0 copies the step's
+    # ids in and, once the last stage's tokens landed (device-side flag wait), copies them out
+    torch.cuda.synchronize()
+    dist.barrier()
     ea.record()
     for _ in range(args.steps):
         if pipe.plan.first:
@@ -371,11 +416,11 @@ def run_bench_multi(args, metric, step_bytes, peaks, ClockSampler, cpu_sample):
             ids_h.copy_(out_h)
     eb.record()
     eb.synchronize()
-    e2e_ms = ea.elapsed_time(eb) / args.steps
+    e2e_sync_ms = ea.elapsed_time(eb) / args.steps
     pipe.check_status()
-    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=pipe.dev)
+    t = torch.tensor([ms, e2e_ms, e2e_sync_ms], dtype=torch.float64, device=pipe.dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, e2e_ms = t.tolist()
+    ms, e2e_ms, e2e_sync_ms = t.tolist()
     clocks = clk.summary()
     hbm, _, peak_kind = peaks()
     lo, hi = pipe.plan.layers
@@ -398,7 +443,10 @@ def run_bench_multi(args, metric, step_bytes, peaks, ClockSampler, cpu_sample):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
             "e2e": {"value": B / (e2e_ms / 1e3), "unit": "tokens/s",
-                    "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B},
+                    "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B,
+                    "mode": "ids round-trip through pinned host memory per micro-batch inside "
+                            "each step on stage 0 (stream-ordered, no per-step host wait)",
+                    "host_wait_per_step_value": B / (e2e_sync_ms / 1e3)},
             "step_roofline": {"bytes_rank0": sb, "achieved_gbs_rank0": sb / ms / 1e6,
                               "frac_rank0": sb / ms / 1e6 / hbm, "peak": hbm,
                               "peak_kind": peak_kind},
