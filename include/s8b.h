@@ -74,6 +74,14 @@ int s8b_quant_rows(const void *x, int dtype, int8_t *q, float *s, int M, int K, 
 int s8b_rmsnorm_quant(const void *h, const void *residual_in, void *residual_out,
                       const void *w, float eps, int8_t *q, float *s, void *y_out, int M, int H,
                       int dtype, void *stream);
+/* The same with h given as the split-K partials of a tensor-core GEMM (part int32 [C][M][H],
+ * out_kind 2, with that GEMM's activation scales xs [M] and weight scales ws [H]):
+ * h = dtype((f32(sum_c part[c]) * xs[m]) * ws[n]), exactly the GEMM's bf16 output. part
+ * and ws 16-byte aligned, 1 <= C <= 8. No counterpart in the reference. */
+int s8b_rmsnorm_quant_split(const int32_t *part, int C, const float *xs, const float *ws,
+                            const void *residual_in, void *residual_out, const void *w,
+                            float eps, int8_t *q, float *s, void *y_out, int M, int H, int dtype,
+                            void *stream);
 
 /* W8A8 GEMM on CUDA cores (dp4a), for small token counts:
  *   acc[m,n] = sum_k xq[m,k]*w[n,k] (int32);  y[m,n] = dtype((float(acc)*xs[m])*ws[n]).
@@ -84,7 +92,8 @@ int s8b_gemm_w8a8(const int8_t *xq, const float *xs, const int8_t *w, const floa
                   int out_kind, int M, int N, int K, int dtype, void *stream);
 
 /* W8A8 GEMM on the tensor cores (tcgen05.mma kind::i8, TMA-fed, TMEM accumulators), same
- * arithmetic and outputs as s8b_gemm_w8a8, for token counts where the contraction is dense
+ * arithmetic and outputs as s8b_gemm_w8a8 (out_kind 0 and 1; out_kind 2: split-K partials,
+ * see s8b_gemm_tc_split_count), for token counts where the contraction is dense
  * (M >= 16; M > 256 runs in 256-token passes). K % 128 == 0. Split-K partial sums are
  * reduced inside thread-block clusters (distributed shared memory), so the workspace
  * (s8b_gemm_tc_workspace_size bytes, 256-byte aligned, zero-filled once by the caller) only
@@ -94,6 +103,12 @@ int s8b_gemm_w8a8(const int8_t *xq, const float *xs, const int8_t *w, const floa
  * activations, scales and outputs are touched only after that kernel has completed).
  * Replaces superl8.linear / gemm_w8a8 (superl8serve/layers/linear.py:122).               */
 size_t s8b_gemm_tc_workspace_size(int M, int N);
+/* out_kind 2 of the tensor-core GEMM: no dequantization and no reduction of the split-K
+ * partial sums; y is int32 [C][M][N] with C = s8b_gemm_tc_split_count(M, N, K), and
+ * sum_c y[c][m][n] is the int32 accumulator. The row kernels below with a _split suffix read
+ * that layout directly (they sum, dequantize y = dtype((f32(acc) * xs[m]) * ws[n]) and go
+ * on), so the reduction costs no extra launch. No counterpart in the reference. */
+int s8b_gemm_tc_split_count(int M, int N, int K);
 int s8b_gemm_w8a8_tc(const int8_t *xq, const float *xs, const int8_t *w, const float *ws,
                      void *y, int out_kind, int M, int N, int K, int dtype, void *workspace,
                      size_t workspace_bytes, void *stream);
@@ -114,6 +129,11 @@ int s8b_gemm_w8a8_tc_packed(const int8_t *xq, const float *xs, const int8_t *wpa
  * the activation quant of the down projection.                                            */
 int s8b_silu_mul_quant(const void *gu, int M, int F, void *y_out, int8_t *q, float *s,
                        int dtype, void *stream);
+/* The same with gu given as GEMM split-K partials (int32 [C][M][2F], xs [M], ws [2F]; see
+ * s8b_rmsnorm_quant_split). No counterpart in the reference. */
+int s8b_silu_mul_quant_split(const int32_t *part, int C, const float *xs, const float *ws,
+                             int M, int F, void *y_out, int8_t *q, float *s, int dtype,
+                             void *stream);
 
 /* Decode-branch head processing for a merged qkv row [M, (Hq+2*Hkv)*D]:
  * per-head RMSNorm of q and k (q_norm_w, k_norm_w [D]), RoPE at positions[m] with binary32
@@ -131,6 +151,15 @@ int s8b_qkv_post(const void *qkv, const int32_t *positions, const float *cos_tab
                  void *q_out, int8_t *kc, float *ks, int8_t *vc, float *vs,
                  const int32_t *slot_mapping, const int32_t *block_table, int max_blocks,
                  int block_size, int dtype, void *stream);
+/* The same with qkv given as GEMM split-K partials (int32 [C][M][(Hq+2*Hkv)*D], xs [M],
+ * ws [(Hq+2*Hkv)*D]; see s8b_rmsnorm_quant_split). No counterpart in the reference. */
+int s8b_qkv_post_split(const int32_t *part, int C, const float *xs, const float *ws,
+                       const int32_t *positions, const float *cos_tab, const float *sin_tab,
+                       int max_pos, const void *q_norm_w, const void *k_norm_w, float eps, int M,
+                       int Hq, int Hkv, int D, int8_t *q_i8, float *q_s, void *q_out,
+                       int8_t *kc, float *ks, int8_t *vc, float *vs,
+                       const int32_t *slot_mapping, const int32_t *block_table, int max_blocks,
+                       int block_size, int dtype, void *stream);
 
 /* Quantize-on-write of new K/V rows k, v [T, Hkv, D] into one layer's paged stores
  * kc/vc [num_blocks, Hkv, bs, D] int8, ks/vs [num_blocks, Hkv, bs] fp32 at

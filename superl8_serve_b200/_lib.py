@@ -30,7 +30,14 @@ SIGNATURES: dict[str, tuple] = {
     "s8b_rmsnorm_quant": (_i, [_vp, _vp, _vp, _vp, _f, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "s8b_gemm_w8a8": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
     "s8b_silu_mul_quant": (_i, [_vp, _i, _i, _vp, _vp, _vp, _i, _vp]),
+    "s8b_rmsnorm_quant_split": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp, _f, _vp, _vp, _vp, _i,
+                                     _i, _i, _vp]),
+    "s8b_silu_mul_quant_split": (_i, [_vp, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _i, _vp]),
+    "s8b_qkv_post_split": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _f, _i, _i, _i,
+                                _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i,
+                                _vp]),
     "s8b_gemm_tc_workspace_size": (_sz, [_i, _i]),
+    "s8b_gemm_tc_split_count": (_i, [_i, _i, _i]),
     "s8b_gemm_w8a8_tc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
     "s8b_tc_packed_bytes": (_sz, [_i, _i]),
     "s8b_pack_weights_tc": (_i, [_vp, _i, _i, _vp, _vp]),

@@ -101,9 +101,11 @@ __device__ __forceinline__ void store_v_row(const float v[4], int8_t *vc, float 
 }
 
 // --------------------------------------------------------------------------- qkv_post ----
+// One warp per (token, head row): grid (ceil(HR / 8), M) x 256 threads.
+constexpr int kQkvWarps = 8;
 template <typename T>
-__global__ void __launch_bounds__(512)
-    qkv_post_kernel(const T *__restrict__ qkv, const int32_t *__restrict__ positions,
+__global__ void __launch_bounds__(kQkvWarps * 32)
+    qkv_post_kernel(RowSrc<T> qkv, const int32_t *__restrict__ positions,
                     const float *__restrict__ cos_tab, const float *__restrict__ sin_tab,
                     const T *__restrict__ qn, const T *__restrict__ kn, float eps, int Hq,
                     int Hkv, int8_t *__restrict__ q_i8, float *__restrict__ q_s,
@@ -113,17 +115,19 @@ __global__ void __launch_bounds__(512)
                     const int32_t *__restrict__ block_table, int max_blocks, int bs) {
   griddep_launch();  // the next kernel may start its prologue
   griddep_wait();    // launched with programmatic serialization
-  const int m = blockIdx.x;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int m = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int HR = Hq + 2 * Hkv;
+  const int hr = blockIdx.x * kQkvWarps + warp;
+  if (hr >= HR) return;
   const int pos = positions[m];
   const int slot = slot_of(slot_mapping, block_table, max_blocks, bs, m, pos);
   const int blk = slot / bs, off = slot % bs;
   const float *cs = cos_tab + static_cast<size_t>(pos) * kHd;
   const float *sn = sin_tab + static_cast<size_t>(pos) * kHd;
-  for (int hr = warp; hr < HR; hr += nwarps) {
+  {
     float v[4];
-    load4(qkv + (static_cast<size_t>(m) * HR + hr) * kHd + 4 * lane, v);
+    qkv.load4(m, hr * kHd + 4 * lane, v);
     if (hr < Hq) {
       head_rmsnorm<T>(v, qn, eps);
       head_rope<T>(v, cs, sn);
@@ -1471,6 +1475,38 @@ int check_attn_shape(int B, int Hq, int Hkv, int D, int bs, int max_blocks, int 
 
 using namespace s8b;
 
+namespace s8b {
+namespace {
+template <typename T>
+int launch_qkv_post(RowSrc<T> src, const int32_t *positions, const float *cos_tab,
+                    const float *sin_tab, const void *q_norm_w, const void *k_norm_w, float eps,
+                    int M, int Hq, int Hkv, int8_t *q_i8, float *q_s, void *q_out, int8_t *kc,
+                    float *ks, int8_t *vc, float *vs, const int32_t *slot_mapping,
+                    const int32_t *block_table, int max_blocks, int block_size, void *stream) {
+  launch_pdl(qkv_post_kernel<T>, dim3((Hq + 2 * Hkv + kQkvWarps - 1) / kQkvWarps, M),
+             kQkvWarps * 32, 0, (cudaStream_t)stream, src, positions, cos_tab, sin_tab,
+             static_cast<const T *>(q_norm_w), static_cast<const T *>(k_norm_w), eps, Hq, Hkv,
+             q_i8, q_s, static_cast<T *>(q_out), kc, ks, vc, vs, slot_mapping, block_table,
+             max_blocks, block_size);
+  return check_launch();
+}
+
+int check_qkv_post(const int32_t *positions, const float *cos_tab, const float *sin_tab,
+                   int max_pos, const void *q_norm_w, const void *k_norm_w, int M, int Hq,
+                   int Hkv, int D, int8_t *q_i8, float *q_s, int8_t *kc, float *ks, int8_t *vc,
+                   float *vs, const int32_t *slot_mapping, const int32_t *block_table,
+                   int block_size) {
+  if (!positions || !cos_tab || !sin_tab || !q_norm_w || !k_norm_w || !q_i8 || !q_s || !kc ||
+      !ks || !vc || !vs || (!slot_mapping && !block_table))
+    return S8B_ERR_ARG;
+  if (M < 0 || M > 65535 || D != kHd || Hq <= 0 || Hkv <= 0 || block_size <= 0 || max_pos <= 0)
+    return S8B_ERR_SHAPE;
+  if (!aligned(q_i8, 16) || !aligned(kc, 16) || !aligned(vc, 16)) return S8B_ERR_ALIGN;
+  return S8B_OK;
+}
+}  // namespace
+}  // namespace s8b
+
 extern "C" int s8b_qkv_post(const void *qkv, const int32_t *positions, const float *cos_tab,
                             const float *sin_tab, int max_pos, const void *q_norm_w,
                             const void *k_norm_w, float eps, int M, int Hq, int Hkv, int D,
@@ -1478,20 +1514,43 @@ extern "C" int s8b_qkv_post(const void *qkv, const int32_t *positions, const flo
                             int8_t *vc, float *vs, const int32_t *slot_mapping,
                             const int32_t *block_table, int max_blocks, int block_size,
                             int dtype, void *stream) {
-  if (!qkv || !positions || !cos_tab || !sin_tab || !q_norm_w || !k_norm_w || !q_i8 || !q_s ||
-      !kc || !ks || !vc || !vs || (!slot_mapping && !block_table))
-    return S8B_ERR_ARG;
-  if (M < 0 || D != kHd || Hq <= 0 || Hkv <= 0 || block_size <= 0 || max_pos <= 0)
-    return S8B_ERR_SHAPE;
-  if (!aligned(q_i8, 16) || !aligned(kc, 16) || !aligned(vc, 16)) return S8B_ERR_ALIGN;
+  if (!qkv) return S8B_ERR_ARG;
+  const int e = check_qkv_post(positions, cos_tab, sin_tab, max_pos, q_norm_w, k_norm_w, M, Hq,
+                               Hkv, D, q_i8, q_s, kc, ks, vc, vs, slot_mapping, block_table,
+                               block_size);
+  if (e) return e;
+  if (!aligned(qkv, 8)) return S8B_ERR_ALIGN;
   if (M == 0) return S8B_OK;
   S8B_DISPATCH_DTYPE(dtype, T,
-                     launch_pdl(qkv_post_kernel<T>, M, 512, 0, (cudaStream_t)stream,
-                         static_cast<const T *>(qkv), positions, cos_tab, sin_tab,
-                         static_cast<const T *>(q_norm_w), static_cast<const T *>(k_norm_w), eps,
-                         Hq, Hkv, q_i8, q_s, static_cast<T *>(q_out), kc, ks, vc, vs,
-                         slot_mapping, block_table, max_blocks, block_size));
-  return check_launch();
+                     return launch_qkv_post<T>(row_src<T>(qkv, (Hq + 2 * Hkv) * kHd), positions,
+                                               cos_tab, sin_tab, q_norm_w, k_norm_w, eps, M, Hq,
+                                               Hkv, q_i8, q_s, q_out, kc, ks, vc, vs,
+                                               slot_mapping, block_table, max_blocks,
+                                               block_size, stream));
+}
+
+extern "C" int s8b_qkv_post_split(const int32_t *part, int C, const float *xs, const float *ws,
+                                  const int32_t *positions, const float *cos_tab,
+                                  const float *sin_tab, int max_pos, const void *q_norm_w,
+                                  const void *k_norm_w, float eps, int M, int Hq, int Hkv, int D,
+                                  int8_t *q_i8, float *q_s, void *q_out, int8_t *kc, float *ks,
+                                  int8_t *vc, float *vs, const int32_t *slot_mapping,
+                                  const int32_t *block_table, int max_blocks, int block_size,
+                                  int dtype, void *stream) {
+  if (!part || !xs || !ws) return S8B_ERR_ARG;
+  if (C < 1 || C > 8) return S8B_ERR_SHAPE;
+  const int e = check_qkv_post(positions, cos_tab, sin_tab, max_pos, q_norm_w, k_norm_w, M, Hq,
+                               Hkv, D, q_i8, q_s, kc, ks, vc, vs, slot_mapping, block_table,
+                               block_size);
+  if (e) return e;
+  if (!aligned(part, 16) || !aligned(ws, 16)) return S8B_ERR_ALIGN;
+  if (M == 0) return S8B_OK;
+  S8B_DISPATCH_DTYPE(dtype, T,
+                     return launch_qkv_post<T>(
+                         row_src_split<T>(part, C, xs, ws, M, (Hq + 2 * Hkv) * kHd), positions,
+                         cos_tab, sin_tab, q_norm_w, k_norm_w, eps, M, Hq, Hkv, q_i8, q_s, q_out,
+                         kc, ks, vc, vs, slot_mapping, block_table, max_blocks, block_size,
+                         stream));
 }
 
 extern "C" int s8b_kv_write_paged(const void *k, const void *v, int8_t *kc, float *ks, int8_t *vc,

@@ -169,6 +169,54 @@ __device__ __forceinline__ double block_sum_d(double v, double *red) {
   return warp_sum_d(v);
 }
 
+// ------------------------------------------------------------------ row input source ----
+// A row-major [M][ld] input of dtype T, or the split-K partial sums of a tensor-core GEMM
+// (int32 [C][M][ld], out_kind 2) that are summed and dequantized exactly as the GEMM's own
+// epilogue would: v = dtype((f32(sum_c part) * xs[m]) * ws[col]). col is a multiple of 4;
+// x and part are 8- / 16-byte aligned, ws 16-byte aligned.
+template <typename T>
+struct RowSrc {
+  const T *x;
+  const int32_t *part;
+  const float *xs, *ws;
+  size_t cstride;  // M * ld
+  int C, ld;
+  __device__ __forceinline__ void load4(int m, int col, float v[4]) const {
+    const size_t o = static_cast<size_t>(m) * ld + col;
+    if (part == nullptr) {
+      const uint2 raw = *reinterpret_cast<const uint2 *>(x + o);
+      T e[4];
+      memcpy(e, &raw, 8);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = to_f32(e[j]);
+      return;
+    }
+    int4 acc = *reinterpret_cast<const int4 *>(part + o);
+    for (int c = 1; c < C; ++c) {
+      const int4 q = *reinterpret_cast<const int4 *>(part + c * cstride + o);
+      acc.x += q.x;
+      acc.y += q.y;
+      acc.z += q.z;
+      acc.w += q.w;
+    }
+    const float sx = xs[m];
+    const float4 sw = *reinterpret_cast<const float4 *>(ws + col);
+    v[0] = round_to<T>(__fmul_rn(__fmul_rn(static_cast<float>(acc.x), sx), sw.x));
+    v[1] = round_to<T>(__fmul_rn(__fmul_rn(static_cast<float>(acc.y), sx), sw.y));
+    v[2] = round_to<T>(__fmul_rn(__fmul_rn(static_cast<float>(acc.z), sx), sw.z));
+    v[3] = round_to<T>(__fmul_rn(__fmul_rn(static_cast<float>(acc.w), sx), sw.w));
+  }
+};
+template <typename T>
+inline RowSrc<T> row_src(const void *x, int ld) {
+  return RowSrc<T>{static_cast<const T *>(x), nullptr, nullptr, nullptr, 0, 1, ld};
+}
+template <typename T>
+inline RowSrc<T> row_src_split(const int32_t *part, int C, const float *xs, const float *ws,
+                               int M, int ld) {
+  return RowSrc<T>{nullptr, part, xs, ws, static_cast<size_t>(M) * ld, C, ld};
+}
+
 // ----------------------------------------------------------------------- quantizer -----
 // Symmetric round-to-nearest: inv = qmax/amax, code = clamp(rint(x*inv)), scale = amax/qmax.
 struct QParams {

@@ -93,8 +93,8 @@ struct TcArgs {
   void *y;
   int32_t *status;  // workspace status word
   int out_kind, M, N, K, m0, n_tiles, kc;
-  int csplit;     // CTAs per cluster sharing each tile's K range (1: no split)
-  int nclusters;  // clusters in the grid
+  int csplit;     // CTAs sharing each tile's K range (1: no split)
+  int nclusters;  // CTA groups in the grid (launched as clusters unless out_kind == 2)
 };
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -169,7 +169,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t *recvb = part + Lay::kStageRows * Lay::kPartPitch;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C = a.csplit;
-  const uint32_t crank = C > 1 ? cluster_rank() : 0;
+  // out_kind 2 stores each CTA's partial tile (no cluster, no on-chip reduction)
+  const bool clustered = C > 1 && a.out_kind != 2;
+  const uint32_t crank = clustered ? cluster_rank() : static_cast<uint32_t>(blockIdx.x % C);
   const int cid = blockIdx.x / C;
   const int k_lo = static_cast<int>(crank) * a.kc / C, k_hi = (static_cast<int>(crank) + 1) * a.kc / C;
   const int nk = k_hi - k_lo;
@@ -195,7 +197,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&hdr->done, C);
     hdr->abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    if (C > 1 && my_tiles > 0)  // the first tile's receive buffer: C slots of this CTA's rows
+    if (clustered && my_tiles > 0)  // the first tile's receive buffer: C slots of this CTA's rows
       mbar_expect_tx(&hdr->recv, recv_bytes);
   }
   if (warp == 1) {
@@ -207,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (C > 1) {  // peers arrive on this CTA's barriers: all must be initialised first
+  if (clustered) {  // peers arrive on this CTA's barriers: all must be initialised first
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
   }
@@ -319,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // on a timeout all epilogue threads leave the loop at the same point.
       if (et == 0) {
         mbar_wait(&hdr->tmem_full[buf], (seg >> 1) & 1, abort, a.status);
-        if (C > 1 && seg >= 1) {
+        if (clustered && seg >= 1) {
           // the peers reduced the previous tile (receive buffers free) and this CTA's own
           // copies out of the staging tile have been read
           mbar_wait_cluster(&hdr->done, (seg - 1) & 1, abort, a.status);
@@ -329,6 +331,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       epi_bar_sync(kEpi);
       if (*abort) break;
       tc_fence_after();
+      if (a.out_kind == 2) {  // this CTA's int32 partial tile -> partial slice crank
+        const int n = tile * kBM + row;
+        int32_t *yp = static_cast<int32_t *>(a.y) + static_cast<size_t>(crank) * a.M * a.N;
+        if (drains) {
+#pragma unroll 1
+          for (int c0 = cbeg; c0 < cbeg + kHalf; c0 += 16) {
+            uint32_t v[16];
+            tmem_ld16(tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * NT + c0, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int m = a.m0 + c0 + j;
+              if (m < a.M && n < a.N) yp[static_cast<size_t>(m) * a.N + n] = static_cast<int32_t>(v[j]);
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&hdr->tmem_empty[buf]);
+        continue;
+      }
       if (C == 1) {
         const int n = tile * kBM + row;
         const float wsn = hdr->wsc[buf][row];
@@ -430,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (C > 1) {  // no CTA leaves while a peer may still read its buffers or arrive on them
+  if (clustered) {  // no CTA leaves while a peer may still read its buffers or arrive on them
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
   }
@@ -512,13 +534,34 @@ int pick_split(int n_tiles, int kc, int *nclusters) {
   return best_c;
 }
 
+// Split count for the partial-output mode (out_kind 2): CTA groups need no co-scheduling, so
+// C CTAs of a group are any C of the one-per-SM CTAs. Fewest chunk-times per CTA; ties go to
+// the smaller C (fewer partial bytes for the consumer to read).
+inline int pick_split_partials(int n_tiles, int kc, int *ngroups) {
+  const int sms = sm_count();
+  int best_c = 1, best_g = sms < n_tiles ? sms : n_tiles;
+  long best = static_cast<long>((n_tiles + sms - 1) / sms) * kc;
+  for (int C = 2; C <= 8 && C <= kc; ++C) {
+    const int g = sms / C;
+    const long cost = static_cast<long>((n_tiles + g - 1) / g) * ((kc + C - 1) / C);
+    if (cost < best) {
+      best = cost;
+      best_c = C;
+      best_g = g < n_tiles ? g : n_tiles;
+    }
+  }
+  *ngroups = best_g;
+  return best_c;
+}
+
 template <typename T, int NT>
 int launch_tc_nt(const CUtensorMap &mw, const CUtensorMap &mx, TcArgs args, cudaStream_t st) {
   using Lay = TcLayout<NT>;
   auto kern = gemm_tc_kernel<T, NT>;
   ensure_smem(reinterpret_cast<const void *>(kern), Lay::kSmem);
   int ncl = 0;
-  const int C = pick_split<T, NT>(args.n_tiles, args.kc, &ncl);
+  const int C = args.out_kind == 2 ? pick_split_partials(args.n_tiles, args.kc, &ncl)
+                                   : pick_split<T, NT>(args.n_tiles, args.kc, &ncl);
   args.csplit = C;
   args.nclusters = ncl;
   cudaLaunchConfig_t cfg = {};
@@ -530,7 +573,7 @@ int launch_tc_nt(const CUtensorMap &mw, const CUtensorMap &mx, TcArgs args, cuda
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   attr[1].id = cudaLaunchAttributeClusterDimension;
-  attr[1].val.clusterDim.x = C;
+  attr[1].val.clusterDim.x = args.out_kind == 2 ? 1 : C;
   attr[1].val.clusterDim.y = 1;
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
@@ -600,7 +643,7 @@ extern "C" int s8b_gemm_w8a8_tc(const int8_t *xq, const float *xs, const int8_t 
                                 const float *ws, void *y, int out_kind, int M, int N, int K,
                                 int dtype, void *workspace, size_t workspace_bytes, void *stream) {
   if (!xq || !w || !y || (out_kind == 0 && (!xs || !ws))) return S8B_ERR_ARG;
-  if (out_kind != 0 && out_kind != 1) return S8B_ERR_ARG;
+  if (out_kind < 0 || out_kind > 2) return S8B_ERR_ARG;
   if (M < 0 || N <= 0 || K <= 0 || K % kBK != 0) return S8B_ERR_SHAPE;
   if (!aligned(xq, 16) || !aligned(w, 16)) return S8B_ERR_ALIGN;
   if (!workspace || workspace_bytes < s8b_gemm_tc_workspace_size(M, N)) return S8B_ERR_WORKSPACE;
@@ -609,6 +652,12 @@ extern "C" int s8b_gemm_w8a8_tc(const int8_t *xq, const float *xs, const int8_t 
   S8B_DISPATCH_DTYPE(dtype, T,
                      return launch_tc<T>(xq, xs, w, ws, y, out_kind, M, N, K, workspace,
                                          (cudaStream_t)stream));
+}
+
+extern "C" int s8b_gemm_tc_split_count(int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0 || K % kBK != 0) return S8B_ERR_SHAPE;
+  int groups = 0;
+  return pick_split_partials((N + kBM - 1) / kBM, K / kBK, &groups);
 }
 
 extern "C" size_t s8b_tc_packed_bytes(int N, int K) {
@@ -629,7 +678,7 @@ extern "C" int s8b_gemm_w8a8_tc_packed(const int8_t *xq, const float *xs, const 
                                        int K, int dtype, void *workspace,
                                        size_t workspace_bytes, void *stream) {
   if (!xq || !wpacked || !y || (out_kind == 0 && (!xs || !ws))) return S8B_ERR_ARG;
-  if (out_kind != 0 && out_kind != 1) return S8B_ERR_ARG;
+  if (out_kind < 0 || out_kind > 2) return S8B_ERR_ARG;
   if (M < 0 || N <= 0 || K <= 0 || K % kBK != 0) return S8B_ERR_SHAPE;
   if (!aligned(xq, 16) || !aligned(wpacked, 16)) return S8B_ERR_ALIGN;
   if (!workspace || workspace_bytes < s8b_gemm_tc_workspace_size(M, N)) return S8B_ERR_WORKSPACE;

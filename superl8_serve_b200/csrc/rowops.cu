@@ -45,7 +45,7 @@ __device__ __forceinline__ void store_codes(int8_t *dst, const float v[4], float
 
 template <typename T, int VPT>
 __global__ void __launch_bounds__(1024)
-    rmsnorm_quant_v(const T *__restrict__ h, const T *__restrict__ res_in, T *__restrict__ res_out,
+    rmsnorm_quant_v(RowSrc<T> h, const T *__restrict__ res_in, T *__restrict__ res_out,
                     const T *__restrict__ w, float eps, int8_t *__restrict__ q,
                     float *__restrict__ s, T *__restrict__ y_out, int H) {
   griddep_launch();  // the next kernel may start its prologue
@@ -60,21 +60,23 @@ __global__ void __launch_bounds__(1024)
   for (int v = 0; v < VPT; ++v) {
     const int i = threadIdx.x + v * blockDim.x;
     if (i < nvec) {
+      float hv[4];
+      h.load4(m, 4 * i, hv);
       Vec4<T> a;
-      a.load(h + off + 4 * i);
       if (res_in) {
         Vec4<T> r;
         r.load(res_in + off + 4 * i);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          x[v][j] = round_to<T>(__fadd_rn(a.get(j), r.get(j)));
-          a.set(j, x[v][j]);
-        }
+        for (int j = 0; j < 4; ++j) x[v][j] = round_to<T>(__fadd_rn(hv[j], r.get(j)));
       } else {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) x[v][j] = a.get(j);
+        for (int j = 0; j < 4; ++j) x[v][j] = hv[j];
       }
-      if (res_out) a.store(res_out + off + 4 * i);
+      if (res_out) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) a.set(j, x[v][j]);
+        a.store(res_out + off + 4 * i);
+      }
 #pragma unroll
       for (int j = 0; j < 4; ++j) ss += static_cast<double>(x[v][j]) * static_cast<double>(x[v][j]);
     }
@@ -115,27 +117,26 @@ __global__ void __launch_bounds__(1024)
 
 template <typename T, int VPT>
 __global__ void __launch_bounds__(1024)
-    silu_mul_quant_v(const T *__restrict__ gu, int F, T *__restrict__ y_out,
-                     int8_t *__restrict__ q, float *__restrict__ s) {
+    silu_mul_quant_v(RowSrc<T> gu, int F, T *__restrict__ y_out, int8_t *__restrict__ q,
+                     float *__restrict__ s) {
   griddep_launch();  // the next kernel may start its prologue
   griddep_wait();    // launched with programmatic serialization
   __shared__ float red[32];
   const int m = blockIdx.x, nvec = F >> 2;
-  const T *row = gu + static_cast<size_t>(m) * 2 * F;
   float y[VPT][4];
   float amax = 0.0f;
 #pragma unroll
   for (int v = 0; v < VPT; ++v) {
     const int i = threadIdx.x + v * blockDim.x;
     if (i < nvec) {
-      Vec4<T> g, u;
-      g.load(row + 4 * i);
-      u.load(row + F + 4 * i);
+      float g[4], u[4];
+      gu.load4(m, 4 * i, g);
+      gu.load4(m, F + 4 * i, u);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float gf = g.get(j);
+        const float gf = g[j];
         const float a = round_to<T>(__fdiv_rn(gf, __fadd_rn(1.0f, exp_s8b(-gf))));
-        y[v][j] = round_to<T>(__fmul_rn(a, u.get(j)));
+        y[v][j] = round_to<T>(__fmul_rn(a, u[j]));
         amax = fmaxf(amax, fabsf(y[v][j]));
       }
     }
@@ -247,7 +248,7 @@ extern "C" int s8b_rmsnorm_quant(const void *h, const void *residual_in, void *r
   S8B_DISPATCH_DTYPE(dtype, T,
                      S8B_VPT_SWITCH(vpt, V,
                                     launch_pdl(rmsnorm_quant_v<T, V>, M, th, 0, (cudaStream_t)stream,
-                                               static_cast<const T *>(h),
+                                               row_src<T>(h, H),
                                                static_cast<const T *>(residual_in),
                                                static_cast<T *>(residual_out),
                                                static_cast<const T *>(w), eps, q, s,
@@ -266,7 +267,49 @@ extern "C" int s8b_silu_mul_quant(const void *gu, int M, int F, void *y_out, int
   S8B_DISPATCH_DTYPE(dtype, T,
                      S8B_VPT_SWITCH(vpt, V,
                                     launch_pdl(silu_mul_quant_v<T, V>, M, th, 0, (cudaStream_t)stream,
-                                               static_cast<const T *>(gu), F,
+                                               row_src<T>(gu, 2 * F), F,
+                                               static_cast<T *>(y_out), q, s)));
+  return check_launch();
+}
+
+extern "C" int s8b_rmsnorm_quant_split(const int32_t *part, int C, const float *xs,
+                                       const float *ws, const void *residual_in,
+                                       void *residual_out, const void *w, float eps, int8_t *q,
+                                       float *s, void *y_out, int M, int H, int dtype,
+                                       void *stream) {
+  if (!part || !xs || !ws || !w || !q || !s) return S8B_ERR_ARG;
+  if (M < 0 || H <= 0 || H % 4 != 0 || H > 32768 || C < 1 || C > 8) return S8B_ERR_SHAPE;
+  if (!aligned(part, 16) || !aligned(ws, 16) || !aligned(w, 8) || !aligned(q, 4) ||
+      !aligned(residual_in, 8) || !aligned(residual_out, 8) || !aligned(y_out, 8))
+    return S8B_ERR_ALIGN;
+  if (M == 0) return S8B_OK;
+  int th, vpt;
+  row_shape(H / 4, &th, &vpt);
+  S8B_DISPATCH_DTYPE(dtype, T,
+                     S8B_VPT_SWITCH(vpt, V,
+                                    launch_pdl(rmsnorm_quant_v<T, V>, M, th, 0, (cudaStream_t)stream,
+                                               row_src_split<T>(part, C, xs, ws, M, H),
+                                               static_cast<const T *>(residual_in),
+                                               static_cast<T *>(residual_out),
+                                               static_cast<const T *>(w), eps, q, s,
+                                               static_cast<T *>(y_out), H)));
+  return check_launch();
+}
+
+extern "C" int s8b_silu_mul_quant_split(const int32_t *part, int C, const float *xs,
+                                        const float *ws, int M, int F, void *y_out, int8_t *q,
+                                        float *s, int dtype, void *stream) {
+  if (!part || !xs || !ws || !q || !s) return S8B_ERR_ARG;
+  if (M < 0 || F <= 0 || F % 4 != 0 || F > 32768 || C < 1 || C > 8) return S8B_ERR_SHAPE;
+  if (!aligned(part, 16) || !aligned(ws, 16) || !aligned(q, 4) || !aligned(y_out, 8))
+    return S8B_ERR_ALIGN;
+  if (M == 0) return S8B_OK;
+  int th, vpt;
+  row_shape(F / 4, &th, &vpt);
+  S8B_DISPATCH_DTYPE(dtype, T,
+                     S8B_VPT_SWITCH(vpt, V,
+                                    launch_pdl(silu_mul_quant_v<T, V>, M, th, 0, (cudaStream_t)stream,
+                                               row_src_split<T>(part, C, xs, ws, M, 2 * F), F,
                                                static_cast<T *>(y_out), q, s)));
   return check_launch();
 }

@@ -95,6 +95,49 @@ def gemm_w8a8_tc(xq, xs, w, ws, *, out=None, out_dtype=torch.bfloat16, raw=False
     return out
 
 
+def gemm_w8a8_tc_split(xq, xs, w, *, packed=None, workspace=None):
+    """Tensor-core GEMM, split-K partials left unreduced (out_kind 2): returns int32
+    [C, M, N] with sum over C = the int32 accumulators."""
+    from ._lib import load
+
+    K = xq.shape[-1]
+    M = xq.numel() // K
+    N = w.shape[0]
+    C = int(load().s8b_gemm_tc_split_count(M, N, K))
+    part = torch.empty((C, M, N), dtype=torch.int32, device=xq.device)
+    if workspace is None:
+        workspace = gemm_tc_workspace(M, N, xq.device)
+    if packed is not None:
+        call("s8b_gemm_w8a8_tc_packed", ptr(xq), ptr(xs), ptr(packed), None, ptr(part), 2, M, N, K,
+             0, ptr(workspace), workspace.numel(), stream(xq.device))
+    else:
+        call("s8b_gemm_w8a8_tc", ptr(xq), ptr(xs), ptr(w), None, ptr(part), 2, M, N, K, 0,
+             ptr(workspace), workspace.numel(), stream(xq.device))
+    return part
+
+
+def rmsnorm_quant_split(part, xs, ws, residual, w, eps, *, residual_out, dtype=torch.bfloat16):
+    """rmsnorm_quant with h = dequant(sum of the GEMM partials part [C, M, H])."""
+    C, M, H = part.shape
+    q = torch.empty((M, H), dtype=torch.int8, device=part.device)
+    s = torch.empty(M, dtype=torch.float32, device=part.device)
+    call("s8b_rmsnorm_quant_split", ptr(part), C, ptr(xs), ptr(ws), ptr(residual),
+         ptr(residual_out), ptr(w), float(eps), ptr(q), ptr(s), None, M, H, dtype_code(dtype),
+         stream(part.device))
+    return residual_out, q, s
+
+
+def silu_mul_quant_split(part, xs, ws, *, dtype=torch.bfloat16):
+    C, M, F2 = part.shape
+    F = F2 // 2
+    q = torch.empty((M, F), dtype=torch.int8, device=part.device)
+    s = torch.empty(M, dtype=torch.float32, device=part.device)
+    y = torch.empty((M, F), dtype=dtype, device=part.device)
+    call("s8b_silu_mul_quant_split", ptr(part), C, ptr(xs), ptr(ws), M, F, ptr(y), ptr(q), ptr(s),
+         dtype_code(dtype), stream(part.device))
+    return q, s, y
+
+
 def silu_mul_quant(gu, *, y_out=False, q=None, s=None):
     F = gu.shape[-1] // 2
     M = gu.numel() // (2 * F)
@@ -123,6 +166,21 @@ def qkv_post(qkv, positions, cos, sin, q_norm_w, k_norm_w, eps, Hq, Hkv, kc, ks,
          ptr(vc), ptr(vs), ptr(slot_mapping), ptr(block_table), maxb, bs, dtype_code(qkv.dtype),
          stream(dev))
     return q_i8, q_s, qo
+
+
+def qkv_post_split(part, xs, ws, positions, cos, sin, q_norm_w, k_norm_w, eps, Hq, Hkv, kc, ks,
+                   vc, vs, *, block_table, dtype=torch.bfloat16):
+    """qkv_post with the merged qkv rows given as GEMM split-K partials [C, M, (Hq+2Hkv)*D]."""
+    C, M, _ = part.shape
+    D = cos.shape[-1]
+    dev = part.device
+    q_i8 = torch.empty((M, Hq, D), dtype=torch.int8, device=dev)
+    q_s = torch.empty((M, Hq), dtype=torch.float32, device=dev)
+    call("s8b_qkv_post_split", ptr(part), C, ptr(xs), ptr(ws), ptr(positions), ptr(cos), ptr(sin),
+         cos.shape[0], ptr(q_norm_w), ptr(k_norm_w), float(eps), M, Hq, Hkv, D, ptr(q_i8),
+         ptr(q_s), None, ptr(kc), ptr(ks), ptr(vc), ptr(vs), None, ptr(block_table),
+         block_table.shape[-1], kc.shape[-2], dtype_code(dtype), stream(dev))
+    return q_i8, q_s
 
 
 def kv_write_paged(k, v, kc, ks, vc, vs, slot_mapping, *, rotate_k=True):

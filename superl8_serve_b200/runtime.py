@@ -29,7 +29,7 @@ import numpy as np
 import torch
 
 from . import ops
-from ._lib import CODEC, call, ptr, stream
+from ._lib import CODEC, call, load, ptr, stream
 from .weights import quantize_rowwise_np
 
 
@@ -242,6 +242,19 @@ class StageRunner:
             with torch.cuda.device(dev):
                 for w in mats:
                     self.packed[id(w)] = (w, ops.pack_weights_tc(w))
+        # split-K partial outputs (GEMM out_kind 2) consumed by the following row kernel
+        self.splits: dict[tuple[int, int], int] = {}
+        self.part = None
+        if self.tc_ws is not None:
+            lib = load()
+            need = 0
+            for L in model.layers:
+                for w in (L.qkv_w, L.o_w, L.gu_w, L.d_w):
+                    N, K = w.shape
+                    c = int(lib.s8b_gemm_tc_split_count(m, N, K))
+                    self.splits[(N, K)] = c
+                    need = max(need, c * m * N)
+            self.part = torch.empty(need, dtype=torch.int32, device=dev)
 
     # ---------------------------------------------------------------------- pieces ----
     def _gemm(self, xq, xs, w, s, out, M):
@@ -257,31 +270,70 @@ class StageRunner:
             call("s8b_gemm_w8a8", ptr(xq), ptr(xs), ptr(w), ptr(s), ptr(out), 0, M, w.shape[0],
                  w.shape[1], 0, stream())
 
-    def _rms_quant(self, h, res_in, res_out, w, M, K):
-        call("s8b_rmsnorm_quant", ptr(h), ptr(res_in), ptr(res_out), ptr(w), self.eps, ptr(self.xq),
-             ptr(self.xs), None, M, K, 0, stream())
+    def _gemm_split(self, w, M):
+        """Tensor-core GEMM with its split-K partials left in self.part (out_kind 2); returns
+        the split count. The following row kernel sums and dequantizes them."""
+        pk = self.packed[id(w)][1]
+        N, K = w.shape
+        call("s8b_gemm_w8a8_tc_packed", ptr(self.xq), ptr(self.xs), ptr(pk), None, ptr(self.part),
+             2, M, N, K, 0, ptr(self.tc_ws), self.tc_ws.numel(), stream())
+        return self.splits[(N, K)]
 
-    def layer(self, li: int, mb: MicroBatch, M: int, first_layer_of_model: bool):
+    def _rms_quant(self, h, res_in, res_out, w, M, K, src=None):
+        """RMSNorm + activation quant; ``src`` = (C, weight scales) reads h from the split-K
+        partials of the preceding GEMM instead of ``h``."""
+        if src is None:
+            call("s8b_rmsnorm_quant", ptr(h), ptr(res_in), ptr(res_out), ptr(w), self.eps,
+                 ptr(self.xq), ptr(self.xs), None, M, K, 0, stream())
+        else:
+            C, ws = src
+            call("s8b_rmsnorm_quant_split", ptr(self.part), C, ptr(self.xs), ptr(ws), ptr(res_in),
+                 ptr(res_out), ptr(w), self.eps, ptr(self.xq), ptr(self.xs), None, M, K, 0,
+                 stream())
+
+    def layer(self, li: int, mb: MicroBatch, M: int, first_layer_of_model: bool, h_src=None,
+              keep_split: bool = False):
+        """One decoder layer. ``h_src`` says where the layer input comes from (None: self.h;
+        (C, ws): split-K partials of the previous down projection). Returns the same for the
+        layer output: partials when the tensor-core path runs and ``keep_split`` is set."""
         L = self.model.layers[li]
         kc, ks, vc, vs = self.pool.layer(li)
         H, st = self.H, stream()
+        split = self.part is not None and M >= self.tc_min
         # input_layernorm (fused residual add, except on the model's first layer)
-        self._rms_quant(self.h, None if first_layer_of_model else self.res, self.res, L.in_norm, M, H)
-        self._gemm(self.xq, self.xs, L.qkv_w, L.qkv_s, self.qkv, M)
-        call("s8b_qkv_post", ptr(self.qkv), ptr(mb.positions), ptr(self.cos), ptr(self.sin),
-             self.cos.shape[0], ptr(L.q_norm), ptr(L.k_norm), self.eps, M, self.Hq, self.Hkv,
-             self.D, ptr(self.q_i8), ptr(self.q_s), None, ptr(kc), ptr(ks), ptr(vc), ptr(vs),
-             None, ptr(mb.block_table), mb.block_table.shape[1], self.pool.block_size, 0, st)
+        self._rms_quant(self.h, None if first_layer_of_model else self.res, self.res, L.in_norm,
+                        M, H, src=h_src)
+        post = (ptr(mb.positions), ptr(self.cos), ptr(self.sin), self.cos.shape[0], ptr(L.q_norm),
+                ptr(L.k_norm), self.eps, M, self.Hq, self.Hkv, self.D, ptr(self.q_i8),
+                ptr(self.q_s), None, ptr(kc), ptr(ks), ptr(vc), ptr(vs), None,
+                ptr(mb.block_table), mb.block_table.shape[1], self.pool.block_size, 0, st)
+        if split:
+            C = self._gemm_split(L.qkv_w, M)
+            call("s8b_qkv_post_split", ptr(self.part), C, ptr(self.xs), ptr(L.qkv_s), *post)
+        else:
+            self._gemm(self.xq, self.xs, L.qkv_w, L.qkv_s, self.qkv, M)
+            call("s8b_qkv_post", ptr(self.qkv), *post)
         call("s8b_paged_decode_q8", ptr(self.q_i8), ptr(self.q_s), ptr(kc), ptr(ks), ptr(vc),
              ptr(vs), ptr(mb.block_table), ptr(mb.context_lens), ptr(self.attn), ptr(self.xq),
              ptr(self.xs), M, self.Hq, self.Hkv, self.D, self.pool.block_size,
              mb.block_table.shape[1], self.max_ctx, self.scale, ptr(self.ws), self.ws.numel(), 0,
              st)
+        if split:
+            C = self._gemm_split(L.o_w, M)
+            self._rms_quant(None, self.res, self.res, L.post_norm, M, H, src=(C, L.o_s))
+            C = self._gemm_split(L.gu_w, M)
+            call("s8b_silu_mul_quant_split", ptr(self.part), C, ptr(self.xs), ptr(L.gu_s), M,
+                 self.F, None, ptr(self.xq), ptr(self.xs), 0, st)
+            if keep_split:
+                return (self._gemm_split(L.d_w, M), L.d_s)
+            self._gemm(self.xq, self.xs, L.d_w, L.d_s, self.h, M)
+            return None
         self._gemm(self.xq, self.xs, L.o_w, L.o_s, self.h, M)
         self._rms_quant(self.h, self.res, self.res, L.post_norm, M, H)
         self._gemm(self.xq, self.xs, L.gu_w, L.gu_s, self.gu, M)
         call("s8b_silu_mul_quant", ptr(self.gu), M, self.F, None, ptr(self.xq), ptr(self.xs), 0, st)
         self._gemm(self.xq, self.xs, L.d_w, L.d_s, self.h, M)
+        return None
 
     def run(self, mb: MicroBatch, M: int | None = None, *, boundary_in=None, boundary_out=None):
         """Enqueue the stage's work for one micro-batch on the current stream.
@@ -298,10 +350,14 @@ class StageRunner:
             pay, sc, scheme = boundary_in
             call("s8b_codec_decode", pay.data_ptr(), sc.data_ptr(), M, self.H, self.H,
                  CODEC[scheme], ptr(self.h), ptr(self.res), 0, st)
-        for li in range(len(self.model.layers)):
-            self.layer(li, mb, M, first_model_layer and li == 0)
+        n = len(self.model.layers)
+        h_src = None
+        for li in range(n):
+            # the last layer of a non-final stage hands a dtype h to the boundary encoder
+            h_src = self.layer(li, mb, M, first_model_layer and li == 0, h_src=h_src,
+                               keep_split=li < n - 1 or self.model.is_last)
         if self.model.is_last:
-            self._rms_quant(self.h, self.res, self.res, self.model.norm, M, self.H)
+            self._rms_quant(self.h, self.res, self.res, self.model.norm, M, self.H, src=h_src)
             self._gemm(self.xq, self.xs, self.model.head_w, self.model.head_s, self.logits, M)
             call("s8b_argmax", ptr(self.logits), M, self.V, ptr(mb.ids), 0, st)
         else:

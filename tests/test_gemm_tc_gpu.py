@@ -108,3 +108,81 @@ def test_tc_gemm_packed_weights_bit_exact(M, N, K):
     assert np.array_equal(acc.cpu().numpy(), ok.gemm_acc(xq, w))
     assert np.array_equal(y.float().cpu().numpy(), ok.gemm_w8a8(xq, xs, w, ws))
     assert int(wsp.count_nonzero()) == 0
+
+
+@pytest.mark.parametrize("M,N,K,packed", [
+    (64, 4096, 4096, True), (64, 6144, 4096, True), (64, 24576, 4096, True),
+    (64, 4096, 12288, True), (20, 1000, 256, False), (300, 640, 384, False)])
+def test_tc_gemm_split_partials_sum_to_accumulators(M, N, K, packed):
+    """out_kind 2: C int32 partial tiles whose sum is the oracle's accumulator."""
+    from superl8_serve_b200 import ops
+
+    rng = np.random.default_rng(N * 3 + K)
+    xq = rng.integers(-127, 128, (M, K), dtype=np.int8)
+    w = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    xs = rng.uniform(0.001, 0.05, M).astype(np.float32)
+    wd = _t(w)
+    part = ops.gemm_w8a8_tc_split(_t(xq), _t(xs), wd,
+                                  packed=ops.pack_weights_tc(wd) if packed else None)
+    torch.cuda.synchronize()
+    assert 1 <= part.shape[0] <= 8
+    assert np.array_equal(part.sum(0, dtype=torch.int64).cpu().numpy(), ok.gemm_acc(xq, w))
+
+
+def _gemm_inputs(rng, M, N, K):
+    xq = _t(rng.integers(-127, 128, (M, K), dtype=np.int8))
+    xs = _t(rng.uniform(0.001, 0.02, M).astype(np.float32))
+    w = _t(rng.integers(-127, 128, (N, K), dtype=np.int8))
+    ws = _t(rng.uniform(0.0002, 0.002, N).astype(np.float32))
+    return xq, xs, w, ws
+
+
+def test_rmsnorm_and_silu_split_consumers_match_dtype_path():
+    """Reading the GEMM's partials (sum, dequant) inside the row kernel gives exactly what the
+    GEMM's own dtype output followed by the plain row kernel gives."""
+    from superl8_serve_b200 import ops
+
+    rng = np.random.default_rng(21)
+    M, H, F = 64, 4096, 12288
+    xq, xs, w, ws = _gemm_inputs(rng, M, H, 4096)
+    res = _t((rng.standard_normal((M, H)) * 2).astype(np.float32)).to(torch.bfloat16)
+    gain = _t((1 + 0.1 * rng.standard_normal(H)).astype(np.float32)).to(torch.bfloat16)
+    h = ops.gemm_w8a8_tc(xq, xs, w, ws)
+    r1, q1, s1, _ = ops.rmsnorm_quant(h, res, gain, 1e-6, residual_out=torch.empty_like(res))
+    part = ops.gemm_w8a8_tc_split(xq, xs, w)
+    r2, q2, s2 = ops.rmsnorm_quant_split(part, xs, ws, res, gain, 1e-6,
+                                         residual_out=torch.empty_like(res))
+    torch.cuda.synchronize()
+    assert torch.equal(r1, r2) and torch.equal(q1, q2) and torch.equal(s1, s2)
+    xq, xs, w, ws = _gemm_inputs(rng, M, 2 * F, 4096)
+    gu = ops.gemm_w8a8_tc(xq, xs, w, ws)
+    qa, sa, ya = ops.silu_mul_quant(gu, y_out=True)
+    qb, sb, yb = ops.silu_mul_quant_split(ops.gemm_w8a8_tc_split(xq, xs, w), xs, ws)
+    torch.cuda.synchronize()
+    assert torch.equal(qa, qb) and torch.equal(sa, sb) and torch.equal(ya, yb)
+
+
+def test_qkv_post_split_consumer_matches_dtype_path():
+    from superl8_serve_b200 import ops
+    from superl8_serve_b200.layers import rope_tables
+
+    rng = np.random.default_rng(22)
+    M, Hq, Hkv, D, bs = 64, 32, 8, 128, 16
+    xq, xs, w, ws = _gemm_inputs(rng, M, (Hq + 2 * Hkv) * D, 4096)
+    cos, sin = (t.to(DEV) for t in rope_tables(D, 4096, 1e6))
+    qn = _t((1 + 0.1 * rng.standard_normal(D)).astype(np.float32)).to(torch.bfloat16)
+    kn = _t((1 + 0.1 * rng.standard_normal(D)).astype(np.float32)).to(torch.bfloat16)
+    pos = _t(rng.integers(0, 4000, M).astype(np.int32))
+    bt = _t(np.arange(M * 256, dtype=np.int32).reshape(M, 256))
+    pools = [[torch.zeros((M * 256, Hkv, bs, D), dtype=torch.int8, device=DEV),
+              torch.zeros((M * 256, Hkv, bs), dtype=torch.float32, device=DEV),
+              torch.zeros((M * 256, Hkv, bs, D), dtype=torch.int8, device=DEV),
+              torch.zeros((M * 256, Hkv, bs), dtype=torch.float32, device=DEV)] for _ in range(2)]
+    qkv = ops.gemm_w8a8_tc(xq, xs, w, ws)
+    qa, sa, _ = ops.qkv_post(qkv, pos, cos, sin, qn, kn, 1e-6, Hq, Hkv, *pools[0], block_table=bt)
+    qb, sb = ops.qkv_post_split(ops.gemm_w8a8_tc_split(xq, xs, w), xs, ws, pos, cos, sin, qn, kn,
+                                1e-6, Hq, Hkv, *pools[1], block_table=bt)
+    torch.cuda.synchronize()
+    assert torch.equal(qa, qb) and torch.equal(sa, sb)
+    for a, b in zip(pools[0], pools[1]):
+        assert torch.equal(a, b)
