@@ -43,7 +43,56 @@ __device__ __forceinline__ void store_codes(int8_t *dst, const float v[4], float
   *reinterpret_cast<char4 *>(dst) = c;
 }
 
-template <typename T, int VPT>
+// Row-wide totals over a cluster of CL CTAs that split one row: each CTA's block total is
+// published in its shared memory, the cluster barrier orders the writes, and every CTA adds
+// the CL totals in rank order (the same order in every CTA).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t dsmem_addr(const void *p, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+               : "=r"(r)
+               : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))), "r"(rank));
+  return r;
+}
+template <int CL>
+__device__ __forceinline__ double cluster_total_d(double v, double *slot) {
+  if (CL == 1) return v;
+  if (threadIdx.x == 0) *slot = v;
+  cluster_sync_all();
+  double t = 0.0;
+#pragma unroll
+  for (int q = 0; q < CL; ++q) {
+    double x;
+    asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(x) : "r"(dsmem_addr(slot, q)) : "memory");
+    t += x;
+  }
+  return t;
+}
+template <int CL>
+__device__ __forceinline__ float cluster_max(float v, float *slot) {
+  if (CL == 1) return v;
+  if (threadIdx.x == 0) *slot = v;
+  cluster_sync_all();
+  float t = 0.0f;
+#pragma unroll
+  for (int q = 0; q < CL; ++q) {
+    float x;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(dsmem_addr(slot, q)) : "memory");
+    t = fmaxf(t, x);
+  }
+  return t;
+}
+template <int CL>
+__device__ __forceinline__ int cluster_rank_of() {
+  if (CL == 1) return 0;
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return static_cast<int>(r);
+}
+
+template <typename T, int VPT, int CL = 1>
 __global__ void __launch_bounds__(1024)
     rmsnorm_quant_v(RowSrc<T> h, const T *__restrict__ res_in, T *__restrict__ res_out,
                     const T *__restrict__ w, float eps, int8_t *__restrict__ q,
@@ -52,14 +101,17 @@ __global__ void __launch_bounds__(1024)
   griddep_wait();    // launched with programmatic serialization
   __shared__ double redd[32];
   __shared__ float red[32];
-  const int m = blockIdx.x, nvec = H >> 2;
+  __shared__ double cl_ss;
+  __shared__ float cl_amax;
+  // CL CTAs split the row: this CTA owns vectors [rank * nvec, (rank + 1) * nvec)
+  const int m = blockIdx.x / CL, rank = cluster_rank_of<CL>(), nvec = (H >> 2) / CL;
   const size_t off = static_cast<size_t>(m) * H;
   float x[VPT][4];
   double ss = 0.0;
 #pragma unroll
   for (int v = 0; v < VPT; ++v) {
-    const int i = threadIdx.x + v * blockDim.x;
-    if (i < nvec) {
+    const int i = rank * nvec + threadIdx.x + v * blockDim.x;
+    if (threadIdx.x + v * blockDim.x < nvec) {
       float hv[4];
       h.load4(m, 4 * i, hv);
       Vec4<T> a;
@@ -81,13 +133,13 @@ __global__ void __launch_bounds__(1024)
       for (int j = 0; j < 4; ++j) ss += static_cast<double>(x[v][j]) * static_cast<double>(x[v][j]);
     }
   }
-  ss = block_sum_d(ss, redd);
+  ss = cluster_total_d<CL>(block_sum_d(ss, redd), &cl_ss);
   const float rf = rms_factor(ss, H, eps);
   float amax = 0.0f;
 #pragma unroll
   for (int v = 0; v < VPT; ++v) {
-    const int i = threadIdx.x + v * blockDim.x;
-    if (i < nvec) {
+    const int i = rank * nvec + threadIdx.x + v * blockDim.x;
+    if (threadIdx.x + v * blockDim.x < nvec) {
       Vec4<T> wv;
       wv.load(w + 4 * i);
 #pragma unroll
@@ -97,12 +149,12 @@ __global__ void __launch_bounds__(1024)
       }
     }
   }
-  amax = block_max(amax, red);
+  amax = cluster_max<CL>(block_max(amax, red), &cl_amax);
   const QParams p = qparams(amax, 127.0f);
 #pragma unroll
   for (int v = 0; v < VPT; ++v) {
-    const int i = threadIdx.x + v * blockDim.x;
-    if (i < nvec) {
+    const int i = rank * nvec + threadIdx.x + v * blockDim.x;
+    if (threadIdx.x + v * blockDim.x < nvec) {
       store_codes(q + off + 4 * i, x[v], p.inv);
       if (y_out) {
         Vec4<T> yv;
@@ -112,23 +164,25 @@ __global__ void __launch_bounds__(1024)
       }
     }
   }
-  if (threadIdx.x == 0) s[m] = p.scale;
+  if (threadIdx.x == 0 && rank == 0) s[m] = p.scale;
+  if (CL > 1) cluster_sync_all();  // peers may still read this CTA's totals
 }
 
-template <typename T, int VPT>
+template <typename T, int VPT, int CL = 1>
 __global__ void __launch_bounds__(1024)
     silu_mul_quant_v(RowSrc<T> gu, int F, T *__restrict__ y_out, int8_t *__restrict__ q,
                      float *__restrict__ s) {
   griddep_launch();  // the next kernel may start its prologue
   griddep_wait();    // launched with programmatic serialization
   __shared__ float red[32];
-  const int m = blockIdx.x, nvec = F >> 2;
+  __shared__ float cl_amax;
+  const int m = blockIdx.x / CL, rank = cluster_rank_of<CL>(), nvec = (F >> 2) / CL;
   float y[VPT][4];
   float amax = 0.0f;
 #pragma unroll
   for (int v = 0; v < VPT; ++v) {
-    const int i = threadIdx.x + v * blockDim.x;
-    if (i < nvec) {
+    const int i = rank * nvec + threadIdx.x + v * blockDim.x;
+    if (threadIdx.x + v * blockDim.x < nvec) {
       float g[4], u[4];
       gu.load4(m, 4 * i, g);
       gu.load4(m, F + 4 * i, u);
@@ -141,13 +195,13 @@ __global__ void __launch_bounds__(1024)
       }
     }
   }
-  amax = block_max(amax, red);
+  amax = cluster_max<CL>(block_max(amax, red), &cl_amax);
   const QParams p = qparams(amax, 127.0f);
   const size_t off = static_cast<size_t>(m) * F;
 #pragma unroll
   for (int v = 0; v < VPT; ++v) {
-    const int i = threadIdx.x + v * blockDim.x;
-    if (i < nvec) {
+    const int i = rank * nvec + threadIdx.x + v * blockDim.x;
+    if (threadIdx.x + v * blockDim.x < nvec) {
       store_codes(q + off + 4 * i, y[v], p.inv);
       if (y_out) {
         Vec4<T> yv;
@@ -157,7 +211,8 @@ __global__ void __launch_bounds__(1024)
       }
     }
   }
-  if (threadIdx.x == 0) s[m] = p.scale;
+  if (threadIdx.x == 0 && rank == 0) s[m] = p.scale;
+  if (CL > 1) cluster_sync_all();  // peers may still read this CTA's maximum
 }
 
 template <typename T, int VPT>
@@ -234,6 +289,55 @@ extern "C" int s8b_quant_rows(const void *x, int dtype, int8_t *q, float *s, int
   return check_launch();
 }
 
+namespace s8b {
+namespace {
+// Rows of >= 128 vectors are split over a 4-CTA cluster (latency: more SMs per row, each
+// CTA a quarter of the loads); shorter rows keep one CTA per row.
+constexpr int kRowCluster = 4;
+inline int row_cluster(int nvec) { return (nvec % kRowCluster == 0 && nvec / kRowCluster >= 32) ? kRowCluster : 1; }
+
+template <typename T>
+int launch_rms(RowSrc<T> src, const void *res_in, void *res_out, const void *w, float eps,
+               int8_t *q, float *s, void *y_out, int M, int H, void *stream) {
+  const int cl = row_cluster(H / 4);
+  int th, vpt;
+  row_shape(H / 4 / cl, &th, &vpt);
+  const cudaStream_t st = (cudaStream_t)stream;
+  if (cl == 1) {
+    S8B_VPT_SWITCH(vpt, V,
+                   launch_pdl(rmsnorm_quant_v<T, V, 1>, M, th, 0, st, src,
+                              static_cast<const T *>(res_in), static_cast<T *>(res_out),
+                              static_cast<const T *>(w), eps, q, s, static_cast<T *>(y_out), H));
+  } else {
+    S8B_VPT_SWITCH(vpt, V,
+                   launch_pdl_cluster(rmsnorm_quant_v<T, V, kRowCluster>, M * kRowCluster, th, 0,
+                                      kRowCluster, st, src, static_cast<const T *>(res_in),
+                                      static_cast<T *>(res_out), static_cast<const T *>(w), eps,
+                                      q, s, static_cast<T *>(y_out), H));
+  }
+  return check_launch();
+}
+
+template <typename T>
+int launch_silu(RowSrc<T> src, int F, void *y_out, int8_t *q, float *s, int M, void *stream) {
+  const int cl = row_cluster(F / 4);
+  int th, vpt;
+  row_shape(F / 4 / cl, &th, &vpt);
+  const cudaStream_t st = (cudaStream_t)stream;
+  if (cl == 1) {
+    S8B_VPT_SWITCH(vpt, V,
+                   launch_pdl(silu_mul_quant_v<T, V, 1>, M, th, 0, st, src, F,
+                              static_cast<T *>(y_out), q, s));
+  } else {
+    S8B_VPT_SWITCH(vpt, V,
+                   launch_pdl_cluster(silu_mul_quant_v<T, V, kRowCluster>, M * kRowCluster, th, 0,
+                                      kRowCluster, st, src, F, static_cast<T *>(y_out), q, s));
+  }
+  return check_launch();
+}
+}  // namespace
+}  // namespace s8b
+
 extern "C" int s8b_rmsnorm_quant(const void *h, const void *residual_in, void *residual_out,
                                  const void *w, float eps, int8_t *q, float *s, void *y_out,
                                  int M, int H, int dtype, void *stream) {
@@ -243,33 +347,9 @@ extern "C" int s8b_rmsnorm_quant(const void *h, const void *residual_in, void *r
       !aligned(residual_out, 8) || !aligned(y_out, 8))
     return S8B_ERR_ALIGN;
   if (M == 0) return S8B_OK;
-  int th, vpt;
-  row_shape(H / 4, &th, &vpt);
   S8B_DISPATCH_DTYPE(dtype, T,
-                     S8B_VPT_SWITCH(vpt, V,
-                                    launch_pdl(rmsnorm_quant_v<T, V>, M, th, 0, (cudaStream_t)stream,
-                                               row_src<T>(h, H),
-                                               static_cast<const T *>(residual_in),
-                                               static_cast<T *>(residual_out),
-                                               static_cast<const T *>(w), eps, q, s,
-                                               static_cast<T *>(y_out), H)));
-  return check_launch();
-}
-
-extern "C" int s8b_silu_mul_quant(const void *gu, int M, int F, void *y_out, int8_t *q, float *s,
-                                  int dtype, void *stream) {
-  if (!gu || !q || !s) return S8B_ERR_ARG;
-  if (M < 0 || F <= 0 || F % 4 != 0 || F > 32768) return S8B_ERR_SHAPE;
-  if (!aligned(gu, 8) || !aligned(q, 4) || !aligned(y_out, 8)) return S8B_ERR_ALIGN;
-  if (M == 0) return S8B_OK;
-  int th, vpt;
-  row_shape(F / 4, &th, &vpt);
-  S8B_DISPATCH_DTYPE(dtype, T,
-                     S8B_VPT_SWITCH(vpt, V,
-                                    launch_pdl(silu_mul_quant_v<T, V>, M, th, 0, (cudaStream_t)stream,
-                                               row_src<T>(gu, 2 * F), F,
-                                               static_cast<T *>(y_out), q, s)));
-  return check_launch();
+                     return launch_rms<T>(row_src<T>(h, H), residual_in, residual_out, w, eps, q,
+                                          s, y_out, M, H, stream));
 }
 
 extern "C" int s8b_rmsnorm_quant_split(const int32_t *part, int C, const float *xs,
@@ -283,17 +363,19 @@ extern "C" int s8b_rmsnorm_quant_split(const int32_t *part, int C, const float *
       !aligned(residual_in, 8) || !aligned(residual_out, 8) || !aligned(y_out, 8))
     return S8B_ERR_ALIGN;
   if (M == 0) return S8B_OK;
-  int th, vpt;
-  row_shape(H / 4, &th, &vpt);
   S8B_DISPATCH_DTYPE(dtype, T,
-                     S8B_VPT_SWITCH(vpt, V,
-                                    launch_pdl(rmsnorm_quant_v<T, V>, M, th, 0, (cudaStream_t)stream,
-                                               row_src_split<T>(part, C, xs, ws, M, H),
-                                               static_cast<const T *>(residual_in),
-                                               static_cast<T *>(residual_out),
-                                               static_cast<const T *>(w), eps, q, s,
-                                               static_cast<T *>(y_out), H)));
-  return check_launch();
+                     return launch_rms<T>(row_src_split<T>(part, C, xs, ws, M, H), residual_in,
+                                          residual_out, w, eps, q, s, y_out, M, H, stream));
+}
+
+extern "C" int s8b_silu_mul_quant(const void *gu, int M, int F, void *y_out, int8_t *q, float *s,
+                                  int dtype, void *stream) {
+  if (!gu || !q || !s) return S8B_ERR_ARG;
+  if (M < 0 || F <= 0 || F % 4 != 0 || F > 32768) return S8B_ERR_SHAPE;
+  if (!aligned(gu, 8) || !aligned(q, 4) || !aligned(y_out, 8)) return S8B_ERR_ALIGN;
+  if (M == 0) return S8B_OK;
+  S8B_DISPATCH_DTYPE(dtype, T, return launch_silu<T>(row_src<T>(gu, 2 * F), F, y_out, q, s, M,
+                                                     stream));
 }
 
 extern "C" int s8b_silu_mul_quant_split(const int32_t *part, int C, const float *xs,
@@ -304,12 +386,7 @@ extern "C" int s8b_silu_mul_quant_split(const int32_t *part, int C, const float 
   if (!aligned(part, 16) || !aligned(ws, 16) || !aligned(q, 4) || !aligned(y_out, 8))
     return S8B_ERR_ALIGN;
   if (M == 0) return S8B_OK;
-  int th, vpt;
-  row_shape(F / 4, &th, &vpt);
   S8B_DISPATCH_DTYPE(dtype, T,
-                     S8B_VPT_SWITCH(vpt, V,
-                                    launch_pdl(silu_mul_quant_v<T, V>, M, th, 0, (cudaStream_t)stream,
-                                               row_src_split<T>(part, C, xs, ws, M, 2 * F), F,
-                                               static_cast<T *>(y_out), q, s)));
-  return check_launch();
+                     return launch_silu<T>(row_src_split<T>(part, C, xs, ws, M, 2 * F), F, y_out,
+                                           q, s, M, stream));
 }
