@@ -1218,34 +1218,39 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
                  "r"(kTmemCols) : "memory");
 }
 
-// Merge of the persistent kernel's partials. A row is handled by a cluster of kMergeSplit CTAs,
-// CTA c taking heads [c*hpc, (c+1)*hpc): per head M = max m_p, w_p = exp(m_p - M),
-// L = sum w_p l_p, O = sum w_p o_p (partition order), out = dtype(O / L), one output value
-// per thread with all its partial loads in flight. The row's int8 quantization for o_proj
-// takes the row maximum over the cluster through distributed shared memory. Same
-// arithmetic as merge_epilogue.
-constexpr int kMergeThreads = 512;
-constexpr int kMergeSplit = 4;
-constexpr int kMergeVpt = 4;  // hpc * 128 <= 2048 values per CTA (Hq <= 64)
-template <typename T>
+// Merge of the persistent kernel's partials, one CTA per row: per head M = max m_p,
+// w_p = exp(m_p - M), L = sum w_p l_p, O = sum w_p o_p (partition order), out = dtype(O / L),
+// then the row's int8 quantization for o_proj. Same arithmetic as merge_epilogue. Latency is
+// the cost here, so every (m, l) pair and the first kMergeChunk partials of every value are
+// loaded before anything waits on them.
+constexpr int kMergeThreads = 1024;
+constexpr int kMergeChunk = 8;
+template <typename T, int VPT>
 __global__ void __launch_bounds__(kMergeThreads)
     attn_merge_rows_kernel(DecodeWs ws, const int32_t *__restrict__ context_lens, int Hq, int P,
                            T *__restrict__ out, int8_t *__restrict__ out_q,
                            float *__restrict__ out_s) {
   griddep_launch();  // the next kernel may start its prologue
   griddep_wait();    // launched with programmatic serialization
-  extern __shared__ float msm[];  // [hpc][P] (m, l) pairs, then weights; [hpc] denominators
+  extern __shared__ float msm[];  // [Hq][P] (m, l) pairs, then weights; [Hq] denominators
   __shared__ float red[32];
-  __shared__ float cl_amax;
-  const int b = blockIdx.x / kMergeSplit, c = blockIdx.x % kMergeSplit, tid = threadIdx.x;
-  const int hpc = (Hq + kMergeSplit - 1) / kMergeSplit;
-  const int h0 = c * hpc, h1 = min(Hq, h0 + hpc), nh = max(0, h1 - h0);
+  const int b = blockIdx.x, tid = threadIdx.x;
   const int np = (context_lens[b] + kPart - 1) / kPart;
-  float *Wp = msm, *Lh = msm + 2 * hpc * P;
-  const float *mlb = ws.part_ml + (static_cast<size_t>(b) * Hq + h0) * P * 2;
-  for (int i = tid; i < nh * P * 2; i += kMergeThreads) msm[i] = mlb[i];  // all loads in flight
+  const int nv = Hq * kHd;
+  const float *mlb = ws.part_ml + static_cast<size_t>(b) * Hq * P * 2;
+  const float *pob = ws.part_o + static_cast<size_t>(b) * Hq * P * kHd;
+  float x[VPT][kMergeChunk];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int i = tid + j * kMergeThreads, h = i / kHd, d = i % kHd;
+#pragma unroll
+    for (int q = 0; q < kMergeChunk; ++q)
+      x[j][q] = (i < nv && q < np) ? pob[(static_cast<size_t>(h) * P + q) * kHd + d] : 0.0f;
+  }
+  for (int i = tid; i < Hq * P * 2; i += kMergeThreads) msm[i] = mlb[i];
   __syncthreads();
-  for (int h = tid; h < nh; h += kMergeThreads) {
+  float *Wp = msm, *Lh = msm + 2 * Hq * P;
+  for (int h = tid; h < Hq; h += kMergeThreads) {
     const float *ml = msm + h * P * 2;
     float M = -__int_as_float(0x7f800000);
     for (int q = 0; q < np; ++q) M = fmaxf(M, ml[2 * q]);
@@ -1258,26 +1263,22 @@ __global__ void __launch_bounds__(kMergeThreads)
     Lh[h] = Ls;
   }
   __syncthreads();
-  const int nv = nh * kHd;
-  T *orow = out + static_cast<size_t>(b) * Hq * kHd + h0 * kHd;
-  float v[kMergeVpt];
+  T *orow = out + static_cast<size_t>(b) * nv;
+  float v[VPT];
   float amax = 0.0f;
 #pragma unroll
-  for (int j = 0; j < kMergeVpt; ++j) {
+  for (int j = 0; j < VPT; ++j) {
     const int i = tid + j * kMergeThreads;
     v[j] = 0.0f;
     if (i < nv) {
       const int h = i / kHd, d = i % kHd;
-      const float *po = ws.part_o + ((static_cast<size_t>(b) * Hq + h0 + h) * P) * kHd + d;
+      const float *wh = Wp + h * P * 2;
       float O = 0.0f;
-      for (int q0 = 0; q0 < np; q0 += 8) {  // 8 loads in flight, then the ordered sum
-        float x[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) x[q] = q0 + q < np ? po[(q0 + q) * kHd] : 0.0f;
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          if (q0 + q < np) O = __fadd_rn(O, __fmul_rn(Wp[h * P * 2 + 2 * (q0 + q)], x[q]));
-      }
+      for (int q = 0; q < kMergeChunk; ++q)
+        if (q < np) O = __fadd_rn(O, __fmul_rn(wh[2 * q], x[j][q]));
+      for (int q = kMergeChunk; q < np; ++q)
+        O = __fadd_rn(O, __fmul_rn(wh[2 * q], pob[(static_cast<size_t>(h) * P + q) * kHd + d]));
       v[j] = round_to<T>(__fdiv_rn(O, Lh[h]));
       orow[i] = from_f32<T>(v[j]);
       amax = fmaxf(amax, fabsf(v[j]));
@@ -1285,28 +1286,13 @@ __global__ void __launch_bounds__(kMergeThreads)
   }
   if (!out_q) return;
   amax = block_max(amax, red);
-  if (tid == 0) cl_amax = amax;
-  // row maximum over the cluster (the barriers order the DSMEM reads against every CTA's
-  // write and against any CTA leaving)
-  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-  float rmax = 0.0f;
+  const QParams qp = qparams(amax, 127.0f);
 #pragma unroll
-  for (int q = 0; q < kMergeSplit; ++q) {
-    uint32_t ra;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(&cl_amax))), "r"(q));
-    float x;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(ra) : "memory");
-    rmax = fmaxf(rmax, x);
-  }
-  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-  const QParams qp = qparams(rmax, 127.0f);
-  int8_t *qrow = out_q + static_cast<size_t>(b) * Hq * kHd + h0 * kHd;
-#pragma unroll
-  for (int j = 0; j < kMergeVpt; ++j) {
+  for (int j = 0; j < VPT; ++j) {
     const int i = tid + j * kMergeThreads;
-    if (i < nv) qrow[i] = static_cast<int8_t>(qcode(v[j], qp.inv, 127));
+    if (i < nv) out_q[static_cast<size_t>(b) * nv + i] = static_cast<int8_t>(qcode(v[j], qp.inv, 127));
   }
-  if (c == 0 && tid == 0) out_s[b] = qp.scale;
+  if (tid == 0) out_s[b] = qp.scale;
 }
 
 inline int num_parts(int max_ctx) { return (max_ctx + kPart - 1) / kPart; }
@@ -1338,8 +1324,8 @@ DecodeWs carve_ws(void *base, int B, int Hq, int max_ctx) {
 
 // The persistent kernel + row merge, when the shape allows it: blocks of >= 8 tokens (each
 // TMA box then starts on a 1024-byte swizzle atom), 16-byte aligned scale arrays (16-byte
-// cp.async), B <= 1024 rows, Hq <= 64 and the merge weights within 96 KB of shared memory,
-// and K/V buffers whose allocation extent the driver reports (the tensor maps cover
+// cp.async), B <= 1024 rows, Hq <= 64 and the merge's (m, l) pairs within 96 KB of shared
+// memory, and K/V buffers whose allocation extent the driver reports (the tensor maps cover
 // exactly that). Returns 1 when not applicable.
 template <typename T>
 int launch_persistent(const int8_t *q_i8, const float *q_s, const int8_t *kc, const float *ks,
@@ -1348,9 +1334,8 @@ int launch_persistent(const int8_t *q_i8, const float *q_s, const int8_t *kc, co
                       int Hq, int Hkv, int bs, int bs_log2, int max_blocks, int P, float scale,
                       const DecodeWs &w, cudaStream_t st) {
   const int G = Hq / Hkv;
-  const int hpc = (Hq + kMergeSplit - 1) / kMergeSplit;
-  const size_t merge_smem = 4 * (2 * static_cast<size_t>(hpc) * P + hpc);
-  if (bs < 8 || B > pk::kMaxRows || hpc * kHd > kMergeThreads * kMergeVpt || merge_smem > 96 * 1024 ||
+  const size_t merge_smem = 4 * (2 * static_cast<size_t>(Hq) * P + Hq);
+  if (bs < 8 || B > pk::kMaxRows || Hq * kHd > kMergeThreads * 8 || merge_smem > 96 * 1024 ||
       !aligned(ks, 16) || !aligned(vs, 16) || !aligned(q_i8, 16))
     return 1;
   const size_t kb = tc::bytes_to_alloc_end(kc), vb = tc::bytes_to_alloc_end(vc);
@@ -1387,10 +1372,14 @@ int launch_persistent(const int8_t *q_i8, const float *q_s, const int8_t *kc, co
     default:
       return S8B_ERR_SHAPE;
   }
-  auto merge = attn_merge_rows_kernel<T>;
+  const int vpt = (Hq * kHd + kMergeThreads - 1) / kMergeThreads;
+  auto merge = vpt <= 1 ? attn_merge_rows_kernel<T, 1>
+               : vpt <= 2 ? attn_merge_rows_kernel<T, 2>
+               : vpt <= 4 ? attn_merge_rows_kernel<T, 4>
+                          : attn_merge_rows_kernel<T, 8>;
   ensure_smem(reinterpret_cast<const void *>(merge), 96 * 1024);
-  launch_pdl_cluster(merge, B * kMergeSplit, kMergeThreads, merge_smem, kMergeSplit, st, w,
-                     context_lens, Hq, P, static_cast<T *>(out), out_q, out_s);
+  launch_pdl(merge, B, kMergeThreads, merge_smem, st, w, context_lens, Hq, P,
+             static_cast<T *>(out), out_q, out_s);
   return check_launch(2);
 }
 

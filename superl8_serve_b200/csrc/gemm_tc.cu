@@ -66,7 +66,12 @@ __global__ void pack_tc_kernel(const int8_t *__restrict__ w, int N, int K,
   }
 }
 
-template <int NT>
+// PARTS: the layout carries the on-chip split-K buffers (cluster reduction, out_kind 0/1).
+// Without them (out_kind 2: partials go to global memory) the kernel stays under ~200 KB, so
+// a CTA of the small row kernels fits beside it and programmatic dependent launch can start
+// it, and its weight prefetch, while the preceding kernel still runs.
+constexpr int kLeanBudget = 200 * 1024;
+template <int NT, bool PARTS = true>
 struct TcLayout {
   static constexpr int kBBytes = NT * kBK;
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -74,12 +79,13 @@ struct TcLayout {
   // (conflict-free row-per-thread access): the staging tile [128 rows] this CTA sends from,
   // and the receive buffer [C source slots][ceil(128/C) rows] (<= 136 rows for C <= 8)
   static constexpr int kPartPitch = NT * 4 + 16;
-  static constexpr int kStageRows = NT <= 64 ? kBM : 0;
-  static constexpr int kRecvRows = NT <= 64 ? 136 : 0;
+  static constexpr int kStageRows = (PARTS && NT <= 64) ? kBM : 0;
+  static constexpr int kRecvRows = (PARTS && NT <= 64) ? 136 : 0;
   static constexpr int kPartBytes = (kStageRows + kRecvRows) * kPartPitch;
+  static constexpr int kBudget = PARTS ? kSmemBudget : kLeanBudget;
   static constexpr int kStages =
-      (kSmemBudget - 3072 - kPartBytes) / kStageBytes < kMaxStages
-          ? (kSmemBudget - 3072 - kPartBytes) / kStageBytes
+      (kBudget - 4096 - kPartBytes) / kStageBytes < kMaxStages
+          ? (kBudget - 4096 - kPartBytes) / kStageBytes
           : kMaxStages;
   static constexpr int kTmemCols = 2 * NT < 32 ? 32 : 2 * NT;
   static constexpr size_t kSmem =
@@ -156,11 +162,11 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity
 // warps 2-9 drain TMEM: warps w and w + 4 share lane quadrant w % 4 and take one half of the
 // token columns each. The accumulator is double-buffered in TMEM. Every mbarrier wait is
 // bounded: on timeout the kernel records S8B_ERR_TIMEOUT in the status word.
-template <typename T, int NT>
+template <typename T, int NT, bool PARTS = true>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_w,
                    const __grid_constant__ CUtensorMap tmap_x, TcArgs a) {
-  using Lay = TcLayout<NT>;
+  using Lay = TcLayout<NT, PARTS>;
   constexpr int S = Lay::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -554,10 +560,11 @@ inline int pick_split_partials(int n_tiles, int kc, int *ngroups) {
   return best_c;
 }
 
-template <typename T, int NT>
-int launch_tc_nt(const CUtensorMap &mw, const CUtensorMap &mx, TcArgs args, cudaStream_t st) {
-  using Lay = TcLayout<NT>;
-  auto kern = gemm_tc_kernel<T, NT>;
+template <typename T, int NT, bool PARTS>
+int launch_tc_nt_impl(const CUtensorMap &mw, const CUtensorMap &mx, TcArgs args,
+                      cudaStream_t st) {
+  using Lay = TcLayout<NT, PARTS>;
+  auto kern = gemm_tc_kernel<T, NT, PARTS>;
   ensure_smem(reinterpret_cast<const void *>(kern), Lay::kSmem);
   int ncl = 0;
   const int C = args.out_kind == 2 ? pick_split_partials(args.n_tiles, args.kc, &ncl)
@@ -584,6 +591,12 @@ int launch_tc_nt(const CUtensorMap &mw, const CUtensorMap &mx, TcArgs args, cuda
     return S8B_ERR_CUDA;
   }
   return check_launch();
+}
+
+template <typename T, int NT>
+int launch_tc_nt(const CUtensorMap &mw, const CUtensorMap &mx, TcArgs args, cudaStream_t st) {
+  return args.out_kind == 2 ? launch_tc_nt_impl<T, NT, false>(mw, mx, args, st)
+                            : launch_tc_nt_impl<T, NT, true>(mw, mx, args, st);
 }
 
 template <typename T>
