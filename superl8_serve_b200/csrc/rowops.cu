@@ -103,18 +103,21 @@ __global__ void __launch_bounds__(1024)
   __shared__ float red[32];
   __shared__ double cl_ss;
   __shared__ float cl_amax;
-  // CL CTAs split the row: this CTA owns vectors [rank * nvec, (rank + 1) * nvec)
+  // CL CTAs split the row: this CTA owns vectors [rank * nvec, (rank + 1) * nvec). Every
+  // global store comes after the last cluster barrier, so the barriers' release never waits
+  // on outstanding stores.
   const int m = blockIdx.x / CL, rank = cluster_rank_of<CL>(), nvec = (H >> 2) / CL;
   const size_t off = static_cast<size_t>(m) * H;
-  float x[VPT][4];
+  float x[VPT][4], xr[VPT][4], wg[VPT][4];
   double ss = 0.0;
 #pragma unroll
   for (int v = 0; v < VPT; ++v) {
     const int i = rank * nvec + threadIdx.x + v * blockDim.x;
     if (threadIdx.x + v * blockDim.x < nvec) {
+      Vec4<T> wv;
+      wv.load(w + 4 * i);  // independent of the reduction: in flight with the row loads
       float hv[4];
       h.load4(m, 4 * i, hv);
-      Vec4<T> a;
       if (res_in) {
         Vec4<T> r;
         r.load(res_in + off + 4 * i);
@@ -124,13 +127,12 @@ __global__ void __launch_bounds__(1024)
 #pragma unroll
         for (int j = 0; j < 4; ++j) x[v][j] = hv[j];
       }
-      if (res_out) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) a.set(j, x[v][j]);
-        a.store(res_out + off + 4 * i);
+      for (int j = 0; j < 4; ++j) {
+        xr[v][j] = x[v][j];
+        wg[v][j] = wv.get(j);
+        ss += static_cast<double>(x[v][j]) * static_cast<double>(x[v][j]);
       }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) ss += static_cast<double>(x[v][j]) * static_cast<double>(x[v][j]);
     }
   }
   ss = cluster_total_d<CL>(block_sum_d(ss, redd), &cl_ss);
@@ -138,23 +140,27 @@ __global__ void __launch_bounds__(1024)
   float amax = 0.0f;
 #pragma unroll
   for (int v = 0; v < VPT; ++v) {
-    const int i = rank * nvec + threadIdx.x + v * blockDim.x;
     if (threadIdx.x + v * blockDim.x < nvec) {
-      Vec4<T> wv;
-      wv.load(w + 4 * i);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        x[v][j] = round_to<T>(__fmul_rn(__fmul_rn(x[v][j], rf), wv.get(j)));
+        x[v][j] = round_to<T>(__fmul_rn(__fmul_rn(x[v][j], rf), wg[v][j]));
         amax = fmaxf(amax, fabsf(x[v][j]));
       }
     }
   }
   amax = cluster_max<CL>(block_max(amax, red), &cl_amax);
+  if (CL > 1) cluster_sync_all();  // peers have read this CTA's totals
   const QParams p = qparams(amax, 127.0f);
 #pragma unroll
   for (int v = 0; v < VPT; ++v) {
     const int i = rank * nvec + threadIdx.x + v * blockDim.x;
     if (threadIdx.x + v * blockDim.x < nvec) {
+      if (res_out) {
+        Vec4<T> a;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) a.set(j, xr[v][j]);
+        a.store(res_out + off + 4 * i);
+      }
       store_codes(q + off + 4 * i, x[v], p.inv);
       if (y_out) {
         Vec4<T> yv;
@@ -165,7 +171,6 @@ __global__ void __launch_bounds__(1024)
     }
   }
   if (threadIdx.x == 0 && rank == 0) s[m] = p.scale;
-  if (CL > 1) cluster_sync_all();  // peers may still read this CTA's totals
 }
 
 template <typename T, int VPT, int CL = 1>
@@ -196,6 +201,7 @@ __global__ void __launch_bounds__(1024)
     }
   }
   amax = cluster_max<CL>(block_max(amax, red), &cl_amax);
+  if (CL > 1) cluster_sync_all();  // peers have read this CTA's maximum; stores after it
   const QParams p = qparams(amax, 127.0f);
   const size_t off = static_cast<size_t>(m) * F;
 #pragma unroll
@@ -212,7 +218,6 @@ __global__ void __launch_bounds__(1024)
     }
   }
   if (threadIdx.x == 0 && rank == 0) s[m] = p.scale;
-  if (CL > 1) cluster_sync_all();  // peers may still read this CTA's maximum
 }
 
 template <typename T, int VPT>
