@@ -102,69 +102,94 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------- CPU baseline ----
 
+class CpuOracleSample:
+    """CPU oracle on a bounded sample of the config-3 step: one Qwen3-8B layer at batch
+    `batch`, context `ctx`, plus 1/`head_frac` of the LM head, extrapolated to the full
+    36-layer step. Weights and the KV pool are built once; each run() is one sample."""
+
+    def __init__(self, batch=64, ctx=2048, head_frac=16, seed=0):
+        from oracle.kernels import rope_tables
+        from oracle.model import PagedPool, Shape
+        from superl8_serve_b200.config import qwen3_8b
+
+        self.cfg = cfg = qwen3_8b()
+        self.batch, self.ctx, self.head_frac = batch, ctx, head_frac
+        self.s = Shape(cfg.vocab_size, cfg.hidden_size, 1, cfg.num_attention_heads,
+                       cfg.num_key_value_heads, 128, cfg.intermediate_size, 1e-6, 1e6, ctx + 8,
+                       False)
+        rng = np.random.default_rng(seed)
+        H, F, D = self.s.hidden_size, self.s.intermediate_size, 128
+        nh, nkv = self.s.num_attention_heads, self.s.num_key_value_heads
+
+        def w(n, k):
+            return (rng.integers(-127, 128, (n, k), dtype=np.int8),
+                    np.full(n, 0.02 / 73.3, dtype=np.float32))
+
+        g = lambda n: (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)  # noqa: E731
+        self.L = {"qkv": w((nh + 2 * nkv) * D, H), "o": w(H, nh * D), "gu": w(2 * F, H),
+                  "down": w(H, F), "in_norm": g(H), "post_norm": g(H), "q_norm": g(D),
+                  "k_norm": g(D)}
+        pool = PagedPool(1, batch, nkv, ctx + 8, D)
+        pool.kc[:] = rng.integers(-127, 128, pool.kc.shape, dtype=np.int8)
+        pool.vc[:] = rng.integers(-127, 128, pool.vc.shape, dtype=np.int8)
+        pool.ks[:] = rng.uniform(0.01, 0.05, pool.ks.shape)
+        pool.vs[:] = rng.uniform(0.01, 0.05, pool.vs.shape)
+        slots = [pool.alloc() for _ in range(batch)]
+        pool.ensure_capacity(slots, [ctx + 1] * batch)
+        self.pool = pool
+        self.sm = pool.slot_mapping(slots, [ctx] * batch)
+        self.bt = pool.block_table(slots)
+        self.cl = np.full(batch, ctx + 1, dtype=np.int32)
+        self.tabs = rope_tables(D, ctx + 8, 1e6)
+        self.h = (0.5 * rng.standard_normal((batch, H))).astype(np.float32)
+        self.res = (rng.standard_normal((batch, H))).astype(np.float32)
+        self.hw, _ = w(cfg.vocab_size // head_frac, H)
+        self.xq = rng.integers(-127, 128, (batch, H), dtype=np.int8)
+        self.desc = (f"oracle (numpy, BLAS GEMMs on {os.cpu_count()} host threads, Python "
+                     f"attention loop): 1 of {cfg.num_hidden_layers} Qwen3-8B layers + "
+                     f"1/{head_frac} of the LM head at batch {batch}, ctx {ctx}, extrapolated "
+                     f"to one {cfg.num_hidden_layers}-layer decode step")
+
+    def run(self):
+        """One sample: returns (tokens/s, seconds spent)."""
+        from oracle.kernels import gemm_acc
+        from oracle.model import layer_decode
+
+        t0 = time.perf_counter()
+        layer_decode(self.L, 0, self.h.copy(), self.res.copy(), [self.ctx] * self.batch, self.sm,
+                     self.bt, self.cl, self.pool, self.s, self.tabs)
+        t_layer = time.perf_counter() - t0
+        t1 = time.perf_counter()
+        gemm_acc(self.xq, self.hw)
+        t_head = (time.perf_counter() - t1) * self.head_frac
+        step = t_layer * self.cfg.num_hidden_layers + t_head
+        return self.batch / step, time.perf_counter() - t0
+
+
 def cpu_sample_tokens_per_s(batch=64, ctx=2048, n_layers=1, head_frac=16, seed=0):
-    """CPU oracle on a bounded sample of the config-3 step: `n_layers` Qwen3-8B layers at
-    batch `batch`, context `ctx`, plus 1/`head_frac` of the LM head; extrapolated to the full
-    36-layer step. Returns (tokens/s, seconds spent, sample description)."""
-    from oracle.kernels import gemm_acc, rope_tables
-    from oracle.model import PagedPool, Shape, layer_decode
-    from superl8_serve_b200.config import qwen3_8b
+    """One CPU-oracle sample (see CpuOracleSample). Returns (tokens/s, seconds, description)."""
+    smp = CpuOracleSample(batch, ctx, head_frac, seed)
+    v, spent = smp.run()
+    return v, spent, smp.desc
 
-    cfg = qwen3_8b()
-    s = Shape(cfg.vocab_size, cfg.hidden_size, 1, cfg.num_attention_heads,
-              cfg.num_key_value_heads, 128, cfg.intermediate_size, 1e-6, 1e6, ctx + 8, False)
-    rng = np.random.default_rng(seed)
-    H, F, D, nh, nkv = s.hidden_size, s.intermediate_size, 128, s.num_attention_heads, s.num_key_value_heads
 
-    def w(n, k):
-        return (rng.integers(-127, 128, (n, k), dtype=np.int8),
-                np.full(n, 0.02 / 73.3, dtype=np.float32))
-
-    g = lambda n: (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)  # noqa: E731
-    L = {"qkv": w((nh + 2 * nkv) * D, H), "o": w(H, nh * D), "gu": w(2 * F, H), "down": w(H, F),
-         "in_norm": g(H), "post_norm": g(H), "q_norm": g(D), "k_norm": g(D)}
-    pool = PagedPool(1, batch, nkv, ctx + 8, D)
-    pool.kc[:] = rng.integers(-127, 128, pool.kc.shape, dtype=np.int8)
-    pool.vc[:] = rng.integers(-127, 128, pool.vc.shape, dtype=np.int8)
-    pool.ks[:] = rng.uniform(0.01, 0.05, pool.ks.shape)
-    pool.vs[:] = rng.uniform(0.01, 0.05, pool.vs.shape)
-    slots = [pool.alloc() for _ in range(batch)]
-    pool.ensure_capacity(slots, [ctx + 1] * batch)
-    sm = pool.slot_mapping(slots, [ctx] * batch)
-    bt = pool.block_table(slots)
-    cl = np.full(batch, ctx + 1, dtype=np.int32)
-    tabs = rope_tables(D, ctx + 8, 1e6)
-    h = (0.5 * rng.standard_normal((batch, H))).astype(np.float32)
-    res = (rng.standard_normal((batch, H))).astype(np.float32)
-    t0 = time.perf_counter()
-    for _ in range(n_layers):
-        layer_decode(L, 0, h, res, [ctx] * batch, sm, bt, cl, pool, s, tabs)
-    t_layer = (time.perf_counter() - t0) / n_layers
-    hw, _ = w(cfg.vocab_size // head_frac, H)
-    xq = rng.integers(-127, 128, (batch, H), dtype=np.int8)
-    t1 = time.perf_counter()
-    gemm_acc(xq, hw)
-    t_head = (time.perf_counter() - t1) * head_frac
-    step = t_layer * cfg.num_hidden_layers + t_head
-    spent = time.perf_counter() - t0
-    desc = (f"oracle (numpy, BLAS GEMMs on {os.cpu_count()} host threads, Python attention loop):"
-            f" {n_layers} of 36 Qwen3-8B layers + 1/{head_frac} of the LM head at batch {batch},"
-            f" ctx {ctx}, extrapolated to one 36-layer decode step")
-    return batch / step, spent, desc
+REF_MAX_SAMPLES = 6
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    for _ in range(args.warmup):
-        cpu_sample_tokens_per_s(batch=args.batch, ctx=args.ctx, n_layers=1)
+    # one layer of the oracle takes ~10 s on the host: build once, warm once, and time at most
+    # REF_MAX_SAMPLES samples so the whole run stays within a few minutes
+    smp = CpuOracleSample(batch=args.batch, ctx=args.ctx)
+    smp.run()
     vals, spent = [], 0.0
-    desc = ""
-    for _ in range(args.steps):
-        v, t, desc = cpu_sample_tokens_per_s(batch=args.batch, ctx=args.ctx, n_layers=1)
+    for _ in range(min(args.steps, REF_MAX_SAMPLES)):
+        v, t = smp.run()
         vals.append(v)
         spent += t
+    desc = smp.desc + f"; median of {len(vals)} samples after 1 warm-up sample"
     v = statistics.median(vals)
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s",
