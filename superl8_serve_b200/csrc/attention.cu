@@ -813,9 +813,10 @@ __global__ void __launch_bounds__(kTcThreads)
 //                cp.async spread over its lanes, tracked by the same stage barrier; 3-stage
 //                ring of 69 KB stages. Block-table rows (one per lane) are loaded three units
 //                ahead.
-//   warp 1       MMA issuer (one thread): S = K Q^T for unit k+1 is issued before
-//                O^T = V^T W^T of unit k. S and O are double-buffered in TMEM
-//                (S: 2 x 32 columns, O: 2 x 48 columns).
+//   warps 1, 15  MMA issuers (one thread each): warp 1 issues S = K Q^T as soon as a stage has
+//                landed and an S buffer is free, warp 15 issues O^T = V^T W^T as soon as the
+//                unit's weight planes are written and an O buffer is free. S and O are
+//                double-buffered in TMEM (S: 2 x 32 columns, O: 2 x 48 columns).
 //   warps 2-9    two softmax groups of 4 warps; group j takes the units with k % 2 == j, so
 //                each group has two unit-times for its latency-bound chain (thread = TMEM
 //                lane = tokens t and t + 128): scores, partition maxima, exp, the 15-bit
@@ -836,7 +837,7 @@ constexpr int kStage = 70656;  // K/W/E 32 KB | V 32 KB | Q 2 KB | K, V scales 1
 constexpr int kOffV = 32768, kOffQ = 65536, kOffKs = 67584, kOffVs = 68608, kOffQs = 69632;
 constexpr int kWBlock = 6144;  // one 128-token block of the 48-row weight operand
 constexpr int kOffE = 12288;   // e values [G][256] floats, after the two weight blocks
-constexpr int kThreads = 480;
+constexpr int kThreads = 512;
 constexpr int kTmemCols = 256;
 constexpr int kColO = 64;      // O buffer t at kColO + 48 t; S buffer t at 32 t
 constexpr int kMisc = 2048;    // barriers, TMEM base, abort flag, stats, reductions
@@ -890,7 +891,7 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
   uint64_t *sempty = full + 11;                         // [2] S buffer read (4 warp arrivals)
   uint64_t *ofull = full + 13;                          // [2] O buffer + stats ready
   uint64_t *oempty = full + 15;                         // [2] O buffer read (4 warp arrivals)
-  uint64_t *drain = full + 17;                          // [1] MMA drain on exit
+  uint64_t *drain = full + 17;                          // [2] MMA drains on exit (q.k, p.v)
   uint32_t *tmem_base = reinterpret_cast<uint32_t *>(misc + 256);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(misc + 260);
   float *stats = reinterpret_cast<float *>(misc + 512);  // [2][3][8]: m, l, wmax/32767
@@ -915,7 +916,8 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
       mbar_init(&ofull[i], 2);
       mbar_init(&oempty[i], 4);
     }
-    mbar_init(drain, 1);
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -1007,33 +1009,15 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
       for (int j = k > kStages ? k - kStages : 0; j < k; ++j)
         mbar_drain(&full[j % kStages], (j / kStages) & 1);
   } else if (warp == 1) {
-    // -------------------------------------------------------------------- MMA issuer ----
+    // ------------------------------------------------------------- q.k MMA issuer ----
     if (lane == 0) {
       constexpr uint32_t id_s = i8_idesc(128, 16);
-      constexpr uint32_t id_pv = i8_idesc(128, 48, true, true, /*a_mn_major=*/true, false);
-      auto issue_pv = [&](int j) -> bool {
-        const int s = j % kStages, t = j & 1;
-        if (!mbar_wait(&wfull[s], (j / kStages) & 1, abort_flag, ws.status)) return false;
-        if (j >= 2 && !mbar_wait(&oempty[t], ((j >> 1) - 1) & 1, abort_flag, ws.status)) return false;
-        tc_fence_after();
-        uint8_t *st = sm + s * kStage;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const uint64_t vd = sw128_desc(smem_u32(st + kOffV + i * 32 * kHd));
-          const uint64_t wd = sw128_desc(smem_u32(st + (i >> 2) * kWBlock)) + 2 * (i & 3);
-          mma_i8(tmem + kColO + 48 * t, vd, wd, id_pv, i > 0);
-        }
-        mma_commit(&ofull[t]);
-        mma_commit(&empty[s]);
-        return true;
-      };
       int k = 0;
-      bool ok = true;
-      for (UnitIter it(blockIdx.x, gridDim.x, P, Hkv); it.b < B && ok; it.next()) {
+      for (UnitIter it(blockIdx.x, gridDim.x, P, Hkv); it.b < B; it.next()) {
         if (it.p * kPart >= ctx[it.b]) continue;
         const int s = k % kStages, t = k & 1;
-        ok = mbar_wait(&full[s], (k / kStages) & 1, abort_flag, ws.status) &&
-             (k < 2 || mbar_wait(&sempty[t], ((k >> 1) - 1) & 1, abort_flag, ws.status));
+        const bool ok = mbar_wait(&full[s], (k / kStages) & 1, abort_flag, ws.status) &&
+                        (k < 2 || mbar_wait(&sempty[t], ((k >> 1) - 1) & 1, abort_flag, ws.status));
         if (!ok) break;
         tc_fence_after();
         uint8_t *st = sm + s * kStage;
@@ -1045,12 +1029,38 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
           for (int i = 0; i < 4; ++i) mma_i8(tmem + 32 * t + 16 * tile, kd + 2 * i, qd + 2 * i, id_s, i > 0);
         }
         mma_commit(&sfull[t]);
-        if (k > 0) ok = issue_pv(k - 1);
         ++k;
       }
-      if (ok && k > 0) issue_pv(k - 1);
-      mma_commit(drain);  // all MMAs issued by this thread have completed once this arrives
-      mbar_drain(drain, 0);
+      mma_commit(&drain[0]);  // all MMAs issued by this thread have completed once this arrives
+      mbar_drain(&drain[0], 0);
+    }
+  } else if (warp == 15) {
+    // ------------------------------------------------------------- p.v MMA issuer ----
+    // A thread of its own, so that q.k of later units never queues behind a p.v that waits
+    // for its softmax.
+    if (lane == 0) {
+      constexpr uint32_t id_pv = i8_idesc(128, 48, true, true, /*a_mn_major=*/true, false);
+      int k = 0;
+      for (UnitIter it(blockIdx.x, gridDim.x, P, Hkv); it.b < B; it.next()) {
+        if (it.p * kPart >= ctx[it.b]) continue;
+        const int s = k % kStages, t = k & 1;
+        const bool ok = mbar_wait(&wfull[s], (k / kStages) & 1, abort_flag, ws.status) &&
+                        (k < 2 || mbar_wait(&oempty[t], ((k >> 1) - 1) & 1, abort_flag, ws.status));
+        if (!ok) break;
+        tc_fence_after();
+        uint8_t *st = sm + s * kStage;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint64_t vd = sw128_desc(smem_u32(st + kOffV + i * 32 * kHd));
+          const uint64_t wd = sw128_desc(smem_u32(st + (i >> 2) * kWBlock)) + 2 * (i & 3);
+          mma_i8(tmem + kColO + 48 * t, vd, wd, id_pv, i > 0);
+        }
+        mma_commit(&ofull[t]);
+        mma_commit(&empty[s]);
+        ++k;
+      }
+      mma_commit(&drain[1]);
+      mbar_drain(&drain[1], 0);
     }
   } else if (warp < 10) {
     // ------------------------------------------------------------------- softmax ----
@@ -1164,7 +1174,7 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
       }
       ++k;
     }
-  } else {
+  } else if (warp < 14) {
     // ------------------------------------------------------------------ epilogue ----
     const int q4 = warp & 3, tid = threadIdx.x - 320;
     const int d = 32 * q4 + lane;
