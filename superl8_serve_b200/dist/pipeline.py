@@ -66,6 +66,39 @@ def stage_bounds(n_layers: int, n_stages: int) -> list[int]:
     return [i * n_layers // n_stages for i in range(n_stages + 1)]
 
 
+def balanced_stage_bounds(n_layers: int, n_stages: int, last_extra: float = 0.0,
+                          first_extra: float = 0.0) -> list[int]:
+    """Contiguous layer ranges minimising the largest stage cost, where a stage costs its
+    layer count plus ``first_extra`` (stage 0: embedding) or ``last_extra`` (last stage: final
+    norm, LM head, sampler) in layer units. The reference splits evenly (stage_bounds); in a
+    decode pipeline the step time is the slowest stage's, so the head's cost is worth moving
+    layers off the last stage. Exact dynamic programme over split points (ties: earlier
+    boundaries)."""
+    if n_stages > n_layers:
+        raise ValueError("pipeline stage count cannot exceed the model layer count")
+    INF = float("inf")
+    # best[s][i]: minimal max cost of splitting layers [0, i) into s stages; arg: last split
+    best = [[INF] * (n_layers + 1) for _ in range(n_stages + 1)]
+    arg = [[0] * (n_layers + 1) for _ in range(n_stages + 1)]
+    best[0][0] = 0.0
+    for s_ in range(1, n_stages + 1):
+        for i in range(s_, n_layers + 1):
+            for j in range(s_ - 1, i):
+                if best[s_ - 1][j] == INF:
+                    continue
+                cost = i - j + (first_extra if s_ == 1 else 0.0) + (
+                    last_extra if (s_ == n_stages and i == n_layers) else 0.0)
+                c = max(best[s_ - 1][j], cost)
+                if c < best[s_][i] - 1e-12:
+                    best[s_][i], arg[s_][i] = c, j
+    bounds = [n_layers]
+    i = n_layers
+    for s_ in range(n_stages, 0, -1):
+        i = arg[s_][i]
+        bounds.append(i)
+    return bounds[::-1]
+
+
 def make_pipeline(cfg, weights, *, devices: tuple[int, ...] = (0, 1), max_num_seqs: int = 16,
                   max_len: int = 2048, block_size: int = 16, seed: int = 0,
                   allow_single_stage: bool = False) -> tuple[PipelineStage, ...]:

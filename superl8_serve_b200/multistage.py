@@ -33,7 +33,7 @@ import numpy as np
 import torch
 
 from ._lib import CODEC, call, load, ptr, stream
-from .dist.pipeline import stage_bounds
+from .dist.pipeline import balanced_stage_bounds, stage_bounds
 from .ops import codec_sizes
 from .runtime import KVPool, MicroBatch, StageModel, StageRunner
 
@@ -86,11 +86,20 @@ class RankPlan:
         return self.rank == self.world - 1
 
 
+# last-stage extra work (final norm, LM head, sampler) in Qwen3-8B layer units at the bench
+# shape: LM head ~140 us against ~158 us per layer on B200
+HEAD_LAYERS = 0.9
+
+
 def plan_rank(n_layers: int, hidden: int, rank: int, world: int, m: int, scheme: str,
-              payload_bytes_fn=None) -> RankPlan:
+              payload_bytes_fn=None, bounds: list[int] | None = None) -> RankPlan:
+    """``bounds``: layer split (default: the reference's even split, stage_bounds)."""
     if world > n_layers:
         raise ValueError("pipeline stage count cannot exceed the model layer count")
-    b = stage_bounds(n_layers, world)
+    b = stage_bounds(n_layers, world) if bounds is None else list(bounds)
+    if len(b) != world + 1 or b[0] != 0 or b[-1] != n_layers or any(
+            b[i] >= b[i + 1] for i in range(world)):
+        raise ValueError(f"bad stage bounds {b} for {n_layers} layers / {world} stages")
     fn = payload_bytes_fn or (lambda T, D, s: codec_sizes(T, D, s))
     pay, nsc = fn(m, 2 * hidden, scheme)
     pay_al = (pay + 255) // 256 * 256
@@ -146,14 +155,15 @@ class RankPipeline:
 
     def __init__(self, cfg, rank: int, world: int, *, m: int, max_len: int, ctx: int,
                  scheme: str = "int8-had", seed: int = 0, pg=None, state_dict=None,
-                 fill_kv: bool = True):
+                 fill_kv: bool = True, bounds: list[int] | None = None):
         """``state_dict`` (HF-style float weights) selects real weights for this rank's layer
         range; without it the weights are synthetic (benchmarks). ``fill_kv`` pre-fills the
         KV pool with random codes for a synthetic context of ``ctx`` tokens; with
         ``fill_kv=False`` and ``ctx=0`` every sequence starts empty."""
         self.cfg, self.rank, self.world = cfg, rank, world
         self.dev = torch.device("cuda", torch.cuda.current_device())
-        self.plan = plan_rank(cfg.num_hidden_layers, cfg.hidden_size, rank, world, m, scheme)
+        self.plan = plan_rank(cfg.num_hidden_layers, cfg.hidden_size, rank, world, m, scheme,
+                              bounds=bounds)
         self.scheme = scheme
         S, H = world, cfg.hidden_size
         lo, hi = self.plan.layers
@@ -346,8 +356,11 @@ def run_bench_multi(args, metric, step_bytes, peaks, ClockSampler, cpu_sample):
         cfg = cfg.with_(num_hidden_layers=args.layers)
     m, ctx = args.batch, args.ctx
     total_steps = 1 + 2 * args.warmup + 3 * args.steps + 8  # graph, host-I/O and host-wait loops
+    # the last stage also runs the final norm, the LM head and the sampler for every
+    # micro-batch (~0.9 of a Qwen3-8B layer at this shape, measured): balance on that
+    bounds = balanced_stage_bounds(cfg.num_hidden_layers, world, last_extra=HEAD_LAYERS)
     pipe = RankPipeline(cfg, rank, world, m=m, max_len=ctx + total_steps + 16, ctx=ctx,
-                        scheme=args.scheme, seed=1)
+                        scheme=args.scheme, seed=1, bounds=bounds)
     rng = np.random.default_rng(3)
     ids_h = torch.from_numpy(rng.integers(0, cfg.vocab_size, m * world).astype(np.int32)).pin_memory()
     out_h = torch.zeros(m * world, dtype=torch.int32).pin_memory()
@@ -436,6 +449,7 @@ def run_bench_multi(args, metric, step_bytes, peaks, ClockSampler, cpu_sample):
             "data": "synthetic (random int8 weights, KV pre-filled with random codes)",
             "config": {"workload": "qwen3-8b-shaped W8A8 decode (BASELINE config 3)",
                        "micro_batch": m, "n_micro": world, "global_batch": B, "ctx": ctx,
+                       "stage_bounds": bounds,
                        "layers": cfg.num_hidden_layers, "block_size": 16,
                        "parallelism": f"pp{world}", "wire_scheme": args.scheme,
                        "cuda_graph": True, "transport": "NVLink P2P stores + device flags",

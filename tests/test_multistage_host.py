@@ -77,3 +77,25 @@ def test_handle_exchange_gloo(world):
         if r == world - 1:
             assert h["first_tok"] == bytes([0, 2]) and h["first_flag"] == bytes([0, 3])
             assert "next_recv" not in h
+
+
+def test_balanced_stage_bounds():
+    from superl8_serve_b200.dist.pipeline import balanced_stage_bounds
+
+    assert balanced_stage_bounds(36, 1, last_extra=0.9) == [0, 36]
+    assert balanced_stage_bounds(36, 2) == stage_bounds(36, 2)
+    for S in (2, 4, 8):
+        b = balanced_stage_bounds(36, S, last_extra=0.9)
+        assert b[0] == 0 and b[-1] == 36 and all(b[i] < b[i + 1] for i in range(S))
+        cost = [b[i + 1] - b[i] + (0.9 if i == S - 1 else 0.0) for i in range(S)]
+        even = stage_bounds(36, S)
+        even_cost = [even[i + 1] - even[i] + (0.9 if i == S - 1 else 0.0) for i in range(S)]
+        assert max(cost) <= max(even_cost)
+    assert balanced_stage_bounds(36, 8, last_extra=0.9)[-2] >= 32  # head stage gets <= 4
+    with pytest.raises(ValueError):
+        balanced_stage_bounds(4, 8)
+    p = plan_rank(36, 4096, 7, 8, 64, "int8-had", payload_bytes_fn=_sizes,
+                  bounds=balanced_stage_bounds(36, 8, last_extra=0.9))
+    assert p.layers[1] == 36
+    with pytest.raises(ValueError):
+        plan_rank(36, 4096, 0, 2, 64, "int8-had", payload_bytes_fn=_sizes, bounds=[0, 40, 36])
