@@ -238,6 +238,10 @@ int s8b_embed(const int32_t *ids, const void *table, int M, int H, void *out, in
  * Replaces the all-greedy Sampler fast path (superl8serve/layers/sampler.py:51-63).       */
 int s8b_argmax(const void *logits, int M, int V, int32_t *out, int dtype, void *stream);
 
+/* The library's binary32 exponential (softmax weights, partition merge, SiLU), elementwise:
+ * y[i] = exp_s8b(x[i]). A numerics check of the CPU definition, not a reference seam.      */
+int s8b_exp_f32(const float *x, float *y, long long n, void *stream);
+
 /* Inter-stage codec. Rows are the concatenation [a | b] of a [T, Da] and b [T, Db]
  * (b nullable, Db = 0), i.e. the pipeline's packed (hidden, residual) boundary
  * (superl8serve/dist/pipeline.py:246-250). (Da+Db) % 128 == 0 for the int4 / -had schemes.

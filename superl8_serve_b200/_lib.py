@@ -58,6 +58,7 @@ SIGNATURES: dict[str, tuple] = {
                               _i, _f, _vp, _sz, _i, _vp]),
     "s8b_embed": (_i, [_vp, _vp, _i, _i, _vp, _i, _vp]),
     "s8b_argmax": (_i, [_vp, _i, _i, _vp, _i, _vp]),
+    "s8b_exp_f32": (_i, [_vp, _vp, C.c_longlong, _vp]),
     "s8b_codec_payload_bytes": (_sz, [_i, _i, _i, _i]),
     "s8b_codec_scale_count": (_sz, [_i, _i, _i]),
     "s8b_codec_encode": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _i, _vp]),

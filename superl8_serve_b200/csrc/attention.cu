@@ -1104,40 +1104,70 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
         s1[h] = t1 < cnt ? __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(a1[h])), qsc), ks1)
                          : -__int_as_float(0x7f800000);
       }
+      // The reductions below are latency chains on the stage's critical path: one redux per
+      // head, all heads issued back to back.
+      float red[G];
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float m = warp_max(fmaxf(s0[h], s1[h]));
-        if (lane == 0) red_s[q4 * 8 + h] = m;
+      for (int h = 0; h < G; ++h) red[h] = warp_max_redux(fmaxf(s0[h], s1[h]));
+      if (lane == 0) {
+#pragma unroll
+        for (int h = 0; h < G; ++h) red_s[q4 * 8 + h] = red[h];
       }
       group_sync(1 + grp, 128);
+      // Loads, then arithmetic, then stores: a store into E may alias the reductions' shared
+      // memory as far as the compiler knows, so interleaving them would chain the heads' exp
+      // latencies one after another.
       float *E = reinterpret_cast<float *>(st + kOffE);
       float w0[G], w1[G], mh[G];
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
+      for (int h = 0; h < G; ++h)
         mh[h] = fmaxf(fmaxf(red_s[h], red_s[8 + h]), fmaxf(red_s[16 + h], red_s[24 + h]));
-        const float e0 = t0 < cnt ? exp_s8b(__fsub_rn(s0[h], mh[h])) : 0.0f;
-        const float e1 = t1 < cnt ? exp_s8b(__fsub_rn(s1[h], mh[h])) : 0.0f;
-        E[h * kPart + t0] = e0;
-        E[h * kPart + t1] = e1;
-        w0[h] = t0 < cnt ? __fmul_rn(e0, vs0) : 0.0f;
-        w1[h] = t1 < cnt ? __fmul_rn(e1, vs1) : 0.0f;
+      // All 2G exponentials unconditionally (a conditional call puts each ~400-cycle chain
+      // behind its own branch; unconditional, they overlap). A masked token's score is -inf,
+      // so its exp is 0 either way; the select below keeps the CUDA-core kernel's form.
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        w0[h] = exp_s8b(__fsub_rn(s0[h], mh[h]));  // e, until stored
+        w1[h] = exp_s8b(__fsub_rn(s1[h], mh[h]));
       }
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        const float wm = warp_max(fmaxf(w0[h], w1[h]));
-        if (lane == 0) red_w[q4 * 8 + h] = wm;
+        w0[h] = t0 < cnt ? w0[h] : 0.0f;
+        w1[h] = t1 < cnt ? w1[h] : 0.0f;
+        E[h * kPart + t0] = w0[h];
+        E[h * kPart + t1] = w1[h];
+        w0[h] = t0 < cnt ? __fmul_rn(w0[h], vs0) : 0.0f;
+        w1[h] = t1 < cnt ? __fmul_rn(w1[h], vs1) : 0.0f;
+      }
+#pragma unroll
+      for (int h = 0; h < G; ++h) red[h] = warp_max_redux(fmaxf(w0[h], w1[h]));
+      if (lane == 0) {
+#pragma unroll
+        for (int h = 0; h < G; ++h) red_w[q4 * 8 + h] = red[h];
       }
       group_sync(1 + grp, 128);
-      float wsc_h[G];
+      float wm[G];  // per-head weight maxima; their /32767 scales wait until after wfull
+      int qa[G], qb[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h)
+        wm[h] = fmaxf(fmaxf(red_w[h], red_w[8 + h]), fmaxf(red_w[16 + h], red_w[24 + h]));
+      // 32767 / wm: one correctly rounded division per lane (lane h takes head h), shuffled to
+      // the warp, instead of G divisions in a row in every thread.
+      float wl = 1.0f;
+#pragma unroll
+      for (int h = 0; h < G; ++h) wl = lane == h ? wm[h] : wl;
+      const float winv_l = __fdiv_rn(32767.0f, wl);
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        const float wm = fmaxf(fmaxf(red_w[h], red_w[8 + h]), fmaxf(red_w[16 + h], red_w[24 + h]));
-        wsc_h[h] = __fdiv_rn(wm, 32767.0f);
-        const float winv = __fdiv_rn(32767.0f, wm);
-        int q0 = t0 < cnt ? __float2int_rn(__fmul_rn(w0[h], winv)) : 0;
-        int q1 = t1 < cnt ? __float2int_rn(__fmul_rn(w1[h], winv)) : 0;
-        q0 = q0 < 0 ? 0 : (q0 > 32767 ? 32767 : q0);
-        q1 = q1 < 0 ? 0 : (q1 > 32767 ? 32767 : q1);
+        const float winv = __shfl_sync(0xffffffffu, winv_l, h);
+        const int q0 = __float2int_rn(__fmul_rn(w0[h], winv));
+        const int q1 = __float2int_rn(__fmul_rn(w1[h], winv));
+        qa[h] = t0 < cnt ? (q0 < 0 ? 0 : (q0 > 32767 ? 32767 : q0)) : 0;
+        qb[h] = t1 < cnt ? (q1 < 0 ? 0 : (q1 > 32767 ? 32767 : q1)) : 0;
+      }
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const int q0 = qa[h], q1 = qb[h];
         // rows 16*plane + h of the K-major SW128 weight operand; t0 lies in token block 0 and
         // t1 in block 1 at the same in-block position
         const int off = h * 128 + ((((t0 >> 4) ^ (h & 7))) << 4) + (t0 & 15);
@@ -1164,7 +1194,7 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
         if (lane == 0) {
           st_t[h] = mh[h];
           st_t[8 + h] = l;
-          st_t[16 + h] = wsc_h[h];
+          st_t[16 + h] = __fdiv_rn(wm[h], 32767.0f);
         }
       }
       group_sync(1 + grp, 128);

@@ -91,12 +91,16 @@ template <typename T> __device__ __forceinline__ float round_to(float x) {
 // exp(x) by range reduction to 2^t = 2^k * 2^f (k = rint(t), |f| <= 1/2) and the degree-7
 // Taylor polynomial of 2^f = sum (f ln2)^i / i!. Coefficients are the binary32 roundings of
 // ln(2)^i / i!; Horner with separate multiply and add; 2^k built from its exponent bits.
+// Written without branches (the out-of-range cases are selects), so that a thread's
+// independent calls interleave. rint(tc) comes from adding and subtracting 1.5 * 2^23: for
+// |tc| <= 127 the sum's round-to-nearest-even lands exactly on rint(tc), and k's integer value
+// sits in the sum's low mantissa bits (no float-to-int conversion on the chain).
 __device__ __forceinline__ float exp_s8b(float x) {
   const float t = __fmul_rn(x, 0x1.715476p+0f);  // x * log2(e)
-  if (t < -125.0f) return 0.0f;
-  if (t > 127.0f) return __int_as_float(0x7f800000);
-  const float k = rintf(t);
-  const float f = __fsub_rn(t, k);
+  const float tc = fminf(fmaxf(t, -125.0f), 127.0f);  // == t wherever the result is finite
+  const float kb = __fadd_rn(tc, 0x1.8p23f);
+  const float k = __fsub_rn(kb, 0x1.8p23f);      // rint(tc)
+  const float f = __fsub_rn(tc, k);
   float p = 0x1.ffcbfcp-17f;
   p = __fadd_rn(__fmul_rn(p, f), 0x1.430912p-13f);
   p = __fadd_rn(__fmul_rn(p, f), 0x1.5d87fep-10f);
@@ -105,7 +109,18 @@ __device__ __forceinline__ float exp_s8b(float x) {
   p = __fadd_rn(__fmul_rn(p, f), 0x1.ebfbe0p-3f);
   p = __fadd_rn(__fmul_rn(p, f), 0x1.62e430p-1f);
   p = __fadd_rn(__fmul_rn(p, f), 1.0f);
-  return __fmul_rn(p, __int_as_float((static_cast<int>(k) + 127) << 23));
+  const int ki = __float_as_int(kb) - 0x4B400000;  // k as an integer, in [-125, 127]
+  float r = __fmul_rn(p, __int_as_float((ki + 127) << 23));
+  r = t < -125.0f ? 0.0f : r;
+  r = t > 127.0f ? __int_as_float(0x7f800000) : r;
+  return t != t ? t : r;  // NaN in, NaN out
+}
+
+// Warp-wide maximum in one instruction (sm_100a). NaN inputs are ignored, as with fmaxf.
+__device__ __forceinline__ float warp_max_redux(float v) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
 }
 
 constexpr float kHadScale = 0x1.6a09e6p-4f;  // binary32 rounding of 128^-1/2

@@ -116,3 +116,21 @@ extern "C" int s8b_argmax(const void *logits, int M, int V, int32_t *out, int dt
                          static_cast<const T *>(logits), V, out));
   return check_launch();
 }
+
+// The library's exponential (exp_s8b: the softmax, the partition merge, SiLU), elementwise,
+// so that its values can be checked against the CPU definition bit for bit.
+__global__ void exp_kernel(const float *__restrict__ x, float *__restrict__ y, long long n) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    y[i] = exp_s8b(x[i]);
+}
+
+extern "C" int s8b_exp_f32(const float *x, float *y, long long n, void *stream) {
+  if (n < 0) return S8B_ERR_SHAPE;
+  if (n == 0) return S8B_OK;
+  if (!x || !y) return S8B_ERR_ARG;
+  const long long blocks = (n + 255) / 256;
+  exp_kernel<<<static_cast<unsigned>(blocks < 4096 ? blocks : 4096), 256, 0,
+               (cudaStream_t)stream>>>(x, y, n);
+  return check_launch();
+}

@@ -263,6 +263,16 @@ def argmax(logits, *, out=None):
     return out
 
 
+def exp_s8b(x):
+    """The library's binary32 exponential, elementwise (fp32 CUDA tensor in, same shape out)."""
+    if x.dtype != torch.float32 or not x.is_cuda:
+        raise RuntimeError("exp_s8b: fp32 CUDA tensor required")
+    x = x.contiguous()
+    y = torch.empty_like(x)
+    call("s8b_exp_f32", ptr(x), ptr(y), x.numel(), stream(x.device))
+    return y
+
+
 def codec_sizes(T: int, D: int, scheme: str) -> tuple[int, int]:
     """(payload bytes, fp32 scale count) of one encoded [T, D] block."""
     from ._lib import load

@@ -47,6 +47,7 @@ def test_strerror_and_version(lib):
     lambda L: L.s8b_paged_decode_q8(*([None] * 11), 1, 4, 2, 128, 16, 4, 64, 0.1, None, 0, 0, None),
     lambda L: L.s8b_codec_encode(None, None, 1, 128, 0, 1, None, None, 0, None),
     lambda L: L.s8b_flag_wait(None, None, 0, 1000, None, None),
+    lambda L: L.s8b_exp_f32(None, None, 5, None),
 ])
 def test_null_arguments_are_rejected_without_touching_the_gpu(lib, call):
     assert call(lib) == -8

@@ -299,3 +299,21 @@ def test_flag_wait_times_out_and_reports(rng):
     call("s8b_flag_wait", ptr(flag), ptr(epoch), 1, 1_000_000_000, ptr(status), stream())
     torch.cuda.synchronize()
     assert status.cpu().tolist()[0] == 0 and flag.item() == 6
+
+
+def test_exp_matches_definition_bitwise():
+    """exp_s8b on the GPU (the softmax / merge / SiLU exponential) equals the CPU definition
+    bit for bit over every 97th binary32 pattern (both signs, all exponents, NaN and inf)
+    plus the range-reduction boundaries."""
+    from superl8_serve_b200 import ops
+
+    bits = np.arange(0, 1 << 32, 97, dtype=np.uint64).astype(np.uint32)
+    edge = np.array([-125.0, -124.5, 126.5, 127.0, 127.5], dtype=np.float32) / on.LOG2E
+    x = np.concatenate([bits.view(np.float32), edge.astype(np.float32),
+                        np.array([0.0, -0.0, np.inf, -np.inf, np.nan], dtype=np.float32)])
+    got = ops.exp_s8b(torch.from_numpy(x).cuda()).cpu().numpy()
+    with np.errstate(all="ignore"):
+        want = on.exp_s8b(x)
+    nan = np.isnan(want)
+    assert np.array_equal(np.isnan(got), nan)
+    assert np.array_equal(got[~nan].view(np.uint32), want[~nan].view(np.uint32))
