@@ -229,42 +229,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!a.wpacked)
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_w)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_x)) : "memory");
-      auto unit_of = [&](long long i, int *tile, int *kk) {
-        *tile = cid + static_cast<int>(i / nk) * a.nclusters;
-        *kk = k_lo + static_cast<int>(i % nk);
-      };
-      auto load_a = [&](long long i, uint8_t *sa, uint64_t *bar) {
+      // Unit i is (tile cid + (i / nk) * nclusters, K chunk k_lo + i % nk). The (tile, kk)
+      // pair advances by a compare and an add: a 64-bit division per unit costs this one
+      // thread several hundred nanoseconds, which would pace the whole weight stream.
+      struct UnitPos {
         int tile, kk;
-        unit_of(i, &tile, &kk);
+      };
+      auto advance = [&](UnitPos &u) {
+        if (++u.kk == k_hi) {
+          u.kk = k_lo;
+          u.tile += a.nclusters;
+        }
+      };
+      auto load_a = [&](const UnitPos &u, uint8_t *sa, uint64_t *bar) {
         if (a.wpacked)
-          bulk_load(sa, a.wpacked + (static_cast<size_t>(tile) * a.kc + kk) * kABytes, kABytes, bar);
+          bulk_load(sa, a.wpacked + (static_cast<size_t>(u.tile) * a.kc + u.kk) * kABytes, kABytes,
+                    bar);
         else
-          tma_load_2d(sa, &tmap_w, kk * kBK, tile * kBM, bar);
+          tma_load_2d(sa, &tmap_w, u.kk * kBK, u.tile * kBM, bar);
       };
-      auto load_b = [&](long long i, uint8_t *sa, uint64_t *bar) {
-        int tile, kk;
-        unit_of(i, &tile, &kk);
-        tma_load_2d(sa + kABytes, &tmap_x, kk * kBK, a.m0, bar);
+      auto load_b = [&](const UnitPos &u, uint8_t *sa, uint64_t *bar) {
+        tma_load_2d(sa + kABytes, &tmap_x, u.kk * kBK, a.m0, bar);
       };
       // weights of the first stages before the previous kernel has finished
-      const long long pre = n_units < S ? n_units : S;
-      for (long long i = 0; i < pre; ++i) {
-        uint8_t *sa = smem + static_cast<size_t>(i) * Lay::kStageBytes;
+      const int pre = n_units < S ? static_cast<int>(n_units) : S;
+      UnitPos u{cid, k_lo};
+      for (int i = 0; i < pre; ++i, advance(u)) {
         mbar_expect_tx(&hdr->full[i], Lay::kStageBytes);
-        load_a(i, sa, &hdr->full[i]);
+        load_a(u, smem + static_cast<size_t>(i) * Lay::kStageBytes, &hdr->full[i]);
       }
       griddep_wait();
-      for (long long i = 0; i < pre; ++i)
-        load_b(i, smem + static_cast<size_t>(i) * Lay::kStageBytes, &hdr->full[i]);
+      {
+        UnitPos v{cid, k_lo};
+        for (int i = 0; i < pre; ++i, advance(v))
+          load_b(v, smem + static_cast<size_t>(i) * Lay::kStageBytes, &hdr->full[i]);
+      }
       long long issued = pre;
-      for (long long i = pre; i < n_units; ++i, ++issued) {
-        const int s = static_cast<int>(i % S);
-        const uint32_t ph = static_cast<uint32_t>((i / S) & 1);
+      int s = pre % S;
+      uint32_t ph = pre == S ? 1u : 0u;  // phase parity of stage s's next fill
+      for (long long i = pre; i < n_units; ++i, ++issued, advance(u)) {
         if (!mbar_wait(&hdr->empty[s], ph ^ 1, abort, a.status)) break;
         uint8_t *sa = smem + static_cast<size_t>(s) * Lay::kStageBytes;
         mbar_expect_tx(&hdr->full[s], Lay::kStageBytes);
-        load_a(i, sa, &hdr->full[s]);
-        load_b(i, sa, &hdr->full[s]);
+        load_a(u, sa, &hdr->full[s]);
+        load_b(u, sa, &hdr->full[s]);
+        if (++s == S) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
       if (*abort) {
         // let the copies already issued land before the CTA's shared memory goes away
@@ -277,17 +289,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     // -------------------------------------------------------------- MMA issuer ----
     if (lane == 0) {
       constexpr uint32_t idesc = i8_idesc(kBM, NT);
-      int seg = 0;
+      int seg = 0, kk = 0, s = 0;  // counters, no per-unit division
+      uint32_t ph = 0;
       for (long long i = 0; i < n_units && !*abort; ++i) {
-        const int kk = static_cast<int>(i % nk);
         const bool first = kk == 0, last = kk == nk - 1;
         const int buf = seg & 1;
         if (first) {
           if (!mbar_wait(&hdr->tmem_empty[buf], ((seg >> 1) & 1) ^ 1, abort, a.status)) break;
           tc_fence_after();
         }
-        const int s = static_cast<int>(i % S);
-        if (!mbar_wait(&hdr->full[s], static_cast<uint32_t>((i / S) & 1), abort, a.status)) break;
+        if (!mbar_wait(&hdr->full[s], ph, abort, a.status)) break;
         tc_fence_after();
         const uint32_t sa = smem_u32(smem + static_cast<size_t>(s) * Lay::kStageBytes);
         const uint64_t ad = sw128_desc(sa), bd = sw128_desc(sa + kABytes);
@@ -298,6 +309,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (last) {
           mma_commit(&hdr->tmem_full[buf]);
           ++seg;
+        }
+        kk = last ? 0 : kk + 1;
+        if (++s == S) {
+          s = 0;
+          ph ^= 1u;
         }
       }
     }
