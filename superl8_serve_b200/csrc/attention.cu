@@ -1260,68 +1260,91 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
 
 // Merge of the persistent kernel's partials, one CTA per row: per head M = max m_p,
 // w_p = exp(m_p - M), L = sum w_p l_p, O = sum w_p o_p (partition order), out = dtype(O / L),
-// then the row's int8 quantization for o_proj. Same arithmetic as merge_epilogue. Latency is
-// the cost here, so every (m, l) pair and the first kMergeChunk partials of every value are
-// loaded before anything waits on them.
+// then the row's int8 quantization for o_proj. Same arithmetic as merge_epilogue. The kernel
+// is one latency chain, so it is laid out for overlap: each thread first issues its partial
+// loads (float4, the first CH partitions of its 4 values); the Hq x P exponentials run one per
+// thread; only the partition-order sums (L per head, O per value) are sequential.
 constexpr int kMergeThreads = 1024;
-constexpr int kMergeChunk = 8;
-template <typename T, int VPT>
+template <typename T, int VPT>  // VPT: 4-value vectors of the row per thread
 __global__ void __launch_bounds__(kMergeThreads)
     attn_merge_rows_kernel(DecodeWs ws, const int32_t *__restrict__ context_lens, int Hq, int P,
                            T *__restrict__ out, int8_t *__restrict__ out_q,
                            float *__restrict__ out_s) {
+  constexpr int CH = VPT == 1 ? 8 : 4;  // partitions whose partials are loaded up front
   griddep_launch();  // the next kernel may start its prologue
   griddep_wait();    // launched with programmatic serialization
-  extern __shared__ float msm[];  // [Hq][P] (m, l) pairs, then weights; [Hq] denominators
+  extern __shared__ float msm[];  // W [Hq][P] weights, WL [Hq][P] w * l, L [Hq]
   __shared__ float red[32];
   const int b = blockIdx.x, tid = threadIdx.x;
   const int np = (context_lens[b] + kPart - 1) / kPart;
-  const int nv = Hq * kHd;
+  const int nv4 = Hq * (kHd / 4);
   const float *mlb = ws.part_ml + static_cast<size_t>(b) * Hq * P * 2;
   const float *pob = ws.part_o + static_cast<size_t>(b) * Hq * P * kHd;
-  float x[VPT][kMergeChunk];
+  float4 x[VPT][CH];
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
-    const int i = tid + j * kMergeThreads, h = i / kHd, d = i % kHd;
+    const int i4 = tid + j * kMergeThreads, h = i4 / (kHd / 4), d = 4 * (i4 % (kHd / 4));
 #pragma unroll
-    for (int q = 0; q < kMergeChunk; ++q)
-      x[j][q] = (i < nv && q < np) ? pob[(static_cast<size_t>(h) * P + q) * kHd + d] : 0.0f;
+    for (int q = 0; q < CH; ++q)
+      x[j][q] = (i4 < nv4 && q < np)
+                    ? *reinterpret_cast<const float4 *>(pob + (static_cast<size_t>(h) * P + q) * kHd + d)
+                    : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   }
-  for (int i = tid; i < Hq * P * 2; i += kMergeThreads) msm[i] = mlb[i];
-  __syncthreads();
-  float *Wp = msm, *Lh = msm + 2 * Hq * P;
-  for (int h = tid; h < Hq; h += kMergeThreads) {
-    const float *ml = msm + h * P * 2;
-    float M = -__int_as_float(0x7f800000);
-    for (int q = 0; q < np; ++q) M = fmaxf(M, ml[2 * q]);
-    float Ls = 0.0f;
-    for (int q = 0; q < np; ++q) {
+  float *W = msm, *WL = msm + Hq * P, *Lh = msm + 2 * Hq * P;
+  for (int t = tid; t < Hq * P; t += kMergeThreads) {
+    const int h = t / P, q = t - (t / P) * P;
+    if (q < np) {
+      const float *ml = mlb + static_cast<size_t>(h) * P * 2;
+      float M = -__int_as_float(0x7f800000);
+      for (int r = 0; r < np; ++r) M = fmaxf(M, ml[2 * r]);
       const float w = exp_s8b(__fsub_rn(ml[2 * q], M));
-      Ls = __fadd_rn(Ls, __fmul_rn(w, ml[2 * q + 1]));
-      Wp[h * P * 2 + 2 * q] = w;  // overwrites m_q, already consumed
+      W[t] = w;
+      WL[t] = __fmul_rn(w, ml[2 * q + 1]);
     }
+  }
+  __syncthreads();
+  for (int h = tid; h < Hq; h += kMergeThreads) {
+    float Ls = 0.0f;
+    for (int q = 0; q < np; ++q) Ls = __fadd_rn(Ls, WL[h * P + q]);
     Lh[h] = Ls;
   }
   __syncthreads();
-  T *orow = out + static_cast<size_t>(b) * nv;
-  float v[VPT];
+  float v[VPT][4];
   float amax = 0.0f;
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
-    const int i = tid + j * kMergeThreads;
-    v[j] = 0.0f;
-    if (i < nv) {
-      const int h = i / kHd, d = i % kHd;
-      const float *wh = Wp + h * P * 2;
-      float O = 0.0f;
+    const int i4 = tid + j * kMergeThreads, h = i4 / (kHd / 4), d = 4 * (i4 % (kHd / 4));
+    if (i4 < nv4) {
+      const float *wh = W + h * P;
+      float O[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-      for (int q = 0; q < kMergeChunk; ++q)
-        if (q < np) O = __fadd_rn(O, __fmul_rn(wh[2 * q], x[j][q]));
-      for (int q = kMergeChunk; q < np; ++q)
-        O = __fadd_rn(O, __fmul_rn(wh[2 * q], pob[(static_cast<size_t>(h) * P + q) * kHd + d]));
-      v[j] = round_to<T>(__fdiv_rn(O, Lh[h]));
-      orow[i] = from_f32<T>(v[j]);
-      amax = fmaxf(amax, fabsf(v[j]));
+      for (int q = 0; q < CH; ++q) {
+        if (q < np) {
+          const float wq = wh[q];
+          O[0] = __fadd_rn(O[0], __fmul_rn(wq, x[j][q].x));
+          O[1] = __fadd_rn(O[1], __fmul_rn(wq, x[j][q].y));
+          O[2] = __fadd_rn(O[2], __fmul_rn(wq, x[j][q].z));
+          O[3] = __fadd_rn(O[3], __fmul_rn(wq, x[j][q].w));
+        }
+      }
+      for (int q = CH; q < np; ++q) {
+        const float4 xq = *reinterpret_cast<const float4 *>(pob + (static_cast<size_t>(h) * P + q) * kHd + d);
+        const float wq = wh[q];
+        O[0] = __fadd_rn(O[0], __fmul_rn(wq, xq.x));
+        O[1] = __fadd_rn(O[1], __fmul_rn(wq, xq.y));
+        O[2] = __fadd_rn(O[2], __fmul_rn(wq, xq.z));
+        O[3] = __fadd_rn(O[3], __fmul_rn(wq, xq.w));
+      }
+      const float L = Lh[h];
+      T o4[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        v[j][c] = round_to<T>(__fdiv_rn(O[c], L));
+        o4[c] = from_f32<T>(v[j][c]);
+        amax = fmaxf(amax, fabsf(v[j][c]));
+      }
+      *reinterpret_cast<uint2 *>(out + static_cast<size_t>(b) * nv4 * 4 + 4 * i4) =
+          *reinterpret_cast<const uint2 *>(o4);
     }
   }
   if (!out_q) return;
@@ -1329,8 +1352,15 @@ __global__ void __launch_bounds__(kMergeThreads)
   const QParams qp = qparams(amax, 127.0f);
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
-    const int i = tid + j * kMergeThreads;
-    if (i < nv) out_q[static_cast<size_t>(b) * nv + i] = static_cast<int8_t>(qcode(v[j], qp.inv, 127));
+    const int i4 = tid + j * kMergeThreads;
+    if (i4 < nv4) {
+      char4 c;
+      c.x = static_cast<signed char>(qcode(v[j][0], qp.inv, 127));
+      c.y = static_cast<signed char>(qcode(v[j][1], qp.inv, 127));
+      c.z = static_cast<signed char>(qcode(v[j][2], qp.inv, 127));
+      c.w = static_cast<signed char>(qcode(v[j][3], qp.inv, 127));
+      *reinterpret_cast<char4 *>(out_q + static_cast<size_t>(b) * nv4 * 4 + 4 * i4) = c;
+    }
   }
   if (tid == 0) out_s[b] = qp.scale;
 }
@@ -1376,6 +1406,7 @@ int launch_persistent(const int8_t *q_i8, const float *q_s, const int8_t *kc, co
   const int G = Hq / Hkv;
   const size_t merge_smem = 4 * (2 * static_cast<size_t>(Hq) * P + Hq);
   if (bs < 8 || B > pk::kMaxRows || Hq * kHd > kMergeThreads * 8 || merge_smem > 96 * 1024 ||
+      !aligned(out, 8) || !aligned(out_q, 4) ||
       !aligned(ks, 16) || !aligned(vs, 16) || !aligned(q_i8, 16))
     return 1;
   const size_t kb = tc::bytes_to_alloc_end(kc), vb = tc::bytes_to_alloc_end(vc);
@@ -1412,11 +1443,8 @@ int launch_persistent(const int8_t *q_i8, const float *q_s, const int8_t *kc, co
     default:
       return S8B_ERR_SHAPE;
   }
-  const int vpt = (Hq * kHd + kMergeThreads - 1) / kMergeThreads;
-  auto merge = vpt <= 1 ? attn_merge_rows_kernel<T, 1>
-               : vpt <= 2 ? attn_merge_rows_kernel<T, 2>
-               : vpt <= 4 ? attn_merge_rows_kernel<T, 4>
-                          : attn_merge_rows_kernel<T, 8>;
+  const int vpt = (Hq * kHd / 4 + kMergeThreads - 1) / kMergeThreads;
+  auto merge = vpt <= 1 ? attn_merge_rows_kernel<T, 1> : attn_merge_rows_kernel<T, 2>;
   ensure_smem(reinterpret_cast<const void *>(merge), 96 * 1024);
   launch_pdl(merge, B, kMergeThreads, merge_smem, st, w, context_lens, Hq, P,
              static_cast<T *>(out), out_q, out_s);
