@@ -43,12 +43,20 @@ __device__ __forceinline__ void store_codes(int8_t *dst, const float v[4], float
   *reinterpret_cast<char4 *>(dst) = c;
 }
 
-// Row-wide totals over a cluster of CL CTAs that split one row: each CTA's block total is
-// published in its shared memory, the cluster barrier orders the writes, and every CTA adds
-// the CL totals in rank order (the same order in every CTA).
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
+// Row-wide totals over a cluster of CL CTAs that split one row, by pushing: each CTA stores
+// its block total into slot `rank` of every CTA's array with st.async, which completes on
+// that CTA's mbarrier as a byte count, and then waits on its own mbarrier until all CL values
+// are in; every CTA reduces its array in rank order (the same order in every CTA). One
+// one-way transfer per reduction instead of a cluster barrier, and since no CTA reads a
+// peer's shared memory, none has to wait for its peers before it exits. The only cluster
+// barrier (the peers' mbarriers must be initialised before anything is sent) is split:
+// arrive at kernel entry, wait just before the first send, so the row loads hide it.
+constexpr int kMaxRowCluster = 4;
+struct ClusterRed {
+  uint64_t bar[2];  // [0]: double totals, [1]: float maxima (each used once per launch)
+  double d[kMaxRowCluster];
+  float f[kMaxRowCluster];
+};
 __device__ __forceinline__ uint32_t dsmem_addr(const void *p, int rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
@@ -57,31 +65,75 @@ __device__ __forceinline__ uint32_t dsmem_addr(const void *p, int rank) {
   return r;
 }
 template <int CL>
-__device__ __forceinline__ double cluster_total_d(double v, double *slot) {
+__device__ __forceinline__ void cred_init(ClusterRed *r) {
+  if (CL == 1) return;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(
+          static_cast<uint32_t>(__cvta_generic_to_shared(&r->bar[i]))));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+template <int CL>
+__device__ __forceinline__ void cred_ready() {
+  if (CL > 1) asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Sends `bits` (the value's 8 or 4 bytes) to every CTA's slot and waits (bounded) for this
+// CTA's CL slots. Returns false on timeout (the caller poisons its output).
+template <int CL, int BYTES>
+__device__ __forceinline__ bool cred_exchange(uint64_t bits, void *slots, uint64_t *bar, int rank) {
+  const uint32_t lbar = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
+  if (threadIdx.x == 0) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(lbar), "r"(CL * BYTES)
+                 : "memory");
+#pragma unroll
+    for (int q = 0; q < CL; ++q) {
+      const uint32_t dst = dsmem_addr(static_cast<uint8_t *>(slots) + rank * BYTES, q);
+      const uint32_t rb = dsmem_addr(bar, q);
+      if (BYTES == 8)
+        asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b64 [%0], %1, [%2];" ::"r"(dst),
+                     "l"(bits), "r"(rb)
+                     : "memory");
+      else
+        asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(dst),
+                     "r"(static_cast<uint32_t>(bits)), "r"(rb)
+                     : "memory");
+    }
+  }
+  uint64_t t0 = 0;
+  for (int it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], 0;\n"
+        "selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(lbar)
+        : "memory");
+    if (ok) return true;
+    uint64_t now;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+    if (it == 0) t0 = now;
+    if (now - t0 > 100000000ull) return false;  // 100 ms: a peer never sent
+  }
+}
+template <int CL>
+__device__ __forceinline__ double cluster_total_d(double v, ClusterRed *r, int rank, bool *ok) {
   if (CL == 1) return v;
-  if (threadIdx.x == 0) *slot = v;
-  cluster_sync_all();
+  *ok = cred_exchange<CL, 8>(static_cast<uint64_t>(__double_as_longlong(v)), r->d, &r->bar[0], rank) && *ok;
   double t = 0.0;
 #pragma unroll
-  for (int q = 0; q < CL; ++q) {
-    double x;
-    asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(x) : "r"(dsmem_addr(slot, q)) : "memory");
-    t += x;
-  }
+  for (int q = 0; q < CL; ++q) t += r->d[q];
   return t;
 }
 template <int CL>
-__device__ __forceinline__ float cluster_max(float v, float *slot) {
+__device__ __forceinline__ float cluster_max(float v, ClusterRed *r, int rank, bool *ok) {
   if (CL == 1) return v;
-  if (threadIdx.x == 0) *slot = v;
-  cluster_sync_all();
+  *ok = cred_exchange<CL, 4>(static_cast<uint64_t>(__float_as_uint(v)), r->f, &r->bar[1], rank) && *ok;
   float t = 0.0f;
 #pragma unroll
-  for (int q = 0; q < CL; ++q) {
-    float x;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(dsmem_addr(slot, q)) : "memory");
-    t = fmaxf(t, x);
-  }
+  for (int q = 0; q < CL; ++q) t = fmaxf(t, r->f[q]);
   return t;
 }
 template <int CL>
@@ -98,15 +150,14 @@ __global__ void __launch_bounds__(1024)
                     const T *__restrict__ w, float eps, int8_t *__restrict__ q,
                     float *__restrict__ s, T *__restrict__ y_out, int H) {
   griddep_launch();  // the next kernel may start its prologue
-  griddep_wait();    // launched with programmatic serialization
   __shared__ double redd[32];
   __shared__ float red[32];
-  __shared__ double cl_ss;
-  __shared__ float cl_amax;
-  // CL CTAs split the row: this CTA owns vectors [rank * nvec, (rank + 1) * nvec). Every
-  // global store comes after the last cluster barrier, so the barriers' release never waits
-  // on outstanding stores.
+  __shared__ ClusterRed cr;
+  cred_init<CL>(&cr);
+  griddep_wait();    // launched with programmatic serialization
+  // CL CTAs split the row: this CTA owns vectors [rank * nvec, (rank + 1) * nvec).
   const int m = blockIdx.x / CL, rank = cluster_rank_of<CL>(), nvec = (H >> 2) / CL;
+  bool ok = true;
   const size_t off = static_cast<size_t>(m) * H;
   float x[VPT][4], xr[VPT][4], wg[VPT][4];
   double ss = 0.0;
@@ -135,7 +186,9 @@ __global__ void __launch_bounds__(1024)
       }
     }
   }
-  ss = cluster_total_d<CL>(block_sum_d(ss, redd), &cl_ss);
+  ss = block_sum_d(ss, redd);
+  cred_ready<CL>();
+  ss = cluster_total_d<CL>(ss, &cr, rank, &ok);
   const float rf = rms_factor(ss, H, eps);
   float amax = 0.0f;
 #pragma unroll
@@ -148,9 +201,8 @@ __global__ void __launch_bounds__(1024)
       }
     }
   }
-  amax = cluster_max<CL>(block_max(amax, red), &cl_amax);
-  if (CL > 1) cluster_sync_all();  // peers have read this CTA's totals
-  const QParams p = qparams(amax, 127.0f);
+  amax = cluster_max<CL>(block_max(amax, red), &cr, rank, &ok);
+  const QParams p = qparams(ok ? amax : __int_as_float(0x7fffffff), 127.0f);  // timeout: NaN scale
 #pragma unroll
   for (int v = 0; v < VPT; ++v) {
     const int i = rank * nvec + threadIdx.x + v * blockDim.x;
@@ -178,10 +230,12 @@ __global__ void __launch_bounds__(1024)
     silu_mul_quant_v(RowSrc<T> gu, int F, T *__restrict__ y_out, int8_t *__restrict__ q,
                      float *__restrict__ s) {
   griddep_launch();  // the next kernel may start its prologue
-  griddep_wait();    // launched with programmatic serialization
   __shared__ float red[32];
-  __shared__ float cl_amax;
+  __shared__ ClusterRed cr;
+  cred_init<CL>(&cr);
+  griddep_wait();    // launched with programmatic serialization
   const int m = blockIdx.x / CL, rank = cluster_rank_of<CL>(), nvec = (F >> 2) / CL;
+  bool ok = true;
   float y[VPT][4];
   float amax = 0.0f;
 #pragma unroll
@@ -200,9 +254,10 @@ __global__ void __launch_bounds__(1024)
       }
     }
   }
-  amax = cluster_max<CL>(block_max(amax, red), &cl_amax);
-  if (CL > 1) cluster_sync_all();  // peers have read this CTA's maximum; stores after it
-  const QParams p = qparams(amax, 127.0f);
+  amax = block_max(amax, red);
+  cred_ready<CL>();
+  amax = cluster_max<CL>(amax, &cr, rank, &ok);
+  const QParams p = qparams(ok ? amax : __int_as_float(0x7fffffff), 127.0f);  // timeout: NaN scale
   const size_t off = static_cast<size_t>(m) * F;
 #pragma unroll
   for (int v = 0; v < VPT; ++v) {
@@ -298,7 +353,7 @@ namespace s8b {
 namespace {
 // Rows of >= 128 vectors are split over a 4-CTA cluster (latency: more SMs per row, each
 // CTA a quarter of the loads); shorter rows keep one CTA per row.
-constexpr int kRowCluster = 4;
+constexpr int kRowCluster = kMaxRowCluster;
 inline int row_cluster(int nvec) { return (nvec % kRowCluster == 0 && nvec / kRowCluster >= 32) ? kRowCluster : 1; }
 
 template <typename T>
