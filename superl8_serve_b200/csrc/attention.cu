@@ -835,6 +835,7 @@ namespace pk {
 constexpr int kStages = 3;
 constexpr int kStage = 70656;  // K/W/E 32 KB | V 32 KB | Q 2 KB | K, V scales 1 KB each | q scales
 constexpr int kOffV = 32768, kOffQ = 65536, kOffKs = 67584, kOffVs = 68608, kOffQs = 69632;
+constexpr int kOffMode = 70144;  // 1: the unit's blocks landed in reverse order (one 4-D copy)
 constexpr int kWBlock = 6144;  // one 128-token block of the 48-row weight operand
 constexpr int kOffE = 12288;   // e values [G][256] floats, after the two weight blocks
 constexpr int kThreads = 512;
@@ -874,6 +875,8 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     attn_persistent_kernel(const __grid_constant__ CUtensorMap map_k,
                            const __grid_constant__ CUtensorMap map_v,
                            const __grid_constant__ CUtensorMap map_q,
+                           const __grid_constant__ CUtensorMap map_k4,
+                           const __grid_constant__ CUtensorMap map_v4, int runs,
                            const float *__restrict__ q_s, const float *__restrict__ ks,
                            const float *__restrict__ vs, const int32_t *__restrict__ block_table,
                            const int32_t *__restrict__ context_lens, int B, int Hq, int Hkv,
@@ -932,17 +935,17 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
   if (warp == 0 || warp == 14) {
     // ----------------------------------------------------------------- producers ----
     const bool vwarp = warp == 14;
-    const CUtensorMap *map = vwarp ? &map_v : &map_k;
     auto next_valid = [&](UnitIter &it) {
       while (it.b < B && it.p * kPart >= ctx[it.b]) it.next();
     };
-    auto block_row = [&](const UnitIter &it) {  // this lane's KV block row (0 past the end)
-      if (it.b >= B) return 0;
+    auto block_id = [&](const UnitIter &it) {  // this lane's KV block id (-1 past the end)
+      if (it.b >= B) return -1;
       const int nblk = (min(kPart, ctx[it.b] - it.p * kPart) + bs - 1) >> bs_log2;
-      if (lane >= nblk) return 0;
-      return (block_table[static_cast<size_t>(it.b) * max_blocks + ((it.p * kPart) >> bs_log2) +
-                          lane] * Hkv + it.g) << bs_log2;
+      if (lane >= nblk) return -1;
+      return block_table[static_cast<size_t>(it.b) * max_blocks + ((it.p * kPart) >> bs_log2) +
+                         lane];
     };
+    const int nbu = kPart >> bs_log2;  // blocks of a full partition
     // block-table rows three units ahead: under full HBM load a table miss takes a few us
     int k = 0;
     UnitIter i0(blockIdx.x, gridDim.x, P, Hkv);
@@ -953,28 +956,48 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     UnitIter i2 = i1;
     i2.next();
     next_valid(i2);
-    int row0 = block_row(i0), row1 = block_row(i1), row2 = block_row(i2);
+    int blk0 = block_id(i0), blk1 = block_id(i1), blk2 = block_id(i2);
     while (i0.b < B) {
-      const int row = row0;
+      const int blk = blk0;
       UnitIter i3 = i2;
       i3.next();
       next_valid(i3);
-      row0 = row1;
-      row1 = row2;
-      row2 = block_row(i3);
+      blk0 = blk1;
+      blk1 = blk2;
+      blk2 = block_id(i3);
       const int p = i0.p, g = i0.g, b = i0.b;
       const int cnt = min(kPart, ctx[b] - p * kPart);
       const int nblk = (cnt + bs - 1) >> bs_log2;
+      const int row = (blk * Hkv + g) << bs_log2;  // this lane's block rows (lanes < nblk)
+      // A full partition on consecutive block ids (ascending, or descending as the reference's
+      // allocator hands them out) moves in one 4-D copy per tensor instead of nblk 2-D copies,
+      // each of which costs its warp ~50 ns to issue. Descending runs land in reverse block
+      // order; the softmax then stores its exponentials at the canonical token index.
+      const int b0 = __shfl_sync(0xffffffffu, blk, 0);
+      const bool asc = runs && nblk == nbu && __all_sync(0xffffffffu, lane >= nblk || blk == b0 + lane);
+      // (reversed only for a partition with every token present: the softmax masks the
+      // tokens past the context end by shared-memory row)
+      const bool desc = runs && cnt == kPart && !asc &&
+                        __all_sync(0xffffffffu, lane >= nblk || blk == b0 - lane);
       const int s = k % kStages;
       bool ok = true;
       if (lane == 0 && k >= kStages)
         ok = mbar_wait(&empty[s], ((k / kStages) - 1) & 1, abort_flag, ws.status);
       if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
       uint8_t *st = sm + s * kStage;
-      if (lane == 0)
+      if (lane == 0) {
+        if (!vwarp) st[kOffMode] = desc ? 1 : 0;  // before the arrive that publishes the stage
         mbar_expect_tx(&full[s], static_cast<uint32_t>(nblk * bs * kHd + (vwarp ? 0 : G * kHd)));
+      }
       __syncwarp();
-      if (lane < nblk) tma_load_2d(st + (vwarp ? kOffV : 0) + lane * bs * kHd, map, 0, row, &full[s]);
+      if (asc || desc) {
+        if (lane == 0)
+          tma_load_4d(st + (vwarp ? kOffV : 0), vwarp ? &map_v4 : &map_k4, 0, 0, g,
+                      desc ? b0 - (nbu - 1) : b0, &full[s]);
+      } else if (lane < nblk) {
+        tma_load_2d(st + (vwarp ? kOffV : 0) + lane * bs * kHd, vwarp ? &map_v : &map_k, 0, row,
+                    &full[s]);
+      }
       if (!vwarp) {
         if (lane == 0) tma_load_2d(st + kOffQ, &map_q, 0, b * Hq + g * G, &full[s]);
         i0 = i1;
@@ -987,8 +1010,8 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int c = lane + 32 * (i & 1);  // chunk within the array
-        const int j = (4 * c) >> bs_log2;   // block of that chunk
-        const int rj = __shfl_sync(0xffffffffu, row, j & 31);
+        const int j = (4 * c) >> bs_log2;   // smem block of that chunk
+        const int rj = __shfl_sync(0xffffffffu, row, (desc ? nbu - 1 - j : j) & 31);
         if (4 * c < nblk * bs) {
           const float *src = (i < 2 ? ks : vs) + rj + ((4 * c) & (bs - 1));
           cp_async16(st + (i < 2 ? kOffKs : kOffVs) + 16 * c, src);
@@ -1095,6 +1118,11 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
       const float *vsc = reinterpret_cast<const float *>(st + kOffVs);
       const float *qsv = reinterpret_cast<const float *>(st + kOffQs);
       const float ks0 = ksc[t0], ks1 = ksc[t1], vs0 = vsc[t0], vs1 = vsc[t1];
+      // canonical token index of shared-memory rows t0 and t1 (blocks reversed: see producers)
+      const bool rev = st[kOffMode] != 0;
+      const int nbu = kPart >> bs_log2;
+      const int et0 = rev ? (((nbu - 1 - (t0 >> bs_log2)) << bs_log2) | (t0 & (bs - 1))) : t0;
+      const int et1 = rev ? (((nbu - 1 - (t1 >> bs_log2)) << bs_log2) | (t1 & (bs - 1))) : t1;
       float s0[G], s1[G];
 #pragma unroll
       for (int h = 0; h < G; ++h) {
@@ -1134,8 +1162,8 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
       for (int h = 0; h < G; ++h) {
         w0[h] = t0 < cnt ? w0[h] : 0.0f;
         w1[h] = t1 < cnt ? w1[h] : 0.0f;
-        E[h * kPart + t0] = w0[h];
-        E[h * kPart + t1] = w1[h];
+        E[h * kPart + et0] = w0[h];
+        E[h * kPart + et1] = w1[h];
         w0[h] = t0 < cnt ? __fmul_rn(w0[h], vs0) : 0.0f;
         w1[h] = t1 < cnt ? __fmul_rn(w1[h], vs1) : 0.0f;
       }
@@ -1414,11 +1442,23 @@ int launch_persistent(const int8_t *q_i8, const float *q_s, const int8_t *kc, co
   if (rows_k < static_cast<uint64_t>(bs) || rows_v < static_cast<uint64_t>(bs) ||
       rows_k > 0xffffffffull || rows_v > 0xffffffffull)
     return 1;
-  CUtensorMap mk, mv, mq;
+  CUtensorMap mk, mv, mq, mk4, mv4;
   if (tc::make_map_2d(&mk, kc, kHd, rows_k, kHd, kHd, bs) ||
       tc::make_map_2d(&mv, vc, kHd, rows_v, kHd, kHd, bs) ||
       tc::make_map_2d(&mq, q_i8, kHd, static_cast<uint64_t>(B) * Hq, kHd, kHd, G))
     return 1;
+  // 4-D maps for partitions on consecutive blocks: whole blocks of all heads within the
+  // allocation; without them (too small, or an encode failure) every unit takes 2-D copies
+  const int nbu = kPart / bs;
+  const uint64_t nb_k = rows_k / (static_cast<uint64_t>(bs) * Hkv);
+  const uint64_t nb_v = rows_v / (static_cast<uint64_t>(bs) * Hkv);
+  const int runs = nb_k >= static_cast<uint64_t>(nbu) && nb_v >= static_cast<uint64_t>(nbu) &&
+                   tc::make_map_kv4(&mk4, kc, bs, Hkv, nb_k, nbu) == S8B_OK &&
+                   tc::make_map_kv4(&mv4, vc, bs, Hkv, nb_v, nbu) == S8B_OK;
+  if (!runs) {
+    mk4 = mk;
+    mv4 = mv;
+  }
   const long U = static_cast<long>(B) * Hkv * P;
   const int grid = static_cast<int>(U < tc::sm_count() ? U : tc::sm_count());
   switch (G) {
@@ -1426,7 +1466,8 @@ int launch_persistent(const int8_t *q_i8, const float *q_s, const int8_t *kc, co
   case GG: {                                                                                   \
     auto kern = attn_persistent_kernel<T, GG>;                                                  \
     ensure_smem(reinterpret_cast<const void *>(kern), pk::kSmem);                               \
-    launch_pdl(kern, grid, pk::kThreads, pk::kSmem, st, mk, mv, mq, q_s, ks, vs, block_table,   \
+    launch_pdl(kern, grid, pk::kThreads, pk::kSmem, st, mk, mv, mq, mk4, mv4, runs, q_s, ks, vs, \
+               block_table,                                                                    \
                                                 context_lens, B, Hq, Hkv, bs_log2, max_blocks,  \
                                                 P, scale, w);                                   \
     break;                                                                                     \

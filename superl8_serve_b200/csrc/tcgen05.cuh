@@ -70,6 +70,15 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int c0, int c1,
+                                            int c2, int c3, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Bounded wait that ignores the abort flag: used on the way out of an aborted kernel, to let
 // copies already in flight land before the CTA's shared memory is released.
 __device__ __forceinline__ bool mbar_drain(uint64_t *bar, uint32_t parity,
@@ -192,6 +201,24 @@ inline int make_map_2d(CUtensorMap *map, const void *base, uint64_t inner, uint6
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? S8B_OK : S8B_ERR_ALIGN;
+}
+
+// 4-D tiled map over a paged KV pool laid out [blocks][heads][rows][128 B] (dims innermost
+// first: 128 bytes, rows per block, heads, blocks), box {128, rows, 1, nb}: one head's rows of
+// nb consecutive blocks, landing in block order with the same 128B swizzle as the 2-D row maps.
+inline int make_map_kv4(CUtensorMap *map, const void *base, uint32_t rows, uint32_t heads,
+                        uint64_t nblocks, uint32_t nb) {
+  auto fn = encode_fn();
+  if (!fn) return S8B_ERR_CUDA;
+  const cuuint64_t dims[4] = {128, rows, heads, nblocks};
+  const cuuint64_t strides[3] = {128, 128ull * rows, 128ull * rows * heads};
+  const cuuint32_t box[4] = {128, rows, 1, nb};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void *>(base), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);

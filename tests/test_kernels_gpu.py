@@ -205,6 +205,64 @@ def test_paged_decode_bit_exact(rng, attn_impl, B, Hq, Hkv, lens, bs):
     assert np.array_equal(oq.cpu().numpy(), rq) and np.array_equal(osc.cpu().numpy(), rs)
 
 
+def _block_table(layout, B, maxb, nb, rng):
+    """Block tables in the orders an allocator produces: consecutive ascending ids per row,
+    the reference allocator's order (free list range(nb), pop from the end: descending runs),
+    descending runs with one pair swapped in every row (runs broken), or a random permutation."""
+    bt = np.zeros((B, maxb + 2), dtype=np.int32)
+    if layout == "ascending":
+        for b in range(B):
+            bt[b, :maxb] = np.arange(b * maxb, (b + 1) * maxb)
+    elif layout in ("descending", "broken"):
+        free = list(range(nb))
+        for b in range(B):
+            bt[b, :maxb] = [free.pop() for _ in range(maxb)]
+            if layout == "broken" and maxb >= 3:
+                bt[b, [1, 2]] = bt[b, [2, 1]]
+    else:
+        perm = rng.permutation(nb)
+        for b in range(B):
+            bt[b, :maxb] = perm[b * maxb:(b + 1) * maxb]
+    return bt
+
+
+@pytest.mark.parametrize("layout", ["ascending", "descending", "broken"])
+@pytest.mark.parametrize("B,Hq,Hkv,lens,bs", [
+    (4, 32, 8, [1, 17, 256, 257], 16),       # one full partition; full + partial
+    (3, 16, 8, [600, 33, 1000], 16),         # several full partitions per row
+    (1, 32, 4, [4096], 16),                  # 16 full partitions
+    (3, 8, 8, [128, 129, 511], 32),          # 8 blocks per partition
+    (2, 21, 3, [300, 64], 64),               # 4 blocks per partition
+    (2, 24, 8, [255, 700], 256),             # one block per partition
+])
+def test_paged_decode_block_runs(rng, attn_impl, B, Hq, Hkv, lens, bs, layout):
+    """Partitions on consecutive blocks take one 4-D copy per tensor in the persistent kernel
+    (descending runs land reversed in shared memory); results stay bit-exact."""
+    from superl8_serve_b200 import ops
+
+    maxb = (max(lens) + bs - 1) // bs
+    nb = B * maxb + 3
+    kc, ks, vc, vs = make_pool(rng, nb, Hkv, bs)
+    bt = _block_table(layout, B, maxb, nb, rng)
+    qq = rng.integers(-127, 128, (B, Hq, 128), dtype=np.int8)
+    qs = rng.uniform(0.002, 0.02, (B, Hq)).astype(np.float32)
+    cl = np.array(lens, dtype=np.int32)
+    scale = 128 ** -0.5
+    qqd, qsd, kcd, ksd, vcd, vsd, btd, cld = to_dev(qq, qs, kc, ks, vc, vs, bt, cl)
+    oq = torch.empty((B, Hq * 128), dtype=torch.int8, device=DEV)
+    osc = torch.empty(B, dtype=torch.float32, device=DEV)
+    max_ctx = min(max(lens) + 5, bt.shape[1] * bs)
+    ws = torch.zeros(ops.decode_workspace_bytes(B, Hq, 128, max_ctx), dtype=torch.uint8,
+                     device=DEV)
+    out = ops.paged_decode_q8(qqd, qsd, kcd, ksd, vcd, vsd, btd, cld, max_ctx, scale,
+                              out_q=oq, out_s=osc, workspace=ws)
+    assert ops.decode_status(ws, B, Hq) == 0
+    ref = ok.paged_decode(qq, qs, kc, ks, vc, vs, bt, cl, bs, scale).reshape(B, -1)
+    assert np.array_equal(f32(out), ref)
+    rq, rs = on.quant_rows_i8(ref)
+    assert np.array_equal(oq.cpu().numpy(), rq) and np.array_equal(osc.cpu().numpy(), rs)
+
+
 def test_paged_decode_reference_layout(rng):
     """s8b_paged_decode takes the reference's [B, H, 1, D] bf16 query."""
     from superl8_serve_b200 import ops
