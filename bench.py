@@ -225,10 +225,10 @@ def time_kernel(fn, reps: int) -> float:
 # launch shape (profiles/attn_persistent_qwen3_8b_b64_ctx2048.md,
 # profiles/gemm_tc_gate_up_qwen3_8b_m64.md); re-captured whenever the kernel changes.
 NCU_TRAFFIC = {
-    "paged_decode_attention": {"bytes": 279351552 + 9443584,
+    "paged_decode_attention": {"bytes": 279351808 + 10228480,
                                "source": "ncu dram bytes of attn_persistent_kernel (the row "
                                          "merge reads its 8.4 MB of partials from L2)"},
-    "gemm_w8a8_tc_gate_up": {"bytes": 100976896 + 4232704,
+    "gemm_w8a8_tc_gate_up": {"bytes": 100976128 + 4385024,
                              "source": "ncu dram bytes of gemm_tc_kernel (gate_up launch)"},
 }
 
