@@ -407,6 +407,64 @@ def run_single(args):
     print(json.dumps(line), flush=True)
 
 
+def run_prefill(args):
+    """Varlen prefill of ``--batch`` prompts of ``--ctx`` random tokens each (Qwen3-8B shape,
+    one GPU, 256-row chunks): prompt tokens/s, device-timed with CUDA events around whole
+    ``prefill()`` calls (host ids H2D at the start, first tokens D2H at the end)."""
+    from superl8_serve_b200 import _lib
+    from superl8_serve_b200.config import qwen3_8b
+    from superl8_serve_b200.engine import DecodePipeline
+    from superl8_serve_b200.runtime import StageModel
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    cfg = qwen3_8b()
+    if args.layers:
+        cfg = cfg.with_(num_hidden_layers=args.layers)
+    B, P = args.batch, args.ctx
+    model = StageModel.synthetic(cfg, 0, cfg.num_hidden_layers, dev, first=True, last=True, seed=1)
+    pipe = DecodePipeline([model], batch=B, n_micro=1, max_len=P + 16, wire_scheme=args.scheme)
+    rng = np.random.default_rng(3)
+    prompts = rng.integers(0, cfg.vocab_size, (B, P)).tolist()
+    for _ in range(args.warmup):
+        pipe.prefill(prompts)
+    torch.cuda.synchronize()
+    n0 = _lib.load().s8b_launch_count()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        time.sleep(0.3)
+        a.record()
+        for _ in range(args.steps):
+            pipe.prefill(prompts)
+        b.record()
+        b.synchronize()
+    launches = _lib.load().s8b_launch_count() - n0
+    ms = a.elapsed_time(b) / args.steps
+    tokens = B * P
+    H, F, D = cfg.hidden_size, cfg.intermediate_size, 128
+    nh, nkv = cfg.num_attention_heads, cfg.num_key_value_heads
+    params = cfg.num_hidden_layers * (((nh + 2 * nkv) * D + 2 * F) * H + H * nh * D + H * F)
+    gemm_ops = 2.0 * params * tokens + 2.0 * cfg.vocab_size * H * B
+    # attention: q.k and p.v over the causal prefix of every row, every head
+    attn_ops = cfg.num_hidden_layers * B * nh * 4.0 * D * (P * (P + 1) / 2)
+    _, bf16_peak, peak_kind = peaks()
+    line = {
+        "metric": "prefill tokens/s (varlen prefill, one GPU)", "value": tokens / (ms / 1e3),
+        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 x int8 -> int32 GEMM, bf16 activations",
+        "data": "synthetic (random int8 weights, uniform-random prompt ids)",
+        "config": {"workload": "qwen3-8b-shaped W8A8 varlen prefill", "prompts": B,
+                   "prompt_len": P, "layers": cfg.num_hidden_layers,
+                   "chunk_rows": pipe.prefill_chunk, "parallelism": "pp1"},
+        "gpu_launches": int(launches), "clocks": clk.summary(),
+        "tensor": {"gemm_tops": gemm_ops / ms / 1e9, "attn_tops": attn_ops / ms / 1e9,
+                   "int8_peak_tops": 2 * bf16_peak, "peak_kind": peak_kind + " (2 x bf16)",
+                   "gemm_frac": gemm_ops / ms / 1e9 / (2 * bf16_peak)},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -417,6 +475,8 @@ def main():
     ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--scheme", default="int8-had")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mode", default="decode", choices=["decode", "prefill"],
+                    help="prefill: varlen prefill throughput of --batch prompts of --ctx tokens")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: fewer layers than the model's 36 (small ncu case)")
     args = ap.parse_args()
@@ -424,6 +484,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.mode == "prefill":
+        return run_prefill(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world > 1 or args.gpus > 1:
         from superl8_serve_b200.multistage import run_bench_multi

@@ -212,3 +212,36 @@ class OraclePipeline:
                     sq.append(int(toks[i]))
             step += 1
         return outs, logit_log
+
+    def prefill(self, prompts):
+        """``PipelineEngine._prefill`` (``superl8serve/dist/pipeline.py:908-984``): all prompt
+        tokens of all sequences as one varlen batch of rows (``cu_seqlens`` order), each row
+        writing its K/V at its position and attending over positions [0, t] of its sequence;
+        the argmax of each sequence's last row is its first generated token. Returns
+        (first tokens, their logits, slots)."""
+        slots = [self.pools[0].alloc() for _ in prompts]
+        for p in self.pools[1:]:
+            for _ in prompts:
+                p.alloc()
+        ids = np.array([t for p in prompts for t in p], dtype=np.int64)
+        row_slots = [slots[i] for i, p in enumerate(prompts) for _ in p]
+        positions = [t for p in prompts for t in range(len(p))]
+        toks, logits = self.decode(ids, row_slots, positions)
+        last = np.cumsum([len(p) for p in prompts]) - 1
+        return [int(toks[j]) for j in last], [logits[j] for j in last], slots
+
+    def generate_prefilled(self, prompts, max_new_tokens):
+        """Prefill, then greedy decode with every sequence at its own position."""
+        first, first_logits, slots = self.prefill(prompts)
+        outs = [[t] for t in first]
+        logit_log = [[lg] for lg in first_logits]
+        positions = [len(p) for p in prompts]
+        ids = np.array(first, dtype=np.int64)
+        for _ in range(max_new_tokens - 1):
+            toks, logits = self.decode(ids, slots, positions)
+            for i in range(len(prompts)):
+                outs[i].append(int(toks[i]))
+                logit_log[i].append(logits[i])
+            ids = np.asarray(toks, dtype=np.int64)
+            positions = [p + 1 for p in positions]
+        return outs, logit_log

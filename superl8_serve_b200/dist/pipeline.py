@@ -7,8 +7,10 @@ int8 weights on its GPU and gives each stage a paged KV pool sized to its own la
 ``engine.DecodePipeline``: micro-batches flow stage to stage with the codec fused at every
 boundary and no host synchronisation inside a step.
 
-Differences from the reference, all on purpose: prompts are consumed by decode steps (the
-varlen prefill path is a separate, later component), sampling is greedy-only (temperature /
+Prompts go through the varlen prefill first (``DecodePipeline.prefill``, the reference's
+``_prefill`` at ``:908-984``), then every sequence decodes from its own length.
+
+Differences from the reference, all on purpose: sampling is greedy-only (temperature /
 top-k / top-p are not on this path), and the boundary scheme is fixed per engine
 (``wire_scheme``, default "int8") instead of re-running the int4 gate every step, which
 would need a host read-back inside the step.
@@ -130,13 +132,15 @@ class PipelineEngine:
 
     def __init__(self, stage0: PipelineStage, stage1: PipelineStage, cfg, *, max_num_seqs: int = 16,
                  max_len: int = 2048, max_batch_tokens: int = 8192, eos_id: int | None = None,
-                 wire_scheme: str | None = None, n_micro: int | None = None):
+                 wire_scheme: str | None = None, n_micro: int | None = None,
+                 prefill: bool = True):
         self.stages = (stage0, stage1)
         self.cfg = cfg
         self.max_num_seqs, self.max_len = max_num_seqs, max_len
         self.eos_id = eos_id
         self.wire_scheme = wire_scheme or "int8"
         self.n_micro = n_micro
+        self.prefill = prefill  # False: prompts teacher-forced through decode steps
         self._ids = itertools.count()
         self._pending: dict[int, tuple[list[int], SamplingParams]] = {}
         self._out: dict[int, list[int]] = {}
@@ -182,7 +186,7 @@ class PipelineEngine:
         if any(p.temperature != 0.0 for p in params):
             raise NotImplementedError("only greedy sampling is on the s8b decode path")
         max_new = max(p.max_tokens for p in params)
-        outs = self._pipeline(len(prompts)).generate(prompts, max_new)
+        outs = self._pipeline(len(prompts)).generate(prompts, max_new, prefill=self.prefill)
         for sid, out, p in zip(ids, outs, params):
             out = out[: p.max_tokens]
             if self.eos_id is not None and self.eos_id in out:

@@ -74,6 +74,9 @@ class DecodePipeline:
     ``n_micro`` micro-batches of ``m = ceil(batch / n_micro)`` rows.
     """
 
+    # prompt tokens per prefill launch sequence (the tensor-core GEMM's token tile limit)
+    PREFILL_CHUNK = 256
+
     def __init__(self, models: list[StageModel], *, batch: int, n_micro: int = 1,
                  max_len: int = 2048, block_size: int = 16, wire_scheme: str = "int8-had",
                  num_blocks: int | None = None, dtype=torch.bfloat16):
@@ -121,6 +124,9 @@ class DecodePipeline:
         self.slots: list[int] = []
         self.graph = self.graph_io = None
         self.rows = [min(self.m, batch - k * self.m) for k in range(n_micro)]
+        self.dtype = dtype
+        self.prefill_chunk = self.PREFILL_CHUNK
+        self._pf = None
 
     # ----------------------------------------------------------------- sequence state ----
     def add_sequences(self, n: int | None = None):
@@ -238,13 +244,117 @@ class DecodePipeline:
         for mdl in self.models:
             torch.cuda.synchronize(mdl.device)
 
+    # ---------------------------------------------------------------------- prefill ----
+    def _prefill_state(self):
+        """Prefill runners (``prefill_chunk`` rows, packed weights shared with the decode
+        runners) and one boundary buffer per stage boundary."""
+        if self._pf is not None and self._pf[0][0].m == self.prefill_chunk:
+            return self._pf
+        mp = self.prefill_chunk
+        runners = [StageRunner(mdl, pool, mp, self.max_len, self.dtype, share=r)
+                   for mdl, pool, r in zip(self.models, self.pools, self.runners)]
+        from .ops import codec_sizes
+
+        nbytes, nsc = codec_sizes(mp, 2 * self.cfg.hidden_size, self.wire_scheme)
+        bufs = [(torch.empty(nbytes, dtype=torch.uint8, device=self.models[s + 1].device),
+                 torch.empty(max(nsc, 1), dtype=torch.float32, device=self.models[s + 1].device),
+                 self.wire_scheme) for s in range(self.S - 1)]
+        self._pf = (runners, bufs)
+        return self._pf
+
+    def prefill(self, prompts: list[list[int]], *, reserve: int = 1, keep_logits: bool = False):
+        """Varlen batched prefill (``PipelineEngine._prefill``,
+        ``superl8serve/dist/pipeline.py:908-984``): every prompt token of every sequence is
+        one row; rows are packed sequence after sequence (the reference's ``cu_seqlens``
+        order) into chunks of ``prefill_chunk`` rows, and each chunk runs through every
+        stage with the codec at each boundary.
+
+        Row (sequence i, position t) writes its K/V at t and attends over positions [0, t]
+        of the paged cache (context length t + 1), after the same layer's KV write of the
+        whole chunk, so it computes exactly what a decode step of that token computes: the
+        result is bit-identical to feeding the prompt one token per step. The final norm,
+        LM head and argmax run only in chunks where some sequence ends; the argmax of each
+        sequence's last row is its first generated token (returned, one per sequence; with
+        ``keep_logits`` also that row's logits). Block capacity is reserved for
+        ``len(prompt) + reserve`` tokens.
+
+        The row state of all chunks (ids, positions, context lengths, block-table rows) goes
+        to each stage's device in one pinned copy and every chunk reads a view of it, so the
+        chunks are enqueued back to back with one host synchronisation at the end.
+        """
+        n = len(prompts)
+        if n != self.batch:
+            raise ValueError("prefill() expects exactly `batch` prompts")
+        if any(len(p) == 0 for p in prompts):
+            raise ValueError("prefill() needs a non-empty prompt for every sequence")
+        if not self.slots:
+            self.add_sequences(n)
+        self.alloc.ensure_capacity(self.slots, [len(p) + reserve for p in prompts])
+        bt = self.alloc.block_table(self.slots)
+        runners, bufs = self._prefill_state()
+        seq = torch.tensor([i for i, p in enumerate(prompts) for _ in p], dtype=torch.long)
+        pos = torch.cat([torch.arange(len(p), dtype=torch.int32) for p in prompts])
+        ids = torch.tensor([t for p in prompts for t in p], dtype=torch.int32)
+        host = [x.pin_memory() for x in (ids, pos, pos + 1, bt[seq])]
+        T = len(seq)
+        state = []  # per stage: (ids, positions, context_lens, block_table), all T rows
+        for s, mdl in enumerate(self.models):
+            st = torch.cuda.current_stream(mdl.device) if self.single_device else self.streams[s]
+            with torch.cuda.device(mdl.device), torch.cuda.stream(st):
+                state.append([x.to(mdl.device, non_blocking=True) for x in host])
+        # a single stage reads and writes ids in place (argmax after embed, per chunk); a
+        # last stage after others writes its own array
+        out_ids = state[-1][0] if self.S == 1 else torch.empty_like(state[-1][0])
+        ends = torch.cumsum(torch.tensor([len(p) for p in prompts]), 0) - 1
+        lg_rows = None
+        if keep_logits:
+            lg_rows = torch.empty(n, self.cfg.vocab_size, dtype=self.dtype,
+                                  device=self.models[-1].device)
+        ev = [self.events[s][0] for s in range(self.S)]
+        end_list = ends.tolist()
+        for c0 in range(0, T, self.prefill_chunk):
+            r = min(self.prefill_chunk, T - c0)
+            chunk_ends = [(i, e - c0) for i, e in enumerate(end_list) if c0 <= e < c0 + r]
+            for s in range(self.S):
+                dev = self.models[s].device
+                st = torch.cuda.current_stream(dev) if self.single_device else self.streams[s]
+                with torch.cuda.device(dev), torch.cuda.stream(st):
+                    if s > 0 and not self.single_device:
+                        st.wait_event(ev[s - 1])
+                    if s < self.S - 1 and not self.single_device:
+                        st.wait_event(ev[s + 1])  # stage s+1 has decoded the previous chunk
+                    a_ids, a_pos, a_ctx, a_bt = state[s]
+                    mb = MicroBatch(ids=(out_ids if s == self.S - 1 else a_ids)[c0:c0 + r],
+                                    positions=a_pos[c0:c0 + r], context_lens=a_ctx[c0:c0 + r],
+                                    block_table=a_bt[c0:c0 + r])
+                    runners[s].run(mb, r, boundary_in=bufs[s - 1] if s > 0 else None,
+                                   boundary_out=bufs[s] if s < self.S - 1 else None,
+                                   head=bool(chunk_ends))
+                    if s == self.S - 1 and keep_logits:
+                        row_bytes = self.cfg.vocab_size * lg_rows.element_size()
+                        for i, k in chunk_ends:
+                            call("s8b_memcpy_async", ptr(lg_rows[i]), ptr(runners[s].logits[k]),
+                                 row_bytes, stream())
+                    if not self.single_device:
+                        ev[s].record(st)
+        self.synchronize()
+        first = out_ids[ends.to(out_ids.device)].cpu().tolist()
+        if keep_logits:
+            return first, list(lg_rows.float().cpu())
+        return first
+
     # ------------------------------------------------------------------- generation ----
-    def generate(self, prompts: list[list[int]], max_new_tokens: int, *, keep_logits=False):
-        """Greedy generation; every row advances one token per step (prompt tokens are fed
-        teacher-forced, exactly as ``oracle.model.OraclePipeline.generate``)."""
+    def generate(self, prompts: list[list[int]], max_new_tokens: int, *, keep_logits=False,
+                 prefill: bool = False):
+        """Greedy generation. Without ``prefill`` every row advances one token per step and
+        prompt tokens are fed teacher-forced, exactly as ``oracle.model.OraclePipeline
+        .generate``; with ``prefill`` the prompts go through ``prefill()`` first and every
+        row then decodes from its own prompt length. Both give identical tokens and logits."""
         n = len(prompts)
         if n != self.batch:
             raise ValueError("generate() expects exactly `batch` prompts")
+        if prefill:
+            return self._generate_prefilled(prompts, max_new_tokens, keep_logits)
         if not self.slots:
             self.add_sequences(n)
         seqs = [list(p) for p in prompts]
@@ -269,4 +379,29 @@ class DecodePipeline:
                 if step + 1 >= len(sq):
                     sq.append(int(toks[i]))
             step += 1
+        return (outs, logit_log) if keep_logits else outs
+
+    def _generate_prefilled(self, prompts, max_new_tokens: int, keep_logits: bool):
+        res = self.prefill(prompts, reserve=max_new_tokens, keep_logits=keep_logits)
+        first, first_logits = res if keep_logits else (res, None)
+        outs = [[t] for t in first]
+        logit_log = [[lg] for lg in first_logits] if keep_logits else None
+        if max_new_tokens <= 0:
+            outs = [[] for _ in prompts]
+            return (outs, [[] for _ in prompts]) if keep_logits else outs
+        # every row decodes its first generated token at its prompt length; the argmax of
+        # each step feeds the next (positions advance on the device)
+        self.set_state([len(p) for p in prompts], first, reserve=max_new_tokens)
+        for _ in range(max_new_tokens - 1):
+            self._enqueue()
+            self.synchronize()
+            toks = self.tokens().cpu().tolist()
+            lg = None
+            if keep_logits:
+                lg = torch.cat([self.runners[-1].logits[: self.rows[k]].float().cpu()
+                                for k in range(self.n_micro)]) if self.n_micro == 1 else None
+            for i in range(len(prompts)):
+                outs[i].append(int(toks[i]))
+                if keep_logits and lg is not None:
+                    logit_log[i].append(lg[i])
         return (outs, logit_log) if keep_logits else outs

@@ -198,7 +198,10 @@ class StageRunner:
     TC_MIN_TOKENS = 16
 
     def __init__(self, model: StageModel, pool: KVPool, m: int, max_ctx: int,
-                 dtype=torch.bfloat16, tc_min_tokens: int | None = None):
+                 dtype=torch.bfloat16, tc_min_tokens: int | None = None,
+                 share: "StageRunner | None" = None):
+        """``share``: another runner of the same model whose packed tensor-core weight images
+        this one reuses (a prefill runner beside the decode runner holds no second copy)."""
         cfg = model.cfg
         self.model, self.pool, self.m, self.max_ctx, self.dtype = model, pool, m, max_ctx, dtype
         self.H = cfg.hidden_size
@@ -235,7 +238,9 @@ class StageRunner:
         self.tc_ws = ops.gemm_tc_workspace(m, n_max, dev) if m >= self.tc_min else None
         # tensor-core path: every weight also kept as contiguous unit images (packed once)
         self.packed: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
-        if self.tc_ws is not None:
+        if self.tc_ws is not None and share is not None and share.model is model and share.packed:
+            self.packed = share.packed
+        elif self.tc_ws is not None:
             mats = [w for L in model.layers for w in (L.qkv_w, L.o_w, L.gu_w, L.d_w)]
             if model.is_last:
                 mats.append(model.head_w)
@@ -335,11 +340,14 @@ class StageRunner:
         self._gemm(self.xq, self.xs, L.d_w, L.d_s, self.h, M)
         return None
 
-    def run(self, mb: MicroBatch, M: int | None = None, *, boundary_in=None, boundary_out=None):
+    def run(self, mb: MicroBatch, M: int | None = None, *, boundary_in=None, boundary_out=None,
+            head: bool = True):
         """Enqueue the stage's work for one micro-batch on the current stream.
 
         boundary_in: (payload, scales, scheme) received from the previous stage.
         boundary_out: (payload, scales, scheme) in the next stage's memory (may be a peer's).
+        head: on the last stage, run the final norm, LM head and argmax (a prefill chunk in
+        which no sequence ends needs only the layers, which fill the KV cache).
         """
         M = self.m if M is None else M
         st = stream()
@@ -357,6 +365,8 @@ class StageRunner:
             h_src = self.layer(li, mb, M, first_model_layer and li == 0, h_src=h_src,
                                keep_split=li < n - 1 or self.model.is_last)
         if self.model.is_last:
+            if not head:
+                return
             self._rms_quant(self.h, self.res, self.res, self.model.norm, M, self.H, src=h_src)
             self._gemm(self.xq, self.xs, self.model.head_w, self.model.head_s, self.logits, M)
             call("s8b_argmax", ptr(self.logits), M, self.V, ptr(mb.ids), 0, st)

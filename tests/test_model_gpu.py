@@ -43,6 +43,48 @@ def test_tiny_pipeline_matches_golden(golden_dir, tiny_sd, tag, stages, scheme, 
         assert np.array_equal(got, d[f"{tag}_logits"])
 
 
+@pytest.mark.parametrize("tag,stages,scheme,chunk", [
+    ("s1", 1, "int8", 256), ("s2_int8had", 2, "int8-had", 4), ("s3_int4had", 3, "int4-had", 7)])
+def test_prefill_then_decode_matches_golden(golden_dir, tiny_sd, tag, stages, scheme, chunk):
+    """Varlen chunked prefill (chunks of 4 and 7 rows cut sequences mid-prompt) then decode
+    from each sequence's own length: the reference graph's tokens and logits, bit for bit."""
+    d = np.load(golden_dir / "tiny_qwen3_decode.npz")
+    cfg, sd = tiny_sd
+    pipe = DecodePipeline(stage_models(cfg, sd, stages), batch=3, n_micro=1, max_len=64,
+                          wire_scheme=scheme)
+    pipe.prefill_chunk = chunk
+    outs, logits = pipe.generate(PROMPTS, 8, keep_logits=True, prefill=True)
+    assert np.array_equal(np.array(outs), d[f"{tag}_tokens"])
+    got = np.stack([np.stack([t.numpy() for t in row]) for row in logits])
+    assert np.array_equal(got, d[f"{tag}_logits"])
+
+
+def test_prefill_tensor_core_chunks_match_oracle(tiny_sd):
+    """Prompts of 40, 17 and 70 tokens in 64-row chunks: every chunk runs the tcgen05 GEMMs
+    with split-K partials; tokens and logits equal the oracle's prefill + decode."""
+    cfg, sd = tiny_sd
+    rng = np.random.default_rng(5)
+    prompts = [rng.integers(0, cfg.vocab_size, n).tolist() for n in (40, 17, 70)]
+    pipe = DecodePipeline(stage_models(cfg, sd, 2), batch=3, n_micro=1, max_len=128,
+                          wire_scheme="int8-had")
+    pipe.prefill_chunk = 64
+    outs, logits = pipe.generate(prompts, 6, keep_logits=True, prefill=True)
+    assert pipe._pf[0][0].tc_ws is not None
+    ref, ref_logits = OraclePipeline(cfg, quantize_state_dict(sd, cfg), n_stages=2,
+                                     wire_scheme="int8-had", num_slots=4,
+                                     max_len=128).generate_prefilled(prompts, 6)
+    assert outs == ref
+    got = np.stack([np.stack([t.numpy() for t in row]) for row in logits])
+    assert np.array_equal(got, np.array(ref_logits, dtype=np.float32))
+
+
+def test_prefill_rejects_empty_prompt(tiny_sd):
+    cfg, sd = tiny_sd
+    pipe = DecodePipeline(stage_models(cfg, sd, 1), batch=2, max_len=64)
+    with pytest.raises(ValueError):
+        pipe.prefill([[1, 2], []])
+
+
 def test_graph_replay_equals_eager(tiny_sd):
     cfg, sd = tiny_sd
     outs = []
@@ -89,6 +131,10 @@ def test_two_gpu_in_process_pipeline(tiny_sd):
     ref, _ = OraclePipeline(cfg, qw, n_stages=2, wire_scheme="int8", num_slots=4,
                             max_len=64).generate(PROMPTS, 8)
     assert outs == ref
+    pipe = DecodePipeline(stage_models(cfg, sd, 2, ["cuda:0", "cuda:1"]), batch=3, n_micro=1,
+                          max_len=64, wire_scheme="int8")
+    pipe.prefill_chunk = 4
+    assert pipe.generate(PROMPTS, 8, prefill=True) == ref
 
 
 @pytest.mark.slow
@@ -104,6 +150,12 @@ def test_config1_qwen3_0_6b_two_stage_greedy_parity():
                           wire_scheme="int8-had")
     assert stage_bounds(28, 2) == [0, 14, 28]
     outs, logits = pipe.generate(prompts, 32, keep_logits=True)
+    # the same prompts through the varlen prefill: 512 rows in two 256-row chunks
+    del pipe
+    pipe = DecodePipeline(stage_models(cfg, sd, 2), batch=4, n_micro=1, max_len=192,
+                          wire_scheme="int8-had")
+    outs_p, logits_p = pipe.generate(prompts, 32, keep_logits=True, prefill=True)
+    del pipe
     qw = quantize_state_dict(sd, cfg)
     del sd
     ref, ref_logits = OraclePipeline(cfg, qw, n_stages=2, wire_scheme="int8-had", num_slots=4,
@@ -113,4 +165,7 @@ def test_config1_qwen3_0_6b_two_stage_greedy_parity():
     want = np.array(ref_logits, dtype=np.float32)
     rel = np.abs(got - want).max() / np.abs(want).max()
     assert rel <= 1e-2
+    assert np.array_equal(got, want)
+    assert outs_p == ref
+    got = np.stack([np.stack([t.numpy() for t in row]) for row in logits_p])
     assert np.array_equal(got, want)

@@ -37,6 +37,19 @@ def test_oracle_pipeline_matches_reference_module_graph(golden_dir, tiny_qw, tag
     assert np.array_equal(np.array(logits, dtype=np.float32), d[f"{tag}_logits"])
 
 
+@pytest.mark.parametrize("tag,stages,scheme", [("s1", 1, "int8"), ("s3_int4had", 3, "int4-had")])
+def test_oracle_prefill_equals_teacher_forced_decode(golden_dir, tiny_qw, tag, stages, scheme):
+    """The varlen prefill (all prompt rows in one batch, each attending over its own prefix)
+    followed by per-sequence decode gives the reference graph's tokens and logits bit for
+    bit: a prompt row computes exactly what the decode step of that token computes."""
+    d = np.load(golden_dir / "tiny_qwen3_decode.npz")
+    cfg, qw = tiny_qw
+    p = OraclePipeline(cfg, qw, n_stages=stages, wire_scheme=scheme, num_slots=4, max_len=64)
+    outs, logits = p.generate_prefilled(PROMPTS, 8)
+    assert np.array_equal(np.array(outs), d[f"{tag}_tokens"])
+    assert np.array_equal(np.array(logits, dtype=np.float32), d[f"{tag}_logits"])
+
+
 def test_eager_rmsnorm_close_to_reference(golden_dir):
     e = np.load(golden_dir / "eager_numerics.npz")
     res = ok.add_residual(e["norm_x"], e["norm_r"])
