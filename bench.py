@@ -107,16 +107,16 @@ class CpuOracleSample:
     `batch`, context `ctx`, plus 1/`head_frac` of the LM head, extrapolated to the full
     36-layer step. Weights and the KV pool are built once; each run() is one sample."""
 
-    def __init__(self, batch=64, ctx=2048, head_frac=16, seed=0):
+    def __init__(self, batch=64, ctx=2048, head_frac=16, seed=0, cfg=None):
         from oracle.kernels import rope_tables
         from oracle.model import PagedPool, Shape
         from superl8_serve_b200.config import qwen3_8b
 
-        self.cfg = cfg = qwen3_8b()
+        self.cfg = cfg = cfg or qwen3_8b()
         self.batch, self.ctx, self.head_frac = batch, ctx, head_frac
         self.s = Shape(cfg.vocab_size, cfg.hidden_size, 1, cfg.num_attention_heads,
                        cfg.num_key_value_heads, 128, cfg.intermediate_size, 1e-6, 1e6, ctx + 8,
-                       False)
+                       False, cfg.num_experts, cfg.num_experts_per_tok, cfg.norm_topk_prob)
         rng = np.random.default_rng(seed)
         H, F, D = self.s.hidden_size, self.s.intermediate_size, 128
         nh, nkv = self.s.num_attention_heads, self.s.num_key_value_heads
@@ -126,9 +126,14 @@ class CpuOracleSample:
                     np.full(n, 0.02 / 73.3, dtype=np.float32))
 
         g = lambda n: (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)  # noqa: E731
-        self.L = {"qkv": w((nh + 2 * nkv) * D, H), "o": w(H, nh * D), "gu": w(2 * F, H),
-                  "down": w(H, F), "in_norm": g(H), "post_norm": g(H), "q_norm": g(D),
-                  "k_norm": g(D)}
+        self.L = {"qkv": w((nh + 2 * nkv) * D, H), "o": w(H, nh * D), "in_norm": g(H),
+                  "post_norm": g(H), "q_norm": g(D), "k_norm": g(D)}
+        if cfg.num_experts:
+            Fe = cfg.moe_intermediate_size
+            self.L["router"] = (0.02 * rng.standard_normal((cfg.num_experts, H))).astype(np.float32)
+            self.L["experts"] = [(w(2 * Fe, H), w(H, Fe)) for _ in range(cfg.num_experts)]
+        else:
+            self.L["gu"], self.L["down"] = w(2 * F, H), w(H, F)
         pool = PagedPool(1, batch, nkv, ctx + 8, D)
         pool.kc[:] = rng.integers(-127, 128, pool.kc.shape, dtype=np.int8)
         pool.vc[:] = rng.integers(-127, 128, pool.vc.shape, dtype=np.int8)
@@ -146,7 +151,8 @@ class CpuOracleSample:
         self.hw, _ = w(cfg.vocab_size // head_frac, H)
         self.xq = rng.integers(-127, 128, (batch, H), dtype=np.int8)
         self.desc = (f"oracle (numpy, BLAS GEMMs on {os.cpu_count()} host threads, Python "
-                     f"attention loop): 1 of {cfg.num_hidden_layers} Qwen3-8B layers + "
+                     f"attention loop): 1 of {cfg.num_hidden_layers} layers"
+                     f"{' (sparse MoE)' if cfg.num_experts else ''} + "
                      f"1/{head_frac} of the LM head at batch {batch}, ctx {ctx}, extrapolated "
                      f"to one {cfg.num_hidden_layers}-layer decode step")
 
@@ -166,9 +172,9 @@ class CpuOracleSample:
         return self.batch / step, time.perf_counter() - t0
 
 
-def cpu_sample_tokens_per_s(batch=64, ctx=2048, n_layers=1, head_frac=16, seed=0):
+def cpu_sample_tokens_per_s(batch=64, ctx=2048, n_layers=1, head_frac=16, seed=0, cfg=None):
     """One CPU-oracle sample (see CpuOracleSample). Returns (tokens/s, seconds, description)."""
-    smp = CpuOracleSample(batch, ctx, head_frac, seed)
+    smp = CpuOracleSample(batch, ctx, head_frac, seed, cfg=cfg)
     v, spent = smp.run()
     return v, spent, smp.desc
 
@@ -182,7 +188,7 @@ def run_reference(args):
         return
     # one layer of the oracle takes ~10 s on the host: build once, warm once, and time at most
     # REF_MAX_SAMPLES samples so the whole run stays within a few minutes
-    smp = CpuOracleSample(batch=args.batch, ctx=args.ctx)
+    smp = CpuOracleSample(batch=args.batch, ctx=args.ctx, cfg=model_config(args.model))
     smp.run()
     vals, spent = [], 0.0
     for _ in range(min(args.steps, REF_MAX_SAMPLES)):
@@ -196,7 +202,7 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": args.batch / v * 1000.0, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": "qwen3-8b-shaped W8A8 decode, config 3", "micro_batch": args.batch,
+        "config": {"workload": CONFIG_NAMES[args.model], "micro_batch": args.batch,
                    "ctx": args.ctx, "stages": 1, "note": "superl8 kernels are not vendored; "
                    "the reference arm is the CPU oracle restating them"},
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
@@ -243,19 +249,38 @@ def kernel_rooflines(pipe, hbm_peak):
     M = pipe.rows[0]
     L = len(r.model.layers)
     out = {}
-    # W8A8 gate_up GEMM (largest weight matrix: 2F x H int8)
-    it = iter(range(10 ** 9))
-
-    def gemm():
-        li = next(it) % L
-        lw = r.model.layers[li]
-        r._gemm(r.xq, r.xs, lw.gu_w, lw.gu_s, r.gu, M)
-
-    ms = time_kernel(gemm, 4 * L)
     lw = r.model.layers[0]
-    N, K = lw.gu_w.shape
-    byts = N * K + N * 4 + M * K + M * 4 + M * N * 2
-    name = "gemm_w8a8_tc_gate_up" if r.tc_ws is not None and M >= r.tc_min else "gemm_w8a8_gate_up"
+    if lw.moe is None:
+        # W8A8 gate_up GEMM (largest weight matrix: 2F x H int8)
+        it = iter(range(10 ** 9))
+
+        def gemm():
+            li = next(it) % L
+            lw = r.model.layers[li]
+            r._gemm(r.xq, r.xs, lw.gu_w, lw.gu_s, r.gu, M)
+
+        ms = time_kernel(gemm, 4 * L)
+        N, K = lw.gu_w.shape
+        byts = N * K + N * 4 + M * K + M * 4 + M * N * 2
+        name = ("gemm_w8a8_tc_gate_up" if r.tc_ws is not None and M >= r.tc_min
+                else "gemm_w8a8_gate_up")
+    else:
+        # grouped expert gate_up GEMM on the routing the last step left behind
+        b, mw = r.moe_buf, lw.moe
+        A, Fe, E = M * mw.top_k, mw.ffn, mw.num_experts
+        it = iter(range(10 ** 9))
+
+        def gemm():
+            w = r.model.layers[next(it) % L].moe
+            call("s8b_moe_gemm_grouped", ptr(r.xq), ptr(r.xs), ptr(b["sorted_token"]),
+                 ptr(w.gu_w), ptr(w.gu_s), ptr(b["offsets"]), ptr(b["gu"]), A, 2 * Fe, r.H, E, 0,
+                 stream())
+
+        ms = time_kernel(gemm, 4 * L)
+        off = b["offsets"].cpu()
+        hit = int(((off[1:] - off[:-1]) > 0).sum())
+        byts = hit * (2 * Fe * r.H + 2 * Fe * 4) + M * r.H + 4 * M + A * 2 * Fe * 2 + 4 * A
+        name = "moe_gemm_grouped_gate_up"
     out[name] = {"ms": ms, "bytes": byts, "gbs": byts / ms / 1e6, "launches_per_step": L}
     # paged decode attention (partition + combine) for one layer
     it2 = iter(range(10 ** 9))
@@ -278,16 +303,43 @@ def kernel_rooflines(pipe, hbm_peak):
     return out
 
 
+MODELS = {"qwen3-8b": "qwen3_8b", "qwen3-30b-a3b": "qwen3_30b_a3b",
+          "qwen3-27b": "qwen3_27b_dense"}
+CONFIG_NAMES = {"qwen3-8b": "qwen3-8b-shaped W8A8 decode (BASELINE config 3)",
+                "qwen3-30b-a3b": "qwen3-30b-a3b-shaped MoE W8A8 decode (BASELINE config 4)",
+                "qwen3-27b": "27b-dense-shaped W8A8 long-context decode (BASELINE config 5)"}
+
+
+def model_config(name: str):
+    from superl8_serve_b200 import config
+
+    return getattr(config, MODELS[name])()
+
+
+def experts_hit(cfg, tokens: int) -> float:
+    """Expected number of distinct experts routed to by `tokens` tokens choosing top-k of E
+    uniformly (the synthetic router's regime)."""
+    E, k = cfg.num_experts, cfg.num_experts_per_tok
+    return E * (1.0 - (1.0 - k / E) ** tokens)
+
+
 def step_bytes(cfg, batch, ctx, layers, last):
     """Algorithmic HBM bytes of one decode step of one stage (weights + scales + KV read +
-    KV write + LM head on the last stage)."""
+    KV write + LM head on the last stage). A sparse-MoE layer streams the router and the
+    experts that the step's tokens route to (expected count for uniform routing)."""
     H, F, D = cfg.hidden_size, cfg.intermediate_size, 128
     nh, nkv = cfg.num_attention_heads, cfg.num_key_value_heads
-    rows = (nh + 2 * nkv) * D + H + 2 * F + H
-    w = layers * (((nh + 2 * nkv) * D + 2 * F) * H + H * nh * D + H * F + 4 * rows)
+    attn_w = ((nh + 2 * nkv) * D) * H + H * nh * D + 4 * ((nh + 2 * nkv) * D + H)
+    if getattr(cfg, "num_experts", 0):
+        Fe = cfg.moe_intermediate_size
+        expert = 2 * Fe * H + H * Fe + 4 * (2 * Fe + H)
+        ffn_w = 4 * cfg.num_experts * H + experts_hit(cfg, batch) * expert
+    else:
+        ffn_w = 2 * F * H + H * F + 4 * (2 * F + H)
+    w = layers * (attn_w + ffn_w)
     kv = layers * batch * (ctx * nkv * (2 * D + 8) + nkv * (2 * D + 8))
     head = (cfg.vocab_size * H + 4 * cfg.vocab_size) if last else 0
-    return w + kv + head
+    return int(w + kv + head)
 
 
 def run_single(args):
@@ -298,7 +350,7 @@ def run_single(args):
 
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
-    cfg = qwen3_8b()
+    cfg = model_config(args.model)
     if args.layers:
         cfg = cfg.with_(num_hidden_layers=args.layers)
     B, ctx = args.batch, args.ctx
@@ -380,7 +432,7 @@ def run_single(args):
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8 x int8 -> int32 GEMM, bf16 activations",
         "data": "synthetic (random int8 weights, KV pre-filled with random codes)",
-        "config": {"workload": "qwen3-8b-shaped W8A8 decode (BASELINE config 3)",
+        "config": {"workload": CONFIG_NAMES[args.model],
                    "micro_batch": B, "n_micro": 1, "global_batch": B, "ctx": ctx,
                    "layers": cfg.num_hidden_layers,
                    "block_size": 16, "parallelism": "pp1", "wire_scheme": args.scheme,
@@ -401,7 +453,8 @@ def run_single(args):
         "step_roofline": {"bytes": sb, "achieved_gbs": sb / ms / 1e6, "frac": sb / ms / 1e6 / hbm},
     }
     if not args.no_cpu_baseline:
-        v, spent, desc = cpu_sample_tokens_per_s(batch=B, ctx=ctx, n_layers=1)
+        v, spent, desc = cpu_sample_tokens_per_s(batch=B, ctx=ctx, n_layers=1,
+                                                 cfg=model_config(args.model))
         line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": os.cpu_count(),
                                 "kind": "port", "sample": desc, "seconds": spent}
     print(json.dumps(line), flush=True)
@@ -412,13 +465,12 @@ def run_prefill(args):
     one GPU, 256-row chunks): prompt tokens/s, device-timed with CUDA events around whole
     ``prefill()`` calls (host ids H2D at the start, first tokens D2H at the end)."""
     from superl8_serve_b200 import _lib
-    from superl8_serve_b200.config import qwen3_8b
     from superl8_serve_b200.engine import DecodePipeline
     from superl8_serve_b200.runtime import StageModel
 
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
-    cfg = qwen3_8b()
+    cfg = model_config(args.model)
     if args.layers:
         cfg = cfg.with_(num_hidden_layers=args.layers)
     B, P = args.batch, args.ctx
@@ -475,6 +527,9 @@ def main():
     ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--scheme", default="int8-had")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--model", default="qwen3-8b", choices=sorted(MODELS),
+                    help="qwen3-8b (config 3, default), qwen3-30b-a3b (config 4, MoE), "
+                         "qwen3-27b (config 5, dense long-context)")
     ap.add_argument("--mode", default="decode", choices=["decode", "prefill"],
                     help="prefill: varlen prefill throughput of --batch prompts of --ctx tokens")
     ap.add_argument("--layers", type=int, default=0,

@@ -297,6 +297,48 @@ int s8b_ipc_close(void *ptr);
  * pinned host addresses: host I/O around the step and set-up copies into raw buffers.      */
 int s8b_memcpy_async(void *dst, const void *src, size_t bytes, void *stream);
 
+/* ---- sparse-MoE FFN (Qwen3-MoE) -----------------------------------------------------
+ * Replaces the router, the per-expert GatedMLP loop and the index_add_ combine of
+ * SparseMoE.forward (superl8serve/models/moe.py:88-141; the experts' LinearW8A8 calls are
+ * superl8.linear, superl8serve/layers/linear.py:122). A layer runs:
+ *   s8b_moe_route(y)                        -> topi, topw, expert groups
+ *   s8b_moe_gemm_grouped(xq, row=sorted_token, W_gate_up)  -> gu   [A, 2F] (A = T*top_k)
+ *   s8b_silu_mul_quant(gu, A, F)            -> aq, as
+ *   s8b_moe_gemm_grouped(aq, row=NULL, W_down)             -> part [A, H]
+ *   s8b_moe_combine(part, topw, topi, assign_pos)          -> out  [T, H]
+ *
+ * s8b_moe_route: y [T, H] dtype (the post-attention RMSNorm output); gate [E, H] fp32
+ * (16-byte aligned). Logits are float64 lane sums rounded to fp32, softmax over all E in
+ * fp32 (exp_s8b), top_k largest (ties: lower expert first) in descending order,
+ * renormalised by their sum (clamped at 1e-9) when norm_topk_prob, times routed_scaling,
+ * rounded to dtype. Outputs: topi [T, top_k] int32, topw [T, top_k] dtype; the T*top_k
+ * assignments a = t*top_k + j sorted by (expert, token): expert_offsets [E+1] (rows of
+ * expert e are [off[e], off[e+1])), sorted_assign [A] (a at each sorted row),
+ * sorted_token [A] (its token), assign_pos [A] (sorted row of each a).
+ * H % 8 == 0, E <= 256, top_k <= min(16, E), T <= 4096. Two launches.                  */
+int s8b_moe_route(const void *y, int dtype, const float *gate, int T, int H, int E, int top_k,
+                  int norm_topk_prob, float routed_scaling, int32_t *topi, void *topw,
+                  int32_t *expert_offsets, int32_t *sorted_assign, int32_t *sorted_token,
+                  int32_t *assign_pos, void *stream);
+
+/* Grouped W8A8 GEMM: for every expert e and row p in [expert_offsets[e], expert_offsets[e+1]),
+ *   y[p, n] = dtype((float(sum_k xq[r, k] * w[e, n, k]) * xs[r]) * ws[e, n]),
+ * r = row_index[p] (or p when row_index is NULL). w is int8 [E, N, K], ws fp32 [E, N];
+ * A = expert_offsets[E] rows. K % 16 == 0, 32*K <= 200 KiB; xq, w 16-byte aligned.
+ * Experts without rows cost nothing; every weight byte of a routed expert is read from HBM
+ * once (staged in shared memory), whatever its row count.                                */
+int s8b_moe_gemm_grouped(const int8_t *xq, const float *xs, const int32_t *row_index,
+                         const int8_t *w, const float *ws, const int32_t *expert_offsets,
+                         void *y, int A, int N, int K, int E, int dtype, void *stream);
+
+/* out[t, :] = running dtype sum, in ascending expert index, of dtype(contrib[p, :] * w)
+ * over the token's top_k assignments (p = assign_pos[t*top_k + j], w = topw[t, j]); each
+ * product and each sum rounded to dtype, starting from zero (the reference's per-expert
+ * out.index_add_). H % 4 == 0; contrib, out 8-byte aligned.                               */
+int s8b_moe_combine(const void *contrib, const void *topw, const int32_t *topi,
+                    const int32_t *assign_pos, void *out, int T, int top_k, int H, int dtype,
+                    void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -37,6 +37,7 @@ from .kernels import (
     rope_tables,
     silu_mul,
 )
+from .moe import moe_ffn
 from .numerics import quant_rows_i8, quantize_weight_rowwise, round_bf16
 
 
@@ -53,10 +54,14 @@ class Shape:
     rope_theta: float = 1e6
     max_position_embeddings: int = 4096
     tie_word_embeddings: bool = False
+    num_experts: int = 0
+    num_experts_per_tok: int = 8
+    norm_topk_prob: bool = True
 
 
 def shape_of(cfg) -> Shape:
-    return Shape(**{f: getattr(cfg, f) for f in Shape.__dataclass_fields__})
+    return Shape(**{f: getattr(cfg, f) for f in Shape.__dataclass_fields__
+                    if hasattr(cfg, f)})
 
 
 def quantize_state_dict(sd: dict, cfg) -> dict:
@@ -68,12 +73,23 @@ def quantize_state_dict(sd: dict, cfg) -> dict:
     for i in range(s.num_hidden_layers):
         p = f"model.layers.{i}"
         qkv = np.concatenate([sd[f"{p}.self_attn.{n}_proj.weight"] for n in "qkv"], axis=0)
-        gu = np.concatenate([sd[f"{p}.mlp.gate_proj.weight"], sd[f"{p}.mlp.up_proj.weight"]], 0)
         L = {}
         L["qkv"] = quantize_weight_rowwise(qkv)
         L["o"] = quantize_weight_rowwise(sd[f"{p}.self_attn.o_proj.weight"])
-        L["gu"] = quantize_weight_rowwise(gu)
-        L["down"] = quantize_weight_rowwise(sd[f"{p}.mlp.down_proj.weight"])
+        if f"{p}.mlp.gate.weight" in sd:
+            # sparse MoE layer (``superl8serve/models/qwen3.py:53-64``): router + per-expert
+            # merged gate_up / down, each quantized per row
+            L["router"] = np.asarray(sd[f"{p}.mlp.gate.weight"], dtype=np.float32)
+            L["experts"] = []
+            for e in range(L["router"].shape[0]):
+                q = f"{p}.mlp.experts.{e}"
+                gu = np.concatenate([sd[f"{q}.gate_proj.weight"], sd[f"{q}.up_proj.weight"]], 0)
+                L["experts"].append((quantize_weight_rowwise(gu),
+                                     quantize_weight_rowwise(sd[f"{q}.down_proj.weight"])))
+        else:
+            gu = np.concatenate([sd[f"{p}.mlp.gate_proj.weight"], sd[f"{p}.mlp.up_proj.weight"]], 0)
+            L["gu"] = quantize_weight_rowwise(gu)
+            L["down"] = quantize_weight_rowwise(sd[f"{p}.mlp.down_proj.weight"])
         L["in_norm"] = np.asarray(sd[f"{p}.input_layernorm.weight"], dtype=np.float32)
         L["post_norm"] = np.asarray(sd[f"{p}.post_attention_layernorm.weight"], dtype=np.float32)
         L["q_norm"] = np.asarray(sd[f"{p}.self_attn.q_norm.weight"], dtype=np.float32)
@@ -142,6 +158,10 @@ def layer_decode(L, li, h, residual, positions, slot_mapping, block_table, ctx_l
     x = add_residual(o, residual)
     residual = x
     y = rmsnorm(x, L["post_norm"], eps)
+    if "experts" in L:
+        h = moe_ffn(y, *quant_rows_i8(y), L["router"], L["experts"], s.num_experts_per_tok,
+                    s.norm_topk_prob)
+        return h, residual
     gu = gemm_w8a8(*quant_rows_i8(y), *L["gu"])
     a = silu_mul(gu)
     h = gemm_w8a8(*quant_rows_i8(a), *L["down"])

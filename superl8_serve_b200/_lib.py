@@ -75,6 +75,10 @@ SIGNATURES: dict[str, tuple] = {
     "s8b_ipc_open": (_i, [_vp, _vp]),
     "s8b_ipc_close": (_i, [_vp]),
     "s8b_memcpy_async": (_i, [_vp, _vp, _sz, _vp]),
+    "s8b_moe_route": (_i, [_vp, _i, _vp, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp, _vp, _vp,
+                           _vp]),
+    "s8b_moe_gemm_grouped": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
+    "s8b_moe_combine": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
 }
 
 

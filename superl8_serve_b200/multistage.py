@@ -341,7 +341,7 @@ def run_bench_multi(args, metric, step_bytes, peaks, ClockSampler, cpu_sample):
 
     import torch.distributed as dist
 
-    from .config import qwen3_8b
+    from . import config as model_configs
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -351,7 +351,9 @@ def run_bench_multi(args, metric, step_bytes, peaks, ClockSampler, cpu_sample):
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                             device_id=torch.device("cuda", local))
-    cfg = qwen3_8b()
+    model = getattr(args, "model", "qwen3-8b")
+    cfg = getattr(model_configs, {"qwen3-8b": "qwen3_8b", "qwen3-30b-a3b": "qwen3_30b_a3b",
+                                  "qwen3-27b": "qwen3_27b_dense"}[model])()
     if args.layers:
         cfg = cfg.with_(num_hidden_layers=args.layers)
     m, ctx = args.batch, args.ctx
@@ -447,7 +449,7 @@ def run_bench_multi(args, metric, step_bytes, peaks, ClockSampler, cpu_sample):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8 x int8 -> int32 GEMM, bf16 activations",
             "data": "synthetic (random int8 weights, KV pre-filled with random codes)",
-            "config": {"workload": "qwen3-8b-shaped W8A8 decode (BASELINE config 3)",
+            "config": {"workload": f"{model}-shaped W8A8 decode",
                        "micro_batch": m, "n_micro": world, "global_batch": B, "ctx": ctx,
                        "stage_bounds": bounds,
                        "layers": cfg.num_hidden_layers, "block_size": 16,

@@ -12,7 +12,7 @@ __all__ = [
     "quant_rows", "rmsnorm_quant", "gemm_w8a8", "gemm_w8a8_tc", "gemm_tc_workspace",
     "silu_mul_quant", "qkv_post", "kv_write_paged",
     "paged_decode_q8", "paged_decode", "embed", "argmax", "codec_encode", "codec_decode",
-    "codec_sizes", "decode_workspace_bytes",
+    "codec_sizes", "decode_workspace_bytes", "moe_route", "moe_gemm_grouped", "moe_combine",
 ]
 
 
@@ -304,3 +304,40 @@ def codec_decode(payload, scales, T, Da, Db, scheme, dtype, *, out_a=None, out_b
     call("s8b_codec_decode", ptr(payload), ptr(scales), T, Da, Db, CODEC[scheme], ptr(out_a),
          ptr(out_b) if Db else None, dtype_code(dtype), stream(dev))
     return out_a, out_b
+
+
+# ------------------------------------------------------------------------- sparse MoE ----
+def moe_route(y, gate, top_k: int, *, norm_topk_prob: bool = True, scaling: float = 1.0):
+    """Router + grouping (``s8b_moe_route``). Returns a dict of device tensors: topi, topw,
+    offsets [E+1], sorted_assign, sorted_token, assign_pos."""
+    T, H = y.shape
+    E = gate.shape[0]
+    dev = y.device
+    i32 = lambda n: torch.empty(n, dtype=torch.int32, device=dev)  # noqa: E731
+    r = {"topi": i32(T * top_k).view(T, top_k),
+         "topw": torch.empty(T, top_k, dtype=y.dtype, device=dev),
+         "offsets": i32(E + 1), "sorted_assign": i32(T * top_k),
+         "sorted_token": i32(T * top_k), "assign_pos": i32(T * top_k)}
+    call("s8b_moe_route", ptr(y), dtype_code(y.dtype), ptr(gate), T, H, E, top_k, int(norm_topk_prob),
+         scaling, ptr(r["topi"]), ptr(r["topw"]), ptr(r["offsets"]), ptr(r["sorted_assign"]),
+         ptr(r["sorted_token"]), ptr(r["assign_pos"]), stream(dev))
+    return r
+
+
+def moe_gemm_grouped(xq, xs, w, ws, offsets, *, row_index=None, A: int, out_dtype=torch.bfloat16):
+    """y [A, N] = grouped W8A8 over expert row groups (``s8b_moe_gemm_grouped``)."""
+    E, N, K = w.shape
+    y = torch.empty(A, N, dtype=out_dtype, device=xq.device)
+    call("s8b_moe_gemm_grouped", ptr(xq), ptr(xs), None if row_index is None else ptr(row_index),
+         ptr(w), ptr(ws), ptr(offsets), ptr(y), A, N, K, E, dtype_code(y.dtype),
+         stream(xq.device))
+    return y
+
+
+def moe_combine(contrib, topw, topi, assign_pos):
+    T, k = topi.shape
+    H = contrib.shape[1]
+    out = torch.empty(T, H, dtype=contrib.dtype, device=contrib.device)
+    call("s8b_moe_combine", ptr(contrib), ptr(topw), ptr(topi), ptr(assign_pos), ptr(out), T, k,
+         H, dtype_code(out.dtype), stream(out.device))
+    return out

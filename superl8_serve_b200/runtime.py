@@ -9,6 +9,8 @@ in ``PipelineEngine._decode_microbatched``, ``superl8serve/dist/pipeline.py:997-
     per layer:  rmsnorm_quant -> W8A8 qkv -> qkv_post (norms, RoPE, paged KV write, q quant)
                 -> paged decode attention (+ fused o_proj input quant) -> W8A8 o
                 -> rmsnorm_quant -> W8A8 gate_up -> SwiGLU + quant -> W8A8 down
+                (sparse-MoE layer: rmsnorm_quant -> route + group -> grouped W8A8 gate_up
+                 -> SwiGLU + quant -> grouped W8A8 down -> combine)
     [last]      rmsnorm_quant(final norm) -> W8A8 lm_head -> argmax
     [not last]  encode (h, res) straight into the next stage's receive buffer
 
@@ -34,22 +36,57 @@ from .weights import quantize_rowwise_np
 
 
 @dataclass
+class MoEWeights:
+    """Sparse-MoE FFN of one layer (``SparseMoE``, ``superl8serve/models/moe.py:46-86``):
+    fp32 router [E, H]; every expert's merged gate_up int8 [E, 2F, H] with row scales [E, 2F]
+    and down int8 [E, H, F] with row scales [E, H] (experts stacked for the grouped GEMM)."""
+
+    router: torch.Tensor
+    gu_w: torch.Tensor
+    gu_s: torch.Tensor
+    d_w: torch.Tensor
+    d_s: torch.Tensor
+    top_k: int
+    norm_topk_prob: bool = True
+    scaling: float = 1.0
+
+    @property
+    def num_experts(self) -> int:
+        return self.router.shape[0]
+
+    @property
+    def ffn(self) -> int:
+        return self.d_w.shape[2]
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size()
+                   for t in (self.router, self.gu_w, self.gu_s, self.d_w, self.d_s))
+
+
+@dataclass
 class LayerWeights:
     qkv_w: torch.Tensor
     qkv_s: torch.Tensor
     o_w: torch.Tensor
     o_s: torch.Tensor
-    gu_w: torch.Tensor
-    gu_s: torch.Tensor
-    d_w: torch.Tensor
-    d_s: torch.Tensor
+    gu_w: torch.Tensor | None  # dense FFN (None in a sparse-MoE layer)
+    gu_s: torch.Tensor | None
+    d_w: torch.Tensor | None
+    d_s: torch.Tensor | None
     in_norm: torch.Tensor
     post_norm: torch.Tensor
     q_norm: torch.Tensor
     k_norm: torch.Tensor
+    moe: MoEWeights | None = None
 
     def nbytes(self) -> int:
-        return sum(t.numel() * t.element_size() for t in vars(self).values())
+        n = sum(t.numel() * t.element_size() for t in vars(self).values()
+                if isinstance(t, torch.Tensor))
+        return n + (self.moe.nbytes() if self.moe is not None else 0)
+
+    def matrices(self) -> list[torch.Tensor]:
+        """The dense int8 weight matrices of the layer (tensor-core packing, split counts)."""
+        return [w for w in (self.qkv_w, self.o_w, self.gu_w, self.d_w) if w is not None]
 
 
 @dataclass
@@ -103,13 +140,28 @@ class StageModel:
         for i in range(start, end):
             p = f"model.layers.{i}"
             qkv = np.concatenate([f(f"{p}.self_attn.{n}_proj.weight") for n in "qkv"], 0)
-            gu = np.concatenate([f(f"{p}.mlp.gate_proj.weight"), f(f"{p}.mlp.up_proj.weight")], 0)
-            layers.append(LayerWeights(*q(qkv), *q(f(f"{p}.self_attn.o_proj.weight")), *q(gu),
-                                       *q(f(f"{p}.mlp.down_proj.weight")),
+            moe = None
+            if cfg.layer_is_moe(i):
+                ffn = (None, None, None, None)
+                gus, dns = [], []
+                for e in range(cfg.num_experts):
+                    x = f"{p}.mlp.experts.{e}"
+                    gus.append(quantize_rowwise_np(np.concatenate(
+                        [f(f"{x}.gate_proj.weight"), f(f"{x}.up_proj.weight")], 0)))
+                    dns.append(quantize_rowwise_np(f(f"{x}.down_proj.weight")))
+                stack = lambda lst, j: torch.from_numpy(np.stack([t[j] for t in lst])).to(dev)  # noqa: E731
+                moe = MoEWeights(torch.from_numpy(f(f"{p}.mlp.gate.weight")).to(dev),
+                                 stack(gus, 0), stack(gus, 1), stack(dns, 0), stack(dns, 1),
+                                 cfg.num_experts_per_tok, cfg.norm_topk_prob)
+            else:
+                gu = np.concatenate([f(f"{p}.mlp.gate_proj.weight"),
+                                     f(f"{p}.mlp.up_proj.weight")], 0)
+                ffn = (*q(gu), *q(f(f"{p}.mlp.down_proj.weight")))
+            layers.append(LayerWeights(*q(qkv), *q(f(f"{p}.self_attn.o_proj.weight")), *ffn,
                                        g(f"{p}.input_layernorm.weight"),
                                        g(f"{p}.post_attention_layernorm.weight"),
                                        g(f"{p}.self_attn.q_norm.weight"),
-                                       g(f"{p}.self_attn.k_norm.weight")))
+                                       g(f"{p}.self_attn.k_norm.weight"), moe))
         m = cls(cfg, start, end, dev, layers)
         if first:
             m.embed = g("model.embed_tokens.weight")
@@ -138,9 +190,23 @@ class StageModel:
         def gain(n):
             return (1.0 + 0.1 * torch.randn(n, generator=gen, device=dev)).to(dtype)
 
-        layers = [LayerWeights(*w((nh + 2 * nkv) * D, H), *w(H, nh * D), *w(2 * F, H),
-                               *w(H, F), gain(H), gain(H), gain(D), gain(D))
-                  for _ in range(start, end)]
+        def moe_w():
+            E, Fe = cfg.num_experts, cfg.moe_intermediate_size
+            gu, gus = w(E * 2 * Fe, H)
+            dn, dns = w(E * H, Fe)
+            router = (0.02 * torch.randn(E, H, generator=gen, device=dev)).to(dtype).float()
+            return MoEWeights(router, gu.view(E, 2 * Fe, H), gus.view(E, 2 * Fe),
+                              dn.view(E, H, Fe), dns.view(E, H), cfg.num_experts_per_tok,
+                              cfg.norm_topk_prob)
+
+        layers = []
+        for i in range(start, end):
+            if cfg.layer_is_moe(i):
+                ffn, moe = (None, None, None, None), moe_w()
+            else:
+                ffn, moe = (*w(2 * F, H), *w(H, F)), None
+            layers.append(LayerWeights(*w((nh + 2 * nkv) * D, H), *w(H, nh * D), *ffn, gain(H),
+                                       gain(H), gain(D), gain(D), moe))
         m = cls(cfg, start, end, dev, layers)
         if first:
             m.embed = (0.02 * torch.randn(cfg.vocab_size, H, generator=gen, device=dev)).to(dtype)
@@ -233,7 +299,7 @@ class StageRunner:
             self.logits = e(m, self.V)
         self.dev = dev
         self.tc_min = self.TC_MIN_TOKENS if tc_min_tokens is None else tc_min_tokens
-        n_max = max([L.gu_w.shape[0] for L in model.layers] + [L.qkv_w.shape[0] for L in model.layers]
+        n_max = max([w.shape[0] for L in model.layers for w in L.matrices()]
                     + ([model.head_w.shape[0]] if model.is_last else []) + [self.H])
         self.tc_ws = ops.gemm_tc_workspace(m, n_max, dev) if m >= self.tc_min else None
         # tensor-core path: every weight also kept as contiguous unit images (packed once)
@@ -241,7 +307,7 @@ class StageRunner:
         if self.tc_ws is not None and share is not None and share.model is model and share.packed:
             self.packed = share.packed
         elif self.tc_ws is not None:
-            mats = [w for L in model.layers for w in (L.qkv_w, L.o_w, L.gu_w, L.d_w)]
+            mats = [w for L in model.layers for w in L.matrices()]
             if model.is_last:
                 mats.append(model.head_w)
             with torch.cuda.device(dev):
@@ -254,12 +320,26 @@ class StageRunner:
             lib = load()
             need = 0
             for L in model.layers:
-                for w in (L.qkv_w, L.o_w, L.gu_w, L.d_w):
+                for w in L.matrices():
                     N, K = w.shape
                     c = int(lib.s8b_gemm_tc_split_count(m, N, K))
                     self.splits[(N, K)] = c
                     need = max(need, c * m * N)
             self.part = torch.empty(need, dtype=torch.int32, device=dev)
+        # sparse-MoE layers: router input, routing / grouping state and per-assignment rows
+        moes = [L.moe for L in model.layers if L.moe is not None]
+        self.moe_buf = None
+        if moes:
+            k = max(mw.top_k for mw in moes)
+            E = max(mw.num_experts for mw in moes)
+            Fe = max(mw.ffn for mw in moes)
+            A = m * k
+            i32 = lambda *n: torch.empty(n, dtype=torch.int32, device=dev)  # noqa: E731
+            self.moe_buf = {
+                "y": e(m, self.H), "topi": i32(m, k), "topw": e(m, k), "offsets": i32(E + 1),
+                "sorted_assign": i32(A), "sorted_token": i32(A), "assign_pos": i32(A),
+                "gu": e(A, 2 * Fe), "aq": e(A, Fe, dt=torch.int8),
+                "as": e(A, dt=torch.float32), "contrib": e(A, self.H)}
 
     # ---------------------------------------------------------------------- pieces ----
     def _gemm(self, xq, xs, w, s, out, M):
@@ -284,17 +364,37 @@ class StageRunner:
              2, M, N, K, 0, ptr(self.tc_ws), self.tc_ws.numel(), stream())
         return self.splits[(N, K)]
 
-    def _rms_quant(self, h, res_in, res_out, w, M, K, src=None):
+    def _rms_quant(self, h, res_in, res_out, w, M, K, src=None, y_out=None):
         """RMSNorm + activation quant; ``src`` = (C, weight scales) reads h from the split-K
-        partials of the preceding GEMM instead of ``h``."""
+        partials of the preceding GEMM instead of ``h``; ``y_out`` also keeps the normalized
+        dtype row."""
         if src is None:
             call("s8b_rmsnorm_quant", ptr(h), ptr(res_in), ptr(res_out), ptr(w), self.eps,
-                 ptr(self.xq), ptr(self.xs), None, M, K, 0, stream())
+                 ptr(self.xq), ptr(self.xs), ptr(y_out), M, K, 0, stream())
         else:
             C, ws = src
             call("s8b_rmsnorm_quant_split", ptr(self.part), C, ptr(self.xs), ptr(ws), ptr(res_in),
-                 ptr(res_out), ptr(w), self.eps, ptr(self.xq), ptr(self.xs), None, M, K, 0,
-                 stream())
+                 ptr(res_out), ptr(w), self.eps, ptr(self.xq), ptr(self.xs), ptr(y_out), M, K,
+                 0, stream())
+
+    def _moe_ffn(self, mw: MoEWeights, M: int):
+        """Sparse-MoE FFN (``SparseMoE.forward``, ``superl8serve/models/moe.py:88-141``) on
+        the post-attention RMSNorm output: its dtype rows (router) in moe_buf["y"], its int8
+        rows in self.xq / self.xs (expert input). Result: self.h [M, H]."""
+        b, st, k = self.moe_buf, stream(), mw.top_k
+        E, Fe, A = mw.num_experts, mw.ffn, M * mw.top_k
+        call("s8b_moe_route", ptr(b["y"]), 0, ptr(mw.router), M, self.H, E, k,
+             int(mw.norm_topk_prob), mw.scaling, ptr(b["topi"]), ptr(b["topw"]),
+             ptr(b["offsets"]), ptr(b["sorted_assign"]), ptr(b["sorted_token"]),
+             ptr(b["assign_pos"]), st)
+        call("s8b_moe_gemm_grouped", ptr(self.xq), ptr(self.xs), ptr(b["sorted_token"]),
+             ptr(mw.gu_w), ptr(mw.gu_s), ptr(b["offsets"]), ptr(b["gu"]), A, 2 * Fe, self.H, E,
+             0, st)
+        call("s8b_silu_mul_quant", ptr(b["gu"]), A, Fe, None, ptr(b["aq"]), ptr(b["as"]), 0, st)
+        call("s8b_moe_gemm_grouped", ptr(b["aq"]), ptr(b["as"]), None, ptr(mw.d_w), ptr(mw.d_s),
+             ptr(b["offsets"]), ptr(b["contrib"]), A, self.H, Fe, E, 0, st)
+        call("s8b_moe_combine", ptr(b["contrib"]), ptr(b["topw"]), ptr(b["topi"]),
+             ptr(b["assign_pos"]), ptr(self.h), M, k, self.H, 0, st)
 
     def layer(self, li: int, mb: MicroBatch, M: int, first_layer_of_model: bool, h_src=None,
               keep_split: bool = False):
@@ -323,6 +423,17 @@ class StageRunner:
              ptr(self.xs), M, self.Hq, self.Hkv, self.D, self.pool.block_size,
              mb.block_table.shape[1], self.max_ctx, self.scale, ptr(self.ws), self.ws.numel(), 0,
              st)
+        if L.moe is not None:
+            if split:
+                C = self._gemm_split(L.o_w, M)
+                self._rms_quant(None, self.res, self.res, L.post_norm, M, H, src=(C, L.o_s),
+                                y_out=self.moe_buf["y"])
+            else:
+                self._gemm(self.xq, self.xs, L.o_w, L.o_s, self.h, M)
+                self._rms_quant(self.h, self.res, self.res, L.post_norm, M, H,
+                                y_out=self.moe_buf["y"])
+            self._moe_ffn(L.moe, M)
+            return None
         if split:
             C = self._gemm_split(L.o_w, M)
             self._rms_quant(None, self.res, self.res, L.post_norm, M, H, src=(C, L.o_s))

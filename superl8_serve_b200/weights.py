@@ -73,7 +73,8 @@ def _rng(seed: int, name: str) -> np.random.Generator:
 
 
 def state_dict_names(cfg) -> list[tuple[str, tuple[int, ...], str]]:
-    """(name, shape, kind) of every HF-style tensor of a Qwen3 dense model."""
+    """(name, shape, kind) of every HF-style tensor of a Qwen3 dense or Qwen3-MoE model
+    (``mlp.gate`` router and ``mlp.experts.{e}.*`` in sparse layers)."""
     H, hd = cfg.hidden_size, cfg.resolved_head_dim()
     nh, nkv, F, V = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.intermediate_size, cfg.vocab_size
     out = [("model.embed_tokens.weight", (V, H), "w"), ("model.norm.weight", (H,), "g")]
@@ -88,10 +89,20 @@ def state_dict_names(cfg) -> list[tuple[str, tuple[int, ...], str]]:
             (f"{p}.self_attn.o_proj.weight", (H, nh * hd), "w"),
             (f"{p}.self_attn.q_norm.weight", (hd,), "g"),
             (f"{p}.self_attn.k_norm.weight", (hd,), "g"),
-            (f"{p}.mlp.gate_proj.weight", (F, H), "w"),
-            (f"{p}.mlp.up_proj.weight", (F, H), "w"),
-            (f"{p}.mlp.down_proj.weight", (H, F), "w"),
         ]
+        if cfg.layer_is_moe(i):
+            Fe = cfg.moe_intermediate_size
+            out.append((f"{p}.mlp.gate.weight", (cfg.num_experts, H), "w"))
+            for e in range(cfg.num_experts):
+                q = f"{p}.mlp.experts.{e}"
+                out += [(f"{q}.gate_proj.weight", (Fe, H), "w"), (f"{q}.up_proj.weight", (Fe, H), "w"),
+                        (f"{q}.down_proj.weight", (H, Fe), "w")]
+        else:
+            out += [
+                (f"{p}.mlp.gate_proj.weight", (F, H), "w"),
+                (f"{p}.mlp.up_proj.weight", (F, H), "w"),
+                (f"{p}.mlp.down_proj.weight", (H, F), "w"),
+            ]
     if not cfg.tie_word_embeddings:
         out.append(("lm_head.weight", (V, H), "w"))
     return out

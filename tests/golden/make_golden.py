@@ -25,6 +25,7 @@ and the CUDA path are then tested against. Outputs go next to this script.
 from __future__ import annotations
 
 import dataclasses
+import importlib
 import json
 import os
 import sys
@@ -183,7 +184,7 @@ def import_reference(ref_root: Path):
     mods = {}
     for n in ("layers.linear", "layers.norm", "layers.rotary", "layers.activation",
               "layers.embedding", "layers.sampler", "layers.gqa_attention", "models.config",
-              "models.base", "models.qwen3", "engine.kv_cache"):
+              "models.base", "models.qwen3", "models.weights", "engine.kv_cache"):
         mods[n] = importlib.import_module(f"superl8serve.{n}")
     # dist/__init__ holds send/recv/TransferHandle/accuracy_report; import it as a module.
     spec = importlib.util.spec_from_file_location(
@@ -215,12 +216,17 @@ def force_kernel_paths(mods):
 
 # ------------------------------------------------------------------------ fixtures ----
 
-def tiny_cfg_ref(mods, **kw):
-    from superl8_serve_b200.config import tiny
+def tiny_cfg_ref(mods, moe: bool = False, **kw):
+    from superl8_serve_b200.config import tiny, tiny_moe
 
-    c = tiny(**kw)
+    c = (tiny_moe if moe else tiny)(**kw)
     MC = mods["models.config"].ModelConfig
-    return c, MC(arch="qwen3", vocab_size=c.vocab_size, hidden_size=c.hidden_size,
+    extra = {}
+    if moe:
+        extra = dict(num_experts=c.num_experts, num_experts_per_tok=c.num_experts_per_tok,
+                     moe_intermediate_size=c.moe_intermediate_size,
+                     norm_topk_prob=c.norm_topk_prob)
+    return c, MC(arch="qwen3", **extra, vocab_size=c.vocab_size, hidden_size=c.hidden_size,
                  num_hidden_layers=c.num_hidden_layers,
                  num_attention_heads=c.num_attention_heads,
                  num_key_value_heads=c.num_key_value_heads,
@@ -231,14 +237,16 @@ def tiny_cfg_ref(mods, **kw):
                  torch_dtype="bfloat16")
 
 
-def gen_model_golden(mods, out: dict, n_stages: int, scheme: str, seed: int, tag: str):
-    """Greedy decode through the reference module graph, stage-sliced like make_pipeline."""
+def gen_model_golden(mods, out: dict, n_stages: int, scheme: str, seed: int, tag: str,
+                     moe: bool = False):
+    """Greedy decode through the reference module graph, stage-sliced like make_pipeline.
+    ``moe``: the tiny Qwen3-MoE shape (every layer's MLP is the reference ``SparseMoE``)."""
     from superl8_serve_b200.weights import random_state_dict
 
     pipe = mods["dist.pipeline"]
     kvm = mods["engine.kv_cache"]
     base = mods["models.base"]
-    cfg, rcfg = tiny_cfg_ref(mods)
+    cfg, rcfg = tiny_cfg_ref(mods, moe=moe)
     sd = {k: torch.from_numpy(v).to(torch.bfloat16) for k, v in random_state_dict(cfg, seed, w_std=0.1).items()}
 
     pipe._move_stage_groups = lambda groups, devices: None
@@ -302,6 +310,54 @@ def gen_model_golden(mods, out: dict, n_stages: int, scheme: str, seed: int, tag
     out[f"{tag}_tokens"] = np.array(outs, dtype=np.int32)
     out[f"{tag}_logits"] = np.array(logits_log, dtype=np.float32)
     out[f"{tag}_bounds"] = np.array([st.layer_offset for st in stages] + [cfg.num_hidden_layers])
+
+
+def gen_moe_module_golden(mods, out: dict):
+    """The reference ``SparseMoE.forward`` (``superl8serve/models/moe.py:88-141``) on random
+    bf16 rows: its output and the router's top-k choice and weights, recorded by wrapping
+    ``torch.topk`` for the duration of the call (the wrapper returns torch's own result)."""
+    from superl8_serve_b200.weights import random_tensor
+
+    moe_mod = importlib.import_module("superl8serve.models.moe")
+    weights = mods["models.weights"]
+    T, H, E, Fe, k = 24, 256, 16, 128, 4
+    g = torch.Generator().manual_seed(21)
+    x = (torch.randn(T, H, generator=g) * 1.5).to(torch.bfloat16)
+    gate = torch.from_numpy(random_tensor(21, "gate", (E, H), "w", 0.1)).to(torch.bfloat16)
+    raw = {}
+    experts = []
+    for e in range(E):
+        gp = random_tensor(21, f"e{e}.gate", (Fe, H), "w", 0.1)
+        up = random_tensor(21, f"e{e}.up", (Fe, H), "w", 0.1)
+        dn = random_tensor(21, f"e{e}.down", (H, Fe), "w", 0.1)
+        raw[f"moe_e{e}_gate"], raw[f"moe_e{e}_up"], raw[f"moe_e{e}_down"] = gp, up, dn
+        t = lambda a: torch.from_numpy(a).to(torch.bfloat16)  # noqa: E731
+        experts.append((weights.merge_qtensor([t(gp), t(up)]), weights.to_qtensor(t(dn))))
+    m = moe_mod.SparseMoE(gate=gate, experts=experts, top_k=k, norm_topk_prob=True)
+    seen = []
+    real_topk = torch.topk
+
+    def rec_topk(*a, **kw):
+        r = real_topk(*a, **kw)
+        seen.append((r[0].detach().clone(), r[1].detach().clone()))
+        return r
+
+    torch.topk = rec_topk
+    try:
+        with torch.no_grad():
+            y = m(x.reshape(1, T, H))
+    finally:
+        torch.topk = real_topk
+    assert len(seen) == 1
+    topv, topi = seen[0]
+    topw = topv / topv.sum(dim=-1, keepdim=True).clamp_min(1e-9)
+    out.update(raw)
+    out["moe_x"] = _np(x)
+    out["moe_gate"] = _np(gate)
+    out["moe_out"] = _np(y.reshape(T, H))
+    out["moe_topi"] = topi.numpy().astype(np.int32)
+    out["moe_topw"] = _np(topw.to(torch.bfloat16))
+    out["moe_shape"] = np.array([T, H, E, Fe, k])
 
 
 def gen_eager_golden(mods, out: dict):
@@ -411,6 +467,11 @@ def main():
     gen_model_golden(mods, model_arrays, 2, "int8-had", seed=11, tag="s2_int8had")
     gen_model_golden(mods, model_arrays, 3, "int4-had", seed=11, tag="s3_int4had")
     np.savez_compressed(HERE / "tiny_qwen3_decode.npz", **model_arrays)
+    moe_arrays: dict = {}
+    gen_moe_module_golden(mods, moe_arrays)
+    gen_model_golden(mods, moe_arrays, 1, "int8", seed=13, tag="moe_s1", moe=True)
+    gen_model_golden(mods, moe_arrays, 2, "int8-had", seed=13, tag="moe_s2_int8had", moe=True)
+    np.savez_compressed(HERE / "tiny_qwen3_moe.npz", **moe_arrays)
     host = gen_host_golden(mods)
     (HERE / "host_logic.json").write_text(json.dumps(host, indent=1, sort_keys=True))
     print("wrote", sorted(p.name for p in HERE.iterdir() if p.suffix in (".npz", ".json")))
