@@ -267,7 +267,7 @@ def kernel_rooflines(pipe, hbm_peak):
     else:
         # grouped expert gate_up GEMM on the routing the last step left behind
         b, mw = r.moe_buf, lw.moe
-        A, Fe, E = M * mw.top_k, mw.ffn, mw.num_experts
+        A, Fe, E = M * mw.top_k, mw.ffn, mw.local_experts  # this GPU's experts only
         it = iter(range(10 ** 9))
 
         def gemm():
@@ -277,7 +277,7 @@ def kernel_rooflines(pipe, hbm_peak):
                  stream())
 
         ms = time_kernel(gemm, 4 * L)
-        off = b["offsets"].cpu()
+        off = b["offsets"].cpu()[: E + 1]
         hit = int(((off[1:] - off[:-1]) > 0).sum())
         byts = hit * (2 * Fe * r.H + 2 * Fe * 4) + M * r.H + 4 * M + A * 2 * Fe * 2 + 4 * A
         name = "moe_gemm_grouped_gate_up"
@@ -356,6 +356,11 @@ def run_single(args):
     B, ctx = args.batch, args.ctx
     max_len = ctx + args.warmup + args.steps + 16
     model = StageModel.synthetic(cfg, 0, cfg.num_hidden_layers, dev, first=True, last=True, seed=1)
+    ep = max(1, args.ep)
+    if ep > 1:
+        # expert parallelism inside the stage: experts split over cuda:0..cuda:ep-1; the step
+        # spans several GPUs, so it runs eagerly (no CUDA graph)
+        model.shard_experts([f"cuda:{i}" for i in range(1, ep)])
     pipe = DecodePipeline([model], batch=B, n_micro=1, max_len=max_len, wire_scheme=args.scheme)
     pipe.pools[0].fill_random(seed=2)
     pipe.add_sequences()
@@ -364,7 +369,8 @@ def run_single(args):
     pipe._enqueue()  # eager warm-up: kernel attributes, lazy init
     torch.cuda.synchronize()
     pipe.set_state([ctx] * B, ids0, reserve=args.warmup + args.steps + 8)
-    pipe.capture()
+    if ep == 1:
+        pipe.capture()
     for _ in range(args.warmup):
         pipe.step()
     torch.cuda.synchronize()
@@ -394,7 +400,10 @@ def run_single(args):
     # step's tokens while the pipeline stays full; the host reads the buffer after the loop.
     ids_h = torch.tensor(ids0, dtype=torch.int32).pin_memory()
     pipe.set_state([ctx] * B, ids0, reserve=args.warmup + args.steps + 8)
-    pipe.capture(host_io=ids_h)
+    if ep == 1:
+        pipe.capture(host_io=ids_h)
+    else:
+        pipe.step_host_io = lambda: pipe._enqueue(ids_h)
     for _ in range(args.warmup):
         pipe.step_host_io()
     torch.cuda.synchronize()
@@ -428,15 +437,17 @@ def run_single(args):
     top_name, top = max(kr.items(), key=lambda kv: kv[1]["ms"] * kv[1]["launches_per_step"])
     sb = step_bytes(cfg, B, ctx, cfg.num_hidden_layers, True)
     line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ep, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8 x int8 -> int32 GEMM, bf16 activations",
         "data": "synthetic (random int8 weights, KV pre-filled with random codes)",
         "config": {"workload": CONFIG_NAMES[args.model],
                    "micro_batch": B, "n_micro": 1, "global_batch": B, "ctx": ctx,
                    "layers": cfg.num_hidden_layers,
-                   "block_size": 16, "parallelism": "pp1", "wire_scheme": args.scheme,
-                   "cuda_graph": True, "l2": "inputs (17.5 GB) > L2, no flush"},
+                   "block_size": 16, "parallelism": "pp1" + (f" x ep{ep}" if ep > 1 else ""),
+                   "wire_scheme": args.scheme, "cuda_graph": ep == 1,
+                   "l2": f"inputs ({step_bytes(cfg, B, ctx, cfg.num_hidden_layers, True) / 1e9:.1f}"
+                         " GB) > L2, no flush"},
         "gpu_launches": int(per_step_launches) * args.steps,
         "clocks": clocks,
         "e2e": {"value": B / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 4 * B,
@@ -530,6 +541,9 @@ def main():
     ap.add_argument("--model", default="qwen3-8b", choices=sorted(MODELS),
                     help="qwen3-8b (config 3, default), qwen3-30b-a3b (config 4, MoE), "
                          "qwen3-27b (config 5, dense long-context)")
+    ap.add_argument("--ep", type=int, default=1,
+                    help="MoE models: experts of each layer split over this many GPUs of the "
+                         "stage (in-process, cuda:0..ep-1)")
     ap.add_argument("--mode", default="decode", choices=["decode", "prefill"],
                     help="prefill: varlen prefill throughput of --batch prompts of --ctx tokens")
     ap.add_argument("--layers", type=int, default=0,

@@ -324,7 +324,7 @@ int s8b_moe_route(const void *y, int dtype, const float *gate, int T, int H, int
 /* Grouped W8A8 GEMM: for every expert e and row p in [expert_offsets[e], expert_offsets[e+1]),
  *   y[p, n] = dtype((float(sum_k xq[r, k] * w[e, n, k]) * xs[r]) * ws[e, n]),
  * r = row_index[p] (or p when row_index is NULL). w is int8 [E, N, K], ws fp32 [E, N];
- * A = expert_offsets[E] rows. K % 16 == 0, 32*K <= 200 KiB; xq, w 16-byte aligned.
+ * A = expert_offsets[E] rows. K % 16 == 0, 40*K + 128 <= 200 KiB; xq, w 16-byte aligned.
  * Experts without rows cost nothing; every weight byte of a routed expert is read from HBM
  * once (staged in shared memory), whatever its row count.                                */
 int s8b_moe_gemm_grouped(const int8_t *xq, const float *xs, const int32_t *row_index,

@@ -180,16 +180,18 @@ __global__ void __launch_bounds__(1024)
 // ------------------------------------------------------------------- grouped GEMM ----
 // One CTA = (expert e, 32 consecutive weight rows). The CTA's weight tile (32 x K int8,
 // contiguous in HBM) lands in shared memory through 16-byte cp.async copies issued by all
-// threads at once (64 KB in flight for K = 2048), so the weight stream is read from HBM
-// exactly once whatever the expert's row count. Warp w then owns tile rows 4w..4w+3; its lanes
-// split K into 16-byte vectors, each lane keeps its 4 weight vectors in registers and applies
-// them to 8 token rows (tokens from L1/L2); shuffle reductions finish the 32 dot products.
-// Experts with more than 8 rows take further passes over the same shared-memory tile; slots
-// past the last row repeat it and are not stored.
+// threads at once (64 KB in flight for K = 2048), so the weight stream is read from HBM once
+// whatever the expert's row count. Each pass then gathers 8 of the expert's token rows into
+// shared memory (rows padded by 16 bytes, so the 8 rows' vectors at one K offset sit in
+// different banks). Warp w owns tile rows 4w..4w+3; its lanes split K into 16-byte vectors,
+// each lane applies its 4 weight vectors to the 8 token vectors (32 int32 sums), and a
+// transpose reduction (31 shuffles) leaves lane l with the finished sum of output (tile row
+// 4w + l/8, token l%8), which it stores. Slots past the expert's last row repeat that row and
+// are not stored.
 constexpr int kGWarps = 8;
 constexpr int kGRows = 4;                   // weight rows per warp
 constexpr int kGTile = kGWarps * kGRows;    // weight rows per CTA
-constexpr int kGTok = 8;                    // token rows per pass
+constexpr int kGTok = 8;                    // token rows per pass (kGRows * kGTok == 32)
 
 __device__ __forceinline__ int dot16(const int4 a, const int4 b, int acc) {
   acc = __dp4a(a.x, b.x, acc);
@@ -205,6 +207,24 @@ __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
                "l"(src)
                : "memory");
 }
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
+// v[0..31] of every lane -> lane l returns the sum over the warp of v[l] (integer adds).
+__device__ __forceinline__ int transpose_reduce32(int (&v)[32], int lane) {
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) {
+    const bool upper = (lane & s) != 0;
+#pragma unroll
+    for (int i = 0; i < s; ++i) {
+      const int send = upper ? v[i] : v[i + s];
+      const int keep = upper ? v[i + s] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+    }
+  }
+  return v[0];
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kGWarps * 32, 2)
@@ -212,7 +232,8 @@ __global__ void __launch_bounds__(kGWarps * 32, 2)
                             const int32_t *__restrict__ row_index, const int8_t *__restrict__ w,
                             const float *__restrict__ ws, const int32_t *__restrict__ offsets,
                             T *__restrict__ y, int N, int K) {
-  extern __shared__ __align__(16) int8_t wtile[];  // [kGTile][K]
+  extern __shared__ __align__(16) int4 gsm[];  // weight tile [kGTile][kv], tokens [kGTok][kv+1]
+  __shared__ float xs_s[kGTok];
   griddep_launch();
   griddep_wait();  // offsets (and the activations) come from the preceding kernels
   const int e = blockIdx.y;
@@ -221,58 +242,54 @@ __global__ void __launch_bounds__(kGWarps * 32, 2)
   if (lo >= hi || n0 >= N) return;  // uniform over the CTA
   const int rows = min(kGTile, N - n0);
   const int kv = K >> 4;
+  int4 *wt = gsm;
+  int4 *xt = gsm + kGTile * kv;
   {
     const int4 *src = reinterpret_cast<const int4 *>(w + (static_cast<size_t>(e) * N + n0) * K);
-    int4 *dst = reinterpret_cast<int4 *>(wtile);
     const int nvec = rows * kv;
-    for (int i = threadIdx.x; i < nvec; i += blockDim.x) cp_async16(dst + i, src + i);
-    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+    for (int i = threadIdx.x; i < nvec; i += blockDim.x) cp_async16(wt + i, src + i);
   }
-  __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int r0 = warp * kGRows;
-  if (r0 >= rows) return;
-  const int4 *wv = reinterpret_cast<const int4 *>(wtile);
   const int4 *xv = reinterpret_cast<const int4 *>(xq);
   const float *wse = ws + static_cast<size_t>(e) * N + n0;
+  int4 *wrow[kGRows];
+#pragma unroll
+  for (int r = 0; r < kGRows; ++r) wrow[r] = wt + min(r0 + r, rows - 1) * kv;
   for (int c0 = lo; c0 < hi; c0 += kGTok) {
-    int src[kGTok];
-#pragma unroll
-    for (int t = 0; t < kGTok; ++t) {
+    if (c0 != lo) __syncthreads();  // every warp is done with the previous pass's tokens
+    for (int i = threadIdx.x; i < kGTok * kv; i += blockDim.x) {
+      const int t = i / kv, j = i - t * kv;
       const int p = min(c0 + t, hi - 1);
-      src[t] = row_index ? row_index[p] : p;
+      const int src = row_index ? row_index[p] : p;
+      cp_async16(xt + t * (kv + 1) + j, xv + static_cast<size_t>(src) * kv + j);
     }
-    int acc[kGRows][kGTok];
+    if (threadIdx.x < kGTok) {
+      const int p = min(c0 + static_cast<int>(threadIdx.x), hi - 1);
+      xs_s[threadIdx.x] = xs[row_index ? row_index[p] : p];
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    int acc[kGRows * kGTok];
 #pragma unroll
-    for (int r = 0; r < kGRows; ++r)
-#pragma unroll
-      for (int t = 0; t < kGTok; ++t) acc[r][t] = 0;
+    for (int i = 0; i < kGRows * kGTok; ++i) acc[i] = 0;
     for (int kk = lane; kk < kv; kk += 32) {
       int4 wr[kGRows];
 #pragma unroll
-      for (int r = 0; r < kGRows; ++r) wr[r] = wv[min(r0 + r, rows - 1) * kv + kk];
+      for (int r = 0; r < kGRows; ++r) wr[r] = wrow[r][kk];
 #pragma unroll
       for (int t = 0; t < kGTok; ++t) {
-        const int4 xr = __ldg(xv + static_cast<size_t>(src[t]) * kv + kk);
+        const int4 xr = xt[t * (kv + 1) + kk];
 #pragma unroll
-        for (int r = 0; r < kGRows; ++r) acc[r][t] = dot16(wr[r], xr, acc[r][t]);
+        for (int r = 0; r < kGRows; ++r) acc[r * kGTok + t] = dot16(wr[r], xr, acc[r * kGTok + t]);
       }
     }
-#pragma unroll
-    for (int r = 0; r < kGRows; ++r)
-#pragma unroll
-      for (int t = 0; t < kGTok; ++t) acc[r][t] = warp_sum_i(acc[r][t]);
-    // lane (r * kGTok + t) stores output (row c0 + t, column n0 + r0 + r)
-#pragma unroll
-    for (int r = 0; r < kGRows; ++r) {
-#pragma unroll
-      for (int t = 0; t < kGTok; ++t) {
-        if (r * kGTok + t != lane) continue;
-        const int p = c0 + t, n = r0 + r;
-        if (p >= hi || n >= rows) continue;
-        const float v = __fmul_rn(__fmul_rn(static_cast<float>(acc[r][t]), xs[src[t]]), wse[n]);
-        y[static_cast<size_t>(p) * N + n0 + n] = from_f32<T>(v);
-      }
+    const int sum = transpose_reduce32(acc, lane);
+    const int r = lane / kGTok, t = lane % kGTok;
+    const int p = c0 + t, n = r0 + r;
+    if (p < hi && n < rows) {
+      const float v = __fmul_rn(__fmul_rn(static_cast<float>(sum), xs_s[t]), wse[n]);
+      y[static_cast<size_t>(p) * N + n0 + n] = from_f32<T>(v);
     }
   }
 }
@@ -390,7 +407,7 @@ extern "C" int s8b_moe_gemm_grouped(const int8_t *xq, const float *xs, const int
   if (A < 0 || N <= 0 || K <= 0 || K % 16 != 0 || E <= 0 || E > 65535) return S8B_ERR_SHAPE;
   if (!aligned(xq, 16) || !aligned(w, 16)) return S8B_ERR_ALIGN;
   if (A == 0) return S8B_OK;
-  const size_t smem = static_cast<size_t>(kGTile) * K;
+  const size_t smem = static_cast<size_t>(kGTile) * K + static_cast<size_t>(kGTok) * (K + 16);
   if (smem > 200 * 1024) return S8B_ERR_SHAPE;
   const dim3 grid((N + kGTile - 1) / kGTile, E);
   S8B_DISPATCH_DTYPE(dtype, TT, {

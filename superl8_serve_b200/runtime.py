@@ -36,10 +36,26 @@ from .weights import quantize_rowwise_np
 
 
 @dataclass
+class ExpertShard:
+    """Experts [e_lo, e_hi) of a MoE layer held on another GPU of the same stage."""
+
+    device: torch.device
+    e_lo: int
+    e_hi: int
+    gu_w: torch.Tensor
+    gu_s: torch.Tensor
+    d_w: torch.Tensor
+    d_s: torch.Tensor
+
+
+@dataclass
 class MoEWeights:
     """Sparse-MoE FFN of one layer (``SparseMoE``, ``superl8serve/models/moe.py:46-86``):
     fp32 router [E, H]; every expert's merged gate_up int8 [E, 2F, H] with row scales [E, 2F]
-    and down int8 [E, H, F] with row scales [E, H] (experts stacked for the grouped GEMM)."""
+    and down int8 [E, H, F] with row scales [E, H] (experts stacked for the grouped GEMM).
+
+    With expert parallelism (``StageModel.shard_experts``) the stage's own GPU keeps experts
+    [0, gu_w.shape[0]) and ``shards`` hold the following contiguous ranges on other GPUs."""
 
     router: torch.Tensor
     gu_w: torch.Tensor
@@ -49,10 +65,15 @@ class MoEWeights:
     top_k: int
     norm_topk_prob: bool = True
     scaling: float = 1.0
+    shards: list = field(default_factory=list)
 
     @property
     def num_experts(self) -> int:
         return self.router.shape[0]
+
+    @property
+    def local_experts(self) -> int:
+        return self.gu_w.shape[0]
 
     @property
     def ffn(self) -> int:
@@ -110,6 +131,29 @@ class StageModel:
     @property
     def is_last(self) -> bool:
         return self.head_w is not None
+
+    def shard_experts(self, devices) -> "StageModel":
+        """Expert parallelism inside the stage (the reference's ``TransportMoELayer``,
+        ``superl8serve/models/moe_transport.py:161-345``): every MoE layer's experts are split
+        into 1 + len(devices) contiguous ranges, the first staying on this stage's GPU, the
+        others moved to ``devices``. The stage's GPU still routes every token and combines
+        every contribution in ascending expert order, so results do not change."""
+        devs = [torch.device(d) for d in devices]
+        for L in self.layers:
+            mw = L.moe
+            if mw is None:
+                continue
+            E = mw.num_experts
+            n = 1 + len(devs)
+            cuts = [i * E // n for i in range(n + 1)]
+            for i, d in enumerate(devs, start=1):
+                lo, hi = cuts[i], cuts[i + 1]
+                mw.shards.append(ExpertShard(d, lo, hi, mw.gu_w[lo:hi].to(d), mw.gu_s[lo:hi].to(d),
+                                             mw.d_w[lo:hi].to(d), mw.d_s[lo:hi].to(d)))
+            h = cuts[1]
+            mw.gu_w, mw.gu_s = mw.gu_w[:h].clone(), mw.gu_s[:h].clone()
+            mw.d_w, mw.d_s = mw.d_w[:h].clone(), mw.d_s[:h].clone()
+        return self
 
     def weight_bytes(self) -> int:
         n = sum(L.nbytes() for L in self.layers)
@@ -340,6 +384,19 @@ class StageRunner:
                 "sorted_assign": i32(A), "sorted_token": i32(A), "assign_pos": i32(A),
                 "gu": e(A, 2 * Fe), "aq": e(A, Fe, dt=torch.int8),
                 "as": e(A, dt=torch.float32), "contrib": e(A, self.H)}
+            # expert-parallel partners: inputs copied in, gate_up / SwiGLU rows of their own
+            self.moe_peer: dict[str, dict] = {}
+            for d in sorted({str(sh.device) for mw in moes for sh in mw.shards}):
+                pd = torch.device(d)
+                call("s8b_enable_peer_access", dev.index, pd.index)
+                call("s8b_enable_peer_access", pd.index, dev.index)
+                z = lambda *n, dt=dtype: torch.zeros(n, dtype=dt, device=pd)  # noqa: E731
+                self.moe_peer[d] = {
+                    "xq": z(m, self.H, dt=torch.int8), "xs": z(m, dt=torch.float32),
+                    "offsets": z(E + 1, dt=torch.int32), "sorted_token": z(A, dt=torch.int32),
+                    "gu": z(A, 2 * Fe), "aq": z(A, Fe, dt=torch.int8),
+                    "as": z(A, dt=torch.float32), "stream": torch.cuda.Stream(device=pd),
+                    "ev_in": torch.cuda.Event(), "ev_out": torch.cuda.Event()}
 
     # ---------------------------------------------------------------------- pieces ----
     def _gemm(self, xq, xs, w, s, out, M):
@@ -382,19 +439,44 @@ class StageRunner:
         the post-attention RMSNorm output: its dtype rows (router) in moe_buf["y"], its int8
         rows in self.xq / self.xs (expert input). Result: self.h [M, H]."""
         b, st, k = self.moe_buf, stream(), mw.top_k
-        E, Fe, A = mw.num_experts, mw.ffn, M * mw.top_k
-        call("s8b_moe_route", ptr(b["y"]), 0, ptr(mw.router), M, self.H, E, k,
+        E, Fe, A, H = mw.num_experts, mw.ffn, M * mw.top_k, self.H
+        call("s8b_moe_route", ptr(b["y"]), 0, ptr(mw.router), M, H, E, k,
              int(mw.norm_topk_prob), mw.scaling, ptr(b["topi"]), ptr(b["topw"]),
              ptr(b["offsets"]), ptr(b["sorted_assign"]), ptr(b["sorted_token"]),
              ptr(b["assign_pos"]), st)
+        # experts on partner GPUs: token rows and routing go over NVLink, the partner runs its
+        # expert range (offsets from e_lo on: the same global row numbering) and its down
+        # projection stores the contribution rows straight into this GPU's buffer
+        home = torch.cuda.current_stream()
+        for sh in mw.shards:
+            pb = self.moe_peer[str(sh.device)]
+            for dst, src, n in ((pb["xq"], self.xq, M * H), (pb["xs"], self.xs, 4 * M),
+                                (pb["offsets"], b["offsets"], 4 * (E + 1)),
+                                (pb["sorted_token"], b["sorted_token"], 4 * A)):
+                call("s8b_memcpy_async", ptr(dst), ptr(src), n, st)
+            pb["ev_in"].record(home)
+            with torch.cuda.device(sh.device), torch.cuda.stream(pb["stream"]):
+                ps, ne = pb["stream"], sh.e_hi - sh.e_lo
+                ps.wait_event(pb["ev_in"])
+                off = ptr(pb["offsets"]) + 4 * sh.e_lo
+                call("s8b_moe_gemm_grouped", ptr(pb["xq"]), ptr(pb["xs"]), ptr(pb["sorted_token"]),
+                     ptr(sh.gu_w), ptr(sh.gu_s), off, ptr(pb["gu"]), A, 2 * Fe, H, ne, 0, stream())
+                call("s8b_silu_mul_quant", ptr(pb["gu"]), A, Fe, None, ptr(pb["aq"]),
+                     ptr(pb["as"]), 0, stream())
+                call("s8b_moe_gemm_grouped", ptr(pb["aq"]), ptr(pb["as"]), None, ptr(sh.d_w),
+                     ptr(sh.d_s), off, ptr(b["contrib"]), A, H, Fe, ne, 0, stream())
+                pb["ev_out"].record(ps)
+        nl = mw.local_experts
         call("s8b_moe_gemm_grouped", ptr(self.xq), ptr(self.xs), ptr(b["sorted_token"]),
-             ptr(mw.gu_w), ptr(mw.gu_s), ptr(b["offsets"]), ptr(b["gu"]), A, 2 * Fe, self.H, E,
-             0, st)
+             ptr(mw.gu_w), ptr(mw.gu_s), ptr(b["offsets"]), ptr(b["gu"]), A, 2 * Fe, H, nl, 0,
+             st)
         call("s8b_silu_mul_quant", ptr(b["gu"]), A, Fe, None, ptr(b["aq"]), ptr(b["as"]), 0, st)
         call("s8b_moe_gemm_grouped", ptr(b["aq"]), ptr(b["as"]), None, ptr(mw.d_w), ptr(mw.d_s),
-             ptr(b["offsets"]), ptr(b["contrib"]), A, self.H, Fe, E, 0, st)
+             ptr(b["offsets"]), ptr(b["contrib"]), A, H, Fe, nl, 0, st)
+        for sh in mw.shards:
+            home.wait_event(self.moe_peer[str(sh.device)]["ev_out"])
         call("s8b_moe_combine", ptr(b["contrib"]), ptr(b["topw"]), ptr(b["topi"]),
-             ptr(b["assign_pos"]), ptr(self.h), M, k, self.H, 0, st)
+             ptr(b["assign_pos"]), ptr(self.h), M, k, H, 0, st)
 
     def layer(self, li: int, mb: MicroBatch, M: int, first_layer_of_model: bool, h_src=None,
               keep_split: bool = False):

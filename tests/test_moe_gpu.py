@@ -163,3 +163,22 @@ def test_tiny_moe_tensor_core_micro_batch_matches_oracle(moe_sd):
     ref, _ = OraclePipeline(cfg, quantize_state_dict(sd, cfg), n_stages=2,
                             wire_scheme="int8-had", num_slots=24, max_len=64).generate(prompts, 4)
     assert outs == ref
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("stages", [1, 2])
+def test_expert_parallel_two_gpus_matches_reference_graph(golden_dir, moe_sd, stages):
+    """Experts of every MoE layer split over cuda:0 (0-7) and cuda:1 (8-15): the partner's
+    down projection stores its rows into cuda:0's buffer over NVLink and cuda:0 combines in
+    ascending expert order — the single-GPU result, bit for bit."""
+    g = np.load(golden_dir / "tiny_qwen3_moe.npz")
+    tag = {1: "moe_s1", 2: "moe_s2_int8had"}[stages]
+    cfg, sd = moe_sd
+    models = [m.shard_experts(["cuda:1"]) for m in stage_models(cfg, sd, stages)]
+    assert models[0].layers[0].moe.local_experts == 8
+    pipe = DecodePipeline(models, batch=3, n_micro=1, max_len=64,
+                          wire_scheme="int8" if stages == 1 else "int8-had")
+    outs, logits = pipe.generate(PROMPTS, 8, keep_logits=True)
+    assert np.array_equal(np.array(outs), g[f"{tag}_tokens"])
+    got = np.stack([np.stack([t.numpy() for t in row]) for row in logits])
+    assert np.array_equal(got, g[f"{tag}_logits"])
