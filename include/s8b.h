@@ -339,6 +339,27 @@ int s8b_moe_combine(const void *contrib, const void *topw, const int32_t *topi,
                     const int32_t *assign_pos, void *out, int T, int top_k, int H, int dtype,
                     void *stream);
 
+/* ---- rANS entropy stage --------------------------------------------------------------
+ * Static byte-level rANS in the wire format of the reference's optional entropy stage
+ * (superl8serve/dist/entropy.py encode / decode, called from superl8serve/dist/__init__.py:
+ * 191-205, 279-288): frequencies freqs[256] normalised to sum 4096 (every symbol that occurs
+ * >= 1), 32-bit state in [2^23, 2^31), symbols coded last to first, bytes emitted low byte
+ * first, final state flushed as 4 bytes. The payload of n bytes is cut into n_streams
+ * chunks (chunk i = [i*n/S, (i+1)*n/S)), each an independent stream coded by one GPU thread
+ * into its own region at s8b_rans_stream_offset(n, S, i); with n_streams == 1 the region's
+ * stream_len[0] bytes are exactly the reference's encode() output. 1 <= n_streams <= n. */
+size_t s8b_rans_encoded_capacity(size_t n, int n_streams); /* 2n + 4*n_streams bytes    */
+size_t s8b_rans_stream_offset(size_t n, int n_streams, int i);
+/* counts[256] (uint32) = symbol histogram of sym[0..n) (zeroed here first).               */
+int s8b_rans_histogram(const uint8_t *sym, size_t n, uint32_t *counts, void *stream);
+/* stream_len[i] = bytes of stream i, or all ones if a symbol of chunk i has frequency 0.   */
+int s8b_rans_encode(const uint8_t *sym, size_t n, const int32_t *freqs, int n_streams,
+                    uint8_t *out, size_t out_capacity, uint64_t *stream_len, void *stream);
+/* Decodes n symbols into out. Reads stay inside each stream's bytes; *bad = 1 if a stream
+ * ends early (corrupt payload or wrong table). freqs must sum to 4096.                    */
+int s8b_rans_decode(const uint8_t *enc, const uint64_t *stream_len, int n_streams,
+                    const int32_t *freqs, size_t n, uint8_t *out, int32_t *bad, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

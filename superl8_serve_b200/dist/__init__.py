@@ -9,8 +9,9 @@ destination. Both record CUDA-event timings in the handle like the reference. Th
 reference-shaped, host-synchronising seam; the pipeline hot path (``engine.DecodePipeline``,
 ``multistage``) fuses the same kernels into the stage step without host involvement.
 
-The reference's opt-in rANS entropy stage (``entropy=True``) runs on the host and is outside
-this decode path; it raises here.
+The reference's opt-in rANS entropy stage (``entropy=True``) codes the payload's bytes
+after compression; here it runs on the GPU (``dist.entropy``) in the reference's format, and
+``recv`` inverts it on the destination GPU before decoding.
 """
 
 from __future__ import annotations
@@ -127,10 +128,10 @@ def send(x: torch.Tensor, dst: int, *, scheme: str = "int8", group_size: int | N
          entropy: bool = False) -> TransferHandle:
     """Compress x on its GPU and deliver the codes to GPU ``dst``
     (``superl8serve/dist/__init__.py:163-265``)."""
-    if entropy:
-        raise NotImplementedError("the rANS entropy stage is outside the s8b decode path")
     if not x.is_cuda:
         raise RuntimeError("send() takes a CUDA tensor")
+    if entropy:
+        return _send_entropy(x, dst, scheme, group_size)
     src = x.device.index
     d = x.shape[-1]
     T = x.numel() // d
@@ -178,10 +179,52 @@ def send(x: torch.Tensor, dst: int, *, scheme: str = "int8", group_size: int | N
                           used_p2p=use_p2p)
 
 
+def _send_entropy(x: torch.Tensor, dst: int, scheme: str, group_size) -> TransferHandle:
+    """``send(..., entropy=True)`` (``superl8serve/dist/__init__.py:191-205``): compress on
+    the source GPU, rANS-code the payload's bytes there, copy the coded bytes and the scales
+    to ``dst``. The handle carries the frequency table and the payload's dtype and shape."""
+    from . import entropy as ent
+
+    src = x.device.index
+    with torch.cuda.device(src):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        c = compress_activation(x, scheme, group_size)
+        raw = c.payload.contiguous().view(torch.uint8).reshape(-1)
+        coded, freqs, _ = ent.encode(raw)
+        end.record()
+        end.synchronize()
+        compress_ms = start.elapsed_time(end)
+    with torch.cuda.device(dst):
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        payload = coded.to(f"cuda:{dst}")
+        scales = c.scales.to(f"cuda:{dst}")
+        t1.record()
+        t1.synchronize()
+        p2p_ms = t0.elapsed_time(t1)
+    _, nsc = ops.codec_sizes(x.numel() // x.shape[-1], x.shape[-1], scheme)
+    return TransferHandle(src, dst, scheme, torch.Size(c.shape), c.dtype, c.group_size,
+                          payload, scales[: (nsc if nsc else 0)], compress_ms, p2p_ms,
+                          used_p2p=_can_use_p2p(src, dst), entropy_freqs=freqs,
+                          entropy_n=int(raw.numel()), entropy_payload_dtype=c.payload.dtype,
+                          entropy_payload_shape=tuple(c.payload.shape))
+
+
 def recv(handle: TransferHandle) -> torch.Tensor:
-    """Decode the transferred codes on the destination GPU (``:268-302``)."""
+    """Decode the transferred codes on the destination GPU (``:268-302``); an entropy-coded
+    payload is first rANS-decoded there, back to the payload's own dtype and shape."""
+    payload = handle.d_payload
+    if handle.entropy_freqs is not None and handle.entropy_n is not None:
+        from . import entropy as ent
+
+        with torch.cuda.device(handle.dst_device):
+            raw = ent.decode(payload, handle.entropy_freqs, handle.entropy_n)
+        payload = raw.view(handle.entropy_payload_dtype or torch.uint8)
+        if handle.entropy_payload_shape is not None:
+            payload = payload.reshape(handle.entropy_payload_shape)
     c = Compressed(handle.scheme, tuple(handle.shape), handle.dtype, handle.group_size,
-                   handle.d_payload, handle.d_scales, handle.shape[-1])
+                   payload, handle.d_scales, handle.shape[-1])
     with torch.cuda.device(handle.dst_device):
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record()

@@ -360,6 +360,41 @@ def gen_moe_module_golden(mods, out: dict):
     out["moe_shape"] = np.array([T, H, E, Fe, k])
 
 
+def gen_entropy_golden(ref_root: Path) -> dict:
+    """The reference's rANS stage (``superl8serve/dist/entropy.py``) on payloads of the
+    kinds it codes: int8 wire codes of activations with outliers, int4-packed codes, a
+    constant buffer (its documented low-entropy case), uniform and skewed bytes, one byte,
+    an empty buffer. Records each payload, the reference's normalised frequency table and
+    its encoded byte stream."""
+    spec = importlib.util.spec_from_file_location("ref_entropy", ref_root / "superl8serve" /
+                                                  "dist" / "entropy.py")
+    ent = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ent)
+    rng = np.random.default_rng(17)
+    x = rng.standard_normal((4, 1024)).astype(np.float32)
+    x[:, rng.choice(1024, 3, replace=False)] *= 20
+    pay8, _ = ocodec.encode(on.round_bf16(x), "int8-had")
+    pay4, _ = ocodec.encode(on.round_bf16(x), "int4-had")
+    cases = {
+        "int8_codes": np.asarray(pay8).view(np.uint8).ravel(),
+        "int4_codes": np.asarray(pay4).view(np.uint8).ravel(),
+        "constant42": np.full(1000, 42, np.uint8),
+        "uniform": rng.integers(0, 256, 4096).astype(np.uint8),
+        "skewed": np.minimum(rng.geometric(0.3, 10000), 255).astype(np.uint8),
+        "one_byte": np.array([7], np.uint8),
+        "empty": np.zeros(0, np.uint8),
+    }
+    out = {}
+    for name, data in cases.items():
+        enc, freqs = ent.encode(data)
+        dec = ent.decode(enc, freqs, data.size)
+        assert np.array_equal(dec, data)
+        out[f"{name}_data"] = data
+        out[f"{name}_freqs"] = np.asarray(freqs, np.int32)
+        out[f"{name}_enc"] = np.frombuffer(enc, np.uint8).copy()
+    return out
+
+
 def gen_eager_golden(mods, out: dict):
     """The reference's own eager (CPU) numerics for norm / RoPE / SwiGLU / sampler."""
     g = torch.Generator().manual_seed(7)
@@ -472,6 +507,7 @@ def main():
     gen_model_golden(mods, moe_arrays, 1, "int8", seed=13, tag="moe_s1", moe=True)
     gen_model_golden(mods, moe_arrays, 2, "int8-had", seed=13, tag="moe_s2_int8had", moe=True)
     np.savez_compressed(HERE / "tiny_qwen3_moe.npz", **moe_arrays)
+    np.savez_compressed(HERE / "rans.npz", **gen_entropy_golden(ref))
     host = gen_host_golden(mods)
     (HERE / "host_logic.json").write_text(json.dumps(host, indent=1, sort_keys=True))
     print("wrote", sorted(p.name for p in HERE.iterdir() if p.suffix in (".npz", ".json")))
