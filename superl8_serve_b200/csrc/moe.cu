@@ -46,19 +46,31 @@ __global__ void __launch_bounds__(kRouteThreads)
   for (int i = threadIdx.x; i < H; i += kRouteThreads) ys[i] = to_f32(yr[i]);
   __syncthreads();
   const int steps = (H + 255) / 256;
+  constexpr int kSteps = 8;  // gate loads issued together before the fp64 chain consumes them
   for (int e = warp; e < E; e += kRouteThreads / 32) {
     const float *g = gate + static_cast<size_t>(e) * H;
     double acc = 0.0;
-    for (int i = 0; i < steps; ++i) {
-      const int base = 256 * i + 8 * lane;
-      if (base < H) {  // H % 8 == 0: a lane's 8 elements are all in range or all out
-        const float4 g0 = *reinterpret_cast<const float4 *>(g + base);
-        const float4 g1 = *reinterpret_cast<const float4 *>(g + base + 4);
-        const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    for (int i0 = 0; i0 < steps; i0 += kSteps) {
+      float4 g0[kSteps], g1[kSteps];
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
-          acc = __dadd_rn(acc, __dmul_rn(static_cast<double>(ys[base + u]),
-                                         static_cast<double>(gv[u])));
+      for (int q = 0; q < kSteps; ++q) {
+        const int base = 256 * (i0 + q) + 8 * lane;
+        if (i0 + q < steps && base < H) {  // H % 8 == 0: a lane's 8 elements all in or out
+          g0[q] = __ldg(reinterpret_cast<const float4 *>(g + base));
+          g1[q] = __ldg(reinterpret_cast<const float4 *>(g + base + 4));
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kSteps; ++q) {
+        const int base = 256 * (i0 + q) + 8 * lane;
+        if (i0 + q < steps && base < H) {
+          const float gv[8] = {g0[q].x, g0[q].y, g0[q].z, g0[q].w,
+                               g1[q].x, g1[q].y, g1[q].z, g1[q].w};
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            acc = __dadd_rn(acc, __dmul_rn(static_cast<double>(ys[base + u]),
+                                           static_cast<double>(gv[u])));
+        }
       }
     }
 #pragma unroll
@@ -325,12 +337,18 @@ __global__ void __launch_bounds__(256)
   }
   __syncthreads();
   for (int col = 4 * threadIdx.x; col < H; col += 4 * blockDim.x) {
+    // all k contribution loads first, then the ordered sums
+    uint2 raw[kMaxTopK];
+#pragma unroll
+    for (int r = 0; r < kMaxTopK; ++r)
+      if (r < k)
+        raw[r] = *reinterpret_cast<const uint2 *>(contrib + static_cast<size_t>(pos_s[r]) * H + col);
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int r = 0; r < k; ++r) {
-      const uint2 raw =
-          *reinterpret_cast<const uint2 *>(contrib + static_cast<size_t>(pos_s[r]) * H + col);
+#pragma unroll
+    for (int r = 0; r < kMaxTopK; ++r) {
+      if (r >= k) break;
       T c[4];
-      memcpy(c, &raw, 8);
+      memcpy(c, &raw[r], 8);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float v = round_to<T>(__fmul_rn(to_f32(c[j]), w_s[r]));
@@ -340,9 +358,9 @@ __global__ void __launch_bounds__(256)
     T o[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) o[j] = from_f32<T>(acc[j]);
-    uint2 raw;
-    memcpy(&raw, o, 8);
-    *reinterpret_cast<uint2 *>(out + static_cast<size_t>(t) * H + col) = raw;
+    uint2 packed;
+    memcpy(&packed, o, 8);
+    *reinterpret_cast<uint2 *>(out + static_cast<size_t>(t) * H + col) = packed;
   }
 }
 
