@@ -360,6 +360,25 @@ int s8b_rans_encode(const uint8_t *sym, size_t n, const int32_t *freqs, int n_st
 int s8b_rans_decode(const uint8_t *enc, const uint64_t *stream_len, int n_streams,
                     const int32_t *freqs, size_t n, uint8_t *out, int32_t *bad, void *stream);
 
+/* ---- sampler ------------------------------------------------------------------------
+ * Replaces Sampler.forward (superl8serve/layers/sampler.py:22-86) for temperature, top_k,
+ * top_p and repetition_penalty. Row r: x = f32(logits[r]); history[r][positions[r]] =
+ * input_ids[r] is written first, then every distinct id of history[r][0..positions[r]]
+ * gets x < 0 ? x*pen : x/pen; temperature 0 -> argmax (lowest index); otherwise
+ * s = x / max(t, 1e-5), top_k > 0 keeps s >= the k-th largest, e = exp_s8b(s - max s),
+ * q = floor(e * 2^32), top_p < 1 keeps every e whose strictly larger masses sum to
+ * <= floor(p * sum q), and the token is the first index whose running sum of q exceeds
+ * floor(u24 * Q * 2^-24), u24 = splitmix64(seeds[r] + positions[r]) >> 40. top_k, top_p and
+ * penalty may be NULL (disabled). The reference draws torch-RNG Gumbel noise instead; the
+ * distribution is the same categorical. workspace: s8b_sample_workspace_size(M, V) bytes.
+ * V <= 2^24.                                                                            */
+size_t s8b_sample_workspace_size(int M, int V);
+int s8b_sample(const void *logits, int dtype, int M, int V, const float *temperature,
+               const int32_t *top_k, const float *top_p, const float *penalty,
+               const int32_t *input_ids, const int32_t *positions, int32_t *history,
+               int history_cap, const uint64_t *seeds, void *workspace, size_t workspace_bytes,
+               int32_t *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -265,3 +265,34 @@ class OraclePipeline:
             ids = np.asarray(toks, dtype=np.int64)
             positions = [p + 1 for p in positions]
         return outs, logit_log
+
+    def generate_sampled(self, prompts, max_new_tokens, params):
+        """Teacher-forced generation with the sampling recipe of ``oracle.sampler`` per row
+        (params[i]: temperature, top_k, top_p, repetition_penalty, seed); the history of a
+        row at a step is every token up to and including that step's input."""
+        from .sampler import sample_row
+
+        slots = [self.pools[0].alloc() for _ in prompts]
+        for p in self.pools[1:]:
+            for _ in prompts:
+                p.alloc()
+        seqs = [list(p) for p in prompts]
+        outs = [[] for _ in prompts]
+        step = 0
+        while any(len(o) < max_new_tokens for o in outs):
+            ids = np.array([sq[step] for sq in seqs], dtype=np.int64)
+            _, logits = self.decode(ids, slots, [step] * len(prompts))
+            for i, sq in enumerate(seqs):
+                if step >= len(prompts[i]) - 1:
+                    # every row past its prompt keeps stepping (as the pipeline does); only
+                    # the first max_new_tokens are its output
+                    pr = params[i]
+                    tok = sample_row(logits[i], pr.get("temperature", 0.0), pr.get("top_k", 0),
+                                     pr.get("top_p", 1.0), pr.get("repetition_penalty", 1.0),
+                                     sq[:step + 1], step, int(pr.get("seed", i)))
+                    if len(outs[i]) < max_new_tokens:
+                        outs[i].append(tok)
+                    if step + 1 >= len(sq):
+                        sq.append(tok)
+            step += 1
+        return outs

@@ -10,8 +10,12 @@ boundary and no host synchronisation inside a step.
 Prompts go through the varlen prefill first (``DecodePipeline.prefill``, the reference's
 ``_prefill`` at ``:908-984``), then every sequence decodes from its own length.
 
-Differences from the reference, all on purpose: sampling is greedy-only (temperature /
-top-k / top-p are not on this path), and the boundary scheme is fixed per engine
+Sampling (temperature, top-k, top-p, repetition penalty) runs on the last stage's GPU
+(``s8b_sample``); its draw is counter-seeded (``SamplingParams.seed``, default the request
+id) instead of the reference's torch-RNG Gumbel noise, so a run is reproducible. Host-side
+``logit_processors`` are not supported.
+
+Differences from the reference, all on purpose: the boundary scheme is fixed per engine
 (``wire_scheme``, default "int8") instead of re-running the int4 gate every step, which
 would need a host read-back inside the step.
 """
@@ -35,6 +39,7 @@ class SamplingParams:
     top_k: int = 0
     repetition_penalty: float = 1.0
     logit_processors: list = field(default_factory=list)
+    seed: int | None = None  # draw seed (this build's; the reference draws from torch's RNG)
 
 
 class PipelineStage:
@@ -183,10 +188,15 @@ class PipelineEngine:
         ids = list(self._pending)
         prompts = [self._pending[i][0] for i in ids]
         params = [self._pending[i][1] for i in ids]
-        if any(p.temperature != 0.0 for p in params):
-            raise NotImplementedError("only greedy sampling is on the s8b decode path")
+        if any(p.logit_processors for p in params):
+            raise NotImplementedError("host logit processors are not on the s8b decode path")
         max_new = max(p.max_tokens for p in params)
-        outs = self._pipeline(len(prompts)).generate(prompts, max_new, prefill=self.prefill)
+        pipe = self._pipeline(len(prompts))
+        pipe.set_sampling([{"temperature": p.temperature, "top_k": p.top_k, "top_p": p.top_p,
+                            "repetition_penalty": p.repetition_penalty,
+                            "seed": sid if p.seed is None else p.seed}
+                           for sid, p in zip(ids, params)], prompts)
+        outs = pipe.generate(prompts, max_new, prefill=self.prefill)
         for sid, out, p in zip(ids, outs, params):
             out = out[: p.max_tokens]
             if self.eos_id is not None and self.eos_id in out:

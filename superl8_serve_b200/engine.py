@@ -127,6 +127,7 @@ class DecodePipeline:
         self.dtype = dtype
         self.prefill_chunk = self.PREFILL_CHUNK
         self._pf = None
+        self._sampling = None
 
     # ----------------------------------------------------------------- sequence state ----
     def add_sequences(self, n: int | None = None):
@@ -243,6 +244,44 @@ class DecodePipeline:
     def synchronize(self):
         for mdl in self.models:
             torch.cuda.synchronize(mdl.device)
+
+    # --------------------------------------------------------------------- sampling ----
+    def set_sampling(self, params: list[dict] | None, prompts: list[list[int]] | None = None):
+        """Per-row sampling on the last stage (``s8b_sample``; the reference's
+        ``Sampler.forward``, ``superl8serve/layers/sampler.py:22-86``). params[i]: temperature,
+        top_k, top_p, repetition_penalty, seed. ``None`` (or all temperatures 0 with no
+        penalty) keeps the greedy argmax. The token history used by the repetition penalty
+        starts as the prompts; each step adds its input ids on the device."""
+        last = self.models[-1].device
+        if params is None or all(float(p.get("temperature", 0.0)) == 0.0 and
+                                 float(p.get("repetition_penalty", 1.0)) == 1.0 for p in params):
+            for mb in self.mbs[-1]:
+                mb.extra.pop("sampling", None)
+            self._sampling = None
+            return
+        if len(params) != self.batch:
+            raise ValueError("set_sampling() expects one parameter set per row")
+        from ._lib import load
+
+        cap = self.max_len
+        hist = torch.zeros(self.batch, cap, dtype=torch.int32)
+        for i, pr in enumerate(prompts or []):
+            hist[i, : min(len(pr), cap)] = torch.tensor(pr[:cap], dtype=torch.int32)
+        col = lambda key, dflt, dt: torch.tensor([p.get(key, dflt) for p in params], dtype=dt)  # noqa: E731
+        full = {"temperature": col("temperature", 0.0, torch.float32),
+                "top_k": col("top_k", 0, torch.int32), "top_p": col("top_p", 1.0, torch.float32),
+                "penalty": col("repetition_penalty", 1.0, torch.float32),
+                "seeds": torch.tensor([int(p.get("seed", i)) & ((1 << 63) - 1)
+                                       for i, p in enumerate(params)], dtype=torch.int64),
+                "history": hist}
+        ws_bytes = int(load().s8b_sample_workspace_size(self.m, self.cfg.vocab_size))
+        for k in range(self.n_micro):
+            lo, r = k * self.m, self.rows[k]
+            smp = {name: t[lo:lo + r].contiguous().to(last) for name, t in full.items()}
+            smp["workspace"] = torch.empty(ws_bytes, dtype=torch.uint8, device=last)
+            smp["input_ids"] = self.mbs[0][k].ids
+            self.mbs[-1][k].extra["sampling"] = smp
+        self._sampling = params
 
     # ---------------------------------------------------------------------- prefill ----
     def _prefill_state(self):
@@ -382,6 +421,8 @@ class DecodePipeline:
         return (outs, logit_log) if keep_logits else outs
 
     def _generate_prefilled(self, prompts, max_new_tokens: int, keep_logits: bool):
+        if self._sampling is not None:
+            return self._generate_prefilled_sampled(prompts, max_new_tokens)
         res = self.prefill(prompts, reserve=max_new_tokens, keep_logits=keep_logits)
         first, first_logits = res if keep_logits else (res, None)
         outs = [[t] for t in first]
@@ -405,3 +446,21 @@ class DecodePipeline:
                 if keep_logits and lg is not None:
                     logit_log[i].append(lg[i])
         return (outs, logit_log) if keep_logits else outs
+
+    def _generate_prefilled_sampled(self, prompts, max_new_tokens: int):
+        """Sampling after a prefill: the prompts but their last token go through prefill (its
+        argmax is not used), the last prompt token through a sampled decode step, so every
+        generated token comes from the sampler."""
+        if any(len(p) < 2 for p in prompts):
+            return self.generate(prompts, max_new_tokens)
+        self.prefill([p[:-1] for p in prompts], reserve=max_new_tokens + 1)
+        self.set_state([len(p) - 1 for p in prompts], [p[-1] for p in prompts],
+                       reserve=max_new_tokens + 1)
+        outs = [[] for _ in prompts]
+        for _ in range(max_new_tokens):
+            self._enqueue()
+            self.synchronize()
+            toks = self.tokens().cpu().tolist()
+            for i in range(len(prompts)):
+                outs[i].append(int(toks[i]))
+        return outs

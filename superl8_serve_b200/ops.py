@@ -341,3 +341,22 @@ def moe_combine(contrib, topw, topi, assign_pos):
     call("s8b_moe_combine", ptr(contrib), ptr(topw), ptr(topi), ptr(assign_pos), ptr(out), T, k,
          H, dtype_code(out.dtype), stream(out.device))
     return out
+
+
+# ---------------------------------------------------------------------------- sampler ----
+def sample(logits, temperature, *, top_k=None, top_p=None, penalty=None, input_ids, positions,
+           history, seeds, out=None, workspace=None):
+    """Next tokens [M] int32 (``s8b_sample``). history: int32 [M, cap], updated in place at
+    each row's position with its input id."""
+    M, V = logits.shape
+    dev = logits.device
+    if workspace is None:
+        from ._lib import load
+
+        workspace = torch.empty(int(load().s8b_sample_workspace_size(M, V)), dtype=torch.uint8,
+                                device=dev)
+    out = torch.empty(M, dtype=torch.int32, device=dev) if out is None else out
+    call("s8b_sample", ptr(logits), dtype_code(logits.dtype), M, V, ptr(temperature), ptr(top_k),
+         ptr(top_p), ptr(penalty), ptr(input_ids), ptr(positions), ptr(history),
+         history.shape[1], ptr(seeds), ptr(workspace), workspace.numel(), ptr(out), stream(dev))
+    return out

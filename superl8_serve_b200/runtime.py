@@ -562,7 +562,17 @@ class StageRunner:
                 return
             self._rms_quant(self.h, self.res, self.res, self.model.norm, M, self.H, src=h_src)
             self._gemm(self.xq, self.xs, self.model.head_w, self.model.head_s, self.logits, M)
-            call("s8b_argmax", ptr(self.logits), M, self.V, ptr(mb.ids), 0, st)
+            smp = mb.extra.get("sampling")
+            if smp is None:
+                call("s8b_argmax", ptr(self.logits), M, self.V, ptr(mb.ids), 0, st)
+            else:
+                # temperature / top-k / top-p / repetition penalty (s8b_sample); the step's
+                # input ids come from stage 0's buffer of this micro-batch
+                call("s8b_sample", ptr(self.logits), 0, M, self.V, ptr(smp["temperature"]),
+                     ptr(smp["top_k"]), ptr(smp["top_p"]), ptr(smp["penalty"]),
+                     ptr(smp["input_ids"]), ptr(mb.positions), ptr(smp["history"]),
+                     smp["history"].shape[1], ptr(smp["seeds"]), ptr(smp["workspace"]),
+                     smp["workspace"].numel(), ptr(mb.ids), st)
         else:
             pay, sc, scheme = boundary_out
             call("s8b_codec_encode", ptr(self.h), ptr(self.res), M, self.H, self.H, CODEC[scheme],
