@@ -128,6 +128,7 @@ class DecodePipeline:
         self.prefill_chunk = self.PREFILL_CHUNK
         self._pf = None
         self._sampling = None
+        self.scratch_block = None
 
     # ----------------------------------------------------------------- sequence state ----
     def add_sequences(self, n: int | None = None):
@@ -152,6 +153,56 @@ class DecodePipeline:
                 mb.context_lens[:r].copy_(pos[lo:lo + r] + 1)
                 if ids_t is not None and s == 0:
                     mb.ids[:r].copy_(ids_t[lo:lo + r])
+
+    def set_rows(self, rows: list[int], positions: list[int], ids: list[int],
+                 slots: list[int | None]):
+        """Host -> device state of some rows only (continuous batching): row r decodes
+        ``ids[i]`` at ``positions[i]`` with the block table of KV slot ``slots[i]``; a slot of
+        None parks the row on the reserved scratch block (``scratch_block``), so an idle row
+        writes and reads nothing that belongs to a sequence."""
+        bt = torch.zeros(len(rows), self.max_blocks, dtype=torch.int32)
+        for j, sl in enumerate(slots):
+            if sl is None:
+                bt[j].fill_(self.scratch_block)
+            else:
+                b = self.alloc._slot_blocks[sl]
+                bt[j, : len(b)] = torch.tensor(b, dtype=torch.int32)
+                bt[j, len(b):] = self.scratch_block
+        pos = torch.tensor(positions, dtype=torch.int32)
+        ids_t = torch.tensor(ids, dtype=torch.int32)
+        for j, row in enumerate(rows):
+            k, r = divmod(row, self.m)
+            for s in range(self.S):
+                mb = self.mbs[s][k]
+                mb.block_table[r].copy_(bt[j])
+                mb.positions[r:r + 1].copy_(pos[j:j + 1])
+                mb.context_lens[r:r + 1].copy_(pos[j:j + 1] + 1)
+                if s == 0:
+                    mb.ids[r:r + 1].copy_(ids_t[j:j + 1])
+
+    def reserve_scratch_block(self) -> int:
+        """Take one physical block out of the allocator for idle rows (``set_rows``)."""
+        if self.scratch_block is None:
+            self.scratch_block = self.alloc._free_blocks.pop(0)
+        return self.scratch_block
+
+    def set_sampling_rows(self, rows: list[int], params: list[dict], prompts: list[list[int]]):
+        """Sampling parameters and token history of some rows only, leaving the other rows'
+        state (and their histories) as they are; the first call switches every row to the
+        sampler (greedy rows stay greedy)."""
+        if self._sampling is None:
+            self.set_sampling([{} for _ in range(self.batch)], force=True)
+        for row, pr, prompt in zip(rows, params, prompts):
+            k, r = divmod(row, self.m)
+            smp = self.mbs[-1][k].extra["sampling"]
+            smp["temperature"][r] = float(pr.get("temperature", 0.0))
+            smp["top_k"][r] = int(pr.get("top_k", 0))
+            smp["top_p"][r] = float(pr.get("top_p", 1.0))
+            smp["penalty"][r] = float(pr.get("repetition_penalty", 1.0))
+            smp["seeds"][r] = int(pr.get("seed", row)) & ((1 << 63) - 1)
+            h = torch.zeros(smp["history"].shape[1], dtype=torch.int32)
+            h[: min(len(prompt), h.numel())] = torch.tensor(prompt[: h.numel()], dtype=torch.int32)
+            smp["history"][r].copy_(h)
 
     def set_ids(self, ids: list[int]):
         ids_t = torch.tensor(ids, dtype=torch.int32)
@@ -246,15 +297,17 @@ class DecodePipeline:
             torch.cuda.synchronize(mdl.device)
 
     # --------------------------------------------------------------------- sampling ----
-    def set_sampling(self, params: list[dict] | None, prompts: list[list[int]] | None = None):
+    def set_sampling(self, params: list[dict] | None, prompts: list[list[int]] | None = None,
+                     *, force: bool = False):
         """Per-row sampling on the last stage (``s8b_sample``; the reference's
         ``Sampler.forward``, ``superl8serve/layers/sampler.py:22-86``). params[i]: temperature,
         top_k, top_p, repetition_penalty, seed. ``None`` (or all temperatures 0 with no
-        penalty) keeps the greedy argmax. The token history used by the repetition penalty
-        starts as the prompts; each step adds its input ids on the device."""
+        penalty) keeps the greedy argmax unless ``force``. The token history used by the
+        repetition penalty starts as the prompts; each step adds its input ids on the device."""
         last = self.models[-1].device
-        if params is None or all(float(p.get("temperature", 0.0)) == 0.0 and
-                                 float(p.get("repetition_penalty", 1.0)) == 1.0 for p in params):
+        if params is None or (not force and all(
+                float(p.get("temperature", 0.0)) == 0.0 and
+                float(p.get("repetition_penalty", 1.0)) == 1.0 for p in params)):
             for mb in self.mbs[-1]:
                 mb.extra.pop("sampling", None)
             self._sampling = None
@@ -301,7 +354,8 @@ class DecodePipeline:
         self._pf = (runners, bufs)
         return self._pf
 
-    def prefill(self, prompts: list[list[int]], *, reserve: int = 1, keep_logits: bool = False):
+    def prefill(self, prompts: list[list[int]], *, reserve: int = 1, keep_logits: bool = False,
+                slots: list[int] | None = None):
         """Varlen batched prefill (``PipelineEngine._prefill``,
         ``superl8serve/dist/pipeline.py:908-984``): every prompt token of every sequence is
         one row; rows are packed sequence after sequence (the reference's ``cu_seqlens``
@@ -315,21 +369,26 @@ class DecodePipeline:
         LM head and argmax run only in chunks where some sequence ends; the argmax of each
         sequence's last row is its first generated token (returned, one per sequence; with
         ``keep_logits`` also that row's logits). Block capacity is reserved for
-        ``len(prompt) + reserve`` tokens.
+        ``len(prompt) + reserve`` tokens. ``slots`` prefills only those KV slots (one prompt
+        each; continuous batching admits requests this way), default every row's.
 
         The row state of all chunks (ids, positions, context lengths, block-table rows) goes
         to each stage's device in one pinned copy and every chunk reads a view of it, so the
         chunks are enqueued back to back with one host synchronisation at the end.
         """
         n = len(prompts)
-        if n != self.batch:
+        if slots is None and n != self.batch:
             raise ValueError("prefill() expects exactly `batch` prompts")
+        if slots is not None and len(slots) != n:
+            raise ValueError("prefill() needs one slot per prompt")
         if any(len(p) == 0 for p in prompts):
             raise ValueError("prefill() needs a non-empty prompt for every sequence")
-        if not self.slots:
-            self.add_sequences(n)
-        self.alloc.ensure_capacity(self.slots, [len(p) + reserve for p in prompts])
-        bt = self.alloc.block_table(self.slots)
+        if slots is None:
+            if not self.slots:
+                self.add_sequences(n)
+            slots = self.slots
+        self.alloc.ensure_capacity(slots, [len(p) + reserve for p in prompts])
+        bt = self.alloc.block_table(slots)
         runners, bufs = self._prefill_state()
         seq = torch.tensor([i for i, p in enumerate(prompts) for _ in p], dtype=torch.long)
         pos = torch.cat([torch.arange(len(p), dtype=torch.int32) for p in prompts])

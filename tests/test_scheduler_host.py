@@ -1,0 +1,160 @@
+"""CPU: the continuous-batching policy (``Scheduler``) against the reference's own policy
+tests (``tests/test_scheduler.py`` in superl8-serve), driven with an in-memory cache and no
+model: count caps never preempt, FIFO completion with bounded work, preemption only under
+genuine block-pool exhaustion, cancellation."""
+
+from superl8_serve_b200.dist.pipeline import SamplingParams
+from superl8_serve_b200.scheduler import Scheduler, Sequence, Status
+
+
+class FakeCache:
+    def __init__(self, num_slots, *, block_size=16, max_len=256, num_blocks=None):
+        self.block_size = block_size
+        self.max_blocks_per_seq = (max_len + block_size - 1) // block_size
+        self.num_blocks = num_blocks if num_blocks is not None else num_slots * self.max_blocks_per_seq
+        self._free_slots = list(range(num_slots))
+        self._free_blocks = list(range(self.num_blocks))
+        self._slot_blocks = {s: [] for s in range(num_slots)}
+
+    def alloc(self):
+        return self._free_slots.pop()
+
+    def free(self, slot):
+        self._free_blocks.extend(self._slot_blocks[slot])
+        self._slot_blocks[slot] = []
+        self._free_slots.append(slot)
+
+    def has_free_slot(self):
+        return bool(self._free_slots)
+
+    def has_free_block(self):
+        return bool(self._free_blocks)
+
+    def ensure_capacity(self, slots, lengths):
+        for slot, n in zip(slots, lengths):
+            need = (n + self.block_size - 1) // self.block_size
+            while len(self._slot_blocks[slot]) < need:
+                self._slot_blocks[slot].append(self._free_blocks.pop())
+
+    def lookup_prefix(self, token_ids):
+        return 0, []
+
+    def share_blocks(self, slot, blocks):
+        pass
+
+
+def _run(sched, seqs, max_tokens):
+    for s in seqs:
+        sched.add(s)
+    count = {"preempt": 0}
+    orig = sched._preempt_one
+
+    def counting():
+        count["preempt"] += 1
+        orig()
+
+    sched._preempt_one = counting
+    work, calls, steps = 0, {}, 0
+    while sched.has_work():
+        assert steps < 100_000
+        batch, is_prefill = sched.schedule()
+        if not batch:
+            break
+        steps += 1
+        for seq in batch:
+            if is_prefill:
+                sched.cache.ensure_capacity([seq.slot], [seq.num_prompt])
+                seq.length = seq.num_prompt
+                work += seq.num_prompt
+                calls[seq.seq_id] = calls.get(seq.seq_id, 0) + 1
+            else:
+                seq.length += 1
+                sched.cache.ensure_capacity([seq.slot], [seq.length + 1])
+            seq.output_ids.append(7)
+        sched.postprocess(batch, is_prefill)
+    return count["preempt"], work, calls, steps
+
+
+def _mk(prompts, max_tokens):
+    return [Sequence(i, list(p), SamplingParams(max_tokens=max_tokens)) for i, p in enumerate(prompts)]
+
+
+def test_no_preemption_under_count_cap():
+    sched = Scheduler(FakeCache(4), max_num_seqs=4, max_batch_tokens=8192, eos_id=None)
+    prompts = [[1, 2, 3], [4, 5, 6, 7], [8], [9, 10], [11, 12, 13, 14, 15], [16], [17, 18], [19]]
+    seqs = _mk(prompts, 6)
+    pre, work, calls, _ = _run(sched, seqs, 6)
+    assert pre == 0 and all(c == 1 for c in calls.values())
+    assert work == sum(len(p) for p in prompts)
+    assert all(len(s.output_ids) == 6 and s.status is Status.FINISHED for s in seqs)
+
+
+def test_all_requests_complete_with_bounded_work():
+    sched = Scheduler(FakeCache(4), max_num_seqs=4, max_batch_tokens=8192, eos_id=None)
+    seqs = _mk([[i + 1, i + 2, i + 3] for i in range(24)], 5)
+    pre, _, _, steps = _run(sched, seqs, 5)
+    assert pre == 0 and all(len(s.output_ids) == 5 for s in seqs)
+    assert steps <= 6 * (24 // 4 + 5)
+
+
+def _admit(sched, seq):
+    sched.add(seq)
+    batch, is_prefill = sched.schedule()
+    assert is_prefill and seq in batch
+    sched.cache.ensure_capacity([seq.slot], [seq.num_prompt])
+    seq.length = seq.num_prompt
+    seq.output_ids.append(7)
+    sched.postprocess(batch, is_prefill)
+
+
+def test_count_cap_never_preempts():
+    cache = FakeCache(3)
+    sched = Scheduler(cache, max_num_seqs=3, max_batch_tokens=8192, eos_id=None)
+    for i, p in enumerate([[1, 2], [3, 4], [5, 6]]):
+        _admit(sched, Sequence(i, p, SamplingParams(max_tokens=50)))
+    sched.add(Sequence(99, [7, 8], SamplingParams(max_tokens=50)))
+    batch, is_prefill = sched.schedule()
+    assert not is_prefill and len(batch) == 3 and len(sched.waiting) == 1
+
+
+def test_preemption_only_on_block_exhaustion():
+    cache = FakeCache(4)
+    sched = Scheduler(cache, max_num_seqs=4, max_batch_tokens=8192, eos_id=None)
+    _admit(sched, Sequence(0, [1, 2, 3], SamplingParams(max_tokens=50)))
+    _admit(sched, Sequence(1, [4, 5, 6], SamplingParams(max_tokens=50)))
+    sched.running[1].output_ids.append(7)
+    cache._free_blocks.clear()
+    sched.add(Sequence(2, [8, 9], SamplingParams(max_tokens=50)))
+    batch, is_prefill = sched.schedule()
+    assert is_prefill and batch
+    assert 0 not in {s.seq_id for s in sched.running}
+    victim = next(s for s in list(sched.waiting) + batch if s.seq_id == 0)
+    assert victim.prompt_ids == [1, 2, 3, 7]  # recomputed through its generated token
+
+
+def test_batch_token_budget_splits_admission():
+    sched = Scheduler(FakeCache(8), max_num_seqs=8, max_batch_tokens=10, eos_id=None)
+    for i in range(4):
+        sched.add(Sequence(i, [1] * 6, SamplingParams(max_tokens=3)))
+    batch, is_prefill = sched.schedule()
+    assert is_prefill and [s.seq_id for s in batch] == [0]  # 6 + 6 > 10
+
+
+def test_eos_finishes_and_frees_the_slot():
+    cache = FakeCache(2)
+    sched = Scheduler(cache, max_num_seqs=2, max_batch_tokens=8192, eos_id=5)
+    _admit(sched, Sequence(0, [1, 2], SamplingParams(max_tokens=50)))
+    sched.running[0].output_ids.append(5)
+    sched.postprocess([], False)
+    assert not sched.running and cache.has_free_slot() and len(cache._free_slots) == 2
+
+
+def test_cancel_waiting_and_running():
+    cache = FakeCache(2)
+    sched = Scheduler(cache, max_num_seqs=2, max_batch_tokens=8192, eos_id=None)
+    _admit(sched, Sequence(0, [1, 2], SamplingParams(max_tokens=50)))
+    sched.add(Sequence(1, [3], SamplingParams(max_tokens=50)))
+    free_before = len(cache._free_slots)
+    assert sched.cancel(1) and len(cache._free_slots) == free_before
+    assert sched.cancel(0) and len(cache._free_slots) == free_before + 1
+    assert not sched.cancel(0) and not sched.has_work()
