@@ -528,6 +528,63 @@ def run_prefill(args):
     print(json.dumps(line), flush=True)
 
 
+def run_codec(args):
+    """the inter-stage codec. x bf16 [T, 4096], N(0,1) with 0.1% of the
+    channels (4) scaled x20; block-128 Hadamard, per-token absmax, int8 and int4. The
+    encoder on GPU 0 stores its codes straight into GPU 1's buffer over NVLink (local when
+    only one GPU is visible); GPU 1 decodes. Device time (CUDA events) of encode (codes
+    crossing NVLink inside it) and of decode, per T; bytes moved per token; round-trip SQNR
+    against the reference's bars."""
+    from superl8_serve_b200 import ops
+    from superl8_serve_b200._lib import call
+    from superl8_serve_b200.dist import accuracy_report
+
+    src = torch.device("cuda", 0)
+    dst = torch.device("cuda", 1 if torch.cuda.device_count() > 1 else 0)
+    if dst != src:
+        call("s8b_enable_peer_access", 0, 1)
+    D, reps = 4096, 50
+    rng = np.random.default_rng(0)
+    cols = rng.choice(D, 4, replace=False)
+    rows = []
+    for scheme in ("int8-had", "int4-had"):
+        for T in (1, 16, 64, 256, 1024):
+            xh = rng.standard_normal((T, D)).astype(np.float32)
+            xh[:, cols] *= 20
+            x = torch.from_numpy(xh).to(torch.bfloat16).to(src)
+            nbytes, nsc = ops.codec_sizes(T, D, scheme)
+            pay = torch.empty(nbytes, dtype=torch.uint8, device=dst)
+            sc = torch.empty(max(nsc, 1), dtype=torch.float32, device=dst)
+            with torch.cuda.device(src):
+                ms_enc = time_kernel(lambda: ops.codec_encode(x, None, scheme, payload=pay,
+                                                              scales=sc), reps)
+            with torch.cuda.device(dst):
+                out = torch.empty(T, D, dtype=torch.bfloat16, device=dst)
+                ms_dec = time_kernel(lambda: ops.codec_decode(pay, sc, T, D, 0, scheme,
+                                                              torch.bfloat16, out_a=out), reps)
+                torch.cuda.synchronize(dst)
+            rep = accuracy_report(x.float().cpu(), out.float().cpu(), scheme)
+            wire = nbytes + 4 * nsc
+            rows.append({"scheme": scheme, "T": T, "encode_us": ms_enc * 1e3,
+                         "decode_us": ms_dec * 1e3, "wire_bytes_per_token": wire / T,
+                         "encode_gbs": (2 * T * D + wire) / ms_enc / 1e6,
+                         "sqnr_db": rep["sqnr_db"], "sqnr_pass": rep["sqnr_pass"],
+                         "cos": rep["cos"]})
+    big = [r for r in rows if r["T"] == 1024 and r["scheme"] == "int8-had"][0]
+    line = {
+        "metric": "inter-stage codec: encode + NVLink store + decode (BASELINE config 2)",
+        "value": 1024 / ((big["encode_us"] + big["decode_us"]) / 1e6), "unit": "tokens/s",
+        "n_gpus": 2 if dst != src else 1, "steps": reps, "warmup": 1,
+        "ms_per_step": (big["encode_us"] + big["decode_us"]) / 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 -> int8 / int4 codes",
+        "data": "synthetic N(0,1), 4 outlier channels x20",
+        "config": {"workload": "codec microbench, D = 4096", "transfer":
+                   "peer stores GPU0 -> GPU1" if dst != src else "local (one GPU visible)"},
+        "rows": rows,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -544,8 +601,9 @@ def main():
     ap.add_argument("--ep", type=int, default=1,
                     help="MoE models: experts of each layer split over this many GPUs of the "
                          "stage (in-process, cuda:0..ep-1)")
-    ap.add_argument("--mode", default="decode", choices=["decode", "prefill"],
-                    help="prefill: varlen prefill throughput of --batch prompts of --ctx tokens")
+    ap.add_argument("--mode", default="decode", choices=["decode", "prefill", "codec"],
+                    help="prefill: varlen prefill throughput of --batch prompts of --ctx tokens; "
+                         "codec: the inter-stage codec microbench (config 2)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: fewer layers than the model's 36 (small ncu case)")
     args = ap.parse_args()
@@ -555,6 +613,8 @@ def main():
         return run_reference(args)
     if args.mode == "prefill":
         return run_prefill(args)
+    if args.mode == "codec":
+        return run_codec(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world > 1 or args.gpus > 1:
         from superl8_serve_b200.multistage import run_bench_multi
