@@ -578,6 +578,3 @@ class StageRunner:
             call("s8b_codec_encode", ptr(self.h), ptr(self.res), M, self.H, self.H, CODEC[scheme],
                  pay.data_ptr(), sc.data_ptr(), 0, st)
 
-    def kernels_per_run(self) -> int:
-        n = 1 + 9 * len(self.model.layers)
-        return n + (3 if self.model.is_last else 1)
