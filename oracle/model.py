@@ -13,8 +13,9 @@ Restates, on the CPU, one decode step of superl8-serve's layer-split pipeline:
 * last stage: final RMSNorm with the residual, int8 LM head (quantized even when tied,
   ``superl8serve/models/qwen3.py:161-166``), greedy argmax.
 
-Prompts are consumed by decode steps (token t of every prompt at step t); the varlen
-prefill kernel is outside this path.
+``generate`` consumes prompts by decode steps (token t of every prompt at step t);
+``prefill`` restates the varlen prefill, which gives the same tokens and logits;
+``generate_sampled`` restates the sampler (``oracle.sampler``).
 """
 
 from __future__ import annotations

@@ -105,11 +105,44 @@ class LMHead(nn.Module):
 
 
 class Sampler(nn.Module):
-    """Greedy fast path of ``Sampler`` (``superl8serve/layers/sampler.py:51-63``): argmax,
-    lowest index on ties. Temperature sampling is outside this path and raises."""
+    """``Sampler`` (``superl8serve/layers/sampler.py:20-156``) with its signature. An
+    all-greedy batch is the argmax kernel (lowest index on ties, ``:51-63``); otherwise
+    ``s8b_sample`` applies the repetition penalty over each row's ``input_ids`` history,
+    temperature, top-k and top-p, and draws one token per row. The draw is an inverse-CDF
+    draw keyed by a per-row seed taken from torch's RNG (``torch.manual_seed`` makes it
+    repeatable) instead of the reference's Gumbel noise; the distribution is the same.
+    Host-side ``logit_processors`` are not supported."""
 
-    def forward(self, logits, temperatures=None, *args, all_greedy=None, **kw):
+    def forward(self, logits, temperatures=None, top_p=None, top_k=None,
+                repetition_penalty=None, logit_processors=None, input_ids=None, *,
+                all_greedy=None, **kw):
         _cuda(logits, "Sampler")
-        if temperatures is not None and not bool((temperatures == 0).all()):
-            raise NotImplementedError("only greedy sampling is on the s8b decode path")
-        return ops.argmax(logits.contiguous()).long()
+        if logit_processors is not None and any(logit_processors):
+            raise NotImplementedError("host logit processors are not on the s8b decode path")
+        logits = logits.contiguous()
+        M, V = logits.shape
+        dev = logits.device
+        greedy = temperatures is None or bool((temperatures == 0).all())
+        no_pen = repetition_penalty is None or bool((repetition_penalty == 1.0).all())
+        if greedy and no_pen:
+            return ops.argmax(logits).long()
+        if not no_pen and input_ids is None:
+            raise ValueError("input_ids are required for repetition_penalty")
+        hist_rows = input_ids if input_ids is not None else [[] for _ in range(M)]
+        cap = max(1, max(len(h) for h in hist_rows))
+        hist = torch.zeros(M, cap, dtype=torch.int32)
+        for i, h in enumerate(hist_rows):
+            if h:
+                hist[i, : len(h)] = torch.tensor(h, dtype=torch.int32)
+        pos = torch.tensor([max(len(h) - 1, 0) for h in hist_rows], dtype=torch.int32)
+        last = torch.tensor([h[-1] if h else 0 for h in hist_rows], dtype=torch.int32)
+        f32 = lambda t, d: (torch.full((M,), d, dtype=torch.float32) if t is None  # noqa: E731
+                            else t.detach().float().reshape(M).cpu())
+        seeds = torch.randint(0, 2 ** 62, (M,), dtype=torch.int64)
+        out = ops.sample(logits, f32(temperatures, 0.0).to(dev),
+                         top_k=None if top_k is None else top_k.to(torch.int32).reshape(M).to(dev),
+                         top_p=None if top_p is None else f32(top_p, 1.0).to(dev),
+                         penalty=None if repetition_penalty is None else f32(repetition_penalty, 1.0).to(dev),
+                         input_ids=last.to(dev), positions=pos.to(dev), history=hist.to(dev),
+                         seeds=seeds.to(dev))
+        return out.long()

@@ -112,3 +112,22 @@ def test_pipeline_engine_sampling_params():
         prompts, 6, [{"temperature": 0.9, "top_k": 30, "top_p": 0.9, "repetition_penalty": 1.1,
                       "seed": 3}, {"temperature": 0.0}])
     assert outs == ref
+
+
+def test_sampler_layer_reference_signature():
+    """``layers.Sampler`` with the reference's arguments: greedy rows are the argmax; a
+    top_k = 1 row is its argmax too; a penalised greedy row follows the oracle recipe."""
+    from superl8_serve_b200.layers import Sampler
+
+    rng = np.random.default_rng(2)
+    V = 1000
+    logits = on.round_bf16((2.0 * rng.standard_normal((3, V))).astype(np.float32))
+    x = torch.from_numpy(logits).to(torch.bfloat16).to(DEV)
+    hist = [[5, 9, int(np.argmax(logits[2]))], [1], [int(np.argmax(logits[2])), 4]]
+    torch.manual_seed(0)
+    out = Sampler()(x, torch.tensor([0.0, 1.0, 0.0], device=DEV),
+                    top_k=torch.tensor([0, 1, 0], device=DEV),
+                    repetition_penalty=torch.tensor([1.0, 1.0, 3.0], device=DEV),
+                    input_ids=hist).cpu().tolist()
+    assert out[0] == int(np.argmax(logits[0])) and out[1] == int(np.argmax(logits[1]))
+    assert out[2] == sample_row(logits[2], 0.0, 0, 1.0, 3.0, hist[2], len(hist[2]) - 1, 0)
