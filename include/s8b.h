@@ -379,6 +379,67 @@ int s8b_sample(const void *logits, int dtype, int M, int V, const float *tempera
                int history_cap, const uint64_t *seeds, void *workspace, size_t workspace_bytes,
                int32_t *out, void *stream);
 
+/* ---- whole stage step ------------------------------------------------------------------
+ * One decode (or prefill-chunk) step of one pipeline stage for one micro-batch of M rows,
+ * enqueued on `stream` from a plain-pointer descriptor: the per-stage loop of
+ * PipelineEngine._decode_microbatched (superl8serve/dist/pipeline.py:997-1040) over
+ * Qwen3DecoderLayer.forward (superl8serve/models/qwen3.py:70-80), for hosts that drive the
+ * library without Python. It launches exactly the kernels, in the same order, that the
+ * Python stage runtime launches, so the two give identical results:
+ *   [first] s8b_embed(ids) | [else] s8b_codec_decode(in_payload)
+ *   per layer: rmsnorm_quant -> qkv GEMM -> qkv_post -> paged attention -> o GEMM ->
+ *              rmsnorm_quant -> gate_up GEMM -> silu_mul_quant -> down GEMM
+ *              (MoE layer: route -> grouped gate_up -> silu_mul_quant -> grouped down -> combine)
+ *   [last]  rmsnorm_quant(final norm) -> head GEMM -> argmax | s8b_sample (writes ids)
+ *   [else]  s8b_codec_encode(h, res) into out_payload (may be a peer's memory)
+ * GEMMs run on the tensor cores (packed weight images) when tc_min > 0, M >= tc_min and a
+ * packed image is given, with split-K partials in `part` between a GEMM and the row kernel
+ * that follows it; otherwise on the dp4a path. Buffers are sized for M rows as the Python
+ * runtime sizes them (StageRunner). Expert shards on other GPUs are not handled here.   */
+typedef struct S8bLayerDesc {
+  const int8_t *qkv_w, *qkv_packed; const float *qkv_s;
+  const int8_t *o_w, *o_packed; const float *o_s;
+  const int8_t *gu_w, *gu_packed; const float *gu_s; /* NULL in a sparse-MoE layer     */
+  const int8_t *d_w, *d_packed; const float *d_s;
+  const void *in_norm, *post_norm, *q_norm, *k_norm; /* gains, activation dtype        */
+  int8_t *kc; float *ks; int8_t *vc; float *vs;      /* this layer's paged KV pool      */
+  int moe_experts;                                   /* > 0: sparse-MoE FFN below       */
+  int moe_top_k, moe_ffn, moe_norm_topk;
+  float moe_scaling;
+  const float *router;
+  const int8_t *moe_gu_w; const float *moe_gu_s; const int8_t *moe_d_w; const float *moe_d_s;
+} S8bLayerDesc;
+
+typedef struct S8bStageDesc {
+  int n_layers, M, H, Hq, Hkv, D, F, V;
+  int block_size, max_blocks, max_ctx, rope_len, dtype, tc_min;
+  int first_model_layer; /* 1: this stage's first layer is the model's layer 0            */
+  int head;              /* last stage: 0 skips final norm / head / token choice           */
+  float eps, scale;
+  const S8bLayerDesc *layers;
+  const float *cos_tab, *sin_tab;
+  const void *embed;     /* first stage only                                               */
+  const void *final_norm; const int8_t *head_w, *head_packed; const float *head_s; /* last */
+  int32_t *ids, *positions, *context_lens, *block_table;
+  const void *in_payload; const float *in_scales;  /* stages > 0                          */
+  void *out_payload; float *out_scales;            /* all but the last stage              */
+  int scheme;                                      /* S8B_CODEC_*                         */
+  void *h, *res, *qkv, *attn, *gu, *logits;
+  int8_t *xq; float *xs; int8_t *q_i8; float *q_s; int32_t *part;
+  void *attn_ws; size_t attn_ws_bytes; void *tc_ws; size_t tc_ws_bytes;
+  void *moe_y, *moe_topw, *moe_gu, *moe_contrib; int8_t *moe_aq; float *moe_as;
+  int32_t *moe_topi, *moe_offsets, *moe_sorted_assign, *moe_sorted_token, *moe_assign_pos;
+  /* sampling (temperature NULL: greedy argmax)                                           */
+  const float *temperature, *top_p, *penalty; const int32_t *top_k;
+  const int32_t *input_ids; int32_t *history; int history_cap; const uint64_t *seeds;
+  void *sample_ws; size_t sample_ws_bytes;
+} S8bStageDesc;
+
+int s8b_stage_step(const S8bStageDesc *desc, void *stream);
+/* sizeof of the two descriptors, for bindings that build them field by field */
+size_t s8b_stage_desc_size(void);
+size_t s8b_layer_desc_size(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -84,6 +84,9 @@ SIGNATURES: dict[str, tuple] = {
     "s8b_rans_histogram": (_i, [_vp, _sz, _vp, _vp]),
     "s8b_rans_encode": (_i, [_vp, _sz, _vp, _i, _vp, _sz, _vp, _vp]),
     "s8b_rans_decode": (_i, [_vp, _vp, _i, _vp, _sz, _vp, _vp, _vp]),
+    "s8b_stage_step": (_i, [_vp, _vp]),
+    "s8b_stage_desc_size": (_sz, []),
+    "s8b_layer_desc_size": (_sz, []),
     "s8b_sample_workspace_size": (_sz, [_i, _i]),
     "s8b_sample": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _sz,
                         _vp, _vp]),

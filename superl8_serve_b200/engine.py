@@ -129,6 +129,13 @@ class DecodePipeline:
         self._pf = None
         self._sampling = None
         self.scratch_block = None
+        self.native = False
+
+    def set_native(self, on: bool = True):
+        """Run every stage step (decode and prefill) as one ``s8b_stage_step`` call."""
+        self.native = on
+        for r in self.runners + (self._pf[0] if self._pf is not None else []):
+            r.native = on
 
     # ----------------------------------------------------------------- sequence state ----
     def add_sequences(self, n: int | None = None):
@@ -345,6 +352,8 @@ class DecodePipeline:
         mp = self.prefill_chunk
         runners = [StageRunner(mdl, pool, mp, self.max_len, self.dtype, share=r)
                    for mdl, pool, r in zip(self.models, self.pools, self.runners)]
+        for r in runners:
+            r.native = self.native
         from .ops import codec_sizes
 
         nbytes, nsc = codec_sizes(mp, 2 * self.cfg.hidden_size, self.wire_scheme)

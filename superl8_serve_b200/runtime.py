@@ -314,6 +314,8 @@ class StageRunner:
         this one reuses (a prefill runner beside the decode runner holds no second copy)."""
         cfg = model.cfg
         self.model, self.pool, self.m, self.max_ctx, self.dtype = model, pool, m, max_ctx, dtype
+        # True: run() is one s8b_stage_step call (native replay of the same launches)
+        self.native = False
         self.H = cfg.hidden_size
         self.D = cfg.resolved_head_dim()
         self.Hq, self.Hkv = cfg.num_attention_heads, cfg.num_key_value_heads
@@ -544,6 +546,14 @@ class StageRunner:
         """
         M = self.m if M is None else M
         st = stream()
+        if self.native:
+            import ctypes
+
+            from .native import stage_desc
+
+            d = stage_desc(self, mb, M, boundary_in, boundary_out, head)
+            call("s8b_stage_step", ctypes.addressof(d), st)
+            return
         first_model_layer = self.model.start == 0
         if self.model.is_first:
             call("s8b_embed", ptr(mb.ids), ptr(self.model.embed), M, self.H, ptr(self.h), 0, st)

@@ -165,3 +165,15 @@ def test_transfer_handle_wire_bytes_match_reference(host_golden):
                            torch.empty(shp, dtype=dt), torch.empty(sc), 0.0, 0.0)
         assert h.on_wire_bytes == want
         assert h.theoretical_wire_ms == pytest.approx(want_ms)
+
+
+def test_stage_descriptor_layout_matches_the_library(lib):
+    """The ctypes mirrors of S8bStageDesc / S8bLayerDesc have the C sizes, and a missing
+    descriptor is rejected before any CUDA call."""
+    import ctypes
+
+    from superl8_serve_b200.native import LayerDesc, StageDesc
+
+    assert ctypes.sizeof(StageDesc) == lib.s8b_stage_desc_size()
+    assert ctypes.sizeof(LayerDesc) == lib.s8b_layer_desc_size()
+    assert lib.s8b_stage_step(None, None) == -8
