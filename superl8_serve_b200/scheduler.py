@@ -184,12 +184,16 @@ class ContinuousEngine:
 
     def __init__(self, models, *, max_num_seqs: int = 8, max_len: int = 2048,
                  max_batch_tokens: int = 8192, eos_id: int | None = None,
-                 wire_scheme: str = "int8-had"):
-        from .engine import DecodePipeline
+                 wire_scheme: str = "int8-had", pipeline=None):
+        """``pipeline``: an already built pipeline with ``max_num_seqs`` rows and one spare
+        block (default: a ``DecodePipeline`` over ``models``)."""
+        if pipeline is None:
+            from .engine import DecodePipeline
 
-        self.pipe = DecodePipeline(models, batch=max_num_seqs, n_micro=1, max_len=max_len,
-                                   wire_scheme=wire_scheme,
-                                   num_blocks=max_num_seqs * -(-max_len // 16) + 1)
+            pipeline = DecodePipeline(models, batch=max_num_seqs, n_micro=1, max_len=max_len,
+                                      wire_scheme=wire_scheme,
+                                      num_blocks=max_num_seqs * -(-max_len // 16) + 1)
+        self.pipe = pipeline
         self.pipe.reserve_scratch_block()
         self.max_len = max_len
         self.sched = Scheduler(_SlotCache(self.pipe.alloc), max_num_seqs=max_num_seqs,

@@ -158,3 +158,108 @@ def test_cancel_waiting_and_running():
     assert sched.cancel(1) and len(cache._free_slots) == free_before
     assert sched.cancel(0) and len(cache._free_slots) == free_before + 1
     assert not sched.cancel(0) and not sched.has_work()
+
+
+# ---- ContinuousEngine bookkeeping on a model-free pipeline -----------------------------
+
+class FakePipe:
+    """Rows with the DecodePipeline state calls the engine uses; a row's next token is a
+    fixed function of its input id and position (what a per-row model step computes)."""
+
+    def __init__(self, batch, max_len, V=97):
+        from superl8_serve_b200.engine import BlockAllocator
+
+        self.batch, self.max_len, self.V = batch, max_len, V
+        self.max_blocks = -(-max_len // 16)
+        self.alloc = BlockAllocator(batch * self.max_blocks + 1, batch, 16, self.max_blocks)
+        self.scratch_block = None
+        self.pos = [0] * batch
+        self.ids = [0] * batch
+        self.slot_of = [None] * batch
+        self.out = [0] * batch
+        self.kv = {}  # (slot, position) -> token written there
+        self.max_seen_pos = 0
+
+    def reserve_scratch_block(self):
+        self.scratch_block = self.alloc._free_blocks.pop(0)
+        return self.scratch_block
+
+    def set_rows(self, rows, positions, ids, slots):
+        for r, p, i, s in zip(rows, positions, ids, slots):
+            self.pos[r], self.ids[r], self.slot_of[r] = p, i, s
+
+    def prefill(self, prompts, *, slots, reserve=1):
+        for p, s in zip(prompts, slots):
+            for t, tok in enumerate(p):
+                self.kv[(s, t)] = tok
+
+    def set_sampling_rows(self, rows, params, prompts):
+        raise AssertionError("greedy only here")
+
+    @staticmethod
+    def model(tok, pos, V):
+        return (tok * 31 + pos * 7 + 3) % V
+
+    def _enqueue(self):
+        for r in range(self.batch):
+            assert self.pos[r] < self.max_len
+            self.max_seen_pos = max(self.max_seen_pos, self.pos[r])
+            s = self.slot_of[r]
+            if s is not None:
+                # causal history must be present: every position before this one
+                assert all((s, t) in self.kv for t in range(self.pos[r])), (r, s, self.pos[r])
+                self.kv[(s, self.pos[r])] = self.ids[r]
+            self.out[r] = self.model(self.ids[r], self.pos[r], self.V)
+            self.ids[r] = self.out[r]
+            self.pos[r] += 1
+
+    def synchronize(self):
+        pass
+
+    def tokens(self):
+        import torch
+
+        return torch.tensor(self.out)
+
+
+def _solo(prompt, n, V=97):
+    toks, pos, tok, out = list(prompt), len(prompt) - 1, prompt[-1], []
+    for _ in range(n):
+        tok = FakePipe.model(tok, pos, V)
+        out.append(tok)
+        pos += 1
+    return out
+
+
+def test_continuous_engine_bookkeeping_on_a_fake_pipeline():
+    from superl8_serve_b200.dist.pipeline import SamplingParams
+    from superl8_serve_b200.scheduler import ContinuousEngine
+
+    pipe = FakePipe(batch=3, max_len=48)
+    eng = ContinuousEngine(None, max_num_seqs=3, max_len=48, max_batch_tokens=10, pipeline=pipe)
+    prompts = [[5, 6, 7], [1], [9, 9, 9, 9, 9, 9], [2, 3], [4, 4, 4, 4], [8], [11, 12, 13]]
+    maxt = [5, 9, 3, 7, 4, 12, 6]
+    outs = eng.generate(prompts, [SamplingParams(max_tokens=m) for m in maxt])
+    for p, m, o in zip(prompts, maxt, outs):
+        assert o == _solo(p, m)
+    assert not eng.sched.has_work()
+    assert len(pipe.alloc._free_slots) == 3  # every slot back
+    assert pipe.max_seen_pos < 48
+
+
+def test_continuous_engine_stops_at_eos_and_cancels():
+    from superl8_serve_b200.dist.pipeline import SamplingParams
+    from superl8_serve_b200.scheduler import ContinuousEngine
+
+    pipe = FakePipe(batch=2, max_len=64)
+    first = _solo([5, 6, 7], 1)[0]
+    eng = ContinuousEngine(None, max_num_seqs=2, max_len=64, eos_id=first, pipeline=pipe)
+    a = eng.add_request([5, 6, 7], SamplingParams(max_tokens=20))
+    b = eng.add_request([1, 2], SamplingParams(max_tokens=20))
+    c = eng.add_request([3], SamplingParams(max_tokens=20))
+    while eng.seqs[a].status.name != "FINISHED":
+        eng.step()
+    assert eng.seqs[a].output_ids == [first]
+    assert eng.cancel(b) and eng.cancel(c)
+    eng.run()
+    assert len(pipe.alloc._free_slots) == 2
