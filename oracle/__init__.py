@@ -20,7 +20,12 @@ What it restates (all citations are paths inside the superl8-serve project):
   paged GQA decode attention (``superl8serve/engine/kv_cache.py:1148-1201``);
 * the inter-stage activation codec (``superl8serve/dist/__init__.py:163-302``,
   ``superl8serve/dist/transfer_model.py:25-41``) and the stage split
-  (``superl8serve/dist/pipeline.py:452``).
+  (``superl8serve/dist/pipeline.py:452``);
+* the varlen prefill (``superl8serve/dist/pipeline.py:908-984``; ``model.OraclePipeline
+  .prefill``);
+* the sparse-MoE FFN of Qwen3-MoE (``superl8serve/models/moe.py:88-141``; ``moe``);
+* the rANS entropy stage (``superl8serve/dist/entropy.py``; ``entropy``) and the sampling
+  recipe that follows ``superl8serve/layers/sampler.py:22-156`` (``sampler``).
 
 The arithmetic kernels themselves live in the third-party ``superl8`` package, which is
 not vendored in the reference and is not installed here (only its call sites are
@@ -31,4 +36,4 @@ At the ``superl8`` kernel boundary itself parity is unpinned (no golden integer 
 exist in the reference); the composition around it is pinned.
 """
 
-from . import numerics, kernels, codec, model  # noqa: F401
+from . import numerics, kernels, codec, model, moe, entropy, sampler  # noqa: F401
