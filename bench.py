@@ -528,13 +528,35 @@ def run_prefill(args):
     print(json.dumps(line), flush=True)
 
 
+def time_graph(fn, reps: int, device) -> float:
+    """Average ms of fn() (one launch per call) from a CUDA graph holding `reps` calls, so the
+    host launch rate does not enter the figure."""
+    fn()
+    torch.cuda.synchronize(device)
+    s = torch.cuda.Stream(device=device)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.device(device), torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(reps):
+                fn()
+    g.replay()
+    torch.cuda.synchronize(device)
+    with torch.cuda.device(device):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        b.synchronize()
+    return a.elapsed_time(b) / reps
+
+
 def run_codec(args):
     """the inter-stage codec. x bf16 [T, 4096], N(0,1) with 0.1% of the
     channels (4) scaled x20; block-128 Hadamard, per-token absmax, int8 and int4. The
     encoder on GPU 0 stores its codes straight into GPU 1's buffer over NVLink (local when
-    only one GPU is visible); GPU 1 decodes. Device time (CUDA events) of encode (codes
-    crossing NVLink inside it) and of decode, per T; bytes moved per token; round-trip SQNR
-    against the reference's bars."""
+    only one GPU is visible); GPU 1 decodes. Device time (CUDA events around a CUDA graph of
+    repeated launches) of encode (codes crossing NVLink inside it) and of decode, per T; bytes
+    moved per token; round-trip SQNR against the reference's bars."""
     from superl8_serve_b200 import ops
     from superl8_serve_b200._lib import call
     from superl8_serve_b200.dist import accuracy_report
@@ -555,14 +577,12 @@ def run_codec(args):
             nbytes, nsc = ops.codec_sizes(T, D, scheme)
             pay = torch.empty(nbytes, dtype=torch.uint8, device=dst)
             sc = torch.empty(max(nsc, 1), dtype=torch.float32, device=dst)
-            with torch.cuda.device(src):
-                ms_enc = time_kernel(lambda: ops.codec_encode(x, None, scheme, payload=pay,
-                                                              scales=sc), reps)
-            with torch.cuda.device(dst):
-                out = torch.empty(T, D, dtype=torch.bfloat16, device=dst)
-                ms_dec = time_kernel(lambda: ops.codec_decode(pay, sc, T, D, 0, scheme,
-                                                              torch.bfloat16, out_a=out), reps)
-                torch.cuda.synchronize(dst)
+            ms_enc = time_graph(lambda: ops.codec_encode(x, None, scheme, payload=pay, scales=sc),
+                                reps, src)
+            out = torch.empty(T, D, dtype=torch.bfloat16, device=dst)
+            ms_dec = time_graph(lambda: ops.codec_decode(pay, sc, T, D, 0, scheme, torch.bfloat16,
+                                                         out_a=out), reps, dst)
+            torch.cuda.synchronize(dst)
             rep = accuracy_report(x.float().cpu(), out.float().cpu(), scheme)
             wire = nbytes + 4 * nsc
             rows.append({"scheme": scheme, "T": T, "encode_us": ms_enc * 1e3,
