@@ -22,6 +22,7 @@ would need a host read-back inside the step.
 
 from __future__ import annotations
 
+import dataclasses
 import itertools
 from dataclasses import dataclass, field
 
@@ -147,9 +148,12 @@ class PipelineEngine:
         self.n_micro = n_micro
         self.prefill = prefill  # False: prompts teacher-forced through decode steps
         self._ids = itertools.count()
+        self.max_batch_tokens = max_batch_tokens
         self._pending: dict[int, tuple[list[int], SamplingParams]] = {}
         self._out: dict[int, list[int]] = {}
         self._pipe: DecodePipeline | None = None
+        self._cont = None  # ContinuousEngine behind step()
+        self._cont_ids: dict[int, int] = {}
 
     @classmethod
     def from_stages(cls, stages, cfg, **kwargs):
@@ -205,6 +209,45 @@ class PipelineEngine:
         self._pending.clear()
 
     def generate(self, prompts: list[list[int]], params: SamplingParams | None = None):
+        """All requests as one batch through the stages (prefill, then decode)."""
         sids = [self.add_request(p, params) for p in prompts]
         self.run_pending()
         return [self._out[s] for s in sids]
+
+    # --------------------------------------------------------- continuous batching ----
+    def _continuous(self):
+        if self._cont is None:
+            from ..scheduler import ContinuousEngine
+
+            self._cont = ContinuousEngine([s.model for s in self.stages],
+                                          max_num_seqs=self.max_num_seqs, max_len=self.max_len,
+                                          max_batch_tokens=self.max_batch_tokens,
+                                          eos_id=self.eos_id, wire_scheme=self.wire_scheme)
+            for s, pool in zip(self.stages, self._cont.pipe.pools):
+                s.kv_cache = pool
+        return self._cont
+
+    def step(self):
+        """One scheduler step (``PipelineEngine.step``, ``superl8serve/dist/pipeline.py:620-635``):
+        requests added since the last step join the running batch, then the scheduler
+        either admits (prefills) waiting requests or decodes every running one."""
+        eng = self._continuous()
+        for sid in list(self._pending):
+            prompt, params = self._pending.pop(sid)
+            if params.seed is None:
+                params = dataclasses.replace(params, seed=sid)
+            self._cont_ids[sid] = eng.add_request(prompt, params)
+        eng.step()
+
+    def has_work(self) -> bool:
+        return bool(self._pending) or (self._cont is not None and self._cont.sched.has_work())
+
+    def sequence(self, seq_id: int):
+        """The request's ``Sequence`` (status, prompt, output ids) of a step()-driven run."""
+        return self._cont.seqs[self._cont_ids[seq_id]]
+
+    def forget(self, seq_id: int) -> None:
+        self._out.pop(seq_id, None)
+        cid = self._cont_ids.pop(seq_id, None)
+        if cid is not None:
+            self._cont.seqs.pop(cid, None)

@@ -263,3 +263,29 @@ def test_continuous_engine_stops_at_eos_and_cancels():
     assert eng.cancel(b) and eng.cancel(c)
     eng.run()
     assert len(pipe.alloc._free_slots) == 2
+
+
+def test_pipeline_engine_step_api_on_a_fake_pipeline():
+    """The reference's PipelineEngine request API (add_request / step / sequence / forget)
+    over the continuous engine: requests added between steps join the running batch."""
+    import types
+
+    from superl8_serve_b200.dist.pipeline import PipelineEngine, SamplingParams
+    from superl8_serve_b200.scheduler import ContinuousEngine
+
+    st = types.SimpleNamespace(model=None, kv_cache=None)
+    eng = PipelineEngine.from_stages([st, st], None, max_num_seqs=2, max_len=48)
+    pipe = FakePipe(batch=2, max_len=48)
+    eng._cont = ContinuousEngine(None, max_num_seqs=2, max_len=48, pipeline=pipe)
+    a = eng.add_request([5, 6, 7], SamplingParams(max_tokens=4))
+    eng.step()
+    b = eng.add_request([2, 3], SamplingParams(max_tokens=6))  # joins while a runs
+    c = eng.add_request([9], SamplingParams(max_tokens=3))     # waits for a free slot
+    while eng.has_work():
+        eng.step()
+    assert eng.sequence(a).output_ids == _solo([5, 6, 7], 4)
+    assert eng.sequence(b).output_ids == _solo([2, 3], 6)
+    assert eng.sequence(c).output_ids == _solo([9], 3)
+    assert eng.sequence(a).status.name == "FINISHED"
+    eng.forget(a)
+    assert a not in eng._cont_ids
