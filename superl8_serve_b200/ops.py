@@ -13,6 +13,7 @@ __all__ = [
     "silu_mul_quant", "qkv_post", "kv_write_paged",
     "paged_decode_q8", "paged_decode", "embed", "argmax", "codec_encode", "codec_decode",
     "codec_sizes", "decode_workspace_bytes", "moe_route", "moe_gemm_grouped", "moe_combine",
+    "sample",
 ]
 
 

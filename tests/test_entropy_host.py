@@ -48,3 +48,17 @@ def test_oracle_multi_stream_round_trip(g, S):
     streams, freqs = oe.encode(data, n_streams=S)
     assert len(streams) == S
     assert np.array_equal(oe.decode(streams, freqs, data.size), data)
+
+
+def test_decode_rejects_a_table_that_does_not_sum_to_4096():
+    """Tables are checked on the host before any kernel sees them."""
+    import torch
+
+    from superl8_serve_b200.dist import entropy as ent
+
+    bad = np.zeros(256, np.int32)
+    bad[7] = 4095
+    with pytest.raises(ValueError):
+        ent.decode(torch.zeros(8, dtype=torch.uint8), bad, 10)
+    with pytest.raises(ValueError):
+        ent.decode(torch.zeros(8, dtype=torch.uint8), np.full(255, 16, np.int32), 10)
