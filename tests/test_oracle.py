@@ -194,3 +194,57 @@ def test_paged_decode_matches_dense_softmax():
             ref = (p / p.sum()) @ v
             assert np.abs(out[b, h] - ref).max() < 1e-2 * max(1.0, np.abs(ref).max())
         del rows
+
+
+def test_k_side_int8_meets_reference_bar():
+    """The reference's K-cache bar (superl8-serve tests/test_k8v3_cache.py:113-120): Hadamard
+    rotation, per-row int8, dequantize and rotate back -> cos >= 0.999 and SQNR >= 35 dB."""
+    rng = np.random.default_rng(11)
+    T, Hkv, D, bs = 40, 2, 128, 16
+    k = on.round_bf16(rng.standard_normal((T, Hkv, D)).astype(np.float32))
+    k[:, :, rng.choice(D, 2, replace=False)] *= 10  # outlier channels
+    nb = -(-T // bs)
+    kc = np.zeros((nb, Hkv, bs, D), np.int8)
+    vc = np.zeros_like(kc)
+    ks = np.zeros((nb, Hkv, bs), np.float32)
+    vs = np.zeros_like(ks)
+    ok.kv_write_paged(k, k, kc, ks, vc, vs, np.arange(T, dtype=np.int32), bs)
+    rows = ok.flat_rows(np.arange(T, dtype=np.int32), Hkv, bs).reshape(-1)
+    deq = kc.reshape(-1, D)[rows].astype(np.float32) * ks.reshape(-1)[rows][:, None]
+    back = on.hadamard128(deq).reshape(T, Hkv, D)
+    x, y = k.astype(np.float64).ravel(), back.astype(np.float64).ravel()
+    sqnr = 10 * np.log10((x ** 2).sum() / ((x - y) ** 2).sum())
+    cos = x @ y / np.linalg.norm(x) / np.linalg.norm(y)
+    assert sqnr >= 35.0 and cos >= 0.999
+
+
+def test_paged_int8_decode_meets_reference_bar_against_unquantized_attention():
+    """The reference's paged-decode bar (superl8-serve tests/test_paged_engine.py:98-101):
+    int8 KV (rotated K), int8 query, partitioned softmax with 15-bit p.v against plain fp32
+    attention on the unquantized q, k, v -> cos > 0.995."""
+    rng = np.random.default_rng(12)
+    B, Hq, Hkv, D, bs, ctx = 2, 8, 2, 128, 16, 700
+    q = on.round_bf16(rng.standard_normal((B, Hq, D)).astype(np.float32))
+    k = on.round_bf16(rng.standard_normal((B * ctx, Hkv, D)).astype(np.float32))
+    v = on.round_bf16(rng.standard_normal((B * ctx, Hkv, D)).astype(np.float32))
+    nb = B * -(-ctx // bs)
+    kc = np.zeros((nb, Hkv, bs, D), np.int8)
+    vc = np.zeros_like(kc)
+    ks = np.zeros((nb, Hkv, bs), np.float32)
+    vs = np.zeros_like(ks)
+    per = -(-ctx // bs)
+    bt = np.arange(nb, dtype=np.int32).reshape(B, per)
+    slots = np.concatenate([bt[b][np.arange(ctx) // bs] * bs + np.arange(ctx) % bs
+                            for b in range(B)]).astype(np.int32)
+    ok.kv_write_paged(k, v, kc, ks, vc, vs, slots, bs)
+    qq, qs = ok.quant_q_for_attn(q)
+    out = ok.paged_decode(qq, qs, kc, ks, vc, vs, bt, np.full(B, ctx, np.int32), bs, D ** -0.5)
+    for b in range(B):
+        kb, vb = k[b * ctx:(b + 1) * ctx], v[b * ctx:(b + 1) * ctx]
+        for h in range(Hq):
+            g = h // (Hq // Hkv)
+            s = (kb[:, g].astype(np.float64) @ q[b, h]) * D ** -0.5
+            p = np.exp(s - s.max())
+            ref = (p / p.sum()) @ vb[:, g]
+            got = out[b, h].astype(np.float64)
+            assert got @ ref / np.linalg.norm(got) / np.linalg.norm(ref) > 0.995
