@@ -177,3 +177,40 @@ def test_stage_descriptor_layout_matches_the_library(lib):
     assert ctypes.sizeof(StageDesc) == lib.s8b_stage_desc_size()
     assert ctypes.sizeof(LayerDesc) == lib.s8b_layer_desc_size()
     assert lib.s8b_stage_step(None, None) == -8
+
+
+def test_ctypes_signatures_match_header_prototypes():
+    """Every prototype in include/s8b.h has the same parameter count and C types in the
+    ctypes table the package binds with (a float passed where the C side expects a pointer,
+    or a missing argument, would otherwise go unnoticed until a kernel misbehaves)."""
+    import ctypes as C
+    import re
+
+    text = (REPO / "include" / "s8b.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    text = re.sub(r"typedef struct .*?\} \w+;", "", text, flags=re.S)
+
+    def ctype(param: str):
+        p = " ".join(param.split())
+        if "*" in p:
+            return "ptr"
+        base = p.rsplit(" ", 1)[0] if " " in p else p
+        base = base.replace("const ", "")
+        return {"float": C.c_float, "double": C.c_double, "size_t": C.c_size_t,
+                "int": C.c_int, "int32_t": C.c_int32, "uint32_t": C.c_uint32,
+                "uint64_t": C.c_uint64, "long long": C.c_longlong}[base]
+
+    checked = 0
+    for name, params in re.findall(r"\b(s8b_\w+)\s*\(([^;{]*?)\)\s*;", text):
+        params = params.strip()
+        want = [] if params in ("", "void") else [ctype(q) for q in params.split(",")]
+        got = _lib.SIGNATURES[name][1]
+        assert len(got) == len(want), name
+        for g, w in zip(got, want):
+            if w == "ptr":
+                assert g in (C.c_void_p, C.c_char_p), name
+            else:
+                assert C.sizeof(g) == C.sizeof(w) and (g is C.c_float) == (w is C.c_float) \
+                    and (g is C.c_double) == (w is C.c_double), (name, g, w)
+        checked += 1
+    assert checked >= 55
