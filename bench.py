@@ -228,8 +228,8 @@ def time_kernel(fn, reps: int) -> float:
 
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from one ncu capture of the same
-# launch shape (profiles/attn_persistent_qwen3_8b_b64_ctx2048.md,
-# profiles/gemm_tc_gate_up_qwen3_8b_m64.md); re-captured whenever the kernel changes.
+# launch shape (the attention and gate_up captures summarised under profiles/); re-captured
+# whenever the kernel changes.
 NCU_TRAFFIC = {
     "paged_decode_attention": {"bytes": 279351808 + 10228480,
                                "source": "ncu dram bytes of attn_persistent_kernel (the row "

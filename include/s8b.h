@@ -174,15 +174,17 @@ int s8b_kv_write_paged(const void *k, const void *v, int8_t *kc, float *ks, int8
  * (nullable, together) additionally receive the per-token int8 quantization of the output
  * row (the o_proj input). context_lens[b] >= 1 tokens of row b are attended; max_ctx is an
  * upper bound on every context_lens[b] (sizes the partition grid). Workspace: see
- * s8b_paged_decode_workspace_size; zero-fill it once before first use (it holds completion
- * counters that every launch leaves at zero); launches sharing a workspace must be
- * stream-ordered. D must be 128; block_size a power of two dividing 256.
+ * s8b_paged_decode_workspace_size; zero-fill it once before first use (its first word is the
+ * status word below; the rest needs no initial value, and one workspace serves calls of any
+ * shape it is large enough for); launches sharing a workspace must be stream-ordered.
+ * D must be 128; block_size a power of two dividing 256.
  * Replaces superl8.attn_paged_decode_cached (superl8serve/engine/kv_cache.py:1190-1201). */
 size_t s8b_paged_decode_workspace_size(int B, int Hq, int D, int max_ctx);
 /* Byte offset, inside the decode workspace, of an int32 status word: 0, or S8B_ERR_TIMEOUT
  * when a bounded wait on a tensor-core completion barrier gave up (that launch's output is
- * then invalid). Zero-filled with the workspace; the caller clears it after reading an error.
- * No counterpart in the reference (its kernels have no bounded waits). */
+ * then invalid). It is the workspace's first word for every B and Hq (the function returns
+ * 0). Zero-filled with the workspace; it stays set until the caller clears it after reading
+ * an error. No counterpart in the reference (its kernels have no bounded waits). */
 size_t s8b_paged_decode_status_offset(int B, int Hq);
 /* Selects the kernel behind every paged-decode entry point: 0 (default) = the persistent
  * warp-specialized tensor-core kernel (TMA ring, tcgen05 kind::i8 for q.k and p.v) where the
@@ -209,7 +211,11 @@ int s8b_paged_decode_q8(const int8_t *q_i8, const float *q_s, const int8_t *kc, 
  * device address (cudaGetSymbolAddress, with that device current); make that first call
  * before any stream capture. All calls share the one array, so calls that overlap on the GPU
  * (different streams, or different host threads on the same device) race; serialize them.
- * The array keeps the last call's contents; nothing in it needs to start at zero.
+ * The array keeps the last call's contents. Its layout is a workspace's: the status word
+ * first (see s8b_paged_decode_noalloc_status), then the completion counters of the
+ * per-partition kernels, which every call zeroes before it launches them (a stream-ordered
+ * memset), then the partials, which are written before they are read. So a call never
+ * depends on what an earlier call of another shape, or one that gave up, left behind.
  * It calls no cudaMalloc / cudaFree or other allocating routine.
  * This entry point has no counterpart in the reference.                                   */
 int s8b_paged_decode_q8_noalloc(const int8_t *q_i8, const float *q_s, const int8_t *kc,
@@ -218,6 +224,13 @@ int s8b_paged_decode_q8_noalloc(const int8_t *q_i8, const float *q_s, const int8
                                 void *out, int8_t *out_q, float *out_s, int B, int Hq, int Hkv,
                                 int D, int block_size, int max_blocks, int max_ctx, float scale,
                                 int dtype, void *stream);
+/* Status word of the no-allocation entry point on the current device: stores the word's value
+ * in *previous and replaces it with `replace_with` (0 clears it). The word is 0, or
+ * S8B_ERR_TIMEOUT once a bounded wait of a call gave up (that call's output is invalid); it
+ * stays set until replaced. Call it after synchronizing the streams the decode calls ran on:
+ * it reads and writes with plain synchronous copies. It allocates nothing.
+ * No counterpart in the reference (its kernels have no bounded waits).                    */
+int s8b_paged_decode_noalloc_status(int32_t *previous, int32_t replace_with);
 
 /* Same attention with the reference's query layout: q [B, Hq, D] in dtype (rotated and
  * quantized internally into the workspace, which must be zero-filled once likewise).

@@ -246,11 +246,16 @@ __device__ __forceinline__ int dp2a_hi(int a, int b, int c) { return __dp2a_hi(a
 //     memory (integer, exact), o = f32(o_int) * wmax/32767 -> workspace.
 //  5. the CTA that finishes a (row, kv head) last (counter) merges its partitions in index
 //     order into the output; the CTA that finishes a row last quantizes the row (o_proj input).
-//     Both counters return to zero, so the workspace needs zero-filling only once.
+//     The host zeroes both counter arrays (one stream-ordered memset) before every launch of
+//     these kernels, so a previous launch with another shape, or one that gave up, can never
+//     leave a counter behind.
+//
+// Workspace layout: the status word sits at byte 0 for every shape, the counters follow at
+// byte 256 (sized for this launch's B and Hq), the partials after them.
 struct DecodeWs {
+  int32_t *status;     // [1] S8B_ERR_TIMEOUT if a bounded wait of the tensor-core kernel gave up
   int32_t *cnt_group;  // [B*Hq] (row, kv head) completion counters (B*Hkv used)
   int32_t *cnt_row;    // [B]
-  int32_t *status;     // [1] S8B_ERR_TIMEOUT if a bounded wait of the tensor-core kernel gave up
   float *part_o;       // [B, Hq, P, 128]
   float *part_ml;      // [B, Hq, P, 2]
 };
@@ -1399,8 +1404,15 @@ inline int num_parts(int max_ctx) { return (max_ctx + kPart - 1) / kPart; }
 // tensor-core kernel (default); 1: CUDA-core partition kernel; 2: per-partition tensor-core
 int g_attn_impl = 0;
 
+constexpr size_t kStatusBytes = 256;  // the status word, padded to keep the counters aligned
+
+size_t counter_words(int B, int Hq) {
+  return static_cast<size_t>(B) * Hq + static_cast<size_t>(B);
+}
+
+// status region + completion counters, rounded to 256 bytes
 size_t counters_bytes(int B, int Hq) {
-  return (static_cast<size_t>(B) * Hq * 4 + static_cast<size_t>(B) * 4 + 16 + 255) / 256 * 256;
+  return kStatusBytes + (counter_words(B, Hq) * 4 + 255) / 256 * 256;
 }
 
 size_t part_bytes(int B, int Hq, int max_ctx) {
@@ -1412,9 +1424,9 @@ DecodeWs carve_ws(void *base, int B, int Hq, int max_ctx) {
   uint8_t *p = static_cast<uint8_t *>(base);
   const size_t P = num_parts(max_ctx);
   DecodeWs w;
-  w.cnt_group = reinterpret_cast<int32_t *>(p);
+  w.status = reinterpret_cast<int32_t *>(p);
+  w.cnt_group = reinterpret_cast<int32_t *>(p + kStatusBytes);
   w.cnt_row = w.cnt_group + static_cast<size_t>(B) * Hq;
-  w.status = w.cnt_row + B;
   w.part_o = reinterpret_cast<float *>(p + counters_bytes(B, Hq));
   w.part_ml = w.part_o + static_cast<size_t>(B) * Hq * P * kHd;
   return w;
@@ -1508,6 +1520,12 @@ int launch_decode(const int8_t *q_i8, const float *q_s, const int8_t *kc, const 
                                         out_q, out_s, B, Hq, Hkv, bs, bs_log2, max_blocks, P,
                                         scale, w, st);
     if (rc != 1) return rc;
+  }
+  // The partition kernels count completions; their counters start from zero on every launch.
+  const cudaError_t ce = cudaMemsetAsync(w.cnt_group, 0, counter_words(B, Hq) * 4, st);
+  if (ce != cudaSuccess) {
+    record_cuda_error(ce);
+    return S8B_ERR_CUDA;
   }
   if (g_attn_impl != 1) {
     switch (G) {
@@ -1749,13 +1767,31 @@ extern "C" int s8b_paged_decode_q8_noalloc(const int8_t *q_i8, const float *q_s,
   float *part = nullptr;
   const int rc = static_scratch_address(&part);
   if (rc) return rc;
-  // Partition partials are fully written before the combine reads them, so nothing in the
-  // shared array has to start at zero.
+  // The array is laid out like a caller workspace: the status word at byte 0 (sticky until
+  // s8b_paged_decode_noalloc_status replaces it), the completion counters, which launch_decode
+  // zeroes before every launch of the kernels that use them, then the partition partials,
+  // which are fully written before anything reads them.
   S8B_DISPATCH_DTYPE(dtype, T,
                      return launch_decode<T>(q_i8, q_s, kc, ks, vc, vs, block_table,
                                              context_lens, out, out_q, out_s, B, Hq, Hkv,
                                              block_size, max_blocks, max_ctx, scale, part,
                                              (cudaStream_t)stream));
+}
+
+extern "C" int s8b_paged_decode_noalloc_status(int32_t *previous, int32_t replace_with) {
+  if (!previous) return S8B_ERR_ARG;
+  float *part = nullptr;
+  const int rc = static_scratch_address(&part);
+  if (rc) return rc;
+  // Plain synchronous copies of one word: they wait for the device's earlier work on the
+  // legacy default stream and allocate nothing.
+  cudaError_t e = cudaMemcpy(previous, part, sizeof(int32_t), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemcpy(part, &replace_with, sizeof(int32_t), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    record_cuda_error(e);
+    return S8B_ERR_CUDA;
+  }
+  return S8B_OK;
 }
 
 extern "C" size_t s8b_paged_decode_ref_workspace_size(int B, int Hq, int D, int max_ctx) {
@@ -1791,7 +1827,9 @@ extern "C" int s8b_paged_decode(const void *q, const int8_t *kc, const float *ks
 }
 
 extern "C" size_t s8b_paged_decode_status_offset(int B, int Hq) {
-  return static_cast<size_t>(B) * Hq * 4 + static_cast<size_t>(B) * 4;
+  (void)B;
+  (void)Hq;
+  return 0;  // the same word for every shape (see carve_ws)
 }
 
 extern "C" int s8b_set_attention_impl(int impl) {

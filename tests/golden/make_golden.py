@@ -487,7 +487,10 @@ def gen_host_golden(mods) -> dict:
 
 
 def main():
-    ref = Path(os.environ.get("S8B_REFERENCE", "/root/reference"))
+    if "S8B_REFERENCE" not in os.environ:
+        raise SystemExit("set S8B_REFERENCE to a superl8-serve checkout (the directory that "
+                         "holds the superl8serve package)")
+    ref = Path(os.environ["S8B_REFERENCE"])
     if not (ref / "superl8serve").is_dir():
         raise SystemExit(f"reference checkout not found under {ref}")
     os.environ.setdefault("SUPERL8_SERVE_SKIP_TORCH_CHECK", "1")

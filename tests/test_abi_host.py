@@ -66,8 +66,10 @@ def test_shape_and_scheme_validation(lib):
 
 def test_workspace_and_codec_sizes(lib):
     P = (2049 + 255) // 256
-    counters = (64 * 32 * 4 + 64 * 4 + 16 + 255) // 256 * 256
-    assert lib.s8b_paged_decode_status_offset(64, 32) == 64 * 32 * 4 + 64 * 4
+    # status word (256-byte region) first, then the (row, head) and row counters
+    counters = 256 + (64 * 32 * 4 + 64 * 4 + 255) // 256 * 256
+    assert lib.s8b_paged_decode_status_offset(64, 32) == 0
+    assert lib.s8b_paged_decode_status_offset(3, 16) == 0
     assert lib.s8b_set_attention_impl(3) == -8
     assert lib.s8b_paged_decode_workspace_size(64, 32, 128, 2049) == counters + 64 * 32 * P * 130 * 4
     assert lib.s8b_codec_payload_bytes(4, 8192, 2, 0) == 4 * 8192
