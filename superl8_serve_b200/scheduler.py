@@ -1,14 +1,7 @@
-"""Continuous batching over the stage pipeline: the reference's ``Scheduler`` policy
-(``superl8serve/engine/scheduler.py:33-170``) and ``Sequence`` (``engine/sequence.py``),
+"""Continuous batching over the stage pipeline: the reference's admission policy
+(``superl8serve/engine/scheduler.py:33-170``, ``engine/sequence.py``; see ``Scheduler``)
 driving ``engine.DecodePipeline`` (the ``PipelineEngine.step`` loop,
 ``superl8serve/dist/pipeline.py:620-635``).
-
-Policy (as the reference): WAITING requests are admitted FIFO while RUNNING <
-``max_num_seqs``, a slot and a KV block are free and the batch's prompt tokens fit
-``max_batch_tokens``; admission is preferred, otherwise the RUNNING set decodes one step. A
-mere count cap never preempts. Only when a slot is free but the block pool is dry does the
-least-progressed running sequence go back to WAITING (its prompt becomes all its tokens, to
-be recomputed), at most ``max_num_seqs`` times per ``schedule()``.
 
 Execution. A KV slot is a fixed pipeline row. Admission prefills every admitted prompt
 but its last token into that request's slot (one varlen prefill over those rows) and
@@ -29,13 +22,18 @@ from .dist.pipeline import SamplingParams
 
 
 class Status(enum.Enum):
-    WAITING = enum.auto()
-    RUNNING = enum.auto()
-    FINISHED = enum.auto()
+    """Life cycle of a request: queued, holding a KV slot, done (slot returned)."""
+
+    WAITING = "waiting"
+    RUNNING = "running"
+    FINISHED = "finished"
 
 
 @dataclass
 class Sequence:
+    """One request. ``prompt_ids`` is what admission prefills; after an eviction it grows to
+    every token the request has so far, since its KV is gone and is recomputed."""
+
     seq_id: int
     prompt_ids: list[int]
     params: SamplingParams
@@ -54,17 +52,34 @@ class Sequence:
         return self.prompt_ids + self.output_ids
 
     def is_finished(self, eos_id: int | None) -> bool:
-        if len(self.output_ids) >= self.params.max_tokens:
-            return True
-        if self.max_len is not None and self.num_prompt + len(self.output_ids) >= self.max_len:
-            return True
-        return (eos_id is not None and not getattr(self.params, "ignore_eos", False)
-                and bool(self.output_ids) and self.output_ids[-1] == eos_id)
+        """Stop conditions: the token budget, the context limit, or (unless ignored) EOS as
+        the last generated token."""
+        n_out = len(self.output_ids)
+        out_of_budget = n_out >= self.params.max_tokens
+        out_of_context = self.max_len is not None and self.num_prompt + n_out >= self.max_len
+        hit_eos = (n_out > 0 and eos_id is not None and self.output_ids[-1] == eos_id
+                   and not getattr(self.params, "ignore_eos", False))
+        return out_of_budget or out_of_context or hit_eos
 
 
 class Scheduler:
-    """Admission / preemption policy over a cache with ``alloc``, ``free``,
-    ``has_free_slot``, ``has_free_block``, ``lookup_prefix`` and ``share_blocks``."""
+    """Admission and eviction over a KV cache with ``alloc() -> slot``, ``free(slot)``,
+    ``has_free_slot()`` and ``has_free_block()`` (the reference's ``Scheduler`` policy,
+    ``superl8serve/engine/scheduler.py:33-170``, re-stated below).
+
+    Each ``schedule()`` call returns either a prefill batch (newly admitted requests) or the
+    decode batch (every running request), never both:
+
+    1. Admission, FIFO: the head of the queue is admitted while the running count plus the
+       batch stays under ``max_num_seqs``, a slot and a block are free, and (after the first
+       request of the batch) its prompt fits in what is left of ``max_batch_tokens``.
+       Admission takes precedence over decoding.
+    2. Eviction, only under genuine block starvation (requests wait, requests run, a slot is
+       free but the block pool is empty): the running request with the fewest generated
+       tokens gives its slot back and re-queues at the tail with its whole history as its
+       prompt; admission is then retried. At most ``max_num_seqs`` evictions per call, so a
+       call always ends. Caps on counts or tokens never evict.
+    """
 
     def __init__(self, cache, *, max_num_seqs: int, max_batch_tokens: int, eos_id: int | None):
         self.cache = cache
@@ -74,83 +89,93 @@ class Scheduler:
         self.waiting: deque[Sequence] = deque()
         self.running: list[Sequence] = []
 
+    # ------------------------------------------------------------------ queue edits ----
     def add(self, seq: Sequence):
         self.waiting.append(seq)
 
     def has_work(self) -> bool:
-        return bool(self.waiting or self.running)
+        return len(self.waiting) + len(self.running) > 0
+
+    def _release(self, seq: Sequence, status: Status):
+        """Give a running request's slot back to the cache."""
+        self.running.remove(seq)
+        self.cache.free(seq.slot)
+        seq.status = status
 
     def cancel(self, seq_id: int) -> bool:
-        """Drop a request: a WAITING one holds nothing; a RUNNING one frees its slot."""
-        for seq in self.waiting:
-            if seq.seq_id == seq_id:
-                self.waiting.remove(seq)
-                seq.status = Status.FINISHED
-                return True
-        for seq in self.running:
-            if seq.seq_id == seq_id:
-                self.running.remove(seq)
-                seq.status = Status.FINISHED
-                self.cache.free(seq.slot)
-                seq.slot = -1
-                return True
+        """Drop a request wherever it is; a running one returns its slot. False if unknown."""
+        queued = {s.seq_id: s for s in self.waiting}
+        if seq_id in queued:
+            self.waiting.remove(queued[seq_id])
+            queued[seq_id].status = Status.FINISHED
+            return True
+        live = {s.seq_id: s for s in self.running}
+        if seq_id in live:
+            self._release(live[seq_id], Status.FINISHED)
+            live[seq_id].slot = -1
+            return True
         return False
 
-    def _preempt_one(self):
-        victim = min(self.running, key=lambda s: len(s.output_ids))
-        self.running.remove(victim)
-        self.cache.free(victim.slot)
+    # ------------------------------------------------------------------- the policy ----
+    def _can_admit(self, batch_size: int, batch_tokens: int) -> bool:
+        if not self.waiting:
+            return False
+        if len(self.running) + batch_size >= self.max_num_seqs:
+            return False
+        if not (self.cache.has_free_slot() and self.cache.has_free_block()):
+            return False
+        head = self.waiting[0]
+        return batch_size == 0 or batch_tokens + head.num_prompt <= self.max_batch_tokens
+
+    def _admit(self) -> list[Sequence]:
+        batch: list[Sequence] = []
+        tokens = 0
+        while self._can_admit(len(batch), tokens):
+            seq = self.waiting.popleft()
+            seq.slot = self.cache.alloc()
+            seq.status = Status.RUNNING
+            tokens += seq.num_prompt
+            batch.append(seq)
+        return batch
+
+    def _block_starved(self) -> bool:
+        return bool(self.waiting and self.running and self.cache.has_free_slot()
+                    and not self.cache.has_free_block())
+
+    def evict_least_progressed(self):
+        """Evict the running request with the fewest generated tokens (the first such in
+        running order). A request that has already met a stop condition just finishes."""
+        victim = self.running[0]
+        for seq in self.running[1:]:
+            if len(seq.output_ids) < len(victim.output_ids):
+                victim = seq
         if victim.is_finished(self.eos_id):
-            victim.status = Status.FINISHED
+            self._release(victim, Status.FINISHED)
             return
-        victim.prompt_ids = victim.all_token_ids  # recomputed through its whole context
+        self._release(victim, Status.WAITING)
+        victim.prompt_ids = victim.all_token_ids
         victim.length = 0
         victim.slot = -1
-        victim.status = Status.WAITING
         self.waiting.append(victim)
-
-    def _has_free_block(self) -> bool:
-        probe = getattr(self.cache, "has_free_block", None)
-        return probe() if probe is not None else True
 
     def schedule(self) -> tuple[list[Sequence], bool]:
         """Returns (batch, is_prefill)."""
-        batch, tokens, preempted = [], 0, 0
-        while True:
-            while (self.waiting and len(self.running) + len(batch) < self.max_num_seqs
-                   and self.cache.has_free_slot() and self._has_free_block()):
-                seq = self.waiting[0]
-                if batch and tokens + seq.num_prompt > self.max_batch_tokens:
-                    break
-                self.waiting.popleft()
-                seq.slot = self.cache.alloc()
-                matched, shared = self.cache.lookup_prefix(seq.prompt_ids)
-                if matched > 0 and shared:
-                    self.cache.share_blocks(seq.slot, shared)
-                seq.status = Status.RUNNING
-                tokens += seq.num_prompt
-                batch.append(seq)
+        for evictions in range(self.max_num_seqs + 1):
+            batch = self._admit()
             if batch:
                 return batch, True
-            block_pressure = (self.waiting and self.running and self.cache.has_free_slot()
-                              and not self._has_free_block())
-            if block_pressure and preempted < self.max_num_seqs:
-                self._preempt_one()
-                preempted += 1
-                continue
-            return list(self.running), False
+            if evictions == self.max_num_seqs or not self._block_starved():
+                break
+            self.evict_least_progressed()
+        return list(self.running), False
 
     def postprocess(self, batch: list[Sequence], is_prefill: bool):
+        """After a step: a prefill batch joins the running set; every running request that
+        met a stop condition finishes and returns its slot."""
         if is_prefill:
             self.running.extend(batch)
-        still = []
-        for seq in self.running:
-            if seq.is_finished(self.eos_id):
-                seq.status = Status.FINISHED
-                self.cache.free(seq.slot)
-            else:
-                still.append(seq)
-        self.running = still
+        for seq in [s for s in self.running if s.is_finished(self.eos_id)]:
+            self._release(seq, Status.FINISHED)
 
 
 class _SlotCache:
@@ -170,12 +195,6 @@ class _SlotCache:
 
     def has_free_block(self) -> bool:
         return bool(self.a._free_blocks)
-
-    def lookup_prefix(self, token_ids):  # prefix sharing is not built
-        return 0, []
-
-    def share_blocks(self, slot, blocks):
-        pass
 
 
 class ContinuousEngine:

@@ -36,24 +36,18 @@ class FakeCache:
             while len(self._slot_blocks[slot]) < need:
                 self._slot_blocks[slot].append(self._free_blocks.pop())
 
-    def lookup_prefix(self, token_ids):
-        return 0, []
-
-    def share_blocks(self, slot, blocks):
-        pass
-
 
 def _run(sched, seqs, max_tokens):
     for s in seqs:
         sched.add(s)
     count = {"preempt": 0}
-    orig = sched._preempt_one
+    orig = sched.evict_least_progressed
 
     def counting():
         count["preempt"] += 1
         orig()
 
-    sched._preempt_one = counting
+    sched.evict_least_progressed = counting
     work, calls, steps = 0, {}, 0
     while sched.has_work():
         assert steps < 100_000
