@@ -25,7 +25,9 @@ What it restates (all citations are paths inside the superl8-serve project):
   .prefill``);
 * the sparse-MoE FFN of Qwen3-MoE (``superl8serve/models/moe.py:88-141``; ``moe``);
 * the rANS entropy stage (``superl8serve/dist/entropy.py``; ``entropy``) and the sampling
-  recipe that follows ``superl8serve/layers/sampler.py:22-156`` (``sampler``).
+  recipe that follows ``superl8serve/layers/sampler.py:22-156`` (``sampler``);
+* the float contract the attention recipe approximates (``read_dense`` dequantization and
+  an fp32 softmax, ``superl8serve/engine/kv_cache.py:1233-1299``; ``float_contract``).
 
 The arithmetic kernels themselves live in the third-party ``superl8`` package, which is
 not vendored in the reference and is not installed here (only its call sites are
@@ -36,4 +38,4 @@ At the ``superl8`` kernel boundary itself parity is unpinned (no golden integer 
 exist in the reference); the composition around it is pinned.
 """
 
-from . import numerics, kernels, codec, model, moe, entropy, sampler  # noqa: F401
+from . import numerics, kernels, codec, model, moe, entropy, sampler, float_contract  # noqa: F401

@@ -141,9 +141,18 @@ class PagedPool:
         return bt
 
 
+def recipe_attention(q, kc, ks, vc, vs, block_table, ctx_lens, block_size, scale, li=None):
+    """The attention recipe the kernels reproduce: the query rotated and quantized per head
+    (``quant_q_for_attn``), then ``paged_decode``. q [M, Hq, D] float32 (bf16-valued)."""
+    qq, qs = quant_q_for_attn(q)
+    return paged_decode(qq, qs, kc, ks, vc, vs, block_table, ctx_lens, block_size, scale)
+
+
 def layer_decode(L, li, h, residual, positions, slot_mapping, block_table, ctx_lens, pool,
-                 s: Shape, tabs):
-    """One ``Qwen3DecoderLayer.forward`` in decode (``superl8serve/models/qwen3.py:70-80``)."""
+                 s: Shape, tabs, attention=None):
+    """One ``Qwen3DecoderLayer.forward`` in decode (``superl8serve/models/qwen3.py:70-80``).
+    ``attention`` replaces ``recipe_attention`` (same arguments), e.g. with the float
+    contract of ``oracle.float_contract``."""
     nh, nkv, hd, eps = s.num_attention_heads, s.num_key_value_heads, s.head_dim, s.rms_norm_eps
     x = h if residual is None else add_residual(h, residual)
     residual = x
@@ -152,9 +161,9 @@ def layer_decode(L, li, h, residual, positions, slot_mapping, block_table, ctx_l
     q, k, v = qkv_post(qkv, positions, nh, nkv, hd, L["q_norm"], L["k_norm"], eps, *tabs)
     kv_write_paged(k, v, pool.kc[li], pool.ks[li], pool.vc[li], pool.vs[li], slot_mapping,
                    pool.block_size)
-    qq, qs = quant_q_for_attn(q)
-    att = paged_decode(qq, qs, pool.kc[li], pool.ks[li], pool.vc[li], pool.vs[li],
-                       block_table, ctx_lens, pool.block_size, hd ** -0.5)
+    att = (attention or recipe_attention)(q, pool.kc[li], pool.ks[li], pool.vc[li],
+                                          pool.vs[li], block_table, ctx_lens, pool.block_size,
+                                          hd ** -0.5, li=li)
     o = gemm_w8a8(*quant_rows_i8(att.reshape(att.shape[0], -1)), *L["o"])
     x = add_residual(o, residual)
     residual = x
@@ -173,7 +182,8 @@ class OraclePipeline:
     """Greedy W8A8 decode through S contiguous stages with a codec at each boundary."""
 
     def __init__(self, cfg, qw: dict, *, n_stages=1, wire_scheme="int8-had", num_slots=8,
-                 max_len=256, block_size=16):
+                 max_len=256, block_size=16, attention=None):
+        self.attention = attention  # None: the recipe (``recipe_attention``)
         self.s = shape_of(cfg)
         self.qw = qw
         L = self.s.num_hidden_layers
@@ -200,7 +210,8 @@ class OraclePipeline:
             cl = np.array(lengths, dtype=np.int32)
             for li in range(self.bounds[si], self.bounds[si + 1]):
                 h, residual = layer_decode(self.qw["layers"][li], li - self.bounds[si], h,
-                                           residual, positions, sm, bt, cl, pool, s, self.tabs)
+                                           residual, positions, sm, bt, cl, pool, s, self.tabs,
+                                           attention=self.attention)
             if si != len(self.pools) - 1:
                 packed = np.concatenate([h, residual], axis=-1)
                 pay, sc = ocodec.encode(packed, self.wire_scheme)

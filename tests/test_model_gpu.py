@@ -140,26 +140,29 @@ def test_two_gpu_in_process_pipeline(tiny_sd):
 @pytest.mark.slow
 def test_config1_qwen3_0_6b_two_stage_greedy_parity():
     """Qwen3-0.6B shape, 2 stages (layers 0-13 / 14-27), batch 4, prompts
-    of 128 uniform-random ids, int8 paged KV (block 16), greedy 32 steps: GPU tokens ==
-    oracle tokens and logits within 1e-2 relative (they are in fact identical)."""
+    of 128 uniform-random ids, int8 paged KV (block 16), greedy decoding for 64 steps (the
+    north star's greedy-identity length): GPU tokens == oracle tokens and logits within 1e-2
+    relative (they are in fact identical), token by token and through the varlen prefill."""
     cfg = qwen3_0_6b(max_position_embeddings=4096)
     sd = random_state_dict(cfg, 0)
     rng = np.random.default_rng(0)
     prompts = rng.integers(0, cfg.vocab_size, (4, 128)).tolist()
-    pipe = DecodePipeline(stage_models(cfg, sd, 2), batch=4, n_micro=1, max_len=192,
+    steps = 64
+    pipe = DecodePipeline(stage_models(cfg, sd, 2), batch=4, n_micro=1, max_len=208,
                           wire_scheme="int8-had")
     assert stage_bounds(28, 2) == [0, 14, 28]
-    outs, logits = pipe.generate(prompts, 32, keep_logits=True)
+    outs, logits = pipe.generate(prompts, steps, keep_logits=True)
     # the same prompts through the varlen prefill: 512 rows in two 256-row chunks
     del pipe
-    pipe = DecodePipeline(stage_models(cfg, sd, 2), batch=4, n_micro=1, max_len=192,
+    pipe = DecodePipeline(stage_models(cfg, sd, 2), batch=4, n_micro=1, max_len=208,
                           wire_scheme="int8-had")
-    outs_p, logits_p = pipe.generate(prompts, 32, keep_logits=True, prefill=True)
+    outs_p, logits_p = pipe.generate(prompts, steps, keep_logits=True, prefill=True)
     del pipe
     qw = quantize_state_dict(sd, cfg)
     del sd
     ref, ref_logits = OraclePipeline(cfg, qw, n_stages=2, wire_scheme="int8-had", num_slots=4,
-                                     max_len=192).generate(prompts, 32)
+                                     max_len=208).generate_prefilled(prompts, steps)
+    assert all(len(r) == steps for r in ref)
     assert outs == ref
     got = np.stack([np.stack([t.numpy() for t in row]) for row in logits])
     want = np.array(ref_logits, dtype=np.float32)
