@@ -93,3 +93,26 @@ def accuracy(original: np.ndarray, reconstructed: np.ndarray):
     sqnr = float("inf") if noise == 0.0 else float(10.0 * np.log10(np.sum(x * x) / noise))
     den = max(np.linalg.norm(x) * np.linalg.norm(xr), 1e-12)
     return sqnr, float(np.dot(x, xr) / den)
+
+
+GATE_INPUTS = ("gauss", "outliers", "laplace", "const")
+
+
+def gate_activation(kind: str, seed: int = 0, T: int = 8, D: int = 2048) -> np.ndarray:
+    """Seeded bf16-valued activations [T, D] for the wire-scheme gate
+    (``superl8serve/dist/codec_quality.py:68-93``): ``gauss`` N(0, 1); ``outliers`` N(0, 1)
+    with 0.1% of the channels scaled x20 (BASELINE config 2's distribution); ``laplace``
+    Laplace(0, 1); ``const`` every element 0.5 (exact round trip)."""
+    rng = np.random.default_rng(seed)
+    if kind == "gauss":
+        x = rng.standard_normal((T, D))
+    elif kind == "outliers":
+        x = rng.standard_normal((T, D))
+        x[:, rng.choice(D, max(1, D // 1000), replace=False)] *= 20.0
+    elif kind == "laplace":
+        x = rng.laplace(0.0, 1.0, (T, D))
+    elif kind == "const":
+        x = np.full((T, D), 0.5)
+    else:
+        raise ValueError(kind)
+    return round_bf16(x.astype(np.float32))

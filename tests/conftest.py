@@ -31,6 +31,14 @@ def golden_dir():
 
 
 @pytest.fixture(scope="session")
+def host_golden(golden_dir):
+    """Host-logic fixtures recorded from the reference's own modules."""
+    import json
+
+    return json.loads((golden_dir / "host_logic.json").read_text())
+
+
+@pytest.fixture(scope="session")
 def lib():
     from superl8_serve_b200 import _lib
 

@@ -425,9 +425,28 @@ def gen_eager_golden(mods, out: dict):
         logits, torch.zeros(3), all_greedy=True).numpy())
 
 
+def gen_codec_gate_golden() -> dict:
+    """The reference's wire-scheme gate (``superl8serve/dist/codec_quality.py``:
+    ``verify_boundary_fidelity`` and ``select_wire_scheme``) on seeded activations, with the
+    oracle codec standing in for ``superl8``. The module refers to the codec as ``fni8``, a
+    name it never binds (an unfinished rename); the stand-in is bound to that name here."""
+    cq = importlib.import_module("superl8serve.dist.codec_quality")
+    cq.fni8 = sys.modules["superl8"]
+    res = {}
+    for kind in ocodec.GATE_INPUTS:
+        x = torch.from_numpy(ocodec.gate_activation(kind, seed=3)).to(torch.bfloat16)
+        out = {"seed": 3, "scheme": cq.select_wire_scheme(x)}
+        for scheme in ("int4", "int8"):
+            sq, cos = cq.verify_boundary_fidelity(x, scheme)
+            out[scheme] = [sq if np.isfinite(sq) else "inf", cos]
+        res[kind] = out
+    return res
+
+
 def gen_host_golden(mods) -> dict:
-    """Pure host logic: stage bounds, peer-route policy, cache addressing, wire bytes."""
-    res: dict = {}
+    """Pure host logic: stage bounds, peer-route policy, cache addressing, wire bytes, the
+    wire-scheme gate."""
+    res: dict = {"codec_gate": gen_codec_gate_golden()}
     pipe = mods["dist.pipeline"]
     res["stage_bounds"] = {f"{L}_{S}": [i * L // S for i in range(S + 1)]
                            for L in (2, 6, 28, 36, 48, 64) for S in (1, 2, 3, 4, 8) if S <= L}

@@ -2,7 +2,6 @@
 host-side logic (block allocator, stage split, peer-route policy, wire accounting) matches the
 reference's own behaviour recorded in tests/golden/host_logic.json."""
 
-import json
 import re
 from pathlib import Path
 
@@ -84,11 +83,6 @@ def test_product_fails_loudly_on_cpu_tensors():
 
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.quant_rows(torch.zeros(2, 16, dtype=torch.bfloat16))
-
-
-@pytest.fixture(scope="module")
-def host_golden(golden_dir):
-    return json.loads((golden_dir / "host_logic.json").read_text())
 
 
 def test_stage_bounds_match_reference(host_golden):
@@ -216,3 +210,30 @@ def test_ctypes_signatures_match_header_prototypes():
                     and (g is C.c_double) == (w is C.c_double), (name, g, w)
         checked += 1
     assert checked >= 55
+
+
+@pytest.mark.parametrize("kind", ["gauss", "outliers", "laplace", "const"])
+def test_wire_scheme_gate_logic_matches_reference(host_golden, monkeypatch, kind):
+    """``select_wire_scheme`` / ``verify_boundary_fidelity`` against the reference's own gate
+    on the same seeded inputs, with the oracle codec standing in for the GPU codec (the GPU
+    run of the same check is in test_transport_gpu)."""
+    from oracle import codec as oc
+    from superl8_serve_b200.dist import Compressed, codec_quality as cq
+
+    def compress(x, scheme="int8", group_size=None):
+        pay, sc = oc.encode(x.float().numpy(), scheme)
+        return Compressed(scheme, tuple(x.shape), x.dtype, group_size, pay, sc, x.shape[-1])
+
+    def decompress(c):
+        return torch.from_numpy(oc.decode(c.payload, c.scales, c.scheme, c.d)).to(c.dtype)
+
+    monkeypatch.setattr(cq, "compress_activation", compress)
+    monkeypatch.setattr(cq, "decompress_activation", decompress)
+    g = host_golden["codec_gate"][kind]
+    x = torch.from_numpy(oc.gate_activation(kind, seed=g["seed"])).to(torch.bfloat16)
+    assert cq.select_wire_scheme(x) == g["scheme"]
+    for scheme in ("int4", "int8"):
+        sq, cos = cq.verify_boundary_fidelity(x, scheme)
+        want_sq, want_cos = g[scheme]
+        assert sq == (float("inf") if want_sq == "inf" else pytest.approx(want_sq, rel=1e-6))
+        assert cos == pytest.approx(want_cos, rel=1e-6)
