@@ -199,6 +199,19 @@ int s8b_paged_decode_q8(const int8_t *q_i8, const float *q_s, const int8_t *kc, 
                         int B, int Hq, int Hkv, int D, int block_size, int max_blocks,
                         int max_ctx, float scale, void *workspace, size_t workspace_bytes,
                         int dtype, void *stream);
+/* s8b_paged_decode_q8 for a decode step: the kernel just before this call on `stream` writes
+ * the queries and each row's K/V at position context_lens[b] - 1 only, and the block tables,
+ * context lengths and older K/V are final before it starts (the write_decode + decode_attn
+ * pair of one decode step, superl8serve/layers/gqa_attention.py:180-190). The persistent
+ * kernel then starts streaming the partitions before that position while the previous
+ * kernel still runs. Results are identical to s8b_paged_decode_q8. Not for prefill rows
+ * (their chunk writes many positions). No counterpart in the reference.                  */
+int s8b_paged_decode_q8_step(const int8_t *q_i8, const float *q_s, const int8_t *kc,
+                             const float *ks, const int8_t *vc, const float *vs,
+                             const int32_t *block_table, const int32_t *context_lens, void *out,
+                             int8_t *out_q, float *out_s, int B, int Hq, int Hkv, int D,
+                             int block_size, int max_blocks, int max_ctx, float scale,
+                             void *workspace, size_t workspace_bytes, int dtype, void *stream);
 
 /* No-allocation form of s8b_paged_decode_q8, for callers that cannot allocate device
  * memory: a host-language binding (cgo, JNI, ctypes) that is handed device buffers but owns no

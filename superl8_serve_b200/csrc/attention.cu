@@ -885,7 +885,8 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
                            const float *__restrict__ q_s, const float *__restrict__ ks,
                            const float *__restrict__ vs, const int32_t *__restrict__ block_table,
                            const int32_t *__restrict__ context_lens, int B, int Hq, int Hkv,
-                           int bs_log2, int max_blocks, int P, float scale, DecodeWs ws) {
+                           int bs_log2, int max_blocks, int P, float scale, DecodeWs ws,
+                           int early) {
   griddep_launch();  // the next kernel may start its prologue
   using namespace tc;
   using namespace pk;
@@ -929,13 +930,94 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  const int bs = 1 << bs_log2;
+  const int nbu = kPart >> bs_log2;  // blocks of a full partition
+
+  // ---------------------------------------------------------- producer helpers ----
+  // This lane's KV block id for unit `it` of a row with context n (-1 past the end).
+  auto block_id = [&](const UnitIter &it, int n) {
+    if (it.b >= B) return -1;
+    const int nblk = (min(kPart, n - it.p * kPart) + bs - 1) >> bs_log2;
+    if (lane >= nblk) return -1;
+    return block_table[static_cast<size_t>(it.b) * max_blocks + ((it.p * kPart) >> bs_log2) +
+                       lane];
+  };
+  // Issues unit (p, g, b)'s K (warp 0, with the tx count of K and the query tile) or V and
+  // the K/V scales (warp 14) into stage s; not the query tile, its scales or the V warp's
+  // cp.async arrival. `blk` is this lane's block id, n the row's context length.
+  auto issue_kv = [&](int p, int g, int b, int n, int blk, int s) {
+    const bool vwarp = warp == 14;
+    const int cnt = min(kPart, n - p * kPart);
+    const int nblk = (cnt + bs - 1) >> bs_log2;
+    const int row = (blk * Hkv + g) << bs_log2;  // this lane's block rows (lanes < nblk)
+    // A full partition on consecutive block ids (ascending, or descending as the reference's
+    // allocator hands them out) moves in one 4-D copy per tensor instead of nblk 2-D copies,
+    // each of which costs its warp ~50 ns to issue. Descending runs land in reverse block
+    // order; the softmax then stores its exponentials at the canonical token index.
+    const int b0 = __shfl_sync(0xffffffffu, blk, 0);
+    const bool asc = runs && nblk == nbu && __all_sync(0xffffffffu, lane >= nblk || blk == b0 + lane);
+    // (reversed only for a partition with every token present: the softmax masks the
+    // tokens past the context end by shared-memory row)
+    const bool desc = runs && cnt == kPart && !asc &&
+                      __all_sync(0xffffffffu, lane >= nblk || blk == b0 - lane);
+    uint8_t *st = sm + s * kStage;
+    if (lane == 0) {
+      if (!vwarp) st[kOffMode] = desc ? 1 : 0;  // before the arrive that publishes the stage
+      mbar_expect_tx(&full[s], static_cast<uint32_t>(nblk * bs * kHd + (vwarp ? 0 : G * kHd)));
+    }
+    __syncwarp();
+    if (asc || desc) {
+      if (lane == 0)
+        tma_load_4d(st + (vwarp ? kOffV : 0), vwarp ? &map_v4 : &map_k4, 0, 0, g,
+                    desc ? b0 - (nbu - 1) : b0, &full[s]);
+    } else if (lane < nblk) {
+      tma_load_2d(st + (vwarp ? kOffV : 0) + lane * bs * kHd, vwarp ? &map_v : &map_k, 0, row,
+                  &full[s]);
+    }
+    if (!vwarp) return;
+    // scales: 16-byte chunks c of 4 tokens; chunk c of array a goes to lane c % 32
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int c = lane + 32 * (i & 1);  // chunk within the array
+      const int j = (4 * c) >> bs_log2;   // smem block of that chunk
+      const int rj = __shfl_sync(0xffffffffu, row, (desc ? nbu - 1 - j : j) & 31);
+      if (4 * c < nblk * bs) {
+        const float *src = (i < 2 ? ks : vs) + rj + ((4 * c) & (bs - 1));
+        cp_async16(st + (i < 2 ? kOffKs : kOffVs) + 16 * c, src);
+      }
+    }
+  };
+
+  // Early phase (decode launches only): the kernel before this one writes each row's K/V at
+  // position context_lens[b] - 1 and the queries, nothing else this kernel reads. The first
+  // ring stages whose partitions end before that position are filled before waiting for it
+  // (block tables, context lengths and older K/V are final before the step begins), so the
+  // ring fills while that kernel still runs. Both producer warps walk the same units and stop
+  // at the same one; `npre` stages then only need their query tile and scales.
+  int npre = 0;
+  if (early) {
+    __syncthreads();  // the stage barriers are initialised
+    if (warp == 0 || warp == 14) {
+      UnitIter it(blockIdx.x, gridDim.x, P, Hkv);
+      while (npre < kStages) {
+        int n = it.b < B ? __ldg(context_lens + it.b) : 0;
+        while (it.b < B && it.p * kPart >= n) {
+          it.next();
+          n = it.b < B ? __ldg(context_lens + it.b) : 0;
+        }
+        if (it.b >= B || (it.p + 1) * kPart >= n) break;  // holds the newest token
+        issue_kv(it.p, it.g, it.b, n, block_id(it, n), npre);
+        ++npre;
+        it.next();
+      }
+    }
+  }
   griddep_wait();  // launched with programmatic serialization: the prologue above overlaps
   for (int i = threadIdx.x; i < B; i += kThreads) ctx[i] = context_lens[i];
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_base;
-  const int bs = 1 << bs_log2;
 
   if (warp == 0 || warp == 14) {
     // ----------------------------------------------------------------- producers ----
@@ -943,14 +1025,7 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     auto next_valid = [&](UnitIter &it) {
       while (it.b < B && it.p * kPart >= ctx[it.b]) it.next();
     };
-    auto block_id = [&](const UnitIter &it) {  // this lane's KV block id (-1 past the end)
-      if (it.b >= B) return -1;
-      const int nblk = (min(kPart, ctx[it.b] - it.p * kPart) + bs - 1) >> bs_log2;
-      if (lane >= nblk) return -1;
-      return block_table[static_cast<size_t>(it.b) * max_blocks + ((it.p * kPart) >> bs_log2) +
-                         lane];
-    };
-    const int nbu = kPart >> bs_log2;  // blocks of a full partition
+    auto bid = [&](const UnitIter &it) { return block_id(it, it.b < B ? ctx[it.b] : 0); };
     // block-table rows three units ahead: under full HBM load a table miss takes a few us
     int k = 0;
     UnitIter i0(blockIdx.x, gridDim.x, P, Hkv);
@@ -961,7 +1036,7 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     UnitIter i2 = i1;
     i2.next();
     next_valid(i2);
-    int blk0 = block_id(i0), blk1 = block_id(i1), blk2 = block_id(i2);
+    int blk0 = bid(i0), blk1 = bid(i1), blk2 = bid(i2);
     while (i0.b < B) {
       const int blk = blk0;
       UnitIter i3 = i2;
@@ -969,40 +1044,15 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
       next_valid(i3);
       blk0 = blk1;
       blk1 = blk2;
-      blk2 = block_id(i3);
+      blk2 = bid(i3);
       const int p = i0.p, g = i0.g, b = i0.b;
-      const int cnt = min(kPart, ctx[b] - p * kPart);
-      const int nblk = (cnt + bs - 1) >> bs_log2;
-      const int row = (blk * Hkv + g) << bs_log2;  // this lane's block rows (lanes < nblk)
-      // A full partition on consecutive block ids (ascending, or descending as the reference's
-      // allocator hands them out) moves in one 4-D copy per tensor instead of nblk 2-D copies,
-      // each of which costs its warp ~50 ns to issue. Descending runs land in reverse block
-      // order; the softmax then stores its exponentials at the canonical token index.
-      const int b0 = __shfl_sync(0xffffffffu, blk, 0);
-      const bool asc = runs && nblk == nbu && __all_sync(0xffffffffu, lane >= nblk || blk == b0 + lane);
-      // (reversed only for a partition with every token present: the softmax masks the
-      // tokens past the context end by shared-memory row)
-      const bool desc = runs && cnt == kPart && !asc &&
-                        __all_sync(0xffffffffu, lane >= nblk || blk == b0 - lane);
       const int s = k % kStages;
       bool ok = true;
       if (lane == 0 && k >= kStages)
         ok = mbar_wait(&empty[s], ((k / kStages) - 1) & 1, abort_flag, ws.status);
       if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
       uint8_t *st = sm + s * kStage;
-      if (lane == 0) {
-        if (!vwarp) st[kOffMode] = desc ? 1 : 0;  // before the arrive that publishes the stage
-        mbar_expect_tx(&full[s], static_cast<uint32_t>(nblk * bs * kHd + (vwarp ? 0 : G * kHd)));
-      }
-      __syncwarp();
-      if (asc || desc) {
-        if (lane == 0)
-          tma_load_4d(st + (vwarp ? kOffV : 0), vwarp ? &map_v4 : &map_k4, 0, 0, g,
-                      desc ? b0 - (nbu - 1) : b0, &full[s]);
-      } else if (lane < nblk) {
-        tma_load_2d(st + (vwarp ? kOffV : 0) + lane * bs * kHd, vwarp ? &map_v : &map_k, 0, row,
-                    &full[s]);
-      }
+      if (k >= npre) issue_kv(p, g, b, ctx[b], blk, s);
       if (!vwarp) {
         if (lane == 0) tma_load_2d(st + kOffQ, &map_q, 0, b * Hq + g * G, &full[s]);
         i0 = i1;
@@ -1010,17 +1060,6 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
         i2 = i3;
         ++k;
         continue;
-      }
-      // scales: 16-byte chunks c of 4 tokens; chunk c of array a goes to lane c % 32
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int c = lane + 32 * (i & 1);  // chunk within the array
-        const int j = (4 * c) >> bs_log2;   // smem block of that chunk
-        const int rj = __shfl_sync(0xffffffffu, row, (desc ? nbu - 1 - j : j) & 31);
-        if (4 * c < nblk * bs) {
-          const float *src = (i < 2 ? ks : vs) + rj + ((4 * c) & (bs - 1));
-          cp_async16(st + (i < 2 ? kOffKs : kOffVs) + 16 * c, src);
-        }
       }
       if (lane < G)  // the G query scales of this (row, kv head)
         asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(st + kOffQs + 4 * lane)),
@@ -1442,7 +1481,7 @@ int launch_persistent(const int8_t *q_i8, const float *q_s, const int8_t *kc, co
                       const int8_t *vc, const float *vs, const int32_t *block_table,
                       const int32_t *context_lens, void *out, int8_t *out_q, float *out_s, int B,
                       int Hq, int Hkv, int bs, int bs_log2, int max_blocks, int P, float scale,
-                      const DecodeWs &w, cudaStream_t st) {
+                      const DecodeWs &w, int early, cudaStream_t st) {
   const int G = Hq / Hkv;
   const size_t merge_smem = 4 * (2 * static_cast<size_t>(Hq) * P + Hq);
   if (bs < 8 || B > pk::kMaxRows || Hq * kHd > kMergeThreads * 8 || merge_smem > 96 * 1024 ||
@@ -1481,7 +1520,7 @@ int launch_persistent(const int8_t *q_i8, const float *q_s, const int8_t *kc, co
     launch_pdl(kern, grid, pk::kThreads, pk::kSmem, st, mk, mv, mq, mk4, mv4, runs, q_s, ks, vs, \
                block_table,                                                                    \
                                                 context_lens, B, Hq, Hkv, bs_log2, max_blocks,  \
-                                                P, scale, w);                                   \
+                                                P, scale, w, early);                            \
     break;                                                                                     \
   }
     S8B_PK_CASE(1)
@@ -1509,7 +1548,7 @@ int launch_decode(const int8_t *q_i8, const float *q_s, const int8_t *kc, const 
                   const int8_t *vc, const float *vs, const int32_t *block_table,
                   const int32_t *context_lens, void *out, int8_t *out_q, float *out_s, int B,
                   int Hq, int Hkv, int bs, int max_blocks, int max_ctx, float scale,
-                  void *workspace, cudaStream_t st) {
+                  void *workspace, cudaStream_t st, int early = 0) {
   const int P = num_parts(max_ctx);
   const int G = Hq / Hkv;
   int bs_log2 = 0;
@@ -1518,7 +1557,7 @@ int launch_decode(const int8_t *q_i8, const float *q_s, const int8_t *kc, const 
   if (g_attn_impl == 0) {
     const int rc = launch_persistent<T>(q_i8, q_s, kc, ks, vc, vs, block_table, context_lens, out,
                                         out_q, out_s, B, Hq, Hkv, bs, bs_log2, max_blocks, P,
-                                        scale, w, st);
+                                        scale, w, early, st);
     if (rc != 1) return rc;
   }
   // The partition kernels count completions; their counters start from zero on every launch.
@@ -1688,13 +1727,13 @@ extern "C" size_t s8b_paged_decode_workspace_size(int B, int Hq, int D, int max_
   return part_bytes(B, Hq, max_ctx);
 }
 
-extern "C" int s8b_paged_decode_q8(const int8_t *q_i8, const float *q_s, const int8_t *kc,
-                                   const float *ks, const int8_t *vc, const float *vs,
-                                   const int32_t *block_table, const int32_t *context_lens,
-                                   void *out, int8_t *out_q, float *out_s, int B, int Hq, int Hkv,
-                                   int D, int block_size, int max_blocks, int max_ctx,
-                                   float scale, void *workspace, size_t workspace_bytes,
-                                   int dtype, void *stream) {
+namespace {
+int paged_decode_q8(const int8_t *q_i8, const float *q_s, const int8_t *kc, const float *ks,
+                    const int8_t *vc, const float *vs, const int32_t *block_table,
+                    const int32_t *context_lens, void *out, int8_t *out_q, float *out_s, int B,
+                    int Hq, int Hkv, int D, int block_size, int max_blocks, int max_ctx,
+                    float scale, void *workspace, size_t workspace_bytes, int dtype,
+                    void *stream, int early) {
   if (!q_i8 || !q_s || !kc || !ks || !vc || !vs || !block_table || !context_lens || !out ||
       ((out_q == nullptr) != (out_s == nullptr)))
     return S8B_ERR_ARG;
@@ -1708,7 +1747,33 @@ extern "C" int s8b_paged_decode_q8(const int8_t *q_i8, const float *q_s, const i
                                              context_lens, out, out_q, out_s, B, Hq, Hkv,
                                              block_size, max_blocks, max_ctx, scale,
                                              static_cast<float *>(workspace),
-                                             (cudaStream_t)stream));
+                                             (cudaStream_t)stream, early));
+}
+}  // namespace
+
+extern "C" int s8b_paged_decode_q8(const int8_t *q_i8, const float *q_s, const int8_t *kc,
+                                   const float *ks, const int8_t *vc, const float *vs,
+                                   const int32_t *block_table, const int32_t *context_lens,
+                                   void *out, int8_t *out_q, float *out_s, int B, int Hq, int Hkv,
+                                   int D, int block_size, int max_blocks, int max_ctx,
+                                   float scale, void *workspace, size_t workspace_bytes,
+                                   int dtype, void *stream) {
+  return paged_decode_q8(q_i8, q_s, kc, ks, vc, vs, block_table, context_lens, out, out_q, out_s,
+                         B, Hq, Hkv, D, block_size, max_blocks, max_ctx, scale, workspace,
+                         workspace_bytes, dtype, stream, 0);
+}
+
+extern "C" int s8b_paged_decode_q8_step(const int8_t *q_i8, const float *q_s, const int8_t *kc,
+                                        const float *ks, const int8_t *vc, const float *vs,
+                                        const int32_t *block_table,
+                                        const int32_t *context_lens, void *out, int8_t *out_q,
+                                        float *out_s, int B, int Hq, int Hkv, int D,
+                                        int block_size, int max_blocks, int max_ctx, float scale,
+                                        void *workspace, size_t workspace_bytes, int dtype,
+                                        void *stream) {
+  return paged_decode_q8(q_i8, q_s, kc, ks, vc, vs, block_table, context_lens, out, out_q, out_s,
+                         B, Hq, Hkv, D, block_size, max_blocks, max_ctx, scale, workspace,
+                         workspace_bytes, dtype, stream, 1);
 }
 
 // ---------------------------------------------------------- no-allocation variant ----

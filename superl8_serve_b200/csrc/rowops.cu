@@ -308,9 +308,16 @@ __global__ void __launch_bounds__(1024)
   if (threadIdx.x == 0) s[m] = p.scale;
 }
 
-// threads = min(1024, nvec rounded up to a warp), VPT = ceil(nvec / threads) <= 8
+// threads = min(kRowThreads, nvec rounded up to a warp), VPT = ceil(nvec / threads) <= 8.
+// 256-thread CTAs (about 12K registers) fit four to an SM, so a launch of 256 CTAs (64 rows x
+// a 4-CTA cluster) runs in one wave beside a resident GEMM CTA; 768-thread CTAs fit one to an
+// SM by registers and took two waves. Longer rows take more threads (up to 1024) so that VPT
+// stays <= 8.
+constexpr int kRowThreads = 256;
 inline void row_shape(int nvec, int *threads, int *vpt) {
   int t = ((nvec + 31) / 32) * 32;
+  if (t > kRowThreads) t = kRowThreads;
+  if ((nvec + t - 1) / t > 8) t = (((nvec + 7) / 8 + 31) / 32) * 32;
   if (t > 1024) t = 1024;
   *threads = t;
   *vpt = (nvec + t - 1) / t;

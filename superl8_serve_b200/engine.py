@@ -354,6 +354,7 @@ class DecodePipeline:
                    for mdl, pool, r in zip(self.models, self.pools, self.runners)]
         for r in runners:
             r.native = self.native
+            r.decode_step = False  # a chunk's rows write many positions of a sequence
         from .ops import codec_sizes
 
         nbytes, nsc = codec_sizes(mp, 2 * self.cfg.hidden_size, self.wire_scheme)

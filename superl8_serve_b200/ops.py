@@ -216,7 +216,10 @@ def decode_status(workspace, B, Hq) -> int:
 
 
 def paged_decode_q8(q_i8, q_s, kc, ks, vc, vs, block_table, context_lens, max_ctx, scale, *,
-                    out=None, out_q=None, out_s=None, workspace=None, dtype=torch.bfloat16):
+                    out=None, out_q=None, out_s=None, workspace=None, dtype=torch.bfloat16,
+                    step=False):
+    """``step``: the decode-step form (``s8b_paged_decode_q8_step``), for a call whose
+    preceding kernel wrote only each row's newest K/V; same results."""
     B, Hq, D = q_i8.shape
     Hkv, bs = kc.shape[-3], kc.shape[-2]
     dev = q_i8.device
@@ -224,7 +227,8 @@ def paged_decode_q8(q_i8, q_s, kc, ks, vc, vs, block_table, context_lens, max_ct
     need = decode_workspace_bytes(B, Hq, D, max_ctx)
     if workspace is None:  # zero-filled once; the kernel leaves its counters at zero
         workspace = torch.zeros(need, dtype=torch.uint8, device=dev)
-    call("s8b_paged_decode_q8", ptr(q_i8), ptr(q_s), ptr(kc), ptr(ks), ptr(vc), ptr(vs),
+    call("s8b_paged_decode_q8_step" if step else "s8b_paged_decode_q8", ptr(q_i8), ptr(q_s),
+         ptr(kc), ptr(ks), ptr(vc), ptr(vs),
          ptr(block_table), ptr(context_lens), ptr(out), ptr(out_q), ptr(out_s), B, Hq, Hkv, D, bs,
          block_table.shape[-1], int(max_ctx), float(scale), ptr(workspace), workspace.numel(),
          dtype_code(out.dtype), stream(dev))

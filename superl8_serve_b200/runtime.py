@@ -316,6 +316,10 @@ class StageRunner:
         self.model, self.pool, self.m, self.max_ctx, self.dtype = model, pool, m, max_ctx, dtype
         # True: run() is one s8b_stage_step call (native replay of the same launches)
         self.native = False
+        # True: every row writes only its newest position per launch (a decode step), so the
+        # attention may stream older partitions early (s8b_paged_decode_q8_step); prefill
+        # runners set False
+        self.decode_step = True
         self.H = cfg.hidden_size
         self.D = cfg.resolved_head_dim()
         self.Hq, self.Hkv = cfg.num_attention_heads, cfg.num_key_value_heads
@@ -502,7 +506,8 @@ class StageRunner:
         else:
             self._gemm(self.xq, self.xs, L.qkv_w, L.qkv_s, self.qkv, M)
             call("s8b_qkv_post", ptr(self.qkv), *post)
-        call("s8b_paged_decode_q8", ptr(self.q_i8), ptr(self.q_s), ptr(kc), ptr(ks), ptr(vc),
+        call("s8b_paged_decode_q8_step" if self.decode_step else "s8b_paged_decode_q8",
+             ptr(self.q_i8), ptr(self.q_s), ptr(kc), ptr(ks), ptr(vc),
              ptr(vs), ptr(mb.block_table), ptr(mb.context_lens), ptr(self.attn), ptr(self.xq),
              ptr(self.xs), M, self.Hq, self.Hkv, self.D, self.pool.block_size,
              mb.block_table.shape[1], self.max_ctx, self.scale, ptr(self.ws), self.ws.numel(), 0,

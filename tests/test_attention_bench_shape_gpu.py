@@ -70,13 +70,15 @@ def test_paged_decode_at_bench_shape(B, layout):
     ws = torch.zeros(ops.decode_workspace_bytes(B, Hq, 128, max_ctx), dtype=torch.uint8,
                      device=DEV)
     try:
-        for impl in IMPLS:
+        # the decode-step form (older partitions streamed before the previous kernel ends)
+        # with the persistent kernel, then every implementation through the plain form
+        for impl, step in [("auto", True)] + [(i, False) for i in IMPLS]:
             ops.set_attention_impl(impl)
             oq = torch.zeros((B, Hq * 128), dtype=torch.int8, device=DEV)
             osc = torch.zeros(B, dtype=torch.float32, device=DEV)
             for _ in range(2):  # a second launch on the same workspace
                 out = ops.paged_decode_q8(*dev, max_ctx, scale, out_q=oq, out_s=osc,
-                                          workspace=ws)
+                                          workspace=ws, step=step)
             assert ops.decode_status(ws, B, Hq) == 0, impl
             got = out.float().cpu().numpy()
             bad = np.argwhere(got != want)
