@@ -365,17 +365,24 @@ def kernel_rooflines(pipe, hbm_peak):
         A, Fe, E = M * mw.top_k, mw.ffn, mw.local_experts  # this GPU's experts only
         it = iter(range(10 ** 9))
 
+        tc = r.MOE_TC and r.H % 128 == 0 and Fe % 128 == 0 and E <= 512
+
         def gemm():
             w = r.model.layers[next(it) % L].moe
-            call("s8b_moe_gemm_grouped", ptr(r.xq), ptr(r.xs), ptr(b["sorted_token"]),
-                 ptr(w.gu_w), ptr(w.gu_s), ptr(b["offsets"]), ptr(b["gu"]), A, 2 * Fe, r.H, E, 0,
-                 stream())
+            if tc:  # the step's kernel: tensor cores on the rows it gathered
+                call("s8b_moe_gemm_grouped_tc", ptr(b["xg"]), ptr(b["xgs"]), ptr(w.gu_w),
+                     ptr(w.gu_s), ptr(b["offsets"]), ptr(b["gu"]), A, 2 * Fe, r.H, E, M,
+                     ptr(b["status"]), 0, stream())
+            else:
+                call("s8b_moe_gemm_grouped", ptr(r.xq), ptr(r.xs), ptr(b["sorted_token"]),
+                     ptr(w.gu_w), ptr(w.gu_s), ptr(b["offsets"]), ptr(b["gu"]), A, 2 * Fe, r.H,
+                     E, 0, stream())
 
         ms = time_kernel(gemm, 4 * L)
         off = b["offsets"].cpu()[: E + 1]
         hit = int(((off[1:] - off[:-1]) > 0).sum())
         byts = hit * (2 * Fe * r.H + 2 * Fe * 4) + M * r.H + 4 * M + A * 2 * Fe * 2 + 4 * A
-        name = "moe_gemm_grouped_gate_up"
+        name = "moe_gemm_grouped_tc_gate_up" if tc else "moe_gemm_grouped_gate_up"
     out[name] = {"ms": ms, "bytes": byts, "gbs": byts / ms / 1e6, "launches_per_step": L}
     # paged decode attention (partition + combine) for one layer
     it2 = iter(range(10 ** 9))

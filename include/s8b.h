@@ -356,6 +356,22 @@ int s8b_moe_route(const void *y, int dtype, const float *gate, int T, int H, int
 int s8b_moe_gemm_grouped(const int8_t *xq, const float *xs, const int32_t *row_index,
                          const int8_t *w, const float *ws, const int32_t *expert_offsets,
                          void *y, int A, int N, int K, int E, int dtype, void *stream);
+/* The same grouped GEMM on the tensor cores (tcgen05 kind::i8, swap-AB: 128 weight rows of an
+ * expert as M, the expert's rows as N), for the rows already in assignment order: xg [A, K]
+ * int8 and xgs [A] (s8b_moe_gather_rows), so expert e's rows are xg[expert_offsets[e] ..
+ * expert_offsets[e+1]). max_rows bounds every expert's row count (the token count: a token
+ * routes to an expert at most once); experts with more than 64 rows take several passes.
+ * Bit-identical to s8b_moe_gemm_grouped. K % 128 == 0, E <= 512, xg and w 16-byte aligned;
+ * status: one int32 the caller zeroes, S8B_ERR_TIMEOUT after a bounded wait gave up.
+ * Replaces the per-expert superl8.linear calls of SparseMoE.forward
+ * (superl8serve/models/moe.py:135-141).                                                  */
+int s8b_moe_gemm_grouped_tc(const int8_t *xg, const float *xgs, const int8_t *w, const float *ws,
+                            const int32_t *expert_offsets, void *y, int A, int N, int K, int E,
+                            int max_rows, int32_t *status, int dtype, void *stream);
+/* Row gather into assignment order: xg[r] = xq[index[r]], xgs[r] = xs[index[r]], r < A.
+ * K % 16 == 0. Feeds s8b_moe_gemm_grouped_tc. No counterpart in the reference.           */
+int s8b_moe_gather_rows(const int8_t *xq, const float *xs, const int32_t *index, int A, int K,
+                        int8_t *xg, float *xgs, void *stream);
 
 /* out[t, :] = running dtype sum, in ascending expert index, of dtype(contrib[p, :] * w)
  * over the token's top_k assignments (p = assign_pos[t*top_k + j], w = topw[t, j]); each

@@ -82,6 +82,9 @@ SIGNATURES: dict[str, tuple] = {
                            _vp]),
     "s8b_moe_gemm_grouped": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
     "s8b_moe_combine": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "s8b_moe_gemm_grouped_tc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _i,
+                                     _vp]),
+    "s8b_moe_gather_rows": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _vp]),
     "s8b_rans_encoded_capacity": (_sz, [_sz, _i]),
     "s8b_rans_stream_offset": (_sz, [_sz, _i, _i]),
     "s8b_rans_histogram": (_i, [_vp, _sz, _vp, _vp]),

@@ -994,26 +994,52 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
   // (block tables, context lengths and older K/V are final before the step begins), so the
   // ring fills while that kernel still runs. Both producer warps walk the same units and stop
   // at the same one; `npre` stages then only need their query tile and scales.
+  // Right after the wait the producers issue those stages' query tiles and scales (the first
+  // q.k needs nothing else), and only then join the CTA barrier.
   int npre = 0;
+  int pre_bg[kStages];  // (b * Hq + g * G) of the early stages: their query rows
+  // query tile (warp 0) or query scales and the cp.async arrival (warp 14) of stage s, whose
+  // query rows start at row qrow of the [B * Hq, 128] query array
+  auto issue_q = [&](int qrow, int s) {
+    uint8_t *st = sm + s * kStage;
+    if (warp == 0) {
+      if (lane == 0) tma_load_2d(st + kOffQ, &map_q, 0, qrow, &full[s]);
+      return;
+    }
+    if (lane < G)
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(st + kOffQs + 4 * lane)),
+                   "l"(q_s + static_cast<size_t>(qrow) + lane)
+                   : "memory");
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&full[s]))
+                 : "memory");
+  };
   if (early) {
-    __syncthreads();  // the stage barriers are initialised
+    for (int i = threadIdx.x; i < B; i += kThreads) ctx[i] = __ldg(context_lens + i);
+    __syncthreads();  // the context lengths are in and the stage barriers initialised
     if (warp == 0 || warp == 14) {
       UnitIter it(blockIdx.x, gridDim.x, P, Hkv);
       while (npre < kStages) {
-        int n = it.b < B ? __ldg(context_lens + it.b) : 0;
+        int n = it.b < B ? ctx[it.b] : 0;
         while (it.b < B && it.p * kPart >= n) {
           it.next();
-          n = it.b < B ? __ldg(context_lens + it.b) : 0;
+          n = it.b < B ? ctx[it.b] : 0;
         }
         if (it.b >= B || (it.p + 1) * kPart >= n) break;  // holds the newest token
         issue_kv(it.p, it.g, it.b, n, block_id(it, n), npre);
+        pre_bg[npre] = it.b * Hq + it.g * G;
         ++npre;
         it.next();
       }
     }
   }
   griddep_wait();  // launched with programmatic serialization: the prologue above overlaps
-  for (int i = threadIdx.x; i < B; i += kThreads) ctx[i] = context_lens[i];
+  if (early && (warp == 0 || warp == 14)) {
+#pragma unroll
+    for (int j = 0; j < kStages; ++j)
+      if (j < npre) issue_q(pre_bg[j], j);
+  }
+  if (!early)
+    for (int i = threadIdx.x; i < B; i += kThreads) ctx[i] = context_lens[i];
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -1051,22 +1077,11 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
       if (lane == 0 && k >= kStages)
         ok = mbar_wait(&empty[s], ((k / kStages) - 1) & 1, abort_flag, ws.status);
       if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
-      uint8_t *st = sm + s * kStage;
-      if (k >= npre) issue_kv(p, g, b, ctx[b], blk, s);
-      if (!vwarp) {
-        if (lane == 0) tma_load_2d(st + kOffQ, &map_q, 0, b * Hq + g * G, &full[s]);
-        i0 = i1;
-        i1 = i2;
-        i2 = i3;
-        ++k;
-        continue;
+      if (k >= npre) {  // (early stages were issued whole before the CTA barrier)
+        issue_kv(p, g, b, ctx[b], blk, s);
+        issue_q(b * Hq + g * G, s);
       }
-      if (lane < G)  // the G query scales of this (row, kv head)
-        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(st + kOffQs + 4 * lane)),
-                     "l"(q_s + static_cast<size_t>(b) * Hq + g * G + lane)
-                     : "memory");
-      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&full[s]))
-                   : "memory");
+      (void)vwarp;
       i0 = i1;
       i1 = i2;
       i2 = i3;

@@ -339,6 +339,28 @@ def moe_gemm_grouped(xq, xs, w, ws, offsets, *, row_index=None, A: int, out_dtyp
     return y
 
 
+def moe_gather_rows(xq, xs, index, A: int):
+    """Rows in assignment order: (xq[index], xs[index]) (``s8b_moe_gather_rows``)."""
+    K = xq.shape[-1]
+    xg = torch.empty(A, K, dtype=torch.int8, device=xq.device)
+    xgs = torch.empty(A, dtype=torch.float32, device=xq.device)
+    call("s8b_moe_gather_rows", ptr(xq), ptr(xs), ptr(index), A, K, ptr(xg), ptr(xgs),
+         stream(xq.device))
+    return xg, xgs
+
+
+def moe_gemm_grouped_tc(xg, xgs, w, ws, offsets, *, A: int, max_rows: int, status=None,
+                        out_dtype=torch.bfloat16):
+    """The tensor-core grouped GEMM on gathered rows (``s8b_moe_gemm_grouped_tc``)."""
+    E, N, K = w.shape
+    y = torch.empty(A, N, dtype=out_dtype, device=xg.device)
+    if status is None:
+        status = torch.zeros(1, dtype=torch.int32, device=xg.device)
+    call("s8b_moe_gemm_grouped_tc", ptr(xg), ptr(xgs), ptr(w), ptr(ws), ptr(offsets), ptr(y), A,
+         N, K, E, int(max_rows), ptr(status), dtype_code(y.dtype), stream(xg.device))
+    return y
+
+
 def moe_combine(contrib, topw, topi, assign_pos):
     T, k = topi.shape
     H = contrib.shape[1]

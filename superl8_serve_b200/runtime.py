@@ -49,6 +49,26 @@ class ExpertShard:
 
 
 @dataclass
+class RemoteExperts:
+    """Experts [e_lo, e_hi) of a MoE layer held by another process (another GPU of the same
+    stage): device addresses of that process's input buffers and flag (mapped with CUDA
+    IPC), and of this process's own completion flag, call counter and status word. The
+    counter advances once per MoE call on both sides, so the flags compare against it."""
+
+    e_lo: int
+    e_hi: int
+    xq: int
+    xs: int
+    offsets: int
+    sorted_token: int
+    in_flag: int
+    out_flag: int
+    epoch: int
+    status: int
+    timeout_ns: int
+
+
+@dataclass
 class MoEWeights:
     """Sparse-MoE FFN of one layer (``SparseMoE``, ``superl8serve/models/moe.py:46-86``):
     fp32 router [E, H]; every expert's merged gate_up int8 [E, 2F, H] with row scales [E, 2F]
@@ -66,6 +86,7 @@ class MoEWeights:
     norm_topk_prob: bool = True
     scaling: float = 1.0
     shards: list = field(default_factory=list)
+    remote: list = field(default_factory=list)  # RemoteExperts: ranges in other processes
 
     @property
     def num_experts(self) -> int:
@@ -301,6 +322,44 @@ class MicroBatch:
     extra: dict = field(default_factory=dict)
 
 
+def moe_experts(buf, off, ne, gu_w, gu_s, d_w, d_s, contrib, M, k, Fe, H, st, *, xq=None,
+                xs=None, tc=True):
+    """Experts [off .. off + ne) of a sparse-MoE layer on one GPU: gate_up, SwiGLU + quant,
+    down into ``contrib`` (rows in assignment order; may be another GPU's buffer). ``buf``
+    holds this GPU's buffers (xq / xs copies unless given, sorted_token, xg / xgs, gu, aq / as,
+    status); ``off`` is the device address of the range's first offset."""
+    A = M * k
+    xq = buf["xq"] if xq is None else xq
+    xs = buf["xs"] if xs is None else xs
+    tc = tc and H % 128 == 0 and Fe % 128 == 0 and ne <= 512
+    if tc:
+        call("s8b_moe_gather_rows", ptr(xq), ptr(xs), ptr(buf["sorted_token"]), A, H,
+             ptr(buf["xg"]), ptr(buf["xgs"]), st)
+        call("s8b_moe_gemm_grouped_tc", ptr(buf["xg"]), ptr(buf["xgs"]), ptr(gu_w), ptr(gu_s),
+             off, ptr(buf["gu"]), A, 2 * Fe, H, ne, M, ptr(buf["status"]), 0, st)
+    else:
+        call("s8b_moe_gemm_grouped", ptr(xq), ptr(xs), ptr(buf["sorted_token"]), ptr(gu_w),
+             ptr(gu_s), off, ptr(buf["gu"]), A, 2 * Fe, H, ne, 0, st)
+    call("s8b_silu_mul_quant", ptr(buf["gu"]), A, Fe, None, ptr(buf["aq"]), ptr(buf["as"]), 0, st)
+    if tc:
+        call("s8b_moe_gemm_grouped_tc", ptr(buf["aq"]), ptr(buf["as"]), ptr(d_w), ptr(d_s), off,
+             contrib, A, H, Fe, ne, M, ptr(buf["status"]), 0, st)
+    else:
+        call("s8b_moe_gemm_grouped", ptr(buf["aq"]), ptr(buf["as"]), None, ptr(d_w), ptr(d_s),
+             off, contrib, A, H, Fe, ne, 0, st)
+
+
+def moe_expert_buffers(M: int, k: int, H: int, Fe: int, E: int, device, dtype=torch.bfloat16):
+    """The per-GPU buffers ``moe_experts`` uses, for micro-batches of up to M tokens."""
+    A = M * k
+    z = lambda *n, dt=dtype: torch.zeros(n, dtype=dt, device=device)  # noqa: E731
+    return {"xq": z(M, H, dt=torch.int8), "xs": z(M, dt=torch.float32),
+            "offsets": z(E + 1, dt=torch.int32), "sorted_token": z(A, dt=torch.int32),
+            "gu": z(A, 2 * Fe), "aq": z(A, Fe, dt=torch.int8), "as": z(A, dt=torch.float32),
+            "xg": z(A, H, dt=torch.int8), "xgs": z(A, dt=torch.float32),
+            "status": z(4, dt=torch.int32)}
+
+
 class StageRunner:
     """Launches one stage's decode kernels for a micro-batch of up to ``m`` rows."""
 
@@ -320,6 +379,9 @@ class StageRunner:
         # attention may stream older partitions early (s8b_paged_decode_q8_step); prefill
         # runners set False
         self.decode_step = True
+        # True: MoE layers run their own experts only (no handshake with partner processes):
+        # the stage-time measurement of a multi-process pipeline
+        self.skip_remote = False
         self.H = cfg.hidden_size
         self.D = cfg.resolved_head_dim()
         self.Hq, self.Hkv = cfg.num_attention_heads, cfg.num_key_value_heads
@@ -389,7 +451,10 @@ class StageRunner:
                 "y": e(m, self.H), "topi": i32(m, k), "topw": e(m, k), "offsets": i32(E + 1),
                 "sorted_assign": i32(A), "sorted_token": i32(A), "assign_pos": i32(A),
                 "gu": e(A, 2 * Fe), "aq": e(A, Fe, dt=torch.int8),
-                "as": e(A, dt=torch.float32), "contrib": e(A, self.H)}
+                "as": e(A, dt=torch.float32), "contrib": e(A, self.H),
+                # tensor-core grouped GEMM: expert input rows gathered into assignment order
+                "xg": e(A, self.H, dt=torch.int8), "xgs": e(A, dt=torch.float32),
+                "status": torch.zeros(4, dtype=torch.int32, device=dev)}
             # expert-parallel partners: inputs copied in, gate_up / SwiGLU rows of their own
             self.moe_peer: dict[str, dict] = {}
             for d in sorted({str(sh.device) for mw in moes for sh in mw.shards}):
@@ -401,7 +466,9 @@ class StageRunner:
                     "xq": z(m, self.H, dt=torch.int8), "xs": z(m, dt=torch.float32),
                     "offsets": z(E + 1, dt=torch.int32), "sorted_token": z(A, dt=torch.int32),
                     "gu": z(A, 2 * Fe), "aq": z(A, Fe, dt=torch.int8),
-                    "as": z(A, dt=torch.float32), "stream": torch.cuda.Stream(device=pd),
+                    "as": z(A, dt=torch.float32), "xg": z(A, self.H, dt=torch.int8),
+                    "xgs": z(A, dt=torch.float32), "status": z(4, dt=torch.int32),
+                    "stream": torch.cuda.Stream(device=pd),
                     "ev_in": torch.cuda.Event(), "ev_out": torch.cuda.Event()}
 
     # ---------------------------------------------------------------------- pieces ----
@@ -440,6 +507,13 @@ class StageRunner:
                  ptr(res_out), ptr(w), self.eps, ptr(self.xq), ptr(self.xs), ptr(y_out), M, K,
                  0, stream())
 
+    MOE_TC = True  # expert GEMMs on the tensor cores where the shape allows (K % 128 == 0)
+
+    def _moe_experts(self, buf, off, ne, gu_w, gu_s, d_w, d_s, contrib, M, k, Fe, st, *,
+                     xq=None, xs=None):
+        moe_experts(buf, off, ne, gu_w, gu_s, d_w, d_s, contrib, M, k, Fe, self.H, st,
+                    xq=xq, xs=xs, tc=self.MOE_TC)
+
     def _moe_ffn(self, mw: MoEWeights, M: int):
         """Sparse-MoE FFN (``SparseMoE.forward``, ``superl8serve/models/moe.py:88-141``) on
         the post-attention RMSNorm output: its dtype rows (router) in moe_buf["y"], its int8
@@ -465,20 +539,25 @@ class StageRunner:
                 ps, ne = pb["stream"], sh.e_hi - sh.e_lo
                 ps.wait_event(pb["ev_in"])
                 off = ptr(pb["offsets"]) + 4 * sh.e_lo
-                call("s8b_moe_gemm_grouped", ptr(pb["xq"]), ptr(pb["xs"]), ptr(pb["sorted_token"]),
-                     ptr(sh.gu_w), ptr(sh.gu_s), off, ptr(pb["gu"]), A, 2 * Fe, H, ne, 0, stream())
-                call("s8b_silu_mul_quant", ptr(pb["gu"]), A, Fe, None, ptr(pb["aq"]),
-                     ptr(pb["as"]), 0, stream())
-                call("s8b_moe_gemm_grouped", ptr(pb["aq"]), ptr(pb["as"]), None, ptr(sh.d_w),
-                     ptr(sh.d_s), off, ptr(b["contrib"]), A, H, Fe, ne, 0, stream())
+                self._moe_experts(pb, off, ne, sh.gu_w, sh.gu_s, sh.d_w, sh.d_s,
+                                  ptr(b["contrib"]), M, k, Fe, stream())
                 pb["ev_out"].record(ps)
-        nl = mw.local_experts
-        call("s8b_moe_gemm_grouped", ptr(self.xq), ptr(self.xs), ptr(b["sorted_token"]),
-             ptr(mw.gu_w), ptr(mw.gu_s), ptr(b["offsets"]), ptr(b["gu"]), A, 2 * Fe, H, nl, 0,
-             st)
-        call("s8b_silu_mul_quant", ptr(b["gu"]), A, Fe, None, ptr(b["aq"]), ptr(b["as"]), 0, st)
-        call("s8b_moe_gemm_grouped", ptr(b["aq"]), ptr(b["as"]), None, ptr(mw.d_w), ptr(mw.d_s),
-             ptr(b["offsets"]), ptr(b["contrib"]), A, H, Fe, nl, 0, st)
+        # experts in other processes (one process per GPU): inputs go into the partner's
+        # buffers by peer copies, a release flag starts it, its down projection stores into
+        # this GPU's contribution buffer and raises this GPU's flag (RemoteExperts)
+        remote = [] if self.skip_remote else mw.remote
+        for rx in remote:
+            for dst, src, n in ((rx.xq, self.xq, M * H), (rx.xs, self.xs, 4 * M),
+                                (rx.offsets, b["offsets"], 4 * (E + 1)),
+                                (rx.sorted_token, b["sorted_token"], 4 * A)):
+                call("s8b_memcpy_async", dst, ptr(src), n, st)
+            call("s8b_flag_set", rx.in_flag, rx.epoch, 1, st)
+        self._moe_experts(b, ptr(b["offsets"]), mw.local_experts, mw.gu_w, mw.gu_s, mw.d_w,
+                          mw.d_s, ptr(b["contrib"]), M, k, Fe, st, xq=self.xq, xs=self.xs)
+        for rx in remote:
+            call("s8b_flag_wait", rx.out_flag, rx.epoch, 1, rx.timeout_ns, rx.status, st)
+        if remote:  # one MoE call done on every side
+            call("s8b_counter_add", remote[0].epoch, 1, st)
         for sh in mw.shards:
             home.wait_event(self.moe_peer[str(sh.device)]["ev_out"])
         call("s8b_moe_combine", ptr(b["contrib"]), ptr(b["topw"]), ptr(b["topi"]),

@@ -85,6 +85,64 @@ def test_grouped_gemm_bit_exact(gather, T, N, K, E, k):
     assert np.array_equal(f32(y), want)
 
 
+def _skewed_topi(rng, T, E, k, hot):
+    """Top-k choices where expert `hot` is picked by every token (T rows: several 64-row
+    passes when T > 64) and the rest spread at random; some experts get no rows."""
+    topi = np.zeros((T, k), np.int32)
+    for t in range(T):
+        others = rng.permutation([e for e in range(E) if e != hot])[: k - 1]
+        topi[t] = np.concatenate([[hot], others])
+    return topi
+
+
+@pytest.mark.parametrize("T,N,K,E,k,skew", [
+    (1, 96, 256, 8, 2, False),        # one token: 2 experts of 1 row, 6 empty
+    (32, 1536, 2048, 128, 8, False),  # config-4 gate_up shape, batch 32
+    (128, 1536, 2048, 128, 8, False), # config-4 gate_up shape, batch 128 (about 8 rows each)
+    (128, 2048, 768, 128, 8, False),  # config-4 down shape
+    (130, 256, 384, 16, 4, True),     # one expert with 130 rows: three passes (64, 64, 2)
+    (65, 200, 128, 8, 3, True),       # 65 rows (a pass of 64 and one of 1); N not a tile multiple
+])
+def test_grouped_gemm_tensor_cores_bit_exact(T, N, K, E, k, skew):
+    """s8b_moe_gemm_grouped_tc on rows gathered by s8b_moe_gather_rows: bit-exact against the
+    oracle (the same integer sums and dequantization as the CUDA-core grouped kernel)."""
+    rng = np.random.default_rng(T * 3 + N + K + E)
+    topi = (_skewed_topi(rng, T, E, k, hot=E // 2) if skew else
+            np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32))
+    off, order, _ = om.group_assignments(topi, E)
+    A = T * k
+    xq = rng.integers(-127, 128, (T, K), dtype=np.int8)
+    xs = rng.uniform(0.001, 0.1, T).astype(np.float32)
+    w = rng.integers(-127, 128, (E, N, K), dtype=np.int8)
+    ws = rng.uniform(1e-4, 1e-3, (E, N)).astype(np.float32)
+    src = (order // k).astype(np.int32)
+    xg, xgs = ops.moe_gather_rows(dev(xq), dev(xs), dev(src), A)
+    assert np.array_equal(xg.cpu().numpy(), xq[src])
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    y = ops.moe_gemm_grouped_tc(xg, xgs, dev(w), dev(ws), dev(off), A=A, max_rows=T,
+                                status=status)
+    want = np.zeros((A, N), np.float32)
+    for e in range(E):
+        lo, hi = off[e], off[e + 1]
+        if lo < hi:
+            want[lo:hi] = gemm_w8a8(xq[src[lo:hi]], xs[src[lo:hi]], w[e], ws[e])
+    got = f32(y)
+    bad = np.argwhere(got != want)
+    assert bad.size == 0, (len(bad), bad[:4])
+    assert int(status.item()) == 0
+    # an expert range of a shard: experts [e_lo, E) with the offsets from e_lo on (absolute
+    # row numbers), as the expert-parallel partner runs them
+    e_lo = E // 2
+    y2 = torch.full((A, N), float("nan"), dtype=torch.bfloat16, device=DEV)
+    offd = dev(off)
+    from superl8_serve_b200._lib import call, ptr, stream
+    call("s8b_moe_gemm_grouped_tc", ptr(xg), ptr(xgs), ptr(dev(w[e_lo:].copy())),
+         ptr(dev(ws[e_lo:].copy())), offd.data_ptr() + 4 * e_lo, ptr(y2), A, N, K, E - e_lo, T,
+         ptr(status), 0, stream(xg.device))
+    lo = off[e_lo]
+    assert np.array_equal(f32(y2)[lo:], want[lo:])
+
+
 def test_combine_bit_exact():
     rng = np.random.default_rng(9)
     T, k, E, H = 19, 8, 128, 2048
