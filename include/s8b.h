@@ -42,17 +42,22 @@ extern "C" {
 #define S8B_BF16 0
 #define S8B_FP16 1
 
-/* ---- wire codec schemes (reference names: "fp16", "int8", "int8-had", "int4", "int4-had")
+/* ---- wire codec schemes (reference names: "fp16", "int8", "int8-had", "int4", "int4-had",
+ * "nf4")
  * fp16     : the activation itself, bit-exact (2 bytes/element, no scales)
  * int8     : int8 codes, one fp32 scale per row
  * int8-had : block-128 Hadamard, then int8 with one fp32 scale per row
  * int4     : two's-complement nibbles (low nibble = even element), fp32 scale per 128-group
- * int4-had : block-128 Hadamard, then int4 as above                                       */
+ * int4-had : block-128 Hadamard, then int4 as above
+ * nf4      : 4-bit NormalFloat codes (index into the 16-entry NF4 codebook, nearest entry to
+ *            x / absmax, lowest index on ties), nibbles packed as int4, fp32 absmax scale per
+ *            128-group                                                                    */
 #define S8B_CODEC_FP16 0
 #define S8B_CODEC_INT8 1
 #define S8B_CODEC_INT8_HAD 2
 #define S8B_CODEC_INT4 3
 #define S8B_CODEC_INT4_HAD 4
+#define S8B_CODEC_NF4 5
 
 const char *s8b_strerror(int code);
 int s8b_version(void);
@@ -151,6 +156,16 @@ int s8b_qkv_post(const void *qkv, const int32_t *positions, const float *cos_tab
                  void *q_out, int8_t *kc, float *ks, int8_t *vc, float *vs,
                  const int32_t *slot_mapping, const int32_t *block_table, int max_blocks,
                  int block_size, int dtype, void *stream);
+/* Stage prologue: s8b_rmsnorm_quant on the previous stage's codec payload [T, 2H]
+ * (scheme S8B_CODEC_*): the hidden and residual halves are decoded on load exactly as
+ * s8b_codec_decode does (inverse Hadamard across a warp for the -had schemes), added, normed
+ * and quantized; residual_out [T, H] receives the sum. H % 128 == 0. Identical to
+ * s8b_codec_decode + s8b_rmsnorm_quant. Fuses decompress_activation and the unpack of the
+ * reference (superl8serve/dist/__init__.py:300, superl8serve/dist/pipeline.py:301-305)
+ * with the next layer's input RMSNorm.                                                    */
+int s8b_rmsnorm_quant_codec(const void *payload, const float *scales, int scheme,
+                            void *residual_out, const void *w, float eps, int8_t *q, float *s,
+                            int M, int H, int dtype, void *stream);
 /* The same with qkv given as GEMM split-K partials (int32 [C][M][(Hq+2*Hkv)*D], xs [M],
  * ws [(Hq+2*Hkv)*D]; see s8b_rmsnorm_quant_split). No counterpart in the reference. */
 int s8b_qkv_post_split(const int32_t *part, int C, const float *xs, const float *ws,
@@ -283,6 +298,15 @@ int s8b_codec_encode(const void *a, const void *b, int T, int Da, int Db, int sc
                      void *payload, float *scales, int dtype, void *stream);
 int s8b_codec_decode(const void *payload, const float *scales, int T, int Da, int Db,
                      int scheme, void *out_a, void *out_b, int dtype, void *stream);
+/* Stage epilogue: s8b_codec_encode with the `a` half given as a GEMM's split-K partials
+ * (int32 [C][T][Da], token scales xs [T], row scales ws [Da]; summed and dequantized on load
+ * exactly as the GEMM's own output would be), so a stage's last down projection goes
+ * straight into the boundary codes. Da % 4 == 0, C <= 8. Codes are identical to the unfused
+ * GEMM + s8b_codec_encode. Fuses the boundary pack and compress_activation of the reference
+ * (superl8serve/dist/pipeline.py:246-250, superl8serve/dist/__init__.py:189).              */
+int s8b_codec_encode_split(const int32_t *part, int C, const float *xs, const float *ws,
+                           const void *b, int T, int Da, int Db, int scheme, void *payload,
+                           float *scales, int dtype, void *stream);
 
 /* ---- stage-to-stage signalling (no counterpart call in the reference, whose send()
  * synchronises the host instead: superl8serve/dist/__init__.py:243-247) ---------------------

@@ -7,14 +7,23 @@ fixes the wire format: ``int8`` carries one fp32 scale per row
 one fp32 scale per 128-element group (``superl8serve/dist/transfer_model.py:25-41``,
 nibble order low-first as in ``superl8serve/layers/linear.py:43-50``), ``fp16`` is the raw
 activation (bit-exact). ``int8-had`` is the block-Hadamard per-token-absmax int8 codec the
-pipeline boundary uses.
+pipeline boundary uses. ``nf4`` (listed with its 16 dB / 0.985 bars at
+``superl8serve/dist/__init__.py:51`` and its 4-bit, 128-group wire at
+``superl8serve/dist/transfer_model.py:31,40``) follows the NF4 recipe the reference applies
+to adapter weights (``superl8serve/training/qlora.py:14-36``): absmax scale per group,
+nearest entry of the NF4 codebook to x / absmax (``argmin``, so the lowest index on ties).
+The codebook itself lives in the absent ``superl8.quant.lowbit``; it is rebuilt here from
+its published construction (QLoRA, Dettmers et al. 2023), see ``nf4_codebook``.
 
 Encode of a row x (bf16-valued, length d, d % 128 == 0):
   z = hadamard128 per 128-block (``-had`` schemes) or z = x;
   int8*:  (codes, scale) = quant_sym(z, 127) over the whole row -> scales [rows];
   int4*:  (codes, scale) = quant_sym(z, 7) per 128-group -> scales [rows, d/128];
           byte i of the payload = (code[2i] & 0xF) | (code[2i+1] & 0xF) << 4.
-Decode: z' = f32(code) * scale; x' = bf16(hadamard128(z')) for ``-had``, else bf16(z').
+  nf4:    scale = max|z| per 128-group; code = argmin_i |f32(z / scale) - NF4[i]| (0.0 for an
+          all-zero group: code 7); packed as int4.
+Decode: z' = f32(code) * scale (nf4: NF4[code] * scale); x' = bf16(hadamard128(z')) for
+``-had``, else bf16(z').
 """
 
 from __future__ import annotations
@@ -23,8 +32,47 @@ import numpy as np
 
 from .numerics import hadamard_blocks, quant_sym, round_bf16
 
-SCHEMES = ("fp16", "int8", "int8-had", "int4", "int4-had")
+SCHEMES = ("fp16", "int8", "int8-had", "int4", "int4-had", "nf4")
 GROUP = 128
+
+# NF4 codebook, binary32, ascending (the values of ``nf4_codebook()``, pinned so the GPU
+# kernels' constants and this oracle cannot drift apart).
+NF4 = np.array([
+    -1.0, -0.6961929202079773, -0.5250730514526367, -0.39491748809814453,
+    -0.28444135189056396, -0.18477343022823334, -0.09104999154806137, 0.0,
+    0.07958032935857773, 0.16093017160892487, 0.24611228704452515, 0.33791518211364746,
+    0.44070979952812195, 0.5626169443130493, 0.7229567170143127, 1.0], dtype=np.float32)
+
+
+def nf4_codebook() -> np.ndarray:
+    """The published NF4 construction: 8 positive standard-normal quantiles at probabilities
+    linspace(0.9677083, 0.5, 9)[:-1], the 7 negated quantiles at linspace(0.9677083, 0.5,
+    8)[:-1], and 0; normalised by the largest magnitude; binary32, ascending."""
+    from scipy.stats import norm
+
+    off = 0.9677083
+    pos = norm.ppf(np.linspace(off, 0.5, 9)[:-1])
+    neg = -norm.ppf(np.linspace(off, 0.5, 8)[:-1])
+    v = np.sort(np.concatenate([pos, [0.0], neg]))
+    return (v / np.max(np.abs(v))).astype(np.float32)
+
+
+def _pack4(codes: np.ndarray) -> np.ndarray:
+    lo = (codes[:, 0::2] & 0xF).astype(np.uint8)
+    hi = (codes[:, 1::2] & 0xF).astype(np.uint8)
+    return (lo | (hi << 4)).astype(np.uint8)
+
+
+def _nf4_encode(z: np.ndarray):
+    rows, d = z.shape
+    g = z.reshape(rows, d // GROUP, GROUP).astype(np.float32)
+    amax = np.max(np.abs(g), axis=-1, keepdims=True).astype(np.float32)
+    with np.errstate(invalid="ignore", divide="ignore"):
+        y = np.where(amax > 0, g / np.where(amax > 0, amax, np.float32(1)), np.float32(0))
+    y = y.astype(np.float32)
+    dist = np.abs((y[..., None] - NF4).astype(np.float32))
+    codes = np.argmin(dist, axis=-1).reshape(rows, d).astype(np.int32)
+    return _pack4(codes), amax.reshape(rows, d // GROUP).astype(np.float32)
 
 
 def _rows(x):
@@ -45,12 +93,11 @@ def encode(x: np.ndarray, scheme: str):
     if scheme.startswith("int8"):
         q, s = quant_sym(z, 127)
         return q.astype(np.int8), s
+    if scheme == "nf4":
+        return _nf4_encode(z)
     rows, d = z.shape
     q, s = quant_sym(z.reshape(rows, d // GROUP, GROUP), 7)
-    q = q.reshape(rows, d).astype(np.int32)
-    lo = (q[:, 0::2] & 0xF).astype(np.uint8)
-    hi = (q[:, 1::2] & 0xF).astype(np.uint8)
-    return (lo | (hi << 4)).astype(np.uint8), s.astype(np.float32)
+    return _pack4(q.reshape(rows, d).astype(np.int32)), s.astype(np.float32)
 
 
 def decode(payload: np.ndarray, scales: np.ndarray, scheme: str, d: int) -> np.ndarray:
@@ -65,7 +112,10 @@ def decode(payload: np.ndarray, scales: np.ndarray, scheme: str, d: int) -> np.n
         lo = p & 0xF
         hi = (p >> 4) & 0xF
         codes = np.stack([lo, hi], axis=-1).reshape(p.shape[0], -1)
-        codes = np.where(codes >= 8, codes - 16, codes).astype(np.float32)
+        if scheme == "nf4":
+            codes = NF4[codes]
+        else:
+            codes = np.where(codes >= 8, codes - 16, codes).astype(np.float32)
         rows = codes.shape[0]
         z = (codes.reshape(rows, d // GROUP, GROUP) * scales.reshape(rows, d // GROUP, 1))
         z = z.astype(np.float32).reshape(rows, d)

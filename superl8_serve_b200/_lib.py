@@ -15,7 +15,7 @@ import torch
 LIB_PATH = Path(__file__).resolve().parent / "libs8b.so"
 
 S8B_BF16, S8B_FP16 = 0, 1
-CODEC = {"fp16": 0, "int8": 1, "int8-had": 2, "int4": 3, "int4-had": 4}
+CODEC = {"fp16": 0, "int8": 1, "int8-had": 2, "int4": 3, "int4-had": 4, "nf4": 5}
 ERR_TIMEOUT = -6
 
 _vp, _i, _f, _sz, _u32, _u64 = C.c_void_p, C.c_int, C.c_float, C.c_size_t, C.c_uint32, C.c_uint64
@@ -66,6 +66,8 @@ SIGNATURES: dict[str, tuple] = {
     "s8b_codec_scale_count": (_sz, [_i, _i, _i]),
     "s8b_codec_encode": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _i, _vp]),
     "s8b_codec_decode": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _i, _vp]),
+    "s8b_codec_encode_split": (_i, [_vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _i, _vp]),
+    "s8b_rmsnorm_quant_codec": (_i, [_vp, _vp, _i, _vp, _vp, _f, _vp, _vp, _i, _i, _i, _vp]),
     "s8b_flag_set": (_i, [_vp, _vp, _u32, _vp]),
     "s8b_flag_wait": (_i, [_vp, _vp, _u32, _u64, _vp, _vp]),
     "s8b_counter_add": (_i, [_vp, _u32, _vp]),

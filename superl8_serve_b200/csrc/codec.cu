@@ -1,5 +1,5 @@
 // Inter-stage activation codec: [a | b] rows -> (optional block-128 Hadamard) -> per-row
-// (int8) or per-128-group (int4) absmax scales -> packed codes, and the inverse.
+// (int8) or per-128-group (int4, nf4) absmax scales -> packed codes, and the inverse.
 //
 // The encoder's stores go wherever `payload` / `scales` point; for a pipeline boundary that
 // is the next stage's receive buffer on another GPU (peer pointer or IPC mapping), so the
@@ -11,10 +11,21 @@ namespace {
 
 constexpr int kCodecThreads = 256;
 
+// Values k .. k+3 (k % 4 == 0) of row `row` of [a | b]: a is dtype rows or a GEMM's split-K
+// partials summed and dequantized on load (then Da % 4 == 0, checked on the host).
 template <typename T>
-__device__ __forceinline__ float load_ab(const T *a, const T *b, int Da, int Db, int row, int k) {
-  return k < Da ? to_f32(a[static_cast<size_t>(row) * Da + k])
-                : to_f32(b[static_cast<size_t>(row) * Db + (k - Da)]);
+__device__ __forceinline__ void load4_ab(const RowSrc<T> &a, const T *b, int Da, int Db, int row,
+                                         int k, float v[4]) {
+  if (k + 4 <= Da && (Da & 3) == 0) {
+    a.load4(row, k, v);
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int kk = k + i;
+    v[i] = kk < Da ? to_f32(a.x[static_cast<size_t>(row) * Da + kk])
+                   : to_f32(b[static_cast<size_t>(row) * Db + (kk - Da)]);
+  }
 }
 
 template <typename T>
@@ -27,7 +38,7 @@ __device__ __forceinline__ void store_ab(T *a, T *b, int Da, int Db, int row, in
 
 template <typename T>
 __global__ void __launch_bounds__(kCodecThreads)
-    encode_kernel(const T *__restrict__ a, const T *__restrict__ b, int Da, int Db, int scheme,
+    encode_kernel(RowSrc<T> a, const T *__restrict__ b, int Da, int Db, int scheme,
                   void *__restrict__ payload, float *__restrict__ scales) {
   extern __shared__ float z[];  // [D] binary32 (int8 schemes)
   __shared__ float red[32];
@@ -36,8 +47,12 @@ __global__ void __launch_bounds__(kCodecThreads)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   if (scheme == S8B_CODEC_FP16) {
     T *out = static_cast<T *>(payload) + static_cast<size_t>(row) * D;
-    for (int k = threadIdx.x; k < D; k += blockDim.x)
-      out[k] = from_f32<T>(load_ab(a, b, Da, Db, row, k));
+    for (int k4 = threadIdx.x; k4 < D / 4; k4 += blockDim.x) {
+      float v[4];
+      load4_ab(a, b, Da, Db, row, 4 * k4, v);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) out[4 * k4 + i] = from_f32<T>(v[i]);
+    }
     return;
   }
   const bool had = scheme == S8B_CODEC_INT8_HAD || scheme == S8B_CODEC_INT4_HAD;
@@ -46,8 +61,7 @@ __global__ void __launch_bounds__(kCodecThreads)
     if (had) {
       for (int blk = warp; blk < D / 128; blk += nwarps) {
         float v[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] = load_ab(a, b, Da, Db, row, blk * 128 + 4 * lane + i);
+        load4_ab(a, b, Da, Db, row, blk * 128 + 4 * lane, v);
         fwht128_warp(v);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -57,10 +71,14 @@ __global__ void __launch_bounds__(kCodecThreads)
         }
       }
     } else {
-      for (int k = threadIdx.x; k < D; k += blockDim.x) {
-        const float v = load_ab(a, b, Da, Db, row, k);
-        z[k] = v;
-        amax = fmaxf(amax, fabsf(v));
+      for (int k4 = threadIdx.x; k4 < D / 4; k4 += blockDim.x) {
+        float v[4];
+        load4_ab(a, b, Da, Db, row, 4 * k4, v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          z[4 * k4 + i] = v[i];
+          amax = fmaxf(amax, fabsf(v[i]));
+        }
       }
     }
     amax = block_max(amax, red);
@@ -77,12 +95,12 @@ __global__ void __launch_bounds__(kCodecThreads)
     if (threadIdx.x == 0) scales[row] = p.scale;
     return;
   }
-  // int4 / int4-had: one warp per 128-group.
+  // int4 / int4-had / nf4: one warp per 128-group.
+  const bool nf4 = scheme == S8B_CODEC_NF4;
   uint8_t *out = static_cast<uint8_t *>(payload) + static_cast<size_t>(row) * (D / 2);
   for (int blk = warp; blk < D / 128; blk += nwarps) {
     float v[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = load_ab(a, b, Da, Db, row, blk * 128 + 4 * lane + i);
+    load4_ab(a, b, Da, Db, row, blk * 128 + 4 * lane, v);
     if (had) {
       fwht128_warp(v);
 #pragma unroll
@@ -90,13 +108,24 @@ __global__ void __launch_bounds__(kCodecThreads)
     }
     float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
     amax = warp_max(amax);
-    const QParams p = qparams(amax, 7.0f);
-    const int c0 = qcode(v[0], p.inv, 7), c1 = qcode(v[1], p.inv, 7);
-    const int c2 = qcode(v[2], p.inv, 7), c3 = qcode(v[3], p.inv, 7);
-    const uint16_t packed = static_cast<uint16_t>(((c0 & 0xF) | ((c1 & 0xF) << 4)) |
-                                                  (((c2 & 0xF) | ((c3 & 0xF) << 4)) << 8));
+    int c[4];
+    float scale;
+    if (nf4) {
+      // scale = absmax; code = nearest codebook entry to x / absmax (an all-zero group
+      // gives scale 0 and code 7, the entry 0.0).
+      scale = amax;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) c[i] = nf4_code(amax > 0.0f ? __fdiv_rn(v[i], amax) : 0.0f);
+    } else {
+      const QParams p = qparams(amax, 7.0f);
+      scale = p.scale;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) c[i] = qcode(v[i], p.inv, 7);
+    }
+    const uint16_t packed = static_cast<uint16_t>(((c[0] & 0xF) | ((c[1] & 0xF) << 4)) |
+                                                  (((c[2] & 0xF) | ((c[3] & 0xF) << 4)) << 8));
     reinterpret_cast<uint16_t *>(out + blk * 64)[lane] = packed;
-    if (lane == 0) scales[static_cast<size_t>(row) * (D / 128) + blk] = p.scale;
+    if (lane == 0) scales[static_cast<size_t>(row) * (D / 128) + blk] = scale;
   }
 }
 
@@ -138,8 +167,12 @@ __global__ void __launch_bounds__(kCodecThreads)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         int c = (pk >> (4 * i)) & 0xF;
-        c = c >= 8 ? c - 16 : c;
-        v[i] = __fmul_rn(static_cast<float>(c), s);
+        if (scheme == S8B_CODEC_NF4) {
+          v[i] = __fmul_rn(nf4_value(c), s);
+        } else {
+          c = c >= 8 ? c - 16 : c;
+          v[i] = __fmul_rn(static_cast<float>(c), s);
+        }
       }
     }
     if (had) {
@@ -154,7 +187,7 @@ __global__ void __launch_bounds__(kCodecThreads)
 
 int check_codec(int T_, int Da, int Db, int scheme) {
   if (T_ < 0 || Da <= 0 || Db < 0) return S8B_ERR_SHAPE;
-  if (scheme < S8B_CODEC_FP16 || scheme > S8B_CODEC_INT4_HAD) return S8B_ERR_DTYPE;
+  if (scheme < S8B_CODEC_FP16 || scheme > S8B_CODEC_NF4) return S8B_ERR_DTYPE;
   const int D = Da + Db;
   if (D % 4 != 0) return S8B_ERR_SHAPE;
   if (scheme >= S8B_CODEC_INT8_HAD && (Da % 128 != 0 || Db % 128 != 0)) return S8B_ERR_SHAPE;
@@ -194,7 +227,30 @@ extern "C" int s8b_codec_encode(const void *a, const void *b, int T_, int Da, in
     auto kern = encode_kernel<T>;
     ensure_smem(reinterpret_cast<const void *>(kern), smem);
     kern<<<T_, kCodecThreads, smem, (cudaStream_t)stream>>>(
-        static_cast<const T *>(a), static_cast<const T *>(b), Da, Db, scheme, payload, scales);
+        row_src<T>(a, Da), static_cast<const T *>(b), Da, Db, scheme, payload, scales);
+  });
+  return check_launch();
+}
+
+extern "C" int s8b_codec_encode_split(const int32_t *part, int C, const float *xs,
+                                      const float *ws, const void *b, int T_, int Da, int Db,
+                                      int scheme, void *payload, float *scales, int dtype,
+                                      void *stream) {
+  const int e = check_codec(T_, Da, Db, scheme);
+  if (e) return e;
+  if (!part || !xs || !ws || (Db > 0 && !b) || !payload || (scheme != S8B_CODEC_FP16 && !scales))
+    return S8B_ERR_ARG;
+  if (C < 1 || C > 8 || Da % 4 != 0) return S8B_ERR_SHAPE;
+  if (!aligned(payload, 4) || !aligned(part, 16) || !aligned(ws, 16)) return S8B_ERR_ALIGN;
+  if (T_ == 0) return S8B_OK;
+  const size_t smem = (scheme == S8B_CODEC_INT8 || scheme == S8B_CODEC_INT8_HAD)
+                          ? static_cast<size_t>(Da + Db) * sizeof(float) : 0;
+  S8B_DISPATCH_DTYPE(dtype, T, {
+    auto kern = encode_kernel<T>;
+    ensure_smem(reinterpret_cast<const void *>(kern), smem);
+    kern<<<T_, kCodecThreads, smem, (cudaStream_t)stream>>>(
+        row_src_split<T>(part, C, xs, ws, T_, Da), static_cast<const T *>(b), Da, Db, scheme,
+        payload, scales);
   });
   return check_launch();
 }

@@ -147,6 +147,43 @@ __device__ __forceinline__ void fwht128_warp(float v[4]) {
   }
 }
 
+// ---------------------------------------------------------------------------- NF4 --------
+// The 16-entry 4-bit NormalFloat codebook (QLoRA, Dettmers et al. 2023): 8 positive and 7
+// negative standard-normal quantiles at evenly spaced probabilities between 0.5 and
+// 0.9677083, plus 0, normalised to [-1, 1], rounded to binary32, ascending.
+__device__ constexpr float kNF4[16] = {
+    -1.0f, -0.6961929202079773f, -0.5250730514526367f, -0.39491748809814453f,
+    -0.28444135189056396f, -0.18477343022823334f, -0.09104999154806137f, 0.0f,
+    0.07958032935857773f, 0.16093017160892487f, 0.24611228704452515f, 0.33791518211364746f,
+    0.44070979952812195f, 0.5626169443130493f, 0.7229567170143127f, 1.0f};
+
+// Codebook entry of code c (0..15) by a select tree on c's bits (no memory access).
+__device__ __forceinline__ float nf4_value(int c) {
+  float l[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) l[i] = (c & 1) ? kNF4[2 * i + 1] : kNF4[2 * i];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) l[i] = (c & 2) ? l[2 * i + 1] : l[2 * i];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) l[i] = (c & 4) ? l[2 * i + 1] : l[2 * i];
+  return (c & 8) ? l[1] : l[0];
+}
+
+// Index of the entry nearest to y: argmin_i |y - kNF4[i]| in binary32, lowest i on ties.
+__device__ __forceinline__ int nf4_code(float y) {
+  int best = 0;
+  float bd = fabsf(__fsub_rn(y, kNF4[0]));
+#pragma unroll
+  for (int i = 1; i < 16; ++i) {
+    const float d = fabsf(__fsub_rn(y, kNF4[i]));
+    if (d < bd) {
+      bd = d;
+      best = i;
+    }
+  }
+  return best;
+}
+
 // ------------------------------------------------------------------------- reductions -----
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -196,8 +233,19 @@ struct RowSrc {
   const float *xs, *ws;
   size_t cstride;  // M * ld
   int C, ld;
+  // codec mode (pay != nullptr): rows of the inter-stage codec's payload, D = ld values each
+  // (S8B_CODEC_* scheme); load4 decodes exactly as s8b_codec_decode does, output rounded to
+  // T. For the -had schemes the 32 lanes of a warp must call load4 together on the 128
+  // consecutive values of one block (lane l: values 4l .. 4l + 3), for the inverse Hadamard.
+  const void *pay = nullptr;
+  const float *psc = nullptr;
+  int scheme = 0;
   __device__ __forceinline__ void load4(int m, int col, float v[4]) const {
     const size_t o = static_cast<size_t>(m) * ld + col;
+    if (pay != nullptr) {
+      decode4(m, col, v);
+      return;
+    }
     if (part == nullptr) {
       const uint2 raw = *reinterpret_cast<const uint2 *>(x + o);
       T e[4];
@@ -221,6 +269,48 @@ struct RowSrc {
     v[2] = round_to<T>(__fmul_rn(__fmul_rn(static_cast<float>(acc.z), sx), sw.z));
     v[3] = round_to<T>(__fmul_rn(__fmul_rn(static_cast<float>(acc.w), sx), sw.w));
   }
+  __device__ __forceinline__ void decode4(int m, int col, float v[4]) const {
+    const int D = ld;
+    if (scheme == S8B_CODEC_FP16) {
+      const uint2 raw = *reinterpret_cast<const uint2 *>(static_cast<const T *>(pay) +
+                                                         static_cast<size_t>(m) * D + col);
+      T e[4];
+      memcpy(e, &raw, 8);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = to_f32(e[j]);
+      return;
+    }
+    if (scheme == S8B_CODEC_INT8 || scheme == S8B_CODEC_INT8_HAD) {
+      const char4 c = *reinterpret_cast<const char4 *>(static_cast<const int8_t *>(pay) +
+                                                       static_cast<size_t>(m) * D + col);
+      const float sc = psc[m];
+      v[0] = __fmul_rn(static_cast<float>(c.x), sc);
+      v[1] = __fmul_rn(static_cast<float>(c.y), sc);
+      v[2] = __fmul_rn(static_cast<float>(c.z), sc);
+      v[3] = __fmul_rn(static_cast<float>(c.w), sc);
+    } else {
+      const uint16_t pk = *reinterpret_cast<const uint16_t *>(
+          static_cast<const uint8_t *>(pay) + static_cast<size_t>(m) * (D / 2) + col / 2);
+      const float sc = psc[static_cast<size_t>(m) * (D / 128) + col / 128];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        int c = (pk >> (4 * i)) & 0xF;
+        if (scheme == S8B_CODEC_NF4) {
+          v[i] = __fmul_rn(nf4_value(c), sc);
+        } else {
+          c = c >= 8 ? c - 16 : c;
+          v[i] = __fmul_rn(static_cast<float>(c), sc);
+        }
+      }
+    }
+    if (scheme == S8B_CODEC_INT8_HAD || scheme == S8B_CODEC_INT4_HAD) {
+      fwht128_warp(v);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = __fmul_rn(v[i], kHadScale);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = round_to<T>(v[i]);
+  }
 };
 template <typename T>
 inline RowSrc<T> row_src(const void *x, int ld) {
@@ -230,6 +320,15 @@ template <typename T>
 inline RowSrc<T> row_src_split(const int32_t *part, int C, const float *xs, const float *ws,
                                int M, int ld) {
   return RowSrc<T>{nullptr, part, xs, ws, static_cast<size_t>(M) * ld, C, ld};
+}
+// codec payload rows of D values (see RowSrc::decode4)
+template <typename T>
+inline RowSrc<T> row_src_codec(const void *payload, const float *scales, int scheme, int D) {
+  RowSrc<T> r{nullptr, nullptr, nullptr, nullptr, 0, 1, D};
+  r.pay = payload;
+  r.psc = scales;
+  r.scheme = scheme;
+  return r;
 }
 
 // ----------------------------------------------------------------------- quantizer -----

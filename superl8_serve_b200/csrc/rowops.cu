@@ -69,7 +69,12 @@ __global__ void __launch_bounds__(1024)
       wv.load(w + 4 * i);  // independent of the reduction: in flight with the row loads
       float hv[4];
       h.load4(m, 4 * i, hv);
-      if (res_in) {
+      if (h.pay) {  // the previous stage's codec payload: [hidden | residual] decoded here
+        float rv[4];
+        h.load4(m, H + 4 * i, rv);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x[v][j] = round_to<T>(__fadd_rn(hv[j], rv[j]));
+      } else if (res_in) {
         Vec4<T> r;
         r.load(res_in + off + 4 * i);
 #pragma unroll
@@ -266,7 +271,10 @@ inline int row_cluster(int nvec) { return (nvec % kRowCluster == 0 && nvec / kRo
 template <typename T>
 int launch_rms(RowSrc<T> src, const void *res_in, void *res_out, const void *w, float eps,
                int8_t *q, float *s, void *y_out, int M, int H, void *stream) {
-  const int cl = row_cluster(H / 4);
+  int cl = row_cluster(H / 4);
+  // a codec source needs every warp on whole 128-value blocks (inverse Hadamard across a
+  // warp): each CTA's share of the row a multiple of 32 four-value vectors
+  if (src.pay != nullptr && (H / 4 / cl) % 32 != 0) cl = 1;
   int th, vpt;
   row_shape(H / 4 / cl, &th, &vpt);
   const cudaStream_t st = (cudaStream_t)stream;
@@ -317,6 +325,22 @@ extern "C" int s8b_rmsnorm_quant(const void *h, const void *residual_in, void *r
   S8B_DISPATCH_DTYPE(dtype, T,
                      return launch_rms<T>(row_src<T>(h, H), residual_in, residual_out, w, eps, q,
                                           s, y_out, M, H, stream));
+}
+
+extern "C" int s8b_rmsnorm_quant_codec(const void *payload, const float *scales, int scheme,
+                                       void *residual_out, const void *w, float eps, int8_t *q,
+                                       float *s, int M, int H, int dtype, void *stream) {
+  if (!payload || !w || !q || !s || !residual_out || (scheme != S8B_CODEC_FP16 && !scales))
+    return S8B_ERR_ARG;
+  if (scheme < S8B_CODEC_FP16 || scheme > S8B_CODEC_NF4) return S8B_ERR_DTYPE;
+  if (M < 0 || H <= 0 || H % 128 != 0 || H > 32768) return S8B_ERR_SHAPE;
+  if (!aligned(payload, 8) || !aligned(w, 8) || !aligned(q, 4) || !aligned(residual_out, 8))
+    return S8B_ERR_ALIGN;
+  if (M == 0) return S8B_OK;
+  S8B_DISPATCH_DTYPE(dtype, T,
+                     return launch_rms<T>(row_src_codec<T>(payload, scales, scheme, 2 * H),
+                                          nullptr, residual_out, w, eps, q, s, nullptr, M, H,
+                                          stream));
 }
 
 extern "C" int s8b_rmsnorm_quant_split(const int32_t *part, int C, const float *xs,

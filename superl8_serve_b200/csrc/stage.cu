@@ -59,14 +59,19 @@ struct Step {
   }
 
   // One layer. in_C / in_ws: the layer input as split-K partials (C > 0) of the previous down
-  // projection, else d.h. Returns through out_C / out_ws the same for the layer output.
-  int layer(int li, bool first_of_model, int in_C, const float *in_ws, bool keep_split,
-            int *out_C, const float **out_ws) const {
+  // projection, else d.h; codec_in: the layer input is the received boundary payload (the
+  // stage prologue). Returns through out_C / out_ws the same for the layer output.
+  int layer(int li, bool first_of_model, bool codec_in, int in_C, const float *in_ws,
+            bool keep_split, int *out_C, const float **out_ws) const {
     const S8bLayerDesc &L = d.layers[li];
     const int H = d.H, Nqkv = (d.Hq + 2 * d.Hkv) * d.D;
     *out_C = 0;
     *out_ws = nullptr;
-    S8B_TRY(rms(d.h, first_of_model ? nullptr : d.res, L.in_norm, in_C, in_ws, nullptr));
+    if (codec_in)
+      S8B_TRY(s8b_rmsnorm_quant_codec(d.in_payload, d.in_scales, d.scheme, d.res, L.in_norm,
+                                      d.eps, d.xq, d.xs, M, H, d.dtype, st));
+    else
+      S8B_TRY(rms(d.h, first_of_model ? nullptr : d.res, L.in_norm, in_C, in_ws, nullptr));
     if (tc) {
       const int C = gemm_split(L.qkv_packed, Nqkv, H);
       if (C < 0) return C;
@@ -151,22 +156,26 @@ extern "C" int s8b_stage_step(const S8bStageDesc *desc, void *stream) {
     }
   }
   Step s{d, stream, d.M, tc};
+  // stage prologue: the first RMSNorm decodes the received [hidden | residual] on load
   if (d.embed)
     S8B_TRY(s8b_embed(d.ids, d.embed, d.M, d.H, d.h, d.dtype, stream));
-  else
+  else if (d.n_layers == 0)
     S8B_TRY(s8b_codec_decode(d.in_payload, d.in_scales, d.M, d.H, d.H, d.scheme, d.h, d.res,
                              d.dtype, stream));
   int C = 0;
   const float *ws = nullptr;
   for (int li = 0; li < d.n_layers; ++li) {
-    // the last layer of a non-final stage hands a dtype h to the boundary encoder
-    const bool keep = li < d.n_layers - 1 || last;
     int oc = 0;
     const float *ow = nullptr;
-    S8B_TRY(s.layer(li, d.first_model_layer && li == 0, C, ws, keep, &oc, &ow));
+    S8B_TRY(s.layer(li, d.first_model_layer && li == 0, li == 0 && !d.embed, C, ws, true, &oc,
+                    &ow));
     C = oc;
     ws = ow;
   }
+  // stage epilogue: the encoder reduces the last down projection's split-K partials
+  if (!last && C > 0)
+    return s8b_codec_encode_split(d.part, C, d.xs, ws, d.res, d.M, d.H, d.H, d.scheme,
+                                  d.out_payload, d.out_scales, d.dtype, stream);
   if (!last)
     return s8b_codec_encode(d.h, d.res, d.M, d.H, d.H, d.scheme, d.out_payload, d.out_scales,
                             d.dtype, stream);

@@ -25,12 +25,18 @@ from .peer_routes import peer_route_allowed
 
 _WIRE_BYTES_PER_S = 250e6  # the reference's modeled PCIe-1.0-x1 link, for theoretical_wire_ms
 
+def _grouped(scheme: str) -> bool:
+    """Schemes with one scale per 128-element group (the 4-bit ones)."""
+    return scheme.startswith("int4") or scheme == "nf4"
+
+
 _BARS: dict[str, tuple[float, float]] = {
     "fp16": (float("inf"), 1.0),
     "int8": (35.0, 0.999),
     "int8-had": (35.0, 0.999),
     "int4": (14.0, 0.98),
     "int4-had": (14.0, 0.98),
+    "nf4": (16.0, 0.985),
 }
 
 
@@ -68,13 +74,13 @@ def compress_activation(x: torch.Tensor, scheme: str = "int8", group_size: int |
     """Encode x [..., d] (rows = all leading dims). payload/scales may be preallocated on
     another GPU (peer stores)."""
     if group_size not in (None, 128):
-        raise ValueError("the s8b codec groups int4 scales by 128")
+        raise ValueError("the s8b codec groups int4 / nf4 scales by 128")
     d = x.shape[-1]
     rows = x.reshape(-1, d).contiguous()
     pay, sc = ops.codec_encode(rows, None, scheme, payload=payload, scales=scales)
     if scheme == "fp16":
         sc = sc[:0]
-    return Compressed(scheme, tuple(x.shape), x.dtype, 128 if scheme.startswith("int4") else None,
+    return Compressed(scheme, tuple(x.shape), x.dtype, 128 if _grouped(scheme) else None,
                       pay, sc, d)
 
 

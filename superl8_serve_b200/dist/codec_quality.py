@@ -12,7 +12,7 @@ from . import compress_activation, decompress_activation
 
 def verify_boundary_fidelity(activation: torch.Tensor, compressor: str,
                              group_size: int | None = None) -> tuple[float, float]:
-    if group_size is None and compressor.startswith("int4"):
+    if group_size is None and compressor in ("int4", "int4-had", "nf4"):
         group_size = 128
     c = compress_activation(activation, scheme=compressor, group_size=group_size)
     xr = decompress_activation(c)

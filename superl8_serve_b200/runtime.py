@@ -496,11 +496,16 @@ class StageRunner:
 
     def _rms_quant(self, h, res_in, res_out, w, M, K, src=None, y_out=None):
         """RMSNorm + activation quant; ``src`` = (C, weight scales) reads h from the split-K
-        partials of the preceding GEMM instead of ``h``; ``y_out`` also keeps the normalized
-        dtype row."""
+        partials of the preceding GEMM instead of ``h``, ``src`` = ("codec", payload, scales,
+        scheme) reads h and the residual from the previous stage's codec payload; ``y_out``
+        also keeps the normalized dtype row."""
         if src is None:
             call("s8b_rmsnorm_quant", ptr(h), ptr(res_in), ptr(res_out), ptr(w), self.eps,
                  ptr(self.xq), ptr(self.xs), ptr(y_out), M, K, 0, stream())
+        elif src[0] == "codec":  # the stage prologue: the received payload decoded on load
+            _, pay, sc, scheme = src
+            call("s8b_rmsnorm_quant_codec", pay.data_ptr(), sc.data_ptr(), CODEC[scheme],
+                 ptr(res_out), ptr(w), self.eps, ptr(self.xq), ptr(self.xs), M, K, 0, stream())
         else:
             C, ws = src
             call("s8b_rmsnorm_quant_split", ptr(self.part), C, ptr(self.xs), ptr(ws), ptr(res_in),
@@ -639,18 +644,16 @@ class StageRunner:
             call("s8b_stage_step", ctypes.addressof(d), st)
             return
         first_model_layer = self.model.start == 0
+        h_src = None
         if self.model.is_first:
             call("s8b_embed", ptr(mb.ids), ptr(self.model.embed), M, self.H, ptr(self.h), 0, st)
-        else:
+        else:  # stage prologue: the first RMSNorm decodes the received [hidden | residual]
             pay, sc, scheme = boundary_in
-            call("s8b_codec_decode", pay.data_ptr(), sc.data_ptr(), M, self.H, self.H,
-                 CODEC[scheme], ptr(self.h), ptr(self.res), 0, st)
+            h_src = ("codec", pay, sc, scheme)
         n = len(self.model.layers)
-        h_src = None
         for li in range(n):
-            # the last layer of a non-final stage hands a dtype h to the boundary encoder
             h_src = self.layer(li, mb, M, first_model_layer and li == 0, h_src=h_src,
-                               keep_split=li < n - 1 or self.model.is_last)
+                               keep_split=True)
         if self.model.is_last:
             if not head:
                 return
@@ -667,8 +670,14 @@ class StageRunner:
                      ptr(smp["input_ids"]), ptr(mb.positions), ptr(smp["history"]),
                      smp["history"].shape[1], ptr(smp["seeds"]), ptr(smp["workspace"]),
                      smp["workspace"].numel(), ptr(mb.ids), st)
-        else:
+        else:  # stage epilogue: the encoder reduces the last down projection's partials
             pay, sc, scheme = boundary_out
-            call("s8b_codec_encode", ptr(self.h), ptr(self.res), M, self.H, self.H, CODEC[scheme],
-                 pay.data_ptr(), sc.data_ptr(), 0, st)
+            if h_src is not None:
+                C, ws = h_src
+                call("s8b_codec_encode_split", ptr(self.part), C, ptr(self.xs), ptr(ws),
+                     ptr(self.res), M, self.H, self.H, CODEC[scheme], pay.data_ptr(),
+                     sc.data_ptr(), 0, st)
+            else:
+                call("s8b_codec_encode", ptr(self.h), ptr(self.res), M, self.H, self.H,
+                     CODEC[scheme], pay.data_ptr(), sc.data_ptr(), 0, st)
 

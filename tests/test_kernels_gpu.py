@@ -296,7 +296,7 @@ def test_embed_and_argmax(rng):
     assert np.array_equal(tok.cpu().numpy(), ok.argmax_rows(logits))
 
 
-@pytest.mark.parametrize("scheme", ["fp16", "int8", "int8-had", "int4", "int4-had"])
+@pytest.mark.parametrize("scheme", ["fp16", "int8", "int8-had", "int4", "int4-had", "nf4"])
 @pytest.mark.parametrize("T", [1, 16, 64, 256, 1024])
 def test_codec_bit_exact_config2(rng, scheme, T):
     """BASELINE config 2 inputs: [T, 4096] N(0,1) with 0.1% channels x20 (bf16)."""
@@ -314,7 +314,87 @@ def test_codec_bit_exact_config2(rng, scheme, T):
     assert np.array_equal(f32(rec), oc.decode(po, so, scheme, 4096))
 
 
-@pytest.mark.parametrize("scheme", ["int8", "int8-had", "int4-had"])
+@pytest.mark.parametrize("scheme", ["fp16", "int8", "int8-had", "int4", "int4-had", "nf4"])
+@pytest.mark.parametrize("T,H,C", [(5, 4096, 3), (64, 4096, 2), (3, 1024, 1)])
+def test_codec_encode_from_split_partials(rng, scheme, T, H, C):
+    """Stage epilogue: the encoder reads the down projection's split-K partials (summed and
+    dequantized as the GEMM would) and the residual; codes equal the oracle's."""
+    from superl8_serve_b200 import _lib, ops
+    from superl8_serve_b200._lib import call, ptr
+
+    part = rng.integers(-2 ** 20, 2 ** 20, (C, T, H)).astype(np.int32)
+    xs = rng.uniform(1e-3, 1e-2, T).astype(np.float32)
+    ws = rng.uniform(1e-4, 1e-3, H).astype(np.float32)
+    h = on.round_bf16(on.dequant_acc(part.sum(0), xs, ws))
+    r = rand_act(rng, (T, H), 8.0)
+    nbytes, nsc = ops.codec_sizes(T, 2 * H, scheme)
+    pay = torch.zeros(nbytes, dtype=torch.uint8, device=DEV)
+    sc = torch.zeros(max(nsc, 1), dtype=torch.float32, device=DEV)
+    partd, xsd, wsd = to_dev(part, xs, ws)
+    rd = bf16(r)
+    call("s8b_codec_encode_split", ptr(partd), C, ptr(xsd), ptr(wsd), ptr(rd), T, H, H,
+         _lib.CODEC[scheme], ptr(pay), ptr(sc), 0, torch.cuda.current_stream().cuda_stream)
+    po, so = oc.encode(np.concatenate([h, r], -1), scheme)
+    assert np.array_equal(pay.cpu().numpy()[: po.nbytes].view(po.dtype).reshape(po.shape), po)
+    if so.size:
+        assert np.array_equal(sc.cpu().numpy()[: so.size].reshape(so.shape), so)
+
+
+@pytest.mark.parametrize("scheme", ["fp16", "int8", "int8-had", "int4", "int4-had", "nf4"])
+@pytest.mark.parametrize("T,H", [(5, 4096), (64, 4096), (3, 1024), (2, 256), (4, 5120),
+                                 (3, 640)])
+def test_rmsnorm_quant_from_codec_payload(rng, scheme, T, H):
+    """Stage prologue: RMSNorm + quant reading [hidden | residual] straight from the codec
+    payload equals the oracle's decode followed by its RMSNorm + quant."""
+    from superl8_serve_b200 import _lib, ops
+    from superl8_serve_b200._lib import call, ptr
+
+    h = rand_act(rng, (T, H), 1.0, outliers=4)
+    r = rand_act(rng, (T, H), 8.0)
+    po, so = oc.encode(np.concatenate([h, r], -1), scheme)
+    rec = oc.decode(po, so, scheme, 2 * H)
+    w = on.round_bf16(1 + 0.1 * rng.standard_normal(H).astype(np.float32))
+    xo, qo, s_o, _ = ok.rmsnorm_quant(rec[:, :H], rec[:, H:], w, 1e-6)
+    if scheme == "fp16":
+        payd = bf16(np.concatenate([h, r], -1))
+        scd = torch.zeros(1, dtype=torch.float32, device=DEV)
+    else:
+        payd = torch.from_numpy(np.ascontiguousarray(po)).to(DEV)
+        scd = torch.from_numpy(np.ascontiguousarray(so, np.float32)).to(DEV)
+    res = torch.zeros((T, H), dtype=torch.bfloat16, device=DEV)
+    q = torch.zeros((T, H), dtype=torch.int8, device=DEV)
+    s_ = torch.zeros(T, dtype=torch.float32, device=DEV)
+    call("s8b_rmsnorm_quant_codec", ptr(payd), ptr(scd), _lib.CODEC[scheme], ptr(res),
+         ptr(bf16(w)), 1e-6, ptr(q), ptr(s_), T, H, 0, torch.cuda.current_stream().cuda_stream)
+    assert np.array_equal(f32(res), xo)
+    assert np.array_equal(q.cpu().numpy(), qo) and np.array_equal(s_.cpu().numpy(), s_o)
+
+
+def test_nf4_codes_at_ties_and_zero_groups(rng):
+    """nf4 on the GPU: values exactly halfway between codebook entries (lowest index wins),
+    every entry itself, an all-zero group, a group whose absmax is negative, and a denormal
+    group; codes, scales and decoded values equal the oracle's."""
+    from superl8_serve_b200 import ops
+
+    x = np.zeros((4, 256), np.float32)
+    mids = ((oc.NF4[:-1] + oc.NF4[1:]) / 2).astype(np.float32)
+    x[0, :15] = mids
+    x[0, 15:31] = oc.NF4
+    x[0, 127] = 1.0
+    x[0, 128:256] = -2.0 * rng.random(128).astype(np.float32)
+    x[0, 200] = -2.0
+    x[2, :128] = rng.standard_normal(128).astype(np.float32) * 1e-39
+    x[3] = rng.standard_normal(256).astype(np.float32) * 3
+    x = on.round_bf16(x)
+    pay, sc = ops.codec_encode(bf16(x), None, "nf4")
+    po, so = oc.encode(x, "nf4")
+    assert np.array_equal(pay.cpu().numpy()[: po.nbytes].reshape(po.shape), po)
+    assert np.array_equal(sc.cpu().numpy()[: so.size].reshape(so.shape), so)
+    rec, _ = ops.codec_decode(pay, sc, 4, 256, 0, "nf4", torch.bfloat16)
+    assert np.array_equal(f32(rec), oc.decode(po, so, "nf4", 256))
+
+
+@pytest.mark.parametrize("scheme", ["int8", "int8-had", "int4-had", "nf4"])
 def test_codec_two_sources_pipeline_boundary(rng, scheme):
     """(hidden, residual) packed as one [T, 2H] row without materialising the concat."""
     from superl8_serve_b200 import ops

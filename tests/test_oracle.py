@@ -127,7 +127,8 @@ def _activation(shape, seed, outlier=False):
 
 
 @pytest.mark.parametrize("scheme,bar", [("int8", (35.0, 0.999)), ("int8-had", (35.0, 0.999)),
-                                        ("int4", (14.0, 0.98)), ("int4-had", (14.0, 0.98))])
+                                        ("int4", (14.0, 0.98)), ("int4-had", (14.0, 0.98)),
+                                        ("nf4", (16.0, 0.985))])
 def test_codec_meets_reference_bars(scheme, bar):
     """Acceptance bars of superl8serve/dist/__init__.py:46-52 on Gaussian activations."""
     x = _activation((4 * 64, 256), 2)
@@ -144,6 +145,44 @@ def test_codec_fp16_lossless_and_hadamard_helps_outliers():
     r4 = oc.accuracy(x, oc.decode(*oc.encode(x, "int4"), "int4", 128))[0]
     rh = oc.accuracy(x, oc.decode(*oc.encode(x, "int4-had"), "int4-had", 128))[0]
     assert rh > r4
+
+
+def test_nf4_codebook_is_the_published_construction():
+    """The pinned binary32 table equals the NF4 construction (normal quantiles, normalised)."""
+    cb = oc.nf4_codebook()
+    assert cb.dtype == np.float32 and cb.shape == (16,)
+    np.testing.assert_allclose(cb, oc.NF4, rtol=0, atol=2e-7)
+    assert oc.NF4[0] == -1.0 and oc.NF4[7] == 0.0 and oc.NF4[15] == 1.0
+    assert np.all(np.diff(oc.NF4) > 0)
+
+
+def test_nf4_codes_nearest_entry_lowest_on_ties():
+    """nf4 codes: each value's code is the nearest table entry to x / absmax; a value exactly
+    halfway between two entries takes the lower index; an all-zero group encodes to the
+    0.0 entry with scale 0 and decodes to +0."""
+    x = np.zeros((2, 128), np.float32)
+    mids = ((oc.NF4[:-1] + oc.NF4[1:]) / 2).astype(np.float32)
+    x[0, : mids.size] = mids
+    x[0, 127] = 1.0  # absmax 1: y == x
+    pay, sc = oc.encode(x, "nf4")
+    assert sc.shape == (2, 1) and sc[0, 0] == 1.0 and sc[1, 0] == 0.0
+    codes = np.stack([pay & 0xF, pay >> 4], -1).reshape(2, 128)
+    for i, m in enumerate(mids):
+        d = np.abs(m - oc.NF4).astype(np.float32)
+        assert codes[0, i] == int(np.argmin(d))
+        assert codes[0, i] in (i, i + 1)
+    assert np.all(codes[1] == 7)
+    out = oc.decode(pay, sc, "nf4", 128)
+    assert np.array_equal(out[1], np.zeros(128, np.float32)) and not np.signbit(out[1]).any()
+    assert np.array_equal(out[0, 127:], [1.0])
+
+
+def test_nf4_wire_bytes_equal_int4():
+    """nf4 is a 4-bit code with one fp32 scale per 128 values
+    (superl8serve/dist/transfer_model.py:31,40), so it weighs what int4 weighs."""
+    assert oc.wire_bytes(4, 8192, "nf4") == oc.wire_bytes(4, 8192, "int4")
+    pay, sc = oc.encode(_activation((4, 8192), 9), "nf4")
+    assert pay.nbytes + sc.nbytes == oc.wire_bytes(4, 8192, "nf4")
 
 
 def test_codec_wire_bytes_match_reference_handle(golden_dir):

@@ -21,7 +21,7 @@ from oracle import codec as oc
 from oracle.numerics import round_bf16
 
 pytestmark = pytest.mark.gpu
-SCHEMES = ["int8", "int8-had", "int4", "int4-had", "fp16"]
+SCHEMES = ["int8", "int8-had", "int4", "int4-had", "nf4", "fp16"]
 two_gpus = pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 
 
@@ -103,4 +103,27 @@ def test_wire_scheme_gate_matches_reference(host_golden, kind):
             assert sq == float("inf")
         else:
             assert sq == pytest.approx(want_sq, rel=1e-5)
-        assert cos == pytest.approx(want_cos, rel=1e-6)
+        # (the codes are bit-exact; torch reduces the cosine on the device in another order)
+        assert cos == pytest.approx(want_cos, rel=1e-5)
+
+
+@pytest.mark.parametrize("scheme,bars", [("nf4", (16.0, 0.985)), ("int4", (14.0, 0.98)),
+                                         ("int8", (35.0, 0.999))])
+def test_codec_meets_reference_bars_fp16_input(scheme, bars):
+    """The reference's acceptance checks (tests/test_transport.py:78-86,
+    tests/test_codec_quality.py:57-61): a [4, 64, 256] fp16 N(0, 1) activation round-trips
+    above the scheme's SQNR / cosine bars, through ``verify_boundary_fidelity`` and
+    ``accuracy_report``."""
+    from superl8_serve_b200.dist import accuracy_report, compress_activation, decompress_activation
+    from superl8_serve_b200.dist.codec_quality import verify_boundary_fidelity
+
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn((4, 64, 256), generator=g).half().cuda()
+    sq, cos = verify_boundary_fidelity(x, scheme)
+    assert sq > bars[0] and cos > bars[1]
+    c = compress_activation(x, scheme=scheme, group_size=128 if scheme != "int8" else None)
+    xr = decompress_activation(c)
+    assert xr.dtype == torch.float16 and xr.shape == x.shape
+    rep = accuracy_report(x, xr, scheme)
+    assert rep["sqnr_pass"] and rep["cos_pass"]
+    assert (rep["sqnr_bar"], rep["cos_bar"]) == bars
