@@ -233,19 +233,9 @@ struct RowSrc {
   const float *xs, *ws;
   size_t cstride;  // M * ld
   int C, ld;
-  // codec mode (pay != nullptr): rows of the inter-stage codec's payload, D = ld values each
-  // (S8B_CODEC_* scheme); load4 decodes exactly as s8b_codec_decode does, output rounded to
-  // T. For the -had schemes the 32 lanes of a warp must call load4 together on the 128
-  // consecutive values of one block (lane l: values 4l .. 4l + 3), for the inverse Hadamard.
-  const void *pay = nullptr;
-  const float *psc = nullptr;
-  int scheme = 0;
+  static constexpr bool kCodec = false;
   __device__ __forceinline__ void load4(int m, int col, float v[4]) const {
     const size_t o = static_cast<size_t>(m) * ld + col;
-    if (pay != nullptr) {
-      decode4(m, col, v);
-      return;
-    }
     if (part == nullptr) {
       const uint2 raw = *reinterpret_cast<const uint2 *>(x + o);
       T e[4];
@@ -269,7 +259,29 @@ struct RowSrc {
     v[2] = round_to<T>(__fmul_rn(__fmul_rn(static_cast<float>(acc.z), sx), sw.z));
     v[3] = round_to<T>(__fmul_rn(__fmul_rn(static_cast<float>(acc.w), sx), sw.w));
   }
-  __device__ __forceinline__ void decode4(int m, int col, float v[4]) const {
+};
+template <typename T>
+inline RowSrc<T> row_src(const void *x, int ld) {
+  return RowSrc<T>{static_cast<const T *>(x), nullptr, nullptr, nullptr, 0, 1, ld};
+}
+template <typename T>
+inline RowSrc<T> row_src_split(const int32_t *part, int C, const float *xs, const float *ws,
+                               int M, int ld) {
+  return RowSrc<T>{nullptr, part, xs, ws, static_cast<size_t>(M) * ld, C, ld};
+}
+
+// Rows of the inter-stage codec's payload, D values each (S8B_CODEC_* scheme), as a row
+// source: load4 decodes exactly as s8b_codec_decode does, output rounded to T. For the -had
+// schemes the 32 lanes of a warp must call load4 together on the 128 consecutive values of
+// one block (lane l: values 4l .. 4l + 3), for the inverse Hadamard. A separate type (not a
+// mode of RowSrc) so that kernels on plain or split rows carry none of this code.
+template <typename T>
+struct CodecSrc {
+  const void *pay;
+  const float *psc;
+  int scheme, ld;
+  static constexpr bool kCodec = true;
+  __device__ __forceinline__ void load4(int m, int col, float v[4]) const {
     const int D = ld;
     if (scheme == S8B_CODEC_FP16) {
       const uint2 raw = *reinterpret_cast<const uint2 *>(static_cast<const T *>(pay) +
@@ -313,22 +325,8 @@ struct RowSrc {
   }
 };
 template <typename T>
-inline RowSrc<T> row_src(const void *x, int ld) {
-  return RowSrc<T>{static_cast<const T *>(x), nullptr, nullptr, nullptr, 0, 1, ld};
-}
-template <typename T>
-inline RowSrc<T> row_src_split(const int32_t *part, int C, const float *xs, const float *ws,
-                               int M, int ld) {
-  return RowSrc<T>{nullptr, part, xs, ws, static_cast<size_t>(M) * ld, C, ld};
-}
-// codec payload rows of D values (see RowSrc::decode4)
-template <typename T>
-inline RowSrc<T> row_src_codec(const void *payload, const float *scales, int scheme, int D) {
-  RowSrc<T> r{nullptr, nullptr, nullptr, nullptr, 0, 1, D};
-  r.pay = payload;
-  r.psc = scales;
-  r.scheme = scheme;
-  return r;
+inline CodecSrc<T> row_src_codec(const void *payload, const float *scales, int scheme, int D) {
+  return CodecSrc<T>{payload, scales, scheme, D};
 }
 
 // ----------------------------------------------------------------------- quantizer -----

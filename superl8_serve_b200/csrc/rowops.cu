@@ -44,9 +44,9 @@ __device__ __forceinline__ void store_codes(int8_t *dst, const float v[4], float
   *reinterpret_cast<char4 *>(dst) = c;
 }
 
-template <typename T, int VPT, int CL = 1>
+template <typename T, int VPT, int CL = 1, typename Src = RowSrc<T>>
 __global__ void __launch_bounds__(1024)
-    rmsnorm_quant_v(RowSrc<T> h, const T *__restrict__ res_in, T *__restrict__ res_out,
+    rmsnorm_quant_v(Src h, const T *__restrict__ res_in, T *__restrict__ res_out,
                     const T *__restrict__ w, float eps, int8_t *__restrict__ q,
                     float *__restrict__ s, T *__restrict__ y_out, int H) {
   griddep_launch();  // the next kernel may start its prologue
@@ -69,7 +69,7 @@ __global__ void __launch_bounds__(1024)
       wv.load(w + 4 * i);  // independent of the reduction: in flight with the row loads
       float hv[4];
       h.load4(m, 4 * i, hv);
-      if (h.pay) {  // the previous stage's codec payload: [hidden | residual] decoded here
+      if constexpr (Src::kCodec) {  // the previous stage's payload: [hidden | residual]
         float rv[4];
         h.load4(m, H + 4 * i, rv);
 #pragma unroll
@@ -268,24 +268,26 @@ namespace {
 constexpr int kRowCluster = kMaxRowCluster;
 inline int row_cluster(int nvec) { return (nvec % kRowCluster == 0 && nvec / kRowCluster >= 32) ? kRowCluster : 1; }
 
-template <typename T>
-int launch_rms(RowSrc<T> src, const void *res_in, void *res_out, const void *w, float eps,
+template <typename T, typename Src>
+int launch_rms(Src src, const void *res_in, void *res_out, const void *w, float eps,
                int8_t *q, float *s, void *y_out, int M, int H, void *stream) {
   int cl = row_cluster(H / 4);
   // a codec source needs every warp on whole 128-value blocks (inverse Hadamard across a
   // warp): each CTA's share of the row a multiple of 32 four-value vectors
-  if (src.pay != nullptr && (H / 4 / cl) % 32 != 0) cl = 1;
+  if constexpr (Src::kCodec) {
+    if ((H / 4 / cl) % 32 != 0) cl = 1;
+  }
   int th, vpt;
   row_shape(H / 4 / cl, &th, &vpt);
   const cudaStream_t st = (cudaStream_t)stream;
   if (cl == 1) {
     S8B_VPT_SWITCH(vpt, V,
-                   launch_pdl(rmsnorm_quant_v<T, V, 1>, M, th, 0, st, src,
+                   launch_pdl(rmsnorm_quant_v<T, V, 1, Src>, M, th, 0, st, src,
                               static_cast<const T *>(res_in), static_cast<T *>(res_out),
                               static_cast<const T *>(w), eps, q, s, static_cast<T *>(y_out), H));
   } else {
     S8B_VPT_SWITCH(vpt, V,
-                   launch_pdl_cluster(rmsnorm_quant_v<T, V, kRowCluster>, M * kRowCluster, th, 0,
+                   launch_pdl_cluster(rmsnorm_quant_v<T, V, kRowCluster, Src>, M * kRowCluster, th, 0,
                                       kRowCluster, st, src, static_cast<const T *>(res_in),
                                       static_cast<T *>(res_out), static_cast<const T *>(w), eps,
                                       q, s, static_cast<T *>(y_out), H));

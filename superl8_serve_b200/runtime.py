@@ -363,8 +363,11 @@ def moe_expert_buffers(M: int, k: int, H: int, Fe: int, E: int, device, dtype=to
 class StageRunner:
     """Launches one stage's decode kernels for a micro-batch of up to ``m`` rows."""
 
-    # token count from which the W8A8 GEMMs run on the tensor cores (tcgen05) instead of dp4a
-    TC_MIN_TOKENS = 16
+    # token count from which the W8A8 GEMMs run on the tensor cores (tcgen05) instead of dp4a:
+    # the dp4a GEMV streams weights at HBM speed for one token only (each further token adds
+    # 16 dp4a operations per weight byte; at 4 tokens it runs at 4.2 TB/s against 5.7 for the
+    # tensor cores on a 34816 x 5120 weight, at 2 tokens they tie)
+    TC_MIN_TOKENS = 2
 
     def __init__(self, model: StageModel, pool: KVPool, m: int, max_ctx: int,
                  dtype=torch.bfloat16, tc_min_tokens: int | None = None,
