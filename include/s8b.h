@@ -323,6 +323,13 @@ int s8b_flag_wait(const uint32_t *flag, const uint32_t *value, uint32_t add,
                   uint64_t timeout_ns, int32_t *status, void *stream);
 int s8b_counter_add(uint32_t *ctr, uint32_t inc, void *stream);
 int s8b_flag_status(const int32_t *status_host_copy);
+/* Copies n <= 8 buffers (bytes[i] from src[i] to dst[i], usually a peer's or an IPC-mapped
+ * buffer) with plain stores from one CTA, then, if flag is not null, raises it exactly as
+ * s8b_flag_set does, ordered after every copied byte. One launch instead of n copy-engine
+ * copies and a flag launch: the hand-off of a sparse-MoE layer's token rows and routing to
+ * a partner process holding other experts.                                                */
+int s8b_peer_put_flag(void *const *dst, const void *const *src, const size_t *bytes, int n,
+                      uint32_t *flag, const uint32_t *value, uint32_t add, void *stream);
 
 /* Decode-step bookkeeping on the device: positions[i] += inc; context_lens[i] =
  * positions[i] + 1 (context_lens nullable). Keeps the per-step position state in device

@@ -71,6 +71,7 @@ SIGNATURES: dict[str, tuple] = {
     "s8b_flag_set": (_i, [_vp, _vp, _u32, _vp]),
     "s8b_flag_wait": (_i, [_vp, _vp, _u32, _u64, _vp, _vp]),
     "s8b_counter_add": (_i, [_vp, _u32, _vp]),
+    "s8b_peer_put_flag": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _u32, _vp]),
     "s8b_flag_status": (_i, [_vp]),
     "s8b_advance": (_i, [_vp, _vp, _i, _i, _vp]),
     "s8b_enable_peer_access": (_i, [_i, _i]),

@@ -51,6 +51,45 @@ __global__ void flag_wait_kernel(const uint32_t *flag, const uint32_t *value, ui
 
 __global__ void counter_add_kernel(uint32_t *ctr, uint32_t inc) { *ctr += inc; }
 
+// Copies a short list of buffers (usually into a peer's memory over NVLink) with plain
+// stores from one CTA, then raises `flag` like flag_set_kernel: every thread's stores are
+// ordered before the release by the CTA barrier and thread 0's system-scope fence.
+constexpr int kPutMax = 8;
+struct PutList {
+  void *dst[kPutMax];
+  const void *src[kPutMax];
+  unsigned long long bytes[kPutMax];
+  int n;
+};
+
+__global__ void __launch_bounds__(1024)
+    peer_put_flag_kernel(PutList L, uint32_t *flag, const uint32_t *value, uint32_t add) {
+  for (int i = 0; i < L.n; ++i) {
+    const unsigned long long nb = L.bytes[i];
+    const uintptr_t d = reinterpret_cast<uintptr_t>(L.dst[i]);
+    const uintptr_t sa = reinterpret_cast<uintptr_t>(L.src[i]);
+    if (((d | sa | nb) & 15) == 0) {
+      const int4 *sp = static_cast<const int4 *>(L.src[i]);
+      int4 *dp = static_cast<int4 *>(L.dst[i]);
+      for (unsigned long long k = threadIdx.x; k < nb / 16; k += blockDim.x) dp[k] = sp[k];
+    } else if (((d | sa | nb) & 3) == 0) {
+      const uint32_t *sp = static_cast<const uint32_t *>(L.src[i]);
+      uint32_t *dp = static_cast<uint32_t *>(L.dst[i]);
+      for (unsigned long long k = threadIdx.x; k < nb / 4; k += blockDim.x) dp[k] = sp[k];
+    } else {
+      const uint8_t *sp = static_cast<const uint8_t *>(L.src[i]);
+      uint8_t *dp = static_cast<uint8_t *>(L.dst[i]);
+      for (unsigned long long k = threadIdx.x; k < nb; k += blockDim.x) dp[k] = sp[k];
+    }
+  }
+  if (flag == nullptr) return;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    st_release_sys(flag, *value + add);
+  }
+}
+
 __global__ void advance_kernel(int32_t *positions, int32_t *context_lens, int M, int inc) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < M) {
@@ -75,6 +114,23 @@ extern "C" int s8b_flag_wait(const uint32_t *flag, const uint32_t *value, uint32
                              uint64_t timeout_ns, int32_t *status, void *stream) {
   if (!flag || !value) return S8B_ERR_ARG;
   flag_wait_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(flag, value, add, timeout_ns, status);
+  return check_launch();
+}
+
+extern "C" int s8b_peer_put_flag(void *const *dst, const void *const *src, const size_t *bytes,
+                                 int n, uint32_t *flag, const uint32_t *value, uint32_t add,
+                                 void *stream) {
+  if (n < 0 || n > kPutMax) return S8B_ERR_SHAPE;
+  if ((n > 0 && (!dst || !src || !bytes)) || (flag && !value)) return S8B_ERR_ARG;
+  PutList L{};
+  L.n = n;
+  for (int i = 0; i < n; ++i) {
+    if (bytes[i] > 0 && (!dst[i] || !src[i])) return S8B_ERR_ARG;
+    L.dst[i] = dst[i];
+    L.src[i] = src[i];
+    L.bytes[i] = bytes[i];
+  }
+  peer_put_flag_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(L, flag, value, add);
   return check_launch();
 }
 

@@ -25,6 +25,7 @@ table (stage 0), int8 LM head (last stage); KV pools [layers, blocks, Hkv, 16, 1
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -554,12 +555,14 @@ class StageRunner:
         # buffers by peer copies, a release flag starts it, its down projection stores into
         # this GPU's contribution buffer and raises this GPU's flag (RemoteExperts)
         remote = [] if self.skip_remote else mw.remote
-        for rx in remote:
-            for dst, src, n in ((rx.xq, self.xq, M * H), (rx.xs, self.xs, 4 * M),
-                                (rx.offsets, b["offsets"], 4 * (E + 1)),
-                                (rx.sorted_token, b["sorted_token"], 4 * A)):
-                call("s8b_memcpy_async", dst, ptr(src), n, st)
-            call("s8b_flag_set", rx.in_flag, rx.epoch, 1, st)
+        for rx in remote:  # one launch: the four copies, then the partner's flag
+            put = ((rx.xq, self.xq, M * H), (rx.xs, self.xs, 4 * M),
+                   (rx.offsets, b["offsets"], 4 * (E + 1)),
+                   (rx.sorted_token, b["sorted_token"], 4 * A))
+            dsts = (ctypes.c_void_p * 4)(*[d for d, _, _ in put])
+            srcs = (ctypes.c_void_p * 4)(*[ptr(x) for _, x, _ in put])
+            nbytes = (ctypes.c_size_t * 4)(*[n for _, _, n in put])
+            call("s8b_peer_put_flag", dsts, srcs, nbytes, 4, rx.in_flag, rx.epoch, 1, st)
         self._moe_experts(b, ptr(b["offsets"]), mw.local_experts, mw.gu_w, mw.gu_s, mw.d_w,
                           mw.d_s, ptr(b["contrib"]), M, k, Fe, st, xq=self.xq, xs=self.xs)
         for rx in remote:
@@ -639,8 +642,6 @@ class StageRunner:
         M = self.m if M is None else M
         st = stream()
         if self.native:
-            import ctypes
-
             from .native import stage_desc
 
             d = stage_desc(self, mb, M, boundary_in, boundary_out, head)

@@ -439,6 +439,33 @@ def test_flag_wait_times_out_and_reports(rng):
     assert status.cpu().tolist()[0] == 0 and flag.item() == 6
 
 
+def test_peer_put_flag_copies_then_raises_flag(rng):
+    """One launch copies several buffers (16-byte, 4-byte and odd sizes and offsets) and then
+    stores the epoch into the flag; a bounded wait on the flag then sees it at once."""
+    import ctypes
+
+    from superl8_serve_b200._lib import call, ptr, stream
+
+    srcs = [torch.from_numpy(rng.integers(0, 256, n, dtype=np.uint8)).to(DEV)
+            for n in (65536, 132, 517, 4096)]
+    dsts = [torch.zeros(n + 32, dtype=torch.uint8, device=DEV) for n in (65536, 132, 517, 4096)]
+    offs = [0, 4, 3, 16]  # destination offsets: aligned, 4-byte, odd, aligned
+    dst_p = (ctypes.c_void_p * 4)(*[ptr(d) + o for d, o in zip(dsts, offs)])
+    src_p = (ctypes.c_void_p * 4)(*[ptr(x) for x in srcs])
+    nb = (ctypes.c_size_t * 4)(*[x.numel() for x in srcs])
+    flag = torch.zeros(1, dtype=torch.int32, device=DEV)
+    epoch = torch.tensor([41], dtype=torch.int32, device=DEV)
+    status = torch.zeros(3, dtype=torch.int32, device=DEV)
+    call("s8b_peer_put_flag", dst_p, src_p, nb, 4, ptr(flag), ptr(epoch), 1, stream())
+    call("s8b_flag_wait", ptr(flag), ptr(epoch), 1, 1_000_000_000, ptr(status), stream())
+    torch.cuda.synchronize()
+    assert flag.item() == 42 and status.cpu().tolist()[0] == 0
+    for d, o, x in zip(dsts, offs, srcs):
+        n = x.numel()
+        assert torch.equal(d[o:o + n], x)
+        assert int(d[:o].sum()) == 0 and int(d[o + n:].sum()) == 0
+
+
 def test_exp_matches_definition_bitwise():
     """exp_s8b on the GPU (the softmax / merge / SiLU exponential) equals the CPU definition
     bit for bit over every 97th binary32 pattern (both signs, all exponents, NaN and inf)
