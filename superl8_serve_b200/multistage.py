@@ -557,6 +557,37 @@ class ExpertPartner:
         self.own, self.opened = [], []
 
 
+def attention_rate(pipe) -> dict:
+    """Paged attention of micro-batch 0 on this rank's layers, launched back to back and
+    timed with CUDA events on the launching stream (each layer's pool streams from HBM):
+    ms per launch, algorithmic bytes per launch (K/V codes and scales over the rows'
+    contexts, queries, outputs) and GB/s."""
+    r, mb = pipe.runner, pipe.mbs[0]
+    M, L = pipe.m, len(r.model.layers)
+    st = stream()
+
+    def launch(li):
+        kc, ks, vc, vs = r.pool.layer(li % L)
+        call("s8b_paged_decode_q8", ptr(r.q_i8), ptr(r.q_s), ptr(kc), ptr(ks), ptr(vc), ptr(vs),
+             ptr(mb.block_table), ptr(mb.context_lens), ptr(r.attn), ptr(r.xq), ptr(r.xs), M,
+             r.Hq, r.Hkv, r.D, r.pool.block_size, mb.block_table.shape[1], r.max_ctx, r.scale,
+             ptr(r.ws), r.ws.numel(), 0, st)
+
+    launch(0)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 4 * L
+    a.record()
+    for i in range(reps):
+        launch(i)
+    b.record()
+    b.synchronize()
+    ms = a.elapsed_time(b) / reps
+    ctx = int(mb.context_lens[0].item())
+    byts = M * ctx * r.Hkv * (2 * 128 + 2 * 4) + M * r.Hq * (128 + 4) + M * r.Hq * 128 * 3
+    return {"ms": ms, "bytes": byts, "gbs": byts / ms / 1e6}
+
+
 def run_bench_multi(args, metric, step_bytes, peaks, ClockSampler, cpu_sample):
     """bench.py at N > 1: each rank one stage; rank 0 prints the JSON line."""
     import datetime
@@ -679,6 +710,8 @@ def run_bench_multi(args, metric, step_bytes, peaks, ClockSampler, cpu_sample):
     if role == "home":
         lo, hi = pipe.plan.layers
         sb = step_bytes(cfg, m * S, ctx, hi - lo, pipe.plan.last)
+    # the dominant kernel (paged attention) timed live on rank 0's own layers and buffers
+    attn = attention_rate(pipe) if rank == 0 else None
     pipe.close()
     B = m * S
     if rank == 0:
@@ -712,6 +745,10 @@ def run_bench_multi(args, metric, step_bytes, peaks, ClockSampler, cpu_sample):
             "step_roofline": {"bytes_rank0": sb, "achieved_gbs_rank0": sb / ms / 1e6,
                               "frac_rank0": sb / ms / 1e6 / hbm, "peak": hbm,
                               "peak_kind": peak_kind},
+            "roofline": {"bound": "hbm", "kernel": "paged_decode_attention (rank 0)",
+                         "achieved": attn["gbs"], "peak": hbm, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": attn["gbs"] / hbm, "traffic": None,
+                         "bytes_per_launch": attn["bytes"], "ms_per_launch": attn["ms"]},
         }
         print(json.dumps(line), flush=True)
     dist.barrier()
