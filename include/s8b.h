@@ -227,6 +227,23 @@ int s8b_paged_decode_q8_step(const int8_t *q_i8, const float *q_s, const int8_t 
                              int8_t *out_q, float *out_s, int B, int Hq, int Hkv, int D,
                              int block_size, int max_blocks, int max_ctx, float scale,
                              void *workspace, size_t workspace_bytes, int dtype, void *stream);
+/* Varlen prefill attention over the int8 paged cache (replaces the superl8
+ * attn_int8_varlen call of the reference's prefill, superl8serve/dist/pipeline.py:908-984):
+ * rows, queries, cache and output exactly as s8b_paged_decode_q8 (row b attends over the
+ * first context_lens[b] positions of block-table row b), output identical to it. The rows
+ * are grouped into n_row_blocks row blocks, row_blocks[2i] = first row, row_blocks[2i + 1]
+ * = row count (1 .. s8b_paged_prefill_block_rows(Hq, Hkv); larger counts are cut there):
+ * consecutive rows of one sequence, whose block-table rows are equal; every row in exactly
+ * one block. Each block's K/V partitions are read once for all its rows (a row's heads are
+ * columns of the tensor-core tiles). Workspace as s8b_paged_decode_q8.                   */
+int s8b_paged_prefill_block_rows(int Hq, int Hkv);
+int s8b_paged_prefill_q8(const int8_t *q_i8, const float *q_s, const int8_t *kc,
+                         const float *ks, const int8_t *vc, const float *vs,
+                         const int32_t *block_table, const int32_t *context_lens,
+                         const int32_t *row_blocks, int n_row_blocks, void *out, int8_t *out_q,
+                         float *out_s, int B, int Hq, int Hkv, int D, int block_size,
+                         int max_blocks, int max_ctx, float scale, void *workspace,
+                         size_t workspace_bytes, int dtype, void *stream);
 
 /* No-allocation form of s8b_paged_decode_q8, for callers that cannot allocate device
  * memory: a host-language binding (cgo, JNI, ctypes) that is handed device buffers but owns no

@@ -53,6 +53,9 @@ SIGNATURES: dict[str, tuple] = {
                                  _i, _i, _i, _i, _i, _f, _vp, _sz, _i, _vp]),
     "s8b_paged_decode_q8_step": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                       _i, _i, _i, _i, _i, _i, _i, _f, _vp, _sz, _i, _vp]),
+    "s8b_paged_prefill_block_rows": (_i, [_i, _i]),
+    "s8b_paged_prefill_q8": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp,
+                                  _i, _i, _i, _i, _i, _i, _i, _f, _vp, _sz, _i, _vp]),
     "s8b_paged_decode_q8_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                          _i, _i, _i, _i, _i, _i, _i, _f, _i, _vp]),
     "s8b_paged_decode_noalloc_status": (_i, [_vp, C.c_int32]),

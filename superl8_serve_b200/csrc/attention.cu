@@ -849,6 +849,8 @@ constexpr int kColO = 64;      // O buffer t at kColO + 48 t; S buffer t at 32 t
 constexpr int kMisc = 2048;    // barriers, TMEM base, abort flag, stats, reductions
 constexpr int kMaxRows = 1024; // context lengths cached in shared memory
 constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * kStage + kMisc + 4 * kMaxRows;
+// multi-row launches also cache each row block's (first row | rows << 16) and longest context
+constexpr size_t kSmemRows = kSmem + 8 * kMaxRows;
 }  // namespace pk
 
 // Walks units u = start, start + step, ... as (p, g, b) digits of u in radix (P, Hkv), with
@@ -875,7 +877,7 @@ struct UnitIter {
   }
 };
 
-template <typename T, int G>
+template <typename T, int G, int R>
 __global__ void __launch_bounds__(pk::kThreads, 1)
     attn_persistent_kernel(const __grid_constant__ CUtensorMap map_k,
                            const __grid_constant__ CUtensorMap map_v,
@@ -886,7 +888,14 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
                            const float *__restrict__ vs, const int32_t *__restrict__ block_table,
                            const int32_t *__restrict__ context_lens, int B, int Hq, int Hkv,
                            int bs_log2, int max_blocks, int P, float scale, DecodeWs ws,
-                           int early) {
+                           int early, const int8_t *__restrict__ q_i8,
+                           const int32_t *__restrict__ row_blocks, int NB) {
+  // R > 1 (prefill): a unit is (row block, kv head, partition); the block's rows are
+  // consecutive rows of one sequence (one block-table row), and its R x G query heads are the
+  // columns of the unit's S and O tiles (NC <= 16, the tiles' width), each column with its
+  // own row's context. R = 1 (decode): a unit is (row, kv head, partition), NB = B.
+  constexpr int NC = G * R;
+  static_assert(NC <= 16, "a unit's query heads fill at most the 16 tile columns");
   griddep_launch();  // the next kernel may start its prologue
   using namespace tc;
   using namespace pk;
@@ -903,9 +912,24 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
   uint64_t *drain = full + 17;                          // [2] MMA drains on exit (q.k, p.v)
   uint32_t *tmem_base = reinterpret_cast<uint32_t *>(misc + 256);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(misc + 260);
-  float *stats = reinterpret_cast<float *>(misc + 512);  // [2][3][8]: m, l, wmax/32767
-  float *red = reinterpret_cast<float *>(misc + 768);    // [2 groups][2][4 warps][8 heads]
+  float *stats = reinterpret_cast<float *>(misc + 512);  // [2][3][16]: m, l, wmax/32767
+  float *red = reinterpret_cast<float *>(misc + 1024);   // [2 groups][2][4 warps][16 columns]
   int *ctx = reinterpret_cast<int *>(misc + kMisc);      // [B] context lengths
+  int *rbi = ctx + kMaxRows;  // [NB] row block: first row | rows << 16 (R > 1)
+  int *bmx = rbi + kMaxRows;  // [NB] row block's longest context (R > 1)
+  // a unit's context (its longest row's), first row and row count
+  auto unit_n = [&](int b) -> int {
+    if constexpr (R == 1) return ctx[b];
+    else return bmx[b];
+  };
+  auto unit_r0 = [&](int b) -> int {
+    if constexpr (R == 1) return b;
+    else return rbi[b] & 0xffff;
+  };
+  auto unit_nr = [&](int b) -> int {
+    if constexpr (R == 1) return 1;
+    else return rbi[b] >> 16;
+  };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 1) {
@@ -936,11 +960,11 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
   // ---------------------------------------------------------- producer helpers ----
   // This lane's KV block id for unit `it` of a row with context n (-1 past the end).
   auto block_id = [&](const UnitIter &it, int n) {
-    if (it.b >= B) return -1;
+    if (it.b >= NB) return -1;
     const int nblk = (min(kPart, n - it.p * kPart) + bs - 1) >> bs_log2;
     if (lane >= nblk) return -1;
-    return block_table[static_cast<size_t>(it.b) * max_blocks + ((it.p * kPart) >> bs_log2) +
-                       lane];
+    return block_table[static_cast<size_t>(unit_r0(it.b)) * max_blocks +
+                       ((it.p * kPart) >> bs_log2) + lane];
   };
   // Issues unit (p, g, b)'s K (warp 0, with the tx count of K and the query tile) or V and
   // the K/V scales (warp 14) into stage s; not the query tile, its scales or the V warp's
@@ -963,7 +987,8 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     uint8_t *st = sm + s * kStage;
     if (lane == 0) {
       if (!vwarp) st[kOffMode] = desc ? 1 : 0;  // before the arrive that publishes the stage
-      mbar_expect_tx(&full[s], static_cast<uint32_t>(nblk * bs * kHd + (vwarp ? 0 : G * kHd)));
+      mbar_expect_tx(&full[s],
+                     static_cast<uint32_t>(nblk * bs * kHd + (vwarp || R > 1 ? 0 : G * kHd)));
     }
     __syncwarp();
     if (asc || desc) {
@@ -1013,7 +1038,27 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&full[s]))
                  : "memory");
   };
-  if (early) {
+  // R > 1: the V warp copies the unit's query rows (column c = r * G + h at row c of the
+  // 128B-swizzled tile, as a tensor copy would place it) and their scales with cp.async,
+  // covered by its lanes' cp.async arrivals; the K warp has nothing to add.
+  auto issue_q_rows = [&](int b, int g, int s) {
+    if (warp == 0) return;
+    uint8_t *st = sm + s * kStage;
+    const int r0 = unit_r0(b), nr = unit_nr(b);
+    for (int i = lane; i < NC * 8; i += 32) {
+      const int c = i >> 3, ch = i & 7, r = c / G, h = c - (c / G) * G;
+      if (r < nr)
+        cp_async16(st + kOffQ + c * kHd + ((ch ^ (c & 7)) << 4),
+                   q_i8 + (static_cast<size_t>(r0 + r) * Hq + g * G + h) * kHd + ch * 16);
+    }
+    if (lane < NC && lane / G < nr)
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(st + kOffQs + 4 * lane)),
+                   "l"(q_s + static_cast<size_t>(r0 + lane / G) * Hq + g * G + lane % G)
+                   : "memory");
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&full[s]))
+                 : "memory");
+  };
+  if (R == 1 && early) {
     for (int i = threadIdx.x; i < B; i += kThreads) ctx[i] = __ldg(context_lens + i);
     __syncthreads();  // the context lengths are in and the stage barriers initialised
     if (warp == 0 || warp == 14) {
@@ -1033,13 +1078,23 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     }
   }
   griddep_wait();  // launched with programmatic serialization: the prologue above overlaps
-  if (early && (warp == 0 || warp == 14)) {
+  if (R == 1 && early && (warp == 0 || warp == 14)) {
 #pragma unroll
     for (int j = 0; j < kStages; ++j)
       if (j < npre) issue_q(pre_bg[j], j);
   }
-  if (!early)
+  if (R > 1 || !early)
     for (int i = threadIdx.x; i < B; i += kThreads) ctx[i] = context_lens[i];
+  if constexpr (R > 1) {
+    for (int i = threadIdx.x; i < NB; i += kThreads)
+      rbi[i] = row_blocks[2 * i] | (min(row_blocks[2 * i + 1], R) << 16);
+    __syncthreads();
+    for (int i = threadIdx.x; i < NB; i += kThreads) {
+      int m = 0;
+      for (int r = 0; r < (rbi[i] >> 16); ++r) m = max(m, ctx[(rbi[i] & 0xffff) + r]);
+      bmx[i] = m;
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -1049,9 +1104,9 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     // ----------------------------------------------------------------- producers ----
     const bool vwarp = warp == 14;
     auto next_valid = [&](UnitIter &it) {
-      while (it.b < B && it.p * kPart >= ctx[it.b]) it.next();
+      while (it.b < NB && it.p * kPart >= unit_n(it.b)) it.next();
     };
-    auto bid = [&](const UnitIter &it) { return block_id(it, it.b < B ? ctx[it.b] : 0); };
+    auto bid = [&](const UnitIter &it) { return block_id(it, it.b < NB ? unit_n(it.b) : 0); };
     // block-table rows three units ahead: under full HBM load a table miss takes a few us
     int k = 0;
     UnitIter i0(blockIdx.x, gridDim.x, P, Hkv);
@@ -1063,7 +1118,7 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     i2.next();
     next_valid(i2);
     int blk0 = bid(i0), blk1 = bid(i1), blk2 = bid(i2);
-    while (i0.b < B) {
+    while (i0.b < NB) {
       const int blk = blk0;
       UnitIter i3 = i2;
       i3.next();
@@ -1078,8 +1133,9 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
         ok = mbar_wait(&empty[s], ((k / kStages) - 1) & 1, abort_flag, ws.status);
       if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
       if (k >= npre) {  // (early stages were issued whole before the CTA barrier)
-        issue_kv(p, g, b, ctx[b], blk, s);
-        issue_q(b * Hq + g * G, s);
+        issue_kv(p, g, b, unit_n(b), blk, s);
+        if constexpr (R == 1) issue_q(b * Hq + g * G, s);
+        else issue_q_rows(b, g, s);
       }
       (void)vwarp;
       i0 = i1;
@@ -1095,8 +1151,8 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t id_s = i8_idesc(128, 16);
       int k = 0;
-      for (UnitIter it(blockIdx.x, gridDim.x, P, Hkv); it.b < B; it.next()) {
-        if (it.p * kPart >= ctx[it.b]) continue;
+      for (UnitIter it(blockIdx.x, gridDim.x, P, Hkv); it.b < NB; it.next()) {
+        if (it.p * kPart >= unit_n(it.b)) continue;
         const int s = k % kStages, t = k & 1;
         const bool ok = mbar_wait(&full[s], (k / kStages) & 1, abort_flag, ws.status) &&
                         (k < 2 || mbar_wait(&sempty[t], ((k >> 1) - 1) & 1, abort_flag, ws.status));
@@ -1123,8 +1179,8 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t id_pv = i8_idesc(128, 48, true, true, /*a_mn_major=*/true, false);
       int k = 0;
-      for (UnitIter it(blockIdx.x, gridDim.x, P, Hkv); it.b < B; it.next()) {
-        if (it.p * kPart >= ctx[it.b]) continue;
+      for (UnitIter it(blockIdx.x, gridDim.x, P, Hkv); it.b < NB; it.next()) {
+        if (it.p * kPart >= unit_n(it.b)) continue;
         const int s = k % kStages, t = k & 1;
         const bool ok = mbar_wait(&wfull[s], (k / kStages) & 1, abort_flag, ws.status) &&
                         (k < 2 || mbar_wait(&oempty[t], ((k >> 1) - 1) & 1, abort_flag, ws.status));
@@ -1148,11 +1204,11 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     // ------------------------------------------------------------------- softmax ----
     const int grp = (warp - 2) >> 2, q4 = warp & 3, tid = (threadIdx.x - 64) & 127;
     const int t0 = 32 * q4 + lane, t1 = t0 + 128;
-    float *red_s = red + grp * 64, *red_w = red_s + 32;
+    float *red_s = red + grp * 128, *red_w = red_s + 64;
     int k = 0;
-    for (UnitIter it(blockIdx.x, gridDim.x, P, Hkv); it.b < B; it.next()) {
+    for (UnitIter it(blockIdx.x, gridDim.x, P, Hkv); it.b < NB; it.next()) {
       const int p = it.p, g = it.g, b = it.b;
-      const int n = ctx[b], lo = p * kPart;
+      const int n = unit_n(b), lo = p * kPart;
       if (lo >= n) continue;
       if ((k & 1) != grp) {
         ++k;
@@ -1163,7 +1219,13 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
                 mbar_wait(&sfull[t], (k >> 1) & 1, abort_flag, ws.status) &&
                 (k < 2 || mbar_wait(&oempty[t], ((k >> 1) - 1) & 1, abort_flag, ws.status));
       if (group_any(1 + grp, 128, !ok || *abort_flag)) break;
-      const int cnt = min(kPart, n - lo);
+      // tokens of the partition inside each row's context (a row past the partition: 0)
+      int cntr[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        if constexpr (R == 1) cntr[r] = min(kPart, n - lo);
+        else cntr[r] = r < unit_nr(b) ? min(kPart, ctx[unit_r0(b) + r] - lo) : 0;
+      }
       tc_fence_after();
       uint32_t a0[16], a1[16];
       tmem_ld16(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + 32 * t, a0);
@@ -1182,82 +1244,89 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
       const int nbu = kPart >> bs_log2;
       const int et0 = rev ? (((nbu - 1 - (t0 >> bs_log2)) << bs_log2) | (t0 & (bs - 1))) : t0;
       const int et1 = rev ? (((nbu - 1 - (t1 >> bs_log2)) << bs_log2) | (t1 & (bs - 1))) : t1;
-      float s0[G], s1[G];
+      // column c (query head c % G of row c / G) masks by its row's context
+      bool in0[NC], in1[NC];
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float qsc = __fmul_rn(qsv[h], scale);
-        s0[h] = t0 < cnt ? __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(a0[h])), qsc), ks0)
-                         : -__int_as_float(0x7f800000);
-        s1[h] = t1 < cnt ? __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(a1[h])), qsc), ks1)
-                         : -__int_as_float(0x7f800000);
+      for (int c = 0; c < NC; ++c) {
+        in0[c] = et0 < cntr[c / G];
+        in1[c] = et1 < cntr[c / G];
+      }
+      float s0[NC], s1[NC];
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        const float qsc = __fmul_rn(qsv[c], scale);
+        s0[c] = in0[c] ? __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(a0[c])), qsc), ks0)
+                       : -__int_as_float(0x7f800000);
+        s1[c] = in1[c] ? __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(a1[c])), qsc), ks1)
+                       : -__int_as_float(0x7f800000);
       }
       // The reductions below are latency chains on the stage's critical path: one redux per
-      // head, all heads issued back to back.
-      float red[G];
+      // column, all columns issued back to back.
+      float red[NC];
 #pragma unroll
-      for (int h = 0; h < G; ++h) red[h] = warp_max_redux(fmaxf(s0[h], s1[h]));
+      for (int c = 0; c < NC; ++c) red[c] = warp_max_redux(fmaxf(s0[c], s1[c]));
       if (lane == 0) {
 #pragma unroll
-        for (int h = 0; h < G; ++h) red_s[q4 * 8 + h] = red[h];
+        for (int c = 0; c < NC; ++c) red_s[q4 * 16 + c] = red[c];
       }
       group_sync(1 + grp, 128);
       // Loads, then arithmetic, then stores: a store into E may alias the reductions' shared
-      // memory as far as the compiler knows, so interleaving them would chain the heads' exp
+      // memory as far as the compiler knows, so interleaving them would chain the columns' exp
       // latencies one after another.
       float *E = reinterpret_cast<float *>(st + kOffE);
-      float w0[G], w1[G], mh[G];
+      float w0[NC], w1[NC], mh[NC];
 #pragma unroll
-      for (int h = 0; h < G; ++h)
-        mh[h] = fmaxf(fmaxf(red_s[h], red_s[8 + h]), fmaxf(red_s[16 + h], red_s[24 + h]));
-      // All 2G exponentials unconditionally (a conditional call puts each ~400-cycle chain
+      for (int c = 0; c < NC; ++c)
+        mh[c] = fmaxf(fmaxf(red_s[c], red_s[16 + c]), fmaxf(red_s[32 + c], red_s[48 + c]));
+      // All 2 NC exponentials unconditionally (a conditional call puts each ~400-cycle chain
       // behind its own branch; unconditional, they overlap). A masked token's score is -inf,
-      // so its exp is 0 either way; the select below keeps the CUDA-core kernel's form.
+      // so its exp is 0 or NaN (a column with no token); the selects below drop it.
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        w0[h] = exp_s8b(__fsub_rn(s0[h], mh[h]));  // e, until stored
-        w1[h] = exp_s8b(__fsub_rn(s1[h], mh[h]));
+      for (int c = 0; c < NC; ++c) {
+        w0[c] = exp_s8b(__fsub_rn(s0[c], mh[c]));  // e, until stored
+        w1[c] = exp_s8b(__fsub_rn(s1[c], mh[c]));
       }
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        w0[h] = t0 < cnt ? w0[h] : 0.0f;
-        w1[h] = t1 < cnt ? w1[h] : 0.0f;
-        E[h * kPart + et0] = w0[h];
-        E[h * kPart + et1] = w1[h];
-        w0[h] = t0 < cnt ? __fmul_rn(w0[h], vs0) : 0.0f;
-        w1[h] = t1 < cnt ? __fmul_rn(w1[h], vs1) : 0.0f;
+      for (int c = 0; c < NC; ++c) {
+        w0[c] = in0[c] ? w0[c] : 0.0f;
+        w1[c] = in1[c] ? w1[c] : 0.0f;
+        E[c * kPart + et0] = w0[c];
+        E[c * kPart + et1] = w1[c];
+        w0[c] = in0[c] ? __fmul_rn(w0[c], vs0) : 0.0f;
+        w1[c] = in1[c] ? __fmul_rn(w1[c], vs1) : 0.0f;
       }
 #pragma unroll
-      for (int h = 0; h < G; ++h) red[h] = warp_max_redux(fmaxf(w0[h], w1[h]));
+      for (int c = 0; c < NC; ++c) red[c] = warp_max_redux(fmaxf(w0[c], w1[c]));
       if (lane == 0) {
 #pragma unroll
-        for (int h = 0; h < G; ++h) red_w[q4 * 8 + h] = red[h];
+        for (int c = 0; c < NC; ++c) red_w[q4 * 16 + c] = red[c];
       }
       group_sync(1 + grp, 128);
-      float wm[G];  // per-head weight maxima; their /32767 scales wait until after wfull
-      int qa[G], qb[G];
+      float wm[NC];  // per-column weight maxima; their /32767 scales wait until after wfull
+      int qa[NC], qb[NC];
 #pragma unroll
-      for (int h = 0; h < G; ++h)
-        wm[h] = fmaxf(fmaxf(red_w[h], red_w[8 + h]), fmaxf(red_w[16 + h], red_w[24 + h]));
-      // 32767 / wm: one correctly rounded division per lane (lane h takes head h), shuffled to
-      // the warp, instead of G divisions in a row in every thread.
+      for (int c = 0; c < NC; ++c)
+        wm[c] = fmaxf(fmaxf(red_w[c], red_w[16 + c]), fmaxf(red_w[32 + c], red_w[48 + c]));
+      // 32767 / wm: one correctly rounded division per lane (lane c takes column c), shuffled
+      // to the warp, instead of NC divisions in a row in every thread.
       float wl = 1.0f;
 #pragma unroll
-      for (int h = 0; h < G; ++h) wl = lane == h ? wm[h] : wl;
+      for (int c = 0; c < NC; ++c) wl = lane == c ? wm[c] : wl;
       const float winv_l = __fdiv_rn(32767.0f, wl);
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float winv = __shfl_sync(0xffffffffu, winv_l, h);
-        const int q0 = __float2int_rn(__fmul_rn(w0[h], winv));
-        const int q1 = __float2int_rn(__fmul_rn(w1[h], winv));
-        qa[h] = t0 < cnt ? (q0 < 0 ? 0 : (q0 > 32767 ? 32767 : q0)) : 0;
-        qb[h] = t1 < cnt ? (q1 < 0 ? 0 : (q1 > 32767 ? 32767 : q1)) : 0;
+      for (int c = 0; c < NC; ++c) {
+        const float winv = __shfl_sync(0xffffffffu, winv_l, c);
+        const int q0 = __float2int_rn(__fmul_rn(w0[c], winv));
+        const int q1 = __float2int_rn(__fmul_rn(w1[c], winv));
+        qa[c] = in0[c] ? (q0 < 0 ? 0 : (q0 > 32767 ? 32767 : q0)) : 0;
+        qb[c] = in1[c] ? (q1 < 0 ? 0 : (q1 > 32767 ? 32767 : q1)) : 0;
       }
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const int q0 = qa[h], q1 = qb[h];
-        // rows 16*plane + h of the K-major SW128 weight operand; t0 lies in token block 0 and
+      for (int c = 0; c < NC; ++c) {
+        const int q0 = qa[c], q1 = qb[c];
+        // rows 16*plane + c of the K-major SW128 weight operand; t0 lies in token block 0 and
         // t1 in block 1 at the same in-block position
-        const int off = h * 128 + ((((t0 >> 4) ^ (h & 7))) << 4) + (t0 & 15);
+        const int off = c * 128 + ((((t0 >> 4) ^ (c & 7))) << 4) + (t0 & 15);
         st[off] = static_cast<uint8_t>(q0 >> 14);
         st[2048 + off] = static_cast<uint8_t>((q0 >> 7) & 127);
         st[4096 + off] = static_cast<uint8_t>(q0 & 127);
@@ -1268,20 +1337,20 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
       fence_proxy_async_smem();
       group_sync(1 + grp, 128);
       if (tid == 0) mbar_arrive(&wfull[s]);
-      float *st_t = stats + t * 24;
+      float *st_t = stats + t * 48;
 #pragma unroll
-      for (int h = 0; h < G; ++h) {  // denominators, lane order of the CUDA-core kernel
-        if ((h & 3) != q4) continue;  // warp q4 takes heads q4, q4 + 4
-        const float *e = E + h * kPart;
+      for (int c = 0; c < NC; ++c) {  // denominators, lane order of the CUDA-core kernel
+        if ((c & 3) != q4) continue;  // warp q4 takes columns q4, q4 + 4, ...
+        const float *e = E + c * kPart;
         float l = e[lane];
 #pragma unroll
         for (int i = 1; i < kPart / 32; ++i) l = __fadd_rn(l, e[i * 32 + lane]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, o));
         if (lane == 0) {
-          st_t[h] = mh[h];
-          st_t[8 + h] = l;
-          st_t[16 + h] = __fdiv_rn(wm[h], 32767.0f);
+          st_t[c] = mh[c];
+          st_t[16 + c] = l;
+          st_t[32 + c] = __fdiv_rn(wm[c], 32767.0f);
         }
       }
       group_sync(1 + grp, 128);
@@ -1296,9 +1365,9 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     const int q4 = warp & 3, tid = threadIdx.x - 320;
     const int d = 32 * q4 + lane;
     int k = 0;
-    for (UnitIter it(blockIdx.x, gridDim.x, P, Hkv); it.b < B; it.next()) {
+    for (UnitIter it(blockIdx.x, gridDim.x, P, Hkv); it.b < NB; it.next()) {
       const int p = it.p, g = it.g, b = it.b;
-      const int n = ctx[b], lo = p * kPart;
+      const int n = unit_n(b), lo = p * kPart;
       if (lo >= n) continue;
       const int t = k & 1;
       const bool ok = mbar_wait(&ofull[t], (k >> 1) & 1, abort_flag, ws.status);
@@ -1310,29 +1379,35 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
       tmem_ld16(tmem + lanes + kColO + 48 * t + 16, db);
       tmem_ld16(tmem + lanes + kColO + 48 * t + 32, dc);
       tmem_wait_ld();
-      const float *st_t = stats + t * 24;
-      float wsc_h[G];
+      const float *st_t = stats + t * 48;
+      float wsc_c[NC];
 #pragma unroll
-      for (int h = 0; h < G; ++h) wsc_h[h] = st_t[16 + h];
+      for (int c = 0; c < NC; ++c) wsc_c[c] = st_t[32 + c];
       float ml0 = 0.0f, ml1 = 0.0f;
-      if (tid < G) {
+      if (tid < NC) {
         ml0 = st_t[tid];
-        ml1 = st_t[8 + tid];
+        ml1 = st_t[16 + tid];
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&oempty[t]);
+      const int r0 = unit_r0(b), nr = unit_nr(b);
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const int o = static_cast<int32_t>(da[h]) * 16384 + static_cast<int32_t>(db[h]) * 128 +
-                      static_cast<int32_t>(dc[h]);
-        const size_t hq = static_cast<size_t>(b) * Hq + g * G + h;
-        ws.part_o[(hq * P + p) * kHd + d] = __fmul_rn(static_cast<float>(o), wsc_h[h]);
+      for (int c = 0; c < NC; ++c) {
+        const int r = c / G;
+        if (R > 1 && (r >= nr || lo >= ctx[r0 + r])) continue;  // row past this partition
+        const int o = static_cast<int32_t>(da[c]) * 16384 + static_cast<int32_t>(db[c]) * 128 +
+                      static_cast<int32_t>(dc[c]);
+        const size_t hq = static_cast<size_t>(r0 + r) * Hq + g * G + (c - r * G);
+        ws.part_o[(hq * P + p) * kHd + d] = __fmul_rn(static_cast<float>(o), wsc_c[c]);
       }
-      if (tid < G) {
-        const size_t hq = static_cast<size_t>(b) * Hq + g * G + tid;
-        ws.part_ml[(hq * P + p) * 2 + 0] = ml0;
-        ws.part_ml[(hq * P + p) * 2 + 1] = ml1;
+      if (tid < NC) {
+        const int r = tid / G;
+        if (R == 1 || (r < nr && lo < ctx[r0 + r])) {
+          const size_t hq = static_cast<size_t>(r0 + r) * Hq + g * G + (tid - r * G);
+          ws.part_ml[(hq * P + p) * 2 + 0] = ml0;
+          ws.part_ml[(hq * P + p) * 2 + 1] = ml1;
+        }
       }
       ++k;
     }
@@ -1496,8 +1571,10 @@ int launch_persistent(const int8_t *q_i8, const float *q_s, const int8_t *kc, co
                       const int8_t *vc, const float *vs, const int32_t *block_table,
                       const int32_t *context_lens, void *out, int8_t *out_q, float *out_s, int B,
                       int Hq, int Hkv, int bs, int bs_log2, int max_blocks, int P, float scale,
-                      const DecodeWs &w, int early, cudaStream_t st) {
+                      const DecodeWs &w, int early, cudaStream_t st,
+                      const int32_t *row_blocks = nullptr, int NB = 0) {
   const int G = Hq / Hkv;
+  if (row_blocks == nullptr) NB = B;
   const size_t merge_smem = 4 * (2 * static_cast<size_t>(Hq) * P + Hq);
   if (bs < 8 || B > pk::kMaxRows || Hq * kHd > kMergeThreads * 8 || merge_smem > 96 * 1024 ||
       !aligned(out, 8) || !aligned(out_q, 4) ||
@@ -1525,17 +1602,24 @@ int launch_persistent(const int8_t *q_i8, const float *q_s, const int8_t *kc, co
     mk4 = mk;
     mv4 = mv;
   }
-  const long U = static_cast<long>(B) * Hkv * P;
+  const long U = static_cast<long>(NB) * Hkv * P;
   const int grid = static_cast<int>(U < tc::sm_count() ? U : tc::sm_count());
   switch (G) {
 #define S8B_PK_CASE(GG)                                                                        \
   case GG: {                                                                                   \
-    auto kern = attn_persistent_kernel<T, GG>;                                                  \
-    ensure_smem(reinterpret_cast<const void *>(kern), pk::kSmem);                               \
-    launch_pdl(kern, grid, pk::kThreads, pk::kSmem, st, mk, mv, mq, mk4, mv4, runs, q_s, ks, vs, \
-               block_table,                                                                    \
-                                                context_lens, B, Hq, Hkv, bs_log2, max_blocks,  \
-                                                P, scale, w, early);                            \
+    if (row_blocks == nullptr) {                                                               \
+      auto kern = attn_persistent_kernel<T, GG, 1>;                                             \
+      ensure_smem(reinterpret_cast<const void *>(kern), pk::kSmem);                             \
+      launch_pdl(kern, grid, pk::kThreads, pk::kSmem, st, mk, mv, mq, mk4, mv4, runs, q_s, ks,  \
+                 vs, block_table, context_lens, B, Hq, Hkv, bs_log2, max_blocks, P, scale, w,   \
+                 early, q_i8, row_blocks, NB);                                                  \
+    } else {                                                                                   \
+      auto kern = attn_persistent_kernel<T, GG, 16 / GG>;                                       \
+      ensure_smem(reinterpret_cast<const void *>(kern), pk::kSmemRows);                         \
+      launch_pdl(kern, grid, pk::kThreads, pk::kSmemRows, st, mk, mv, mq, mk4, mv4, runs, q_s,  \
+                 ks, vs, block_table, context_lens, B, Hq, Hkv, bs_log2, max_blocks, P, scale,  \
+                 w, 0, q_i8, row_blocks, NB);                                                   \
+    }                                                                                          \
     break;                                                                                     \
   }
     S8B_PK_CASE(1)
@@ -1563,7 +1647,8 @@ int launch_decode(const int8_t *q_i8, const float *q_s, const int8_t *kc, const 
                   const int8_t *vc, const float *vs, const int32_t *block_table,
                   const int32_t *context_lens, void *out, int8_t *out_q, float *out_s, int B,
                   int Hq, int Hkv, int bs, int max_blocks, int max_ctx, float scale,
-                  void *workspace, cudaStream_t st, int early = 0) {
+                  void *workspace, cudaStream_t st, int early = 0,
+                  const int32_t *row_blocks = nullptr, int NB = 0) {
   const int P = num_parts(max_ctx);
   const int G = Hq / Hkv;
   int bs_log2 = 0;
@@ -1572,7 +1657,7 @@ int launch_decode(const int8_t *q_i8, const float *q_s, const int8_t *kc, const 
   if (g_attn_impl == 0) {
     const int rc = launch_persistent<T>(q_i8, q_s, kc, ks, vc, vs, block_table, context_lens, out,
                                         out_q, out_s, B, Hq, Hkv, bs, bs_log2, max_blocks, P,
-                                        scale, w, early, st);
+                                        scale, w, early, st, row_blocks, NB);
     if (rc != 1) return rc;
   }
   // The partition kernels count completions; their counters start from zero on every launch.
@@ -1789,6 +1874,40 @@ extern "C" int s8b_paged_decode_q8_step(const int8_t *q_i8, const float *q_s, co
   return paged_decode_q8(q_i8, q_s, kc, ks, vc, vs, block_table, context_lens, out, out_q, out_s,
                          B, Hq, Hkv, D, block_size, max_blocks, max_ctx, scale, workspace,
                          workspace_bytes, dtype, stream, 1);
+}
+
+extern "C" int s8b_paged_prefill_block_rows(int Hq, int Hkv) {
+  if (Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || Hq / Hkv > 8) return S8B_ERR_SHAPE;
+  return 16 / (Hq / Hkv);
+}
+
+extern "C" int s8b_paged_prefill_q8(const int8_t *q_i8, const float *q_s, const int8_t *kc,
+                                    const float *ks, const int8_t *vc, const float *vs,
+                                    const int32_t *block_table, const int32_t *context_lens,
+                                    const int32_t *row_blocks, int n_row_blocks, void *out,
+                                    int8_t *out_q, float *out_s, int B, int Hq, int Hkv, int D,
+                                    int block_size, int max_blocks, int max_ctx, float scale,
+                                    void *workspace, size_t workspace_bytes, int dtype,
+                                    void *stream) {
+  if (!q_i8 || !q_s || !kc || !ks || !vc || !vs || !block_table || !context_lens || !out ||
+      (n_row_blocks > 0 && !row_blocks) || ((out_q == nullptr) != (out_s == nullptr)))
+    return S8B_ERR_ARG;
+  const int e = check_attn_shape(B, Hq, Hkv, D, block_size, max_blocks, max_ctx);
+  if (e) return e;
+  if (n_row_blocks < 0 || n_row_blocks > B) return S8B_ERR_SHAPE;
+  if (!aligned(q_i8, 16) || !aligned(kc, 16) || !aligned(vc, 16)) return S8B_ERR_ALIGN;
+  if (!workspace || workspace_bytes < part_bytes(B, Hq, max_ctx)) return S8B_ERR_WORKSPACE;
+  if (B == 0) return S8B_OK;
+  // without row blocks (or where the persistent kernel does not apply) every row is its own
+  // unit, as in s8b_paged_decode_q8
+  S8B_DISPATCH_DTYPE(dtype, T,
+                     return launch_decode<T>(q_i8, q_s, kc, ks, vc, vs, block_table,
+                                             context_lens, out, out_q, out_s, B, Hq, Hkv,
+                                             block_size, max_blocks, max_ctx, scale,
+                                             static_cast<float *>(workspace),
+                                             (cudaStream_t)stream, 0,
+                                             n_row_blocks > 0 ? row_blocks : nullptr,
+                                             n_row_blocks));
 }
 
 // ---------------------------------------------------------- no-allocation variant ----

@@ -20,6 +20,7 @@ import math
 
 import torch
 
+from . import ops
 from ._lib import call, ptr, stream
 from .runtime import KVPool, MicroBatch, StageModel, StageRunner
 
@@ -403,9 +404,25 @@ class DecodePipeline:
         seq = torch.tensor([i for i, p in enumerate(prompts) for _ in p], dtype=torch.long)
         pos = torch.cat([torch.arange(len(p), dtype=torch.int32) for p in prompts])
         ids = torch.tensor([t for p in prompts for t in p], dtype=torch.int32)
-        host = [x.pin_memory() for x in (ids, pos, pos + 1, bt[seq])]
         T = len(seq)
-        state = []  # per stage: (ids, positions, context_lens, block_table), all T rows
+        # row blocks of each chunk (rows of one sequence, at most R per block), relative to
+        # the chunk's first row: the prefill attention stages each block's partitions once
+        R = ops.prefill_block_rows(self.cfg.num_attention_heads, self.cfg.num_key_value_heads)
+        seq_l = seq.tolist()
+        blocks, chunk_off = [], [0]
+        for c0 in range(0, T, self.prefill_chunk):
+            c1 = min(T, c0 + self.prefill_chunk)
+            r = c0
+            while r < c1:
+                e = r + 1
+                while e < c1 and e - r < R and seq_l[e] == seq_l[r]:
+                    e += 1
+                blocks.append((r - c0, e - r))
+                r = e
+            chunk_off.append(len(blocks))
+        rbs = torch.tensor(blocks, dtype=torch.int32).reshape(-1, 2)
+        host = [x.pin_memory() for x in (ids, pos, pos + 1, bt[seq], rbs)]
+        state = []  # per stage: (ids, positions, context_lens, block_table, row blocks)
         for s, mdl in enumerate(self.models):
             st = torch.cuda.current_stream(mdl.device) if self.single_device else self.streams[s]
             with torch.cuda.device(mdl.device), torch.cuda.stream(st):
@@ -431,10 +448,12 @@ class DecodePipeline:
                         st.wait_event(ev[s - 1])
                     if s < self.S - 1 and not self.single_device:
                         st.wait_event(ev[s + 1])  # stage s+1 has decoded the previous chunk
-                    a_ids, a_pos, a_ctx, a_bt = state[s]
+                    a_ids, a_pos, a_ctx, a_bt, a_rb = state[s]
+                    ci = c0 // self.prefill_chunk
                     mb = MicroBatch(ids=(out_ids if s == self.S - 1 else a_ids)[c0:c0 + r],
                                     positions=a_pos[c0:c0 + r], context_lens=a_ctx[c0:c0 + r],
-                                    block_table=a_bt[c0:c0 + r])
+                                    block_table=a_bt[c0:c0 + r],
+                                    extra={"row_blocks": a_rb[chunk_off[ci]:chunk_off[ci + 1]]})
                     runners[s].run(mb, r, boundary_in=bufs[s - 1] if s > 0 else None,
                                    boundary_out=bufs[s] if s < self.S - 1 else None,
                                    head=bool(chunk_ends))

@@ -235,6 +235,44 @@ def paged_decode_q8(q_i8, q_s, kc, ks, vc, vs, block_table, context_lens, max_ct
     return out
 
 
+def prefill_block_rows(Hq: int, Hkv: int) -> int:
+    """Most rows one row block of ``paged_prefill_q8`` may hold at this head shape."""
+    from ._lib import load
+
+    return int(load().s8b_paged_prefill_block_rows(Hq, Hkv))
+
+
+def prefill_row_blocks(seq_lens, block_rows: int) -> list[tuple[int, int]]:
+    """Row blocks for rows packed sequence after sequence (``seq_lens`` rows each): runs of
+    at most ``block_rows`` consecutive rows that never cross a sequence."""
+    blocks, r0 = [], 0
+    for n in seq_lens:
+        for i in range(0, n, block_rows):
+            blocks.append((r0 + i, min(block_rows, n - i)))
+        r0 += n
+    return blocks
+
+
+def paged_prefill_q8(q_i8, q_s, kc, ks, vc, vs, block_table, context_lens, row_blocks,
+                     max_ctx, scale, *, out=None, out_q=None, out_s=None, workspace=None,
+                     dtype=torch.bfloat16):
+    """``paged_decode_q8`` over prefill rows grouped into ``row_blocks`` (int32 [n, 2] device
+    tensor of (first row, row count), rows of one sequence each); identical results, each
+    block's K/V partitions read once for all its rows."""
+    B, Hq, D = q_i8.shape
+    Hkv, bs = kc.shape[-3], kc.shape[-2]
+    dev = q_i8.device
+    out = torch.empty((B, Hq * D), dtype=dtype, device=dev) if out is None else out
+    need = decode_workspace_bytes(B, Hq, D, max_ctx)
+    if workspace is None:
+        workspace = torch.zeros(need, dtype=torch.uint8, device=dev)
+    call("s8b_paged_prefill_q8", ptr(q_i8), ptr(q_s), ptr(kc), ptr(ks), ptr(vc), ptr(vs),
+         ptr(block_table), ptr(context_lens), ptr(row_blocks), row_blocks.shape[0], ptr(out),
+         ptr(out_q), ptr(out_s), B, Hq, Hkv, D, bs, block_table.shape[-1], int(max_ctx),
+         float(scale), ptr(workspace), workspace.numel(), dtype_code(out.dtype), stream(dev))
+    return out
+
+
 def paged_decode(q, kc, ks, vc, vs, block_table, context_lens, max_ctx, scale, *, out=None,
                  workspace=None):
     """Reference layout: q [B, Hq, D] (or [B, Hq, 1, D]) -> [B, Hq, D]."""

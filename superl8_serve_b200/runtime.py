@@ -596,12 +596,20 @@ class StageRunner:
         else:
             self._gemm(self.xq, self.xs, L.qkv_w, L.qkv_s, self.qkv, M)
             call("s8b_qkv_post", ptr(self.qkv), *post)
-        call("s8b_paged_decode_q8_step" if self.decode_step else "s8b_paged_decode_q8",
-             ptr(self.q_i8), ptr(self.q_s), ptr(kc), ptr(ks), ptr(vc),
-             ptr(vs), ptr(mb.block_table), ptr(mb.context_lens), ptr(self.attn), ptr(self.xq),
-             ptr(self.xs), M, self.Hq, self.Hkv, self.D, self.pool.block_size,
-             mb.block_table.shape[1], self.max_ctx, self.scale, ptr(self.ws), self.ws.numel(), 0,
-             st)
+        rb = mb.extra.get("row_blocks")
+        if rb is not None:  # prefill rows: each row block's partitions staged once
+            call("s8b_paged_prefill_q8", ptr(self.q_i8), ptr(self.q_s), ptr(kc), ptr(ks),
+                 ptr(vc), ptr(vs), ptr(mb.block_table), ptr(mb.context_lens), ptr(rb),
+                 rb.shape[0], ptr(self.attn), ptr(self.xq), ptr(self.xs), M, self.Hq, self.Hkv,
+                 self.D, self.pool.block_size, mb.block_table.shape[1], self.max_ctx,
+                 self.scale, ptr(self.ws), self.ws.numel(), 0, st)
+        else:
+            call("s8b_paged_decode_q8_step" if self.decode_step else "s8b_paged_decode_q8",
+                 ptr(self.q_i8), ptr(self.q_s), ptr(kc), ptr(ks), ptr(vc),
+                 ptr(vs), ptr(mb.block_table), ptr(mb.context_lens), ptr(self.attn),
+                 ptr(self.xq), ptr(self.xs), M, self.Hq, self.Hkv, self.D,
+                 self.pool.block_size, mb.block_table.shape[1], self.max_ctx, self.scale,
+                 ptr(self.ws), self.ws.numel(), 0, st)
         if L.moe is not None:
             if split:
                 C = self._gemm_split(L.o_w, M)
