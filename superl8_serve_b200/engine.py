@@ -68,6 +68,26 @@ class BlockAllocator:
         return bt
 
 
+def chunk_row_blocks(seq_of_row: list[int], chunk: int, block_rows: int):
+    """Row blocks of packed prefill rows: chunks of ``chunk`` rows are cut into runs of at most
+    ``block_rows`` consecutive rows of one sequence (``seq_of_row[i]``: row i's sequence).
+    Returns (blocks, chunk_off): blocks[chunk_off[c] : chunk_off[c + 1]] are chunk c's blocks
+    as (first row relative to the chunk, row count)."""
+    T = len(seq_of_row)
+    blocks, chunk_off = [], [0]
+    for c0 in range(0, T, chunk):
+        c1 = min(T, c0 + chunk)
+        r = c0
+        while r < c1:
+            e = r + 1
+            while e < c1 and e - r < block_rows and seq_of_row[e] == seq_of_row[r]:
+                e += 1
+            blocks.append((r - c0, e - r))
+            r = e
+        chunk_off.append(len(blocks))
+    return blocks, chunk_off
+
+
 class DecodePipeline:
     """Greedy W8A8 decode through ``len(models)`` stages.
 
@@ -408,18 +428,7 @@ class DecodePipeline:
         # row blocks of each chunk (rows of one sequence, at most R per block), relative to
         # the chunk's first row: the prefill attention stages each block's partitions once
         R = ops.prefill_block_rows(self.cfg.num_attention_heads, self.cfg.num_key_value_heads)
-        seq_l = seq.tolist()
-        blocks, chunk_off = [], [0]
-        for c0 in range(0, T, self.prefill_chunk):
-            c1 = min(T, c0 + self.prefill_chunk)
-            r = c0
-            while r < c1:
-                e = r + 1
-                while e < c1 and e - r < R and seq_l[e] == seq_l[r]:
-                    e += 1
-                blocks.append((r - c0, e - r))
-                r = e
-            chunk_off.append(len(blocks))
+        blocks, chunk_off = chunk_row_blocks(seq.tolist(), self.prefill_chunk, R)
         rbs = torch.tensor(blocks, dtype=torch.int32).reshape(-1, 2)
         host = [x.pin_memory() for x in (ids, pos, pos + 1, bt[seq], rbs)]
         state = []  # per stage: (ids, positions, context_lens, block_table, row blocks)

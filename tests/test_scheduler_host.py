@@ -283,3 +283,28 @@ def test_pipeline_engine_step_api_on_a_fake_pipeline():
     assert eng.sequence(a).status.name == "FINISHED"
     eng.forget(a)
     assert a not in eng._cont_ids
+
+
+def test_prefill_chunk_row_blocks_cover_rows_within_sequences_and_chunks():
+    """Prefill row blocks: every packed row in exactly one block, no block crossing a
+    sequence or a chunk, at most block_rows rows each, in row order."""
+    import random
+
+    from superl8_serve_b200.engine import chunk_row_blocks
+
+    rnd = random.Random(5)
+    for _ in range(50):
+        lens = [rnd.randint(1, 700) for _ in range(rnd.randint(1, 6))]
+        seq = [i for i, n in enumerate(lens) for _ in range(n)]
+        chunk, R = rnd.choice([1, 7, 64, 256]), rnd.choice([1, 2, 3, 4, 8, 16])
+        blocks, off = chunk_row_blocks(seq, chunk, R)
+        assert len(off) == (len(seq) + chunk - 1) // chunk + 1 and off[-1] == len(blocks)
+        covered = []
+        for c in range(len(off) - 1):
+            c0 = c * chunk
+            for first, count in blocks[off[c]:off[c + 1]]:
+                assert 1 <= count <= R and first + count <= chunk
+                rows = list(range(c0 + first, c0 + first + count))
+                assert len({seq[r] for r in rows}) == 1
+                covered += rows
+        assert covered == list(range(len(seq)))
