@@ -654,7 +654,8 @@ def time_graph(fn, reps: int, device) -> float:
 
 def run_codec(args):
     """the inter-stage codec. x bf16 [T, 4096], N(0,1) with 0.1% of the
-    channels (4) scaled x20; block-128 Hadamard, per-token absmax, int8 and int4. The
+    channels (4) scaled x20; block-128 Hadamard, per-token absmax, int8 and int4 (and the
+    reference's nf4 scheme beside them). The
     encoder on GPU 0 stores its codes straight into GPU 1's buffer over NVLink (local when
     only one GPU is visible); GPU 1 decodes. Device time (CUDA events around a CUDA graph of
     repeated launches) of encode (codes crossing NVLink inside it) and of decode, per T; bytes
@@ -671,7 +672,7 @@ def run_codec(args):
     rng = np.random.default_rng(0)
     cols = rng.choice(D, 4, replace=False)
     rows = []
-    for scheme in ("int8-had", "int4-had"):
+    for scheme in ("int8-had", "int4-had", "nf4"):  # config 2's two codecs, and nf4
         for T in (1, 16, 64, 256, 1024):
             xh = rng.standard_normal((T, D)).astype(np.float32)
             xh[:, cols] *= 20
