@@ -877,7 +877,9 @@ struct UnitIter {
   }
 };
 
-template <typename T, int G, int R>
+// EARLY: the kernel carries the early loads (run when `early` is set); without them it streams
+// its steady state faster, which long unit lists need more than an early start.
+template <typename T, int G, int R, bool EARLY>
 __global__ void __launch_bounds__(pk::kThreads, 1)
     attn_persistent_kernel(const __grid_constant__ CUtensorMap map_k,
                            const __grid_constant__ CUtensorMap map_v,
@@ -896,6 +898,7 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
   // own row's context. R = 1 (decode): a unit is (row, kv head, partition), NB = B.
   constexpr int NC = G * R;
   static_assert(NC <= 16, "a unit's query heads fill at most the 16 tile columns");
+  static_assert(R == 1 || !EARLY, "early loads are for decode units");
   griddep_launch();  // the next kernel may start its prologue
   using namespace tc;
   using namespace pk;
@@ -1058,7 +1061,7 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&full[s]))
                  : "memory");
   };
-  if (R == 1 && early) {
+  if (EARLY && R == 1 && early) {
     for (int i = threadIdx.x; i < B; i += kThreads) ctx[i] = __ldg(context_lens + i);
     __syncthreads();  // the context lengths are in and the stage barriers initialised
     if (warp == 0 || warp == 14) {
@@ -1078,12 +1081,12 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
     }
   }
   griddep_wait();  // launched with programmatic serialization: the prologue above overlaps
-  if (R == 1 && early && (warp == 0 || warp == 14)) {
+  if (EARLY && R == 1 && early && (warp == 0 || warp == 14)) {
 #pragma unroll
     for (int j = 0; j < kStages; ++j)
       if (j < npre) issue_q(pre_bg[j], j);
   }
-  if (R > 1 || !early)
+  if (!EARLY || R > 1 || !early)
     for (int i = threadIdx.x; i < B; i += kThreads) ctx[i] = context_lens[i];
   if constexpr (R > 1) {
     for (int i = threadIdx.x; i < NB; i += kThreads)
@@ -1604,21 +1607,26 @@ int launch_persistent(const int8_t *q_i8, const float *q_s, const int8_t *kc, co
   }
   const long U = static_cast<long>(NB) * Hkv * P;
   const int grid = static_cast<int>(U < tc::sm_count() ? U : tc::sm_count());
+  // The early loads shorten a decode step's start, but the kernel that carries them streams
+  // its steady state a little slower (measured 6% at 112 units per CTA, 27B at 16K context):
+  // they pay off only while a CTA has few units to stream.
+  const bool early_ok = early && U <= 48L * grid;
   switch (G) {
 #define S8B_PK_CASE(GG)                                                                        \
   case GG: {                                                                                   \
-    if (row_blocks == nullptr) {                                                               \
-      auto kern = attn_persistent_kernel<T, GG, 1>;                                             \
-      ensure_smem(reinterpret_cast<const void *>(kern), pk::kSmem);                             \
-      launch_pdl(kern, grid, pk::kThreads, pk::kSmem, st, mk, mv, mq, mk4, mv4, runs, q_s, ks,  \
-                 vs, block_table, context_lens, B, Hq, Hkv, bs_log2, max_blocks, P, scale, w,   \
-                 early, q_i8, row_blocks, NB);                                                  \
-    } else {                                                                                   \
-      auto kern = attn_persistent_kernel<T, GG, 16 / GG>;                                       \
+    if (row_blocks != nullptr) {                                                               \
+      auto kern = attn_persistent_kernel<T, GG, 16 / GG, false>;                                \
       ensure_smem(reinterpret_cast<const void *>(kern), pk::kSmemRows);                         \
       launch_pdl(kern, grid, pk::kThreads, pk::kSmemRows, st, mk, mv, mq, mk4, mv4, runs, q_s,  \
                  ks, vs, block_table, context_lens, B, Hq, Hkv, bs_log2, max_blocks, P, scale,  \
                  w, 0, q_i8, row_blocks, NB);                                                   \
+    } else {                                                                                   \
+      auto kern = early_ok ? attn_persistent_kernel<T, GG, 1, true>                             \
+                           : attn_persistent_kernel<T, GG, 1, false>;                           \
+      ensure_smem(reinterpret_cast<const void *>(kern), pk::kSmem);                             \
+      launch_pdl(kern, grid, pk::kThreads, pk::kSmem, st, mk, mv, mq, mk4, mv4, runs, q_s, ks,  \
+                 vs, block_table, context_lens, B, Hq, Hkv, bs_log2, max_blocks, P, scale, w,   \
+                 early_ok ? 1 : 0, q_i8, row_blocks, NB);                                       \
     }                                                                                          \
     break;                                                                                     \
   }

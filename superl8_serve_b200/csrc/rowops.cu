@@ -213,15 +213,29 @@ __global__ void __launch_bounds__(1024)
   if (threadIdx.x == 0) s[m] = p.scale;
 }
 
-// threads = min(kRowThreads, nvec rounded up to a warp), VPT = ceil(nvec / threads) <= 8.
-// 256-thread CTAs (about 12K registers) fit four to an SM, so a launch of 256 CTAs (64 rows x
-// a 4-CTA cluster) runs in one wave beside a resident GEMM CTA; 768-thread CTAs fit one to an
-// SM by registers and took two waves. Longer rows take more threads (up to 1024) so that VPT
-// stays <= 8.
+int row_sm_count() {
+  static int n[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (n[dev] == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    n[dev] = v > 0 ? v : 148;
+  }
+  return n[dev];
+}
+
+// threads = nvec rounded up to a warp (at most 1024), VPT = ceil(nvec / threads) <= 8, so
+// each thread carries as short a chain as the row allows. When the launch has more CTAs than
+// the GPU has SMs (`ctas`), threads are capped at kRowThreads: 256-thread CTAs (about 12K
+// registers) fit four to an SM, so a launch of 256 CTAs (64 rows x a 4-CTA cluster) runs in
+// one wave beside a resident GEMM CTA, where 768-thread CTAs fit one to an SM by registers
+// and took two waves. Longer rows take more threads (up to 1024) so that VPT stays <= 8.
 constexpr int kRowThreads = 256;
-inline void row_shape(int nvec, int *threads, int *vpt) {
+inline void row_shape(int nvec, int *threads, int *vpt, long ctas = 0) {
   int t = ((nvec + 31) / 32) * 32;
-  if (t > kRowThreads) t = kRowThreads;
+  if (t > kRowThreads && ctas > row_sm_count()) t = kRowThreads;
   if ((nvec + t - 1) / t > 8) t = (((nvec + 7) / 8 + 31) / 32) * 32;
   if (t > 1024) t = 1024;
   *threads = t;
@@ -253,7 +267,7 @@ extern "C" int s8b_quant_rows(const void *x, int dtype, int8_t *q, float *s, int
   if (!aligned(x, 8) || !aligned(q, 4)) return S8B_ERR_ALIGN;
   if (M == 0) return S8B_OK;
   int th, vpt;
-  row_shape(K / 4, &th, &vpt);
+  row_shape(K / 4, &th, &vpt, M);
   S8B_DISPATCH_DTYPE(dtype, T,
                      S8B_VPT_SWITCH(vpt, V,
                                     launch_pdl(quant_rows_v<T, V>, M, th, 0, (cudaStream_t)stream,
@@ -278,7 +292,7 @@ int launch_rms(Src src, const void *res_in, void *res_out, const void *w, float 
     if ((H / 4 / cl) % 32 != 0) cl = 1;
   }
   int th, vpt;
-  row_shape(H / 4 / cl, &th, &vpt);
+  row_shape(H / 4 / cl, &th, &vpt, static_cast<long>(M) * cl);
   const cudaStream_t st = (cudaStream_t)stream;
   if (cl == 1) {
     S8B_VPT_SWITCH(vpt, V,
@@ -299,7 +313,7 @@ template <typename T>
 int launch_silu(RowSrc<T> src, int F, void *y_out, int8_t *q, float *s, int M, void *stream) {
   const int cl = row_cluster(F / 4);
   int th, vpt;
-  row_shape(F / 4 / cl, &th, &vpt);
+  row_shape(F / 4 / cl, &th, &vpt, static_cast<long>(M) * cl);
   const cudaStream_t st = (cudaStream_t)stream;
   if (cl == 1) {
     S8B_VPT_SWITCH(vpt, V,
