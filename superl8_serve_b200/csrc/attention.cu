@@ -1423,6 +1423,430 @@ __global__ void __launch_bounds__(pk::kThreads, 1)
                  "r"(kTmemCols) : "memory");
 }
 
+// The persistent kernel's decode form without the early loads and without multi-row units:
+// the same roles, ring, tiles and arithmetic as attn_persistent_kernel<T, G, 1, false>, as a
+// function of its own. Compiled apart from the early and multi-row code it streams its
+// steady state faster for G <= 5 (measured 238.6 against 248.8 us per launch at 112 units
+// per CTA, 27B at 16K context; 61.0 against 64.8 us for Qwen3-8B at batch 64), so those decode
+// launches whose CTAs have many units take it. At G = 8 (Qwen3-30B-A3B) the template kernel
+// is the faster one (142.8 against 165.7 us at batch 128, 4K context) and stays.
+template <typename T, int G>
+__global__ void __launch_bounds__(pk::kThreads, 1)
+    attn_persistent_stream_kernel(const __grid_constant__ CUtensorMap map_k,
+                           const __grid_constant__ CUtensorMap map_v,
+                           const __grid_constant__ CUtensorMap map_q,
+                           const __grid_constant__ CUtensorMap map_k4,
+                           const __grid_constant__ CUtensorMap map_v4, int runs,
+                           const float *__restrict__ q_s, const float *__restrict__ ks,
+                           const float *__restrict__ vs, const int32_t *__restrict__ block_table,
+                           const int32_t *__restrict__ context_lens, int B, int Hq, int Hkv,
+                           int bs_log2, int max_blocks, int P, float scale, DecodeWs ws) {
+  griddep_launch();  // the next kernel may start its prologue
+  using namespace tc;
+  using namespace pk;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *misc = sm + kStages * kStage;
+  uint64_t *full = reinterpret_cast<uint64_t *>(misc);  // [3] stage loaded (tx bytes)
+  uint64_t *empty = full + 3;                           // [3] stage free (p.v done + softmax done)
+  uint64_t *wfull = full + 6;                           // [3] W planes of the stage written
+  uint64_t *sfull = full + 9;                           // [2] S buffer holds a unit's scores
+  uint64_t *sempty = full + 11;                         // [2] S buffer read (4 warp arrivals)
+  uint64_t *ofull = full + 13;                          // [2] O buffer + stats ready
+  uint64_t *oempty = full + 15;                         // [2] O buffer read (4 warp arrivals)
+  uint64_t *drain = full + 17;                          // [2] MMA drains on exit (q.k, p.v)
+  uint32_t *tmem_base = reinterpret_cast<uint32_t *>(misc + 256);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(misc + 260);
+  float *stats = reinterpret_cast<float *>(misc + 512);  // [2][3][8]: m, l, wmax/32767
+  float *red = reinterpret_cast<float *>(misc + 768);    // [2 groups][2][4 warps][8 heads]
+  int *ctx = reinterpret_cast<int *>(misc + kMisc);      // [B] context lengths
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_base)), "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&full[i], 2 + 32);  // two expect_tx arrivals + one cp.async arrival per V lane
+      mbar_init(&empty[i], 2);
+      mbar_init(&wfull[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sfull[i], 1);
+      mbar_init(&sempty[i], 4);
+      mbar_init(&ofull[i], 2);
+      mbar_init(&oempty[i], 4);
+    }
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  griddep_wait();  // launched with programmatic serialization: the prologue above overlaps
+  for (int i = threadIdx.x; i < B; i += kThreads) ctx[i] = context_lens[i];
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_base;
+  const int bs = 1 << bs_log2;
+
+  if (warp == 0 || warp == 14) {
+    // ----------------------------------------------------------------- producers ----
+    const bool vwarp = warp == 14;
+    auto next_valid = [&](UnitIter &it) {
+      while (it.b < B && it.p * kPart >= ctx[it.b]) it.next();
+    };
+    auto block_id = [&](const UnitIter &it) {  // this lane's KV block id (-1 past the end)
+      if (it.b >= B) return -1;
+      const int nblk = (min(kPart, ctx[it.b] - it.p * kPart) + bs - 1) >> bs_log2;
+      if (lane >= nblk) return -1;
+      return block_table[static_cast<size_t>(it.b) * max_blocks + ((it.p * kPart) >> bs_log2) +
+                         lane];
+    };
+    const int nbu = kPart >> bs_log2;  // blocks of a full partition
+    // block-table rows three units ahead: under full HBM load a table miss takes a few us
+    int k = 0;
+    UnitIter i0(blockIdx.x, gridDim.x, P, Hkv);
+    next_valid(i0);
+    UnitIter i1 = i0;
+    i1.next();
+    next_valid(i1);
+    UnitIter i2 = i1;
+    i2.next();
+    next_valid(i2);
+    int blk0 = block_id(i0), blk1 = block_id(i1), blk2 = block_id(i2);
+    while (i0.b < B) {
+      const int blk = blk0;
+      UnitIter i3 = i2;
+      i3.next();
+      next_valid(i3);
+      blk0 = blk1;
+      blk1 = blk2;
+      blk2 = block_id(i3);
+      const int p = i0.p, g = i0.g, b = i0.b;
+      const int cnt = min(kPart, ctx[b] - p * kPart);
+      const int nblk = (cnt + bs - 1) >> bs_log2;
+      const int row = (blk * Hkv + g) << bs_log2;  // this lane's block rows (lanes < nblk)
+      // A full partition on consecutive block ids (ascending, or descending as the reference's
+      // allocator hands them out) moves in one 4-D copy per tensor instead of nblk 2-D copies,
+      // each of which costs its warp ~50 ns to issue. Descending runs land in reverse block
+      // order; the softmax then stores its exponentials at the canonical token index.
+      const int b0 = __shfl_sync(0xffffffffu, blk, 0);
+      const bool asc = runs && nblk == nbu && __all_sync(0xffffffffu, lane >= nblk || blk == b0 + lane);
+      // (reversed only for a partition with every token present: the softmax masks the
+      // tokens past the context end by shared-memory row)
+      const bool desc = runs && cnt == kPart && !asc &&
+                        __all_sync(0xffffffffu, lane >= nblk || blk == b0 - lane);
+      const int s = k % kStages;
+      bool ok = true;
+      if (lane == 0 && k >= kStages)
+        ok = mbar_wait(&empty[s], ((k / kStages) - 1) & 1, abort_flag, ws.status);
+      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+      uint8_t *st = sm + s * kStage;
+      if (lane == 0) {
+        if (!vwarp) st[kOffMode] = desc ? 1 : 0;  // before the arrive that publishes the stage
+        mbar_expect_tx(&full[s], static_cast<uint32_t>(nblk * bs * kHd + (vwarp ? 0 : G * kHd)));
+      }
+      __syncwarp();
+      if (asc || desc) {
+        if (lane == 0)
+          tma_load_4d(st + (vwarp ? kOffV : 0), vwarp ? &map_v4 : &map_k4, 0, 0, g,
+                      desc ? b0 - (nbu - 1) : b0, &full[s]);
+      } else if (lane < nblk) {
+        tma_load_2d(st + (vwarp ? kOffV : 0) + lane * bs * kHd, vwarp ? &map_v : &map_k, 0, row,
+                    &full[s]);
+      }
+      if (!vwarp) {
+        if (lane == 0) tma_load_2d(st + kOffQ, &map_q, 0, b * Hq + g * G, &full[s]);
+        i0 = i1;
+        i1 = i2;
+        i2 = i3;
+        ++k;
+        continue;
+      }
+      // scales: 16-byte chunks c of 4 tokens; chunk c of array a goes to lane c % 32
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int c = lane + 32 * (i & 1);  // chunk within the array
+        const int j = (4 * c) >> bs_log2;   // smem block of that chunk
+        const int rj = __shfl_sync(0xffffffffu, row, (desc ? nbu - 1 - j : j) & 31);
+        if (4 * c < nblk * bs) {
+          const float *src = (i < 2 ? ks : vs) + rj + ((4 * c) & (bs - 1));
+          cp_async16(st + (i < 2 ? kOffKs : kOffVs) + 16 * c, src);
+        }
+      }
+      if (lane < G)  // the G query scales of this (row, kv head)
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(st + kOffQs + 4 * lane)),
+                     "l"(q_s + static_cast<size_t>(b) * Hq + g * G + lane)
+                     : "memory");
+      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&full[s]))
+                   : "memory");
+      i0 = i1;
+      i1 = i2;
+      i2 = i3;
+      ++k;
+    }
+    if (*abort_flag && lane == 0)  // let issued copies land before the CTA exits
+      for (int j = k > kStages ? k - kStages : 0; j < k; ++j)
+        mbar_drain(&full[j % kStages], (j / kStages) & 1);
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- q.k MMA issuer ----
+    if (lane == 0) {
+      constexpr uint32_t id_s = i8_idesc(128, 16);
+      int k = 0;
+      for (UnitIter it(blockIdx.x, gridDim.x, P, Hkv); it.b < B; it.next()) {
+        if (it.p * kPart >= ctx[it.b]) continue;
+        const int s = k % kStages, t = k & 1;
+        const bool ok = mbar_wait(&full[s], (k / kStages) & 1, abort_flag, ws.status) &&
+                        (k < 2 || mbar_wait(&sempty[t], ((k >> 1) - 1) & 1, abort_flag, ws.status));
+        if (!ok) break;
+        tc_fence_after();
+        uint8_t *st = sm + s * kStage;
+        const uint64_t qd = sw128_desc(smem_u32(st + kOffQ));
+#pragma unroll
+        for (int tile = 0; tile < 2; ++tile) {
+          const uint64_t kd = sw128_desc(smem_u32(st + tile * 128 * kHd));
+#pragma unroll
+          for (int i = 0; i < 4; ++i) mma_i8(tmem + 32 * t + 16 * tile, kd + 2 * i, qd + 2 * i, id_s, i > 0);
+        }
+        mma_commit(&sfull[t]);
+        ++k;
+      }
+      mma_commit(&drain[0]);  // all MMAs issued by this thread have completed once this arrives
+      mbar_drain(&drain[0], 0);
+    }
+  } else if (warp == 15) {
+    // ------------------------------------------------------------- p.v MMA issuer ----
+    // A thread of its own, so that q.k of later units never queues behind a p.v that waits
+    // for its softmax.
+    if (lane == 0) {
+      constexpr uint32_t id_pv = i8_idesc(128, 48, true, true, /*a_mn_major=*/true, false);
+      int k = 0;
+      for (UnitIter it(blockIdx.x, gridDim.x, P, Hkv); it.b < B; it.next()) {
+        if (it.p * kPart >= ctx[it.b]) continue;
+        const int s = k % kStages, t = k & 1;
+        const bool ok = mbar_wait(&wfull[s], (k / kStages) & 1, abort_flag, ws.status) &&
+                        (k < 2 || mbar_wait(&oempty[t], ((k >> 1) - 1) & 1, abort_flag, ws.status));
+        if (!ok) break;
+        tc_fence_after();
+        uint8_t *st = sm + s * kStage;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint64_t vd = sw128_desc(smem_u32(st + kOffV + i * 32 * kHd));
+          const uint64_t wd = sw128_desc(smem_u32(st + (i >> 2) * kWBlock)) + 2 * (i & 3);
+          mma_i8(tmem + kColO + 48 * t, vd, wd, id_pv, i > 0);
+        }
+        mma_commit(&ofull[t]);
+        mma_commit(&empty[s]);
+        ++k;
+      }
+      mma_commit(&drain[1]);
+      mbar_drain(&drain[1], 0);
+    }
+  } else if (warp < 10) {
+    // ------------------------------------------------------------------- softmax ----
+    const int grp = (warp - 2) >> 2, q4 = warp & 3, tid = (threadIdx.x - 64) & 127;
+    const int t0 = 32 * q4 + lane, t1 = t0 + 128;
+    float *red_s = red + grp * 64, *red_w = red_s + 32;
+    int k = 0;
+    for (UnitIter it(blockIdx.x, gridDim.x, P, Hkv); it.b < B; it.next()) {
+      const int p = it.p, g = it.g, b = it.b;
+      const int n = ctx[b], lo = p * kPart;
+      if (lo >= n) continue;
+      if ((k & 1) != grp) {
+        ++k;
+        continue;
+      }
+      const int s = k % kStages, t = k & 1;
+      bool ok = mbar_wait(&full[s], (k / kStages) & 1, abort_flag, ws.status) &&
+                mbar_wait(&sfull[t], (k >> 1) & 1, abort_flag, ws.status) &&
+                (k < 2 || mbar_wait(&oempty[t], ((k >> 1) - 1) & 1, abort_flag, ws.status));
+      if (group_any(1 + grp, 128, !ok || *abort_flag)) break;
+      const int cnt = min(kPart, n - lo);
+      tc_fence_after();
+      uint32_t a0[16], a1[16];
+      tmem_ld16(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + 32 * t, a0);
+      tmem_ld16(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + 32 * t + 16, a1);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sempty[t]);
+      uint8_t *st = sm + s * kStage;
+      const float *ksc = reinterpret_cast<const float *>(st + kOffKs);
+      const float *vsc = reinterpret_cast<const float *>(st + kOffVs);
+      const float *qsv = reinterpret_cast<const float *>(st + kOffQs);
+      const float ks0 = ksc[t0], ks1 = ksc[t1], vs0 = vsc[t0], vs1 = vsc[t1];
+      // canonical token index of shared-memory rows t0 and t1 (blocks reversed: see producers)
+      const bool rev = st[kOffMode] != 0;
+      const int nbu = kPart >> bs_log2;
+      const int et0 = rev ? (((nbu - 1 - (t0 >> bs_log2)) << bs_log2) | (t0 & (bs - 1))) : t0;
+      const int et1 = rev ? (((nbu - 1 - (t1 >> bs_log2)) << bs_log2) | (t1 & (bs - 1))) : t1;
+      float s0[G], s1[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float qsc = __fmul_rn(qsv[h], scale);
+        s0[h] = t0 < cnt ? __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(a0[h])), qsc), ks0)
+                         : -__int_as_float(0x7f800000);
+        s1[h] = t1 < cnt ? __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(a1[h])), qsc), ks1)
+                         : -__int_as_float(0x7f800000);
+      }
+      // The reductions below are latency chains on the stage's critical path: one redux per
+      // head, all heads issued back to back.
+      float red[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h) red[h] = warp_max_redux(fmaxf(s0[h], s1[h]));
+      if (lane == 0) {
+#pragma unroll
+        for (int h = 0; h < G; ++h) red_s[q4 * 8 + h] = red[h];
+      }
+      group_sync(1 + grp, 128);
+      // Loads, then arithmetic, then stores: a store into E may alias the reductions' shared
+      // memory as far as the compiler knows, so interleaving them would chain the heads' exp
+      // latencies one after another.
+      float *E = reinterpret_cast<float *>(st + kOffE);
+      float w0[G], w1[G], mh[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h)
+        mh[h] = fmaxf(fmaxf(red_s[h], red_s[8 + h]), fmaxf(red_s[16 + h], red_s[24 + h]));
+      // All 2G exponentials unconditionally (a conditional call puts each ~400-cycle chain
+      // behind its own branch; unconditional, they overlap). A masked token's score is -inf,
+      // so its exp is 0 either way; the select below keeps the CUDA-core kernel's form.
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        w0[h] = exp_s8b(__fsub_rn(s0[h], mh[h]));  // e, until stored
+        w1[h] = exp_s8b(__fsub_rn(s1[h], mh[h]));
+      }
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        w0[h] = t0 < cnt ? w0[h] : 0.0f;
+        w1[h] = t1 < cnt ? w1[h] : 0.0f;
+        E[h * kPart + et0] = w0[h];
+        E[h * kPart + et1] = w1[h];
+        w0[h] = t0 < cnt ? __fmul_rn(w0[h], vs0) : 0.0f;
+        w1[h] = t1 < cnt ? __fmul_rn(w1[h], vs1) : 0.0f;
+      }
+#pragma unroll
+      for (int h = 0; h < G; ++h) red[h] = warp_max_redux(fmaxf(w0[h], w1[h]));
+      if (lane == 0) {
+#pragma unroll
+        for (int h = 0; h < G; ++h) red_w[q4 * 8 + h] = red[h];
+      }
+      group_sync(1 + grp, 128);
+      float wm[G];  // per-head weight maxima; their /32767 scales wait until after wfull
+      int qa[G], qb[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h)
+        wm[h] = fmaxf(fmaxf(red_w[h], red_w[8 + h]), fmaxf(red_w[16 + h], red_w[24 + h]));
+      // 32767 / wm: one correctly rounded division per lane (lane h takes head h), shuffled to
+      // the warp, instead of G divisions in a row in every thread.
+      float wl = 1.0f;
+#pragma unroll
+      for (int h = 0; h < G; ++h) wl = lane == h ? wm[h] : wl;
+      const float winv_l = __fdiv_rn(32767.0f, wl);
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float winv = __shfl_sync(0xffffffffu, winv_l, h);
+        const int q0 = __float2int_rn(__fmul_rn(w0[h], winv));
+        const int q1 = __float2int_rn(__fmul_rn(w1[h], winv));
+        qa[h] = t0 < cnt ? (q0 < 0 ? 0 : (q0 > 32767 ? 32767 : q0)) : 0;
+        qb[h] = t1 < cnt ? (q1 < 0 ? 0 : (q1 > 32767 ? 32767 : q1)) : 0;
+      }
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const int q0 = qa[h], q1 = qb[h];
+        // rows 16*plane + h of the K-major SW128 weight operand; t0 lies in token block 0 and
+        // t1 in block 1 at the same in-block position
+        const int off = h * 128 + ((((t0 >> 4) ^ (h & 7))) << 4) + (t0 & 15);
+        st[off] = static_cast<uint8_t>(q0 >> 14);
+        st[2048 + off] = static_cast<uint8_t>((q0 >> 7) & 127);
+        st[4096 + off] = static_cast<uint8_t>(q0 & 127);
+        st[kWBlock + off] = static_cast<uint8_t>(q1 >> 14);
+        st[kWBlock + 2048 + off] = static_cast<uint8_t>((q1 >> 7) & 127);
+        st[kWBlock + 4096 + off] = static_cast<uint8_t>(q1 & 127);
+      }
+      fence_proxy_async_smem();
+      group_sync(1 + grp, 128);
+      if (tid == 0) mbar_arrive(&wfull[s]);
+      float *st_t = stats + t * 24;
+#pragma unroll
+      for (int h = 0; h < G; ++h) {  // denominators, lane order of the CUDA-core kernel
+        if ((h & 3) != q4) continue;  // warp q4 takes heads q4, q4 + 4
+        const float *e = E + h * kPart;
+        float l = e[lane];
+#pragma unroll
+        for (int i = 1; i < kPart / 32; ++i) l = __fadd_rn(l, e[i * 32 + lane]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, o));
+        if (lane == 0) {
+          st_t[h] = mh[h];
+          st_t[8 + h] = l;
+          st_t[16 + h] = __fdiv_rn(wm[h], 32767.0f);
+        }
+      }
+      group_sync(1 + grp, 128);
+      if (tid == 0) {
+        mbar_arrive(&empty[s]);
+        mbar_arrive(&ofull[t]);
+      }
+      ++k;
+    }
+  } else if (warp < 14) {
+    // ------------------------------------------------------------------ epilogue ----
+    const int q4 = warp & 3, tid = threadIdx.x - 320;
+    const int d = 32 * q4 + lane;
+    int k = 0;
+    for (UnitIter it(blockIdx.x, gridDim.x, P, Hkv); it.b < B; it.next()) {
+      const int p = it.p, g = it.g, b = it.b;
+      const int n = ctx[b], lo = p * kPart;
+      if (lo >= n) continue;
+      const int t = k & 1;
+      const bool ok = mbar_wait(&ofull[t], (k >> 1) & 1, abort_flag, ws.status);
+      if (group_any(3, 128, !ok || *abort_flag)) break;
+      tc_fence_after();
+      uint32_t da[16], db[16], dc[16];
+      const uint32_t lanes = static_cast<uint32_t>(q4 * 32) << 16;
+      tmem_ld16(tmem + lanes + kColO + 48 * t, da);
+      tmem_ld16(tmem + lanes + kColO + 48 * t + 16, db);
+      tmem_ld16(tmem + lanes + kColO + 48 * t + 32, dc);
+      tmem_wait_ld();
+      const float *st_t = stats + t * 24;
+      float wsc_h[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h) wsc_h[h] = st_t[16 + h];
+      float ml0 = 0.0f, ml1 = 0.0f;
+      if (tid < G) {
+        ml0 = st_t[tid];
+        ml1 = st_t[8 + tid];
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&oempty[t]);
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const int o = static_cast<int32_t>(da[h]) * 16384 + static_cast<int32_t>(db[h]) * 128 +
+                      static_cast<int32_t>(dc[h]);
+        const size_t hq = static_cast<size_t>(b) * Hq + g * G + h;
+        ws.part_o[(hq * P + p) * kHd + d] = __fmul_rn(static_cast<float>(o), wsc_h[h]);
+      }
+      if (tid < G) {
+        const size_t hq = static_cast<size_t>(b) * Hq + g * G + tid;
+        ws.part_ml[(hq * P + p) * 2 + 0] = ml0;
+        ws.part_ml[(hq * P + p) * 2 + 1] = ml1;
+      }
+      ++k;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols) : "memory");
+}
+
+
 // Merge of the persistent kernel's partials, one CTA per row: per head M = max m_p,
 // w_p = exp(m_p - M), L = sum w_p l_p, O = sum w_p o_p (partition order), out = dtype(O / L),
 // then the row's int8 quantization for o_proj. Same arithmetic as merge_epilogue. The kernel
@@ -1608,9 +2032,10 @@ int launch_persistent(const int8_t *q_i8, const float *q_s, const int8_t *kc, co
   const long U = static_cast<long>(NB) * Hkv * P;
   const int grid = static_cast<int>(U < tc::sm_count() ? U : tc::sm_count());
   // The early loads shorten a decode step's start, but the kernel that carries them streams
-  // its steady state a little slower (measured 6% at 112 units per CTA, 27B at 16K context):
-  // they pay off only while a CTA has few units to stream.
-  const bool early_ok = early && U <= 48L * grid;
+  // its steady state slower than attn_persistent_stream_kernel: they pay off only while a CTA
+  // has few units to stream (batch 16: 3.25 against 3.31 ms per step; batch 64, 31 units per
+  // CTA: 4.98 against 4.95 ms).
+  const bool early_ok = early && U <= 16L * grid;
   switch (G) {
 #define S8B_PK_CASE(GG)                                                                        \
   case GG: {                                                                                   \
@@ -1621,12 +2046,25 @@ int launch_persistent(const int8_t *q_i8, const float *q_s, const int8_t *kc, co
                  ks, vs, block_table, context_lens, B, Hq, Hkv, bs_log2, max_blocks, P, scale,  \
                  w, 0, q_i8, row_blocks, NB);                                                   \
     } else {                                                                                   \
-      auto kern = early_ok ? attn_persistent_kernel<T, GG, 1, true>                             \
-                           : attn_persistent_kernel<T, GG, 1, false>;                           \
-      ensure_smem(reinterpret_cast<const void *>(kern), pk::kSmem);                             \
-      launch_pdl(kern, grid, pk::kThreads, pk::kSmem, st, mk, mv, mq, mk4, mv4, runs, q_s, ks,  \
-                 vs, block_table, context_lens, B, Hq, Hkv, bs_log2, max_blocks, P, scale, w,   \
-                 early_ok ? 1 : 0, q_i8, row_blocks, NB);                                       \
+      if (early_ok) {                                                                          \
+        auto kern = attn_persistent_kernel<T, GG, 1, true>;                                     \
+        ensure_smem(reinterpret_cast<const void *>(kern), pk::kSmem);                           \
+        launch_pdl(kern, grid, pk::kThreads, pk::kSmem, st, mk, mv, mq, mk4, mv4, runs, q_s,    \
+                   ks, vs, block_table, context_lens, B, Hq, Hkv, bs_log2, max_blocks, P,       \
+                   scale, w, 1, q_i8, row_blocks, NB);                                          \
+      } else if (GG <= 5) {                                                                    \
+        auto kern = attn_persistent_stream_kernel<T, GG>;                                       \
+        ensure_smem(reinterpret_cast<const void *>(kern), pk::kSmem);                           \
+        launch_pdl(kern, grid, pk::kThreads, pk::kSmem, st, mk, mv, mq, mk4, mv4, runs, q_s,    \
+                   ks, vs, block_table, context_lens, B, Hq, Hkv, bs_log2, max_blocks, P,       \
+                   scale, w);                                                                   \
+      } else {                                                                                 \
+        auto kern = attn_persistent_kernel<T, GG, 1, false>;                                    \
+        ensure_smem(reinterpret_cast<const void *>(kern), pk::kSmem);                           \
+        launch_pdl(kern, grid, pk::kThreads, pk::kSmem, st, mk, mv, mq, mk4, mv4, runs, q_s,    \
+                   ks, vs, block_table, context_lens, B, Hq, Hkv, bs_log2, max_blocks, P,       \
+                   scale, w, 0, q_i8, row_blocks, NB);                                          \
+      }                                                                                        \
     }                                                                                          \
     break;                                                                                     \
   }
