@@ -643,6 +643,10 @@ def run_bench_multi(args, metric, step_bytes, peaks, ClockSampler, cpu_sample):
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         time.sleep(0.3)
+        # every rank's clock sampler is up (their start-up times differ by tens of ms): line
+        # the ranks up again so that no rank's timed region includes another's late start
+        dist.barrier()
+        torch.cuda.synchronize()
         a.record()
         for _ in range(args.steps):
             pipe.step()
