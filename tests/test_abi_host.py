@@ -237,3 +237,16 @@ def test_wire_scheme_gate_logic_matches_reference(host_golden, monkeypatch, kind
         want_sq, want_cos = g[scheme]
         assert sq == (float("inf") if want_sq == "inf" else pytest.approx(want_sq, rel=1e-6))
         assert cos == pytest.approx(want_cos, rel=1e-6)
+
+
+def test_nf4_sizes_and_prefill_block_rows(lib):
+    """Host-side answers of the library: nf4 weighs what int4 weighs (4-bit codes, one fp32
+    scale per 128 values); prefill row blocks hold 16 / G rows (the tile's 16 columns)."""
+    assert lib.s8b_codec_payload_bytes(4, 8192, 5, 0) == 4 * 4096
+    assert lib.s8b_codec_scale_count(4, 8192, 5) == 4 * 64
+    for Hq, Hkv in ((32, 8), (40, 8), (32, 4), (8, 8), (16, 8), (24, 8), (12, 2), (21, 3)):
+        assert lib.s8b_paged_prefill_block_rows(Hq, Hkv) == 16 // (Hq // Hkv)
+    assert lib.s8b_paged_prefill_block_rows(36, 4) == -1   # G = 9: more heads than a tile row
+    assert lib.s8b_paged_prefill_block_rows(30, 8) == -1   # Hq not a multiple of Hkv
+    buf = 1
+    assert lib.s8b_codec_encode(buf, None, 1, 128, 0, 6, buf, buf, 0, None) == -2  # past nf4
